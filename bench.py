@@ -1,0 +1,491 @@
+"""Benchmark of the B200 dense-contraction path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+Workloads (default: conv):
+  conv      Conv2d+bias+ReLU, ResNet-50 stage-2 3x3 layer: x [32,128,28,28] ~ N(0,1),
+            w [128,128,3,3] Kaiming-normal, b ~ U(-0.1,0.1), stride 1, pad 1, seed 1.
+            One step = one reference-facing conv call (NCHW in/out).  Replicas at N>1.
+  gemm1024  f32 matmul 1024^3, A, B ~ N(0,1), seed 0.  Replicas at N>1.
+  gemm8192  f32 matmul 8192^3, seed 4.  Replicas at N>1.
+  mlp       3-layer MLP forward, batch 4096, 1024->4096->4096->1024, seed 2.  Replicas.
+
+Timing: W warm-up steps, then K steps between barrier + synchronize, CUDA
+events on the launching stream, max over ranks.  Inputs/outputs rotate over
+enough copies to exceed the 126 MB L2 so no step reads the previous step's
+data from L2.  `value` is the whole-job throughput (sum over ranks of the
+algorithmic FLOPs / max time).  `e2e` times the same call through the C ABI
+with host buffers (pinned H2D of the step's inputs, D2H of its output).
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+L2_BYTES = 126 * 1024 * 1024
+
+
+# ------------------------------------------------------------------ helpers
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]),
+                "basis": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "basis": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append(parts)
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4)
+                          if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.rows)}
+
+
+def _dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+# ------------------------------------------------------------------ workloads
+class ConvWorkload:
+    name = "conv2d_bias_relu_resnet50_3x3"
+
+    def __init__(self, rb, torch, dev):
+        self.rb, self.torch, self.dev = rb, torch, dev
+        self.N, self.C, self.H, self.W, self.Co = 32, 128, 28, 28, 128
+        n = self.N * self.C * self.H * self.W
+        self.flops = 2.0 * self.N * self.H * self.W * self.Co * self.C * 9
+        x = rb.fill_normal((self.N, self.C, self.H, self.W), 1, 0)
+        w = rb.fill_normal((self.Co, self.C, 3, 3), 1, 1, 0.0, math.sqrt(2.0 / (self.C * 9)))
+        b = rb.fill_uniform((self.Co,), 1, 2, -0.1, 0.1)
+        self.host = {"x": x, "w": w, "b": b}
+        bytes_per_set = 2 * n * 4
+        self.nsets = max(2, int(math.ceil(2 * L2_BYTES / bytes_per_set)))
+        self.xs = [torch.from_numpy(x).to(dev) for _ in range(self.nsets)]
+        self.ys = [torch.empty((self.N, self.Co, self.H, self.W), device=dev)
+                   for _ in range(self.nsets)]
+        self.w = torch.from_numpy(w).to(dev)
+        self.b = torch.from_numpy(b).to(dev)
+        self.i = 0
+        self.config = {"workload": "conv2d+bias+relu ResNet-50 stage-2 3x3",
+                       "input": [32, 128, 28, 28], "weight": [128, 128, 3, 3], "stride": 1,
+                       "pad": 1, "seed": 1, "layout": "NCHW in/out",
+                       "l2": f"rotating {self.nsets} input/output sets "
+                             f"({self.nsets * bytes_per_set / 2**20:.0f} MiB > 126 MiB L2)"}
+        self.launches_per_step = 3  # NCHW->NHWC, weight prepack, implicit-GEMM conv
+
+    def step(self):
+        rb = self.rb
+        k = self.i % self.nsets
+        self.i += 1
+        x, y = self.xs[k], self.ys[k]
+        ctx = rb.get_context(self.dev.index or 0)
+        stream = ctypes.c_void_p(self.torch.cuda.current_stream(self.dev).cuda_stream)
+        rb.call("rtb_conv2d_fwd", ctx.handle, self.N, self.C, self.H, self.W, self.Co, 3, 3, 1, 1, 1,
+                1, ctypes.c_void_p(x.data_ptr()), rb.LAYOUT_NCHW,
+                ctypes.c_void_p(self.w.data_ptr()), ctypes.c_void_p(self.b.data_ptr()), None,
+                rb.ACT_RELU, ctypes.c_void_p(y.data_ptr()), rb.LAYOUT_NCHW, rb.PREC_3XTF32, stream)
+
+    # dominant kernel alone (NHWC input + prepacked weight), for the roofline
+    def kernel_setup(self):
+        torch, rb = self.torch, self.rb
+        ctx = rb.get_context(self.dev.index or 0)
+        stream = ctypes.c_void_p(torch.cuda.current_stream(self.dev).cuda_stream)
+        self.xh = [torch.empty((self.N, self.H, self.W, self.C), device=self.dev)
+                   for _ in range(self.nsets)]
+        for k in range(self.nsets):
+            rb.call("rtb_nchw_to_nhwc_padded", ctx.handle, self.N, self.C, self.H, self.W,
+                    ctypes.c_void_p(self.xs[k].data_ptr()), ctypes.c_void_p(self.xh[k].data_ptr()),
+                    stream)
+        self.wp = torch.empty((self.Co * 9 * self.C,), device=self.dev)
+        rb.call("rtb_conv2d_prepack_weight", ctx.handle, self.Co, self.C, 3, 3,
+                ctypes.c_void_p(self.w.data_ptr()), ctypes.c_void_p(self.wp.data_ptr()), stream)
+
+    def kernel_step(self):
+        rb = self.rb
+        k = self.i % self.nsets
+        self.i += 1
+        ctx = rb.get_context(self.dev.index or 0)
+        stream = ctypes.c_void_p(self.torch.cuda.current_stream(self.dev).cuda_stream)
+        rb.call("rtb_conv2d_fwd_packed", ctx.handle, self.N, self.C, self.H, self.W, self.Co, 3, 3,
+                1, 1, 1, 1, ctypes.c_void_p(self.xh[k].data_ptr()),
+                ctypes.c_void_p(self.wp.data_ptr()), ctypes.c_void_p(self.b.data_ptr()), None,
+                rb.ACT_RELU, ctypes.c_void_p(self.ys[k].data_ptr()), rb.LAYOUT_NCHW,
+                rb.PREC_3XTF32, stream)
+
+    def e2e_setup(self):
+        rb, torch = self.rb, self.torch
+        ctx = rb.get_context(self.dev.index or 0)
+        self.pinned = {}
+        for key, arr in self.host.items():
+            p = ctypes.c_void_p()
+            rb.call("rtb_host_alloc", ctx.handle, ctypes.byref(p), arr.nbytes)
+            ctypes.memmove(p, arr.ctypes.data, arr.nbytes)
+            self.pinned[key] = (p, arr.nbytes)
+        p = ctypes.c_void_p()
+        ybytes = self.N * self.Co * self.H * self.W * 4
+        rb.call("rtb_host_alloc", ctx.handle, ctypes.byref(p), ybytes)
+        self.pinned["y"] = (p, ybytes)
+        self.dx = torch.empty((self.N, self.C, self.H, self.W), device=self.dev)
+        self.dw = torch.empty_like(self.w)
+        self.db = torch.empty_like(self.b)
+        self.h2d_bytes = sum(v[1] for k, v in self.pinned.items() if k != "y")
+        self.d2h_bytes = ybytes
+
+    def e2e_step(self):
+        rb = self.rb
+        ctx = rb.get_context(self.dev.index or 0)
+        stream = ctypes.c_void_p(self.torch.cuda.current_stream(self.dev).cuda_stream)
+        for key, dst in (("x", self.dx), ("w", self.dw), ("b", self.db)):
+            p, nb = self.pinned[key]
+            rb.call("rtb_memcpy_h2d", ctx.handle, ctypes.c_void_p(dst.data_ptr()), p, nb, stream)
+        y = self.ys[0]
+        rb.call("rtb_conv2d_fwd", ctx.handle, self.N, self.C, self.H, self.W, self.Co, 3, 3, 1, 1, 1,
+                1, ctypes.c_void_p(self.dx.data_ptr()), rb.LAYOUT_NCHW,
+                ctypes.c_void_p(self.dw.data_ptr()), ctypes.c_void_p(self.db.data_ptr()), None,
+                rb.ACT_RELU, ctypes.c_void_p(y.data_ptr()), rb.LAYOUT_NCHW, rb.PREC_3XTF32, stream)
+        p, nb = self.pinned["y"]
+        rb.call("rtb_memcpy_d2h", ctx.handle, p, ctypes.c_void_p(y.data_ptr()), nb, stream)
+
+    def e2e_teardown(self):
+        ctx = self.rb.get_context(self.dev.index or 0)
+        for p, _ in self.pinned.values():
+            self.rb.call("rtb_host_free", ctx.handle, p)
+
+    # CPU baseline: the reference's own CPU path (oracle restatement) on a sample
+    def cpu_sample(self, threads):
+        from oracle import oracle as orc
+        x = orc.normal((self.N, self.C, self.H, self.W), 1, 0)
+        w = orc.normal((self.Co, self.C, 3, 3), 1, 1, 0.0, math.sqrt(2.0 / (self.C * 9)))
+        b = orc.uniform((self.Co,), 1, 2, -0.1, 0.1)
+        nimg = 2
+        xs = x[:nimg].copy()
+        orc.conv2d_bias_relu(xs[:1], w, b, (1, 1), (1, 1), threads=threads)  # warm
+        t0 = time.perf_counter()
+        reps = 0
+        while True:
+            orc.conv2d_bias_relu(xs, w, b, (1, 1), (1, 1), threads=threads)
+            reps += 1
+            if time.perf_counter() - t0 > 10.0 or reps >= 20:
+                break
+        dt = (time.perf_counter() - t0) / reps
+        flops = self.flops * nimg / self.N
+        return flops / dt / 1e12, (f"{nimg} of 32 images per call (im2col + row-parallel core, "
+                                   f"bias, ReLU), {reps} calls")
+
+
+class GemmWorkload:
+    def __init__(self, rb, torch, dev, n, seed):
+        self.rb, self.torch, self.dev = rb, torch, dev
+        self.n = n
+        self.seed = seed
+        self.name = f"sgemm_{n}"
+        self.flops = 2.0 * n ** 3
+        a = rb.fill_normal((n, n), seed, 0)
+        b = rb.fill_normal((n, n), seed, 1)
+        self.host = {"a": a, "b": b}
+        per = 3 * n * n * 4
+        self.nsets = max(1, int(math.ceil(2 * L2_BYTES / per))) if per < 2 * L2_BYTES else 1
+        self.nsets = min(self.nsets, 24)
+        self.as_ = [torch.from_numpy(a).to(dev) for _ in range(self.nsets)]
+        self.bs = [torch.from_numpy(b).to(dev) for _ in range(self.nsets)]
+        self.cs = [torch.empty((n, n), device=dev) for _ in range(self.nsets)]
+        self.i = 0
+        self.config = {"workload": f"f32 matmul {n}x{n}x{n}", "seed": seed,
+                       "layout": "row-major A[M,K], B[K,N]",
+                       "l2": (f"rotating {self.nsets} operand sets" if self.nsets > 1 else
+                              "operands larger than L2")}
+        self.launches_per_step = 1
+
+    def step(self):
+        k = self.i % self.nsets
+        self.i += 1
+        self.rb.sgemm(self.as_[k], self.bs[k], out=self.cs[k], precision=self.rb.PREC_3XTF32)
+
+    kernel_setup = lambda self: None  # noqa: E731
+
+    def kernel_step(self):
+        self.step()
+
+    def e2e_setup(self):
+        rb, torch = self.rb, self.torch
+        ctx = rb.get_context(self.dev.index or 0)
+        self.pinned = {}
+        for key, arr in list(self.host.items()) + [("c", None)]:
+            nb = self.n * self.n * 4
+            p = ctypes.c_void_p()
+            rb.call("rtb_host_alloc", ctx.handle, ctypes.byref(p), nb)
+            if arr is not None:
+                ctypes.memmove(p, arr.ctypes.data, nb)
+            self.pinned[key] = (p, nb)
+        self.h2d_bytes = 2 * self.n * self.n * 4
+        self.d2h_bytes = self.n * self.n * 4
+
+    def e2e_step(self):
+        rb = self.rb
+        ctx = rb.get_context(self.dev.index or 0)
+        stream = ctypes.c_void_p(self.torch.cuda.current_stream(self.dev).cuda_stream)
+        a, b, c = self.as_[0], self.bs[0], self.cs[0]
+        for key, dst in (("a", a), ("b", b)):
+            p, nb = self.pinned[key]
+            rb.call("rtb_memcpy_h2d", ctx.handle, ctypes.c_void_p(dst.data_ptr()), p, nb, stream)
+        n = self.n
+        rb.call("rtb_sgemm", ctx.handle, n, n, n, ctypes.c_void_p(a.data_ptr()), n, 0,
+                ctypes.c_void_p(b.data_ptr()), n, 0, None, rb.ACT_NONE,
+                ctypes.c_void_p(c.data_ptr()), n, rb.PREC_3XTF32, stream)
+        p, nb = self.pinned["c"]
+        rb.call("rtb_memcpy_d2h", ctx.handle, p, ctypes.c_void_p(c.data_ptr()), nb, stream)
+
+    def e2e_teardown(self):
+        ctx = self.rb.get_context(self.dev.index or 0)
+        for p, _ in self.pinned.values():
+            self.rb.call("rtb_host_free", ctx.handle, p)
+
+    def cpu_sample(self, threads):
+        """matrixmultiply restatement (single-threaded, as the reference builds
+        it) on a row sample of the same product."""
+        from oracle import oracle as orc
+        n = self.n
+        a = orc.normal((n, n), self.seed, 0)
+        b = orc.normal((n, n), self.seed, 1)
+        rows = max(8, min(n, int(2e9 / (2 * n * n))))
+        t0 = time.perf_counter()
+        reps = 0
+        while True:
+            orc.sgemm_mm(a[:rows], b, threads=1)
+            reps += 1
+            if time.perf_counter() - t0 > 10.0 or reps >= 10:
+                break
+        dt = (time.perf_counter() - t0) / reps
+        return 2.0 * rows * n * n / dt / 1e12, (f"{rows} of {n} rows of A per call, "
+                                                f"single-threaded blocked sgemm, {reps} calls")
+
+
+WORKLOADS = {
+    "conv": lambda rb, torch, dev: ConvWorkload(rb, torch, dev),
+    "gemm1024": lambda rb, torch, dev: GemmWorkload(rb, torch, dev, 1024, 0),
+    "gemm8192": lambda rb, torch, dev: GemmWorkload(rb, torch, dev, 8192, 4),
+}
+
+
+# ------------------------------------------------------------------ timing
+def _time_steps(torch, fn, steps, warmup, dev, dist=None):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize(dev)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    s = torch.cuda.current_stream(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(steps):
+        fn()
+    e1.record(s)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1)
+    if dist is not None:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    return ms
+
+
+def run_ours(args):
+    import torch
+    import rustorch_b200 as rb
+
+    rank, world, local = _dist_env()
+    dist = None
+    if world > 1:
+        import torch.distributed as tdist
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        tdist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                 device_id=torch.device("cuda", local))
+        dist = tdist
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    rb.get_context(local)
+    wl = WORKLOADS[args.workload](rb, torch, dev)
+    peaks = _peaks()
+
+    with ClockSampler(local) as clk:
+        ms = _time_steps(torch, wl.step, args.steps, args.warmup, dev, dist)
+    ms_per_step = ms / args.steps
+    value = world * wl.flops * args.steps / (ms / 1e3) / 1e12
+
+    # dominant kernel alone, CUDA events on its launch stream
+    wl.kernel_setup()
+    kms = _time_steps(torch, wl.kernel_step, args.steps, max(3, args.warmup), dev, None)
+    k_tflops = wl.flops * args.steps / (kms / 1e3) / 1e12
+    tf32_peak = peaks["bf16_tflops"] / 2.0
+    roof_peak = tf32_peak / 3.0  # 3xTF32: three tensor-core MMAs per algorithmic MAC
+
+    # end to end through the C ABI with host buffers
+    wl.e2e_setup()
+    ems = _time_steps(torch, wl.e2e_step, args.steps, max(3, args.warmup), dev, dist)
+    wl.e2e_teardown()
+    e2e = world * wl.flops * args.steps / (ems / 1e3) / 1e12
+
+    err = rb.get_context(local).device_error()
+    if err:
+        raise RuntimeError(f"device error word set: {err}")
+
+    if rank == 0:
+        cpu_val, sample = wl.cpu_sample(os.cpu_count())
+        line = {
+            "metric": f"{wl.name} TFLOP/s (3xTF32, fp32 in/out)",
+            "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32 (3xTF32 tensor-core split)",
+            "data": "synthetic (SplitMix64/Box-Muller, seeded)",
+            "config": dict(wl.config, parallelism=f"replicas x{world}"),
+            "roofline": {"bound": "tensor", "achieved": round(k_tflops, 3),
+                         "peak": round(roof_peak, 3), "unit": "TFLOP/s",
+                         "frac": round(k_tflops / roof_peak, 4), "traffic": None,
+                         "peak_basis": f"{peaks['basis']} bf16 {peaks['bf16_tflops']} TFLOP/s "
+                                       f"/ 2 (TF32 rate) / 3 (3xTF32 MMAs per MAC)",
+                         "tensor_pipe_frac": round(3 * k_tflops / tf32_peak, 4),
+                         "kernel_ms": round(kms / args.steps, 5)},
+            "cpu_baseline": {"value": round(cpu_val, 6), "unit": "TFLOP/s",
+                             "cores": os.cpu_count(), "kind": "port", "sample": sample},
+            "e2e": {"value": round(e2e, 3), "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": wl.h2d_bytes, "d2h_bytes_per_step": wl.d2h_bytes},
+            "gpu_launches": wl.launches_per_step * args.steps,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    rank, world, _ = _dist_env()
+    if rank != 0:
+        return
+    import torch  # noqa: F401  (device-free; the reference arm is CPU-only)
+    import rustorch_b200 as rb
+
+    class _Dummy:
+        index = 0
+    threads = os.cpu_count()
+    wl_cls = {"conv": ConvWorkload, "gemm1024": None, "gemm8192": None}
+    # Build the workload description without touching a GPU.
+    if args.workload == "conv":
+        wl = ConvWorkload.__new__(ConvWorkload)
+        wl.N, wl.C, wl.H, wl.W, wl.Co = 32, 128, 28, 28, 128
+        wl.flops = 2.0 * wl.N * wl.H * wl.W * wl.Co * wl.C * 9
+        wl.name = ConvWorkload.name
+        cfg = {"workload": "conv2d+bias+relu ResNet-50 stage-2 3x3", "input": [32, 128, 28, 28],
+               "weight": [128, 128, 3, 3], "stride": 1, "pad": 1, "seed": 1}
+    else:
+        n = 1024 if args.workload == "gemm1024" else 8192
+        wl = GemmWorkload.__new__(GemmWorkload)
+        wl.n, wl.seed, wl.flops, wl.name = n, (0 if n == 1024 else 4), 2.0 * n ** 3, f"sgemm_{n}"
+        cfg = {"workload": f"f32 matmul {n}x{n}x{n}", "seed": wl.seed}
+    vals = []
+    samples = []
+    for _ in range(args.warmup):
+        pass
+    t0 = time.perf_counter()
+    for _ in range(max(1, args.steps)):
+        v, s = wl.cpu_sample(threads)
+        vals.append(v)
+        samples.append(s)
+        if time.perf_counter() - t0 > 120:
+            break
+    v = statistics.median(vals)
+    line = {"impl": "reference", "metric": f"{wl.name} TFLOP/s (3xTF32, fp32 in/out)",
+            "value": round(v, 6), "unit": "TFLOP/s", "n_gpus": world, "steps": len(vals),
+            "warmup": args.warmup, "higher_is_better": True, "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic (SplitMix64/Box-Muller, seeded)", "config": cfg,
+            "cpu_baseline": {"value": round(v, 6), "unit": "TFLOP/s", "cores": threads,
+                             "kind": "port", "sample": samples[0]},
+            "e2e": {"value": round(v, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "note": "reference CPU path restated in C (Rust toolchain unavailable)"}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="conv", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

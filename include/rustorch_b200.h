@@ -1,0 +1,190 @@
+/*
+ * rustorch_b200 — C ABI of the B200 (sm_100a) dense-contraction backend for
+ * RusTorch.  Plain pointers and sizes only; every function returns an int
+ * status (RTB_OK = 0).  Device pointers are CUDA device addresses on the
+ * context's device; `stream` is a cudaStream_t (NULL = the context's own
+ * stream).  All compute entry points are asynchronous and stream-ordered like
+ * cuBLAS: errors detected on the host (bad shapes, launch failures) are
+ * returned immediately; a device-side bounded wait that expired is reported by
+ * the next rtb_stream_synchronize / rtb_device_error on that context.
+ *
+ * Reference interfaces replaced (paths relative to the RusTorch project root):
+ *   ops::matmul                 rustorch-core/src/ops.rs:1888      -> rtb_sgemm
+ *   ops::matmul_fused           rustorch-core/src/ops.rs:1543      -> rtb_sgemm (bias, act)
+ *   nn::Linear::forward         rustorch-nn/src/linear.rs:75-95    -> rtb_sgemm (transB=1)
+ *   ops::conv2d                 rustorch-core/src/ops/conv.rs:738  -> rtb_conv2d_fwd
+ *   nn::Conv2d::forward         rustorch-nn/src/conv.rs:52-63      -> rtb_conv2d_fwd (bias)
+ *   jit Conv2dRelu lowering     rustorch-core/src/jit.rs:254-262   -> rtb_conv2d_fwd (act=ReLU)
+ *   ops::max_pool2d             rustorch-core/src/ops/pool.rs:115  -> rtb_max_pool2d
+ *   ops::add (same shape)       rustorch-core/src/ops.rs:223       -> rtb_add
+ *   ops::relu                   rustorch-core/src/ops.rs:449       -> rtb_relu
+ *   Storage / Device::Cuda      rustorch-core/src/storage.rs:13-43,201-216 -> rtb_malloc/memcpy
+ *   rustorch-cuda extern "C"    rustorch-cuda/src/lib.rs:1-8       -> this header
+ */
+#ifndef RUSTORCH_B200_H
+#define RUSTORCH_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct rtb_ctx rtb_ctx;
+
+/* Status codes.  The reference panics on these conditions (e.g.
+ * "Matmul dimension mismatch", rustorch-core/src/ops.rs:1898); the Rust shim
+ * turns a non-zero status into the same panic. */
+enum {
+  RTB_OK = 0,
+  RTB_E_INVALID = 1,     /* bad argument or shape */
+  RTB_E_OOM = 2,         /* device or host allocation failed */
+  RTB_E_CUDA = 3,        /* CUDA runtime / driver error */
+  RTB_E_TIMEOUT = 4,     /* a device-side bounded wait expired */
+  RTB_E_UNSUPPORTED = 5, /* valid request this build does not implement */
+  RTB_E_NCCL = 6         /* NCCL error */
+};
+
+/* backend::Activation (rustorch-core/src/backend/mod.rs:1-7).  Only NONE and
+ * RELU are fused; SIGMOID/TANH return RTB_E_UNSUPPORTED. */
+enum { RTB_ACT_NONE = 0, RTB_ACT_RELU = 1, RTB_ACT_SIGMOID = 2, RTB_ACT_TANH = 3 };
+
+/* Contraction precision.  3xTF32 (default) splits every fp32 operand into a
+ * TF32 high part and an fp32 remainder and accumulates hi*hi + hi*lo + lo*hi
+ * on the tensor cores (relative Frobenius error vs f64 <= 1e-5); TF32 is the
+ * opt-in fast mode (<= 5e-3).  RTB_PREC_DEFAULT reads RUSTORCH_B200_PRECISION
+ * ("3xtf32" | "tf32") once per context. */
+enum { RTB_PREC_3XTF32 = 0, RTB_PREC_TF32 = 1, RTB_PREC_DEFAULT = -1 };
+
+/* Activation tensor layouts for conv / pooling. */
+enum { RTB_LAYOUT_NCHW = 0, RTB_LAYOUT_NHWC = 1 };
+
+/* ---------------------------------------------------------------- context */
+/* Create a context on `device` (owns a stream, an error word and the
+ * stream-ordered workspace pool).  Thread-safe to use from many threads. */
+int rtb_init(int device, rtb_ctx** out);
+int rtb_destroy(rtb_ctx* ctx);
+int rtb_device_count(int* count);
+int rtb_get_device_info(rtb_ctx* ctx, int* sm_count, int* cc_major, int* cc_minor,
+                        size_t* total_mem);
+const char* rtb_status_string(int status);
+/* Last error message recorded on this thread (empty if none). */
+int rtb_last_error(char* buf, size_t len);
+/* Wall-clock limit for every device-side wait (default 2 s). */
+int rtb_set_timeout_ns(rtb_ctx* ctx, uint64_t ns);
+/* Read and clear the device error word (synchronises the context's device).
+ * *code receives 0 or the device error code; returns RTB_E_TIMEOUT if set. */
+int rtb_device_error(rtb_ctx* ctx, int* code);
+
+/* ---------------------------------------------------------------- memory */
+int rtb_malloc(rtb_ctx* ctx, void** ptr, size_t bytes, void* stream);
+int rtb_free(rtb_ctx* ctx, void* ptr, void* stream);
+int rtb_host_alloc(rtb_ctx* ctx, void** ptr, size_t bytes); /* pinned */
+int rtb_host_free(rtb_ctx* ctx, void* ptr);
+int rtb_memcpy_h2d(rtb_ctx* ctx, void* dst, const void* src, size_t bytes, void* stream);
+int rtb_memcpy_d2h(rtb_ctx* ctx, void* dst, const void* src, size_t bytes, void* stream);
+int rtb_memcpy_d2d(rtb_ctx* ctx, void* dst, const void* src, size_t bytes, void* stream);
+int rtb_memset_zero(rtb_ctx* ctx, void* dst, size_t bytes, void* stream);
+
+/* ---------------------------------------------------------------- streams */
+int rtb_stream_create(rtb_ctx* ctx, void** stream);
+int rtb_stream_destroy(rtb_ctx* ctx, void* stream);
+/* Synchronise `stream`, then report a device-side timeout if one occurred. */
+int rtb_stream_synchronize(rtb_ctx* ctx, void* stream);
+
+/* ---------------------------------------------------------------- GEMM */
+/* C[M,N] = act(op(A) . op(B) + bias), fp32 in/out, row-major C with ldc.
+ *   transA = 0: A is [M,K] row-major (lda >= K); 1: A is [K,M] row-major.
+ *   transB = 0: B is [K,N] row-major (Tensor::matmul's rhs, ldb >= N);
+ *            1: B is [N,K] row-major (nn::Linear's weight, ldb >= K).
+ *   bias: [N] or NULL.  act: RTB_ACT_NONE | RTB_ACT_RELU.
+ * Replaces ops::matmul (rustorch-core/src/ops.rs:1888-2066) and
+ * ops::matmul_fused (ops.rs:1543-1710); M=N=K=0 edge cases follow the
+ * reference (K=0 gives bias or zeros). */
+int rtb_sgemm(rtb_ctx* ctx, int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
+              int transA, const float* B, int64_t ldb, int transB, const float* bias, int act,
+              float* C, int64_t ldc, int precision, void* stream);
+
+/* Strided batch of independent GEMMs (extension: the reference's matmul is
+ * 2-D only, rustorch-core/src/ops.rs:1892-1894; its oracle is a loop of 2-D
+ * matmuls).  strideA/B/C in elements; bias shared by all batches. */
+int rtb_sgemm_batched(rtb_ctx* ctx, int64_t batch, int64_t M, int64_t N, int64_t K,
+                      const float* A, int64_t lda, int64_t strideA, int transA, const float* B,
+                      int64_t ldb, int64_t strideB, int transB, const float* bias, int act,
+                      float* C, int64_t ldc, int64_t strideC, int precision, void* stream);
+
+/* ---------------------------------------------------------------- conv */
+/* y = act(conv2d(x, w, stride, padding) + bias + residual).
+ *   x: [N,Ci,H,W] (NCHW) or [N,H,W,Ci] (NHWC) per x_layout.
+ *   w: [Co,Ci,kh,kw] (the reference's weight layout, rustorch-nn/src/conv.rs:27-32).
+ *   bias: [Co] or NULL; residual: same shape/layout as y, or NULL.
+ *   y: [N,Co,Ho,Wo] or [N,Ho,Wo,Co] per y_layout; Ho = (H+2ph-kh)/sh+1.
+ * Implicit GEMM (M = N*Ho*Wo, N = Co, K = kh*kw*Ci) on the tensor cores with
+ * the bias/residual/ReLU epilogue fused.  Replaces ops::conv2d
+ * (rustorch-core/src/ops/conv.rs:738-919) + nn::Conv2d's bias add
+ * (rustorch-nn/src/conv.rs:52-63) + the JIT's Conv2dRelu lowering
+ * (rustorch-core/src/jit.rs:254-262). */
+int rtb_conv2d_fwd(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, int64_t Co,
+                   int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw,
+                   const float* x, int x_layout, const float* w, const float* bias,
+                   const float* residual, int act, float* y, int y_layout, int precision,
+                   void* stream);
+
+/* Weight prepacking for repeated convs (nn::Conv2d / JIT graphs): packed
+ * layout [Co, kh*kw*Cp] with Cp = roundup(Ci, 4), zero padded.  Size in
+ * floats from rtb_conv2d_packed_weight_size. */
+int64_t rtb_conv2d_packed_weight_size(int64_t Co, int64_t Ci, int64_t kh, int64_t kw);
+int rtb_conv2d_prepack_weight(rtb_ctx* ctx, int64_t Co, int64_t Ci, int64_t kh, int64_t kw,
+                              const float* w, float* w_packed, void* stream);
+/* As rtb_conv2d_fwd with a prepacked weight and NHWC input whose channel
+ * stride is Cp = roundup(Ci, 4) (x_cp_stride must equal Cp). */
+int rtb_conv2d_fwd_packed(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, int64_t Co,
+                          int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw,
+                          const float* x_nhwc_padded, const float* w_packed, const float* bias,
+                          const float* residual, int act, float* y, int y_layout, int precision,
+                          void* stream);
+/* NCHW [N,C,H,W] -> NHWC with channel stride Cp = roundup(C,4), zero padded. */
+int rtb_nchw_to_nhwc_padded(rtb_ctx* ctx, int64_t N, int64_t C, int64_t H, int64_t W,
+                            const float* x, float* y, void* stream);
+
+/* ---------------------------------------------------------------- small ops */
+/* ops::max_pool2d (rustorch-core/src/ops/pool.rs:115-191): -inf init, padding skipped. */
+int rtb_max_pool2d(rtb_ctx* ctx, int64_t N, int64_t C, int64_t H, int64_t W, int64_t kh,
+                   int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw, const float* x,
+                   float* y, int layout, void* stream);
+/* Global average pool -> [N, C] (absent from the reference; needed by ResNet-18). */
+int rtb_global_avg_pool(rtb_ctx* ctx, int64_t N, int64_t C, int64_t H, int64_t W, const float* x,
+                        float* y, int layout, void* stream);
+/* Elementwise: y = a + b (ops::add same shape), y = max(x, 0) (ops::relu). */
+int rtb_add(rtb_ctx* ctx, int64_t n, const float* a, const float* b, float* y, void* stream);
+int rtb_relu(rtb_ctx* ctx, int64_t n, const float* x, float* y, void* stream);
+
+/* ---------------------------------------------------------------- data */
+/* The documented synthetic-input generator: SplitMix64 stream keyed by
+ * (seed, tensor_id); N(mean, std) by Box-Muller on draw pairs; U(lo, hi) from
+ * the top 24 bits of each draw.  Host version (multi-threaded). */
+int rtb_fill_normal_host(float* out, int64_t n, uint64_t seed, uint64_t tensor_id, float mean,
+                         float std_dev);
+int rtb_fill_uniform_host(float* out, int64_t n, uint64_t seed, uint64_t tensor_id, float lo,
+                          float hi);
+
+/* ---------------------------------------------------------------- multi-GPU */
+/* One process per GPU.  Rank 0 creates an id (128 opaque bytes), the caller
+ * broadcasts it (e.g. over torch.distributed), every rank joins. */
+int rtb_nccl_unique_id(void* id_out_128b);
+int rtb_nccl_comm_init(rtb_ctx* ctx, const void* id_128b, int nranks, int rank, void** comm);
+int rtb_nccl_comm_destroy(void* comm);
+/* N-split GEMM: rank r holds A [M,K] (replicated) and B_r = B[:, r*N/P:(r+1)*N/P]
+ * as a [K, N/P] row-major block; computes C_r = A . B_r into its slice and
+ * all-gathers so every rank ends with C [M,N] row-major.  `c_parts` is a
+ * [P, M, N/P] scratch the caller provides (device memory, P*M*(N/P) floats).
+ * Requires N % P == 0. */
+int rtb_sgemm_nsplit_allgather(rtb_ctx* ctx, void* comm, int64_t M, int64_t N, int64_t K,
+                               const float* A, const float* B_local, float* c_parts, float* C,
+                               int precision, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RUSTORCH_B200_H */

@@ -1,0 +1,693 @@
+// C-ABI implementation: contexts, memory, streams, argument validation and
+// dispatch of GEMM / conv / pooling onto the sm_100a kernels.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "rtb_internal.h"
+
+namespace rtb {
+
+static thread_local std::string g_last_error;
+
+int set_error(int status, const std::string& msg) {
+  g_last_error = msg;
+  return status;
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+  const int st = (e == cudaErrorMemoryAllocation) ? RTB_E_OOM : RTB_E_CUDA;
+  return set_error(st, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// ---------------------------------------------------------------- tensor maps
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1,
+                 uint64_t row_stride_elems, uint32_t box0, uint32_t box1) {
+  EncodeTiledFn enc = get_encode_tiled();
+  if (!enc) return set_error(RTB_E_CUDA, "cuTensorMapEncodeTiled unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (row_stride_elems * 4) % 16 != 0)
+    return set_error(RTB_E_INVALID, "tensor map: base must be 16-byte aligned, row stride % 4 == 0");
+  const cuuint64_t dims[2] = {dim0, dim1};
+  const cuuint64_t strides[1] = {row_stride_elems * 4};
+  const cuuint32_t box[2] = {box0, box1};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[160];
+    snprintf(buf, sizeof buf, "cuTensorMapEncodeTiled failed (%d): dims %llu x %llu stride %llu",
+             (int)r, (unsigned long long)dim0, (unsigned long long)dim1,
+             (unsigned long long)row_stride_elems);
+    return set_error(RTB_E_CUDA, buf);
+  }
+  return RTB_OK;
+}
+
+// ---------------------------------------------------------------- workspace
+int ws_alloc(rtb_ctx* ctx, void** p, size_t bytes, cudaStream_t s) {
+  (void)ctx;
+  cudaError_t e = cudaMallocAsync(p, bytes ? bytes : 16, s);
+  if (e != cudaSuccess) return cuda_status(e, "workspace cudaMallocAsync");
+  return RTB_OK;
+}
+
+void ws_free(void* p, cudaStream_t s) {
+  if (p) cudaFreeAsync(p, s);
+}
+
+}  // namespace rtb
+
+using namespace rtb;
+
+#define RTB_CHECK_CTX(ctx)                                              \
+  do {                                                                  \
+    if (!(ctx)) return set_error(RTB_E_INVALID, "null rtb_ctx");        \
+  } while (0)
+
+static inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+static inline int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+extern "C" {
+
+// ---------------------------------------------------------------- context
+int rtb_device_count(int* count) {
+  if (!count) return set_error(RTB_E_INVALID, "null count");
+  cudaError_t e = cudaGetDeviceCount(count);
+  if (e != cudaSuccess) {
+    *count = 0;
+    return cuda_status(e, "cudaGetDeviceCount");
+  }
+  return RTB_OK;
+}
+
+int rtb_init(int device, rtb_ctx** out) {
+  if (!out) return set_error(RTB_E_INVALID, "null output pointer");
+  *out = nullptr;
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) return cuda_status(e, "cudaGetDeviceCount");
+  if (device < 0 || device >= n) return set_error(RTB_E_INVALID, "device index out of range");
+  DeviceGuard g(device);
+  cudaDeviceProp prop;
+  e = cudaGetDeviceProperties(&prop, device);
+  if (e != cudaSuccess) return cuda_status(e, "cudaGetDeviceProperties");
+  if (prop.major != 10)
+    return set_error(RTB_E_UNSUPPORTED, "this library is built for sm_100a (B200) only");
+  rtb_ctx* c = new (std::nothrow) rtb_ctx();
+  if (!c) return set_error(RTB_E_OOM, "context allocation");
+  c->device = device;
+  c->sm_count = prop.multiProcessorCount;
+  c->cc_major = prop.major;
+  c->cc_minor = prop.minor;
+  c->total_mem = prop.totalGlobalMem;
+  e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+  if (e != cudaSuccess) {
+    delete c;
+    return cuda_status(e, "cudaStreamCreate");
+  }
+  e = cudaMalloc(&c->d_err, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(c->d_err, 0, sizeof(int));
+  if (e != cudaSuccess) {
+    cudaStreamDestroy(c->stream);
+    delete c;
+    return cuda_status(e, "error-word allocation");
+  }
+  // Keep freed workspace in the pool (no release back to the OS between calls).
+  cudaMemPool_t pool;
+  if (cudaDeviceGetDefaultMemPool(&pool, device) == cudaSuccess) {
+    uint64_t thr = UINT64_MAX;
+    cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr);
+  }
+  const char* prec = std::getenv("RUSTORCH_B200_PRECISION");
+  if (prec && (std::strcmp(prec, "tf32") == 0 || std::strcmp(prec, "TF32") == 0))
+    c->default_precision = RTB_PREC_TF32;
+  *out = c;
+  return RTB_OK;
+}
+
+int rtb_destroy(rtb_ctx* ctx) {
+  RTB_CHECK_CTX(ctx);
+  DeviceGuard g(ctx->device);
+  cudaStreamSynchronize(ctx->stream);
+  cudaFree(ctx->d_err);
+  cudaStreamDestroy(ctx->stream);
+  delete ctx;
+  return RTB_OK;
+}
+
+int rtb_get_device_info(rtb_ctx* ctx, int* sm_count, int* cc_major, int* cc_minor,
+                        size_t* total_mem) {
+  RTB_CHECK_CTX(ctx);
+  if (sm_count) *sm_count = ctx->sm_count;
+  if (cc_major) *cc_major = ctx->cc_major;
+  if (cc_minor) *cc_minor = ctx->cc_minor;
+  if (total_mem) *total_mem = ctx->total_mem;
+  return RTB_OK;
+}
+
+const char* rtb_status_string(int status) {
+  switch (status) {
+    case RTB_OK: return "ok";
+    case RTB_E_INVALID: return "invalid argument";
+    case RTB_E_OOM: return "out of memory";
+    case RTB_E_CUDA: return "CUDA error";
+    case RTB_E_TIMEOUT: return "device wait timed out";
+    case RTB_E_UNSUPPORTED: return "unsupported";
+    case RTB_E_NCCL: return "NCCL error";
+    default: return "unknown status";
+  }
+}
+
+int rtb_last_error(char* buf, size_t len) {
+  if (!buf || len == 0) return RTB_E_INVALID;
+  std::snprintf(buf, len, "%s", g_last_error.c_str());
+  return RTB_OK;
+}
+
+int rtb_set_timeout_ns(rtb_ctx* ctx, uint64_t ns) {
+  RTB_CHECK_CTX(ctx);
+  if (ns < 1000000ull) return set_error(RTB_E_INVALID, "timeout below 1 ms");
+  ctx->timeout_ns = ns;
+  return RTB_OK;
+}
+
+int rtb_device_error(rtb_ctx* ctx, int* code) {
+  RTB_CHECK_CTX(ctx);
+  DeviceGuard g(ctx->device);
+  int h = 0;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_status(e, "cudaDeviceSynchronize");
+  e = cudaMemcpy(&h, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_status(e, "read error word");
+  if (h) cudaMemset(ctx->d_err, 0, sizeof(int));
+  if (code) *code = h;
+  if (h) {
+    char buf[96];
+    std::snprintf(buf, sizeof buf, "device-side bounded wait expired (code %d)", h);
+    return set_error(RTB_E_TIMEOUT, buf);
+  }
+  return RTB_OK;
+}
+
+// ---------------------------------------------------------------- memory
+int rtb_malloc(rtb_ctx* ctx, void** ptr, size_t bytes, void* stream) {
+  RTB_CHECK_CTX(ctx);
+  if (!ptr) return set_error(RTB_E_INVALID, "null ptr");
+  DeviceGuard g(ctx->device);
+  cudaError_t e = cudaMallocAsync(ptr, bytes ? bytes : 16, pick_stream(ctx, stream));
+  if (e != cudaSuccess) return cuda_status(e, "rtb_malloc");
+  return RTB_OK;
+}
+
+int rtb_free(rtb_ctx* ctx, void* ptr, void* stream) {
+  RTB_CHECK_CTX(ctx);
+  if (!ptr) return RTB_OK;
+  DeviceGuard g(ctx->device);
+  cudaError_t e = cudaFreeAsync(ptr, pick_stream(ctx, stream));
+  if (e != cudaSuccess) return cuda_status(e, "rtb_free");
+  return RTB_OK;
+}
+
+int rtb_host_alloc(rtb_ctx* ctx, void** ptr, size_t bytes) {
+  RTB_CHECK_CTX(ctx);
+  if (!ptr) return set_error(RTB_E_INVALID, "null ptr");
+  DeviceGuard g(ctx->device);
+  cudaError_t e = cudaMallocHost(ptr, bytes ? bytes : 16);
+  if (e != cudaSuccess) return cuda_status(e, "rtb_host_alloc");
+  return RTB_OK;
+}
+
+int rtb_host_free(rtb_ctx* ctx, void* ptr) {
+  RTB_CHECK_CTX(ctx);
+  if (!ptr) return RTB_OK;
+  cudaError_t e = cudaFreeHost(ptr);
+  if (e != cudaSuccess) return cuda_status(e, "rtb_host_free");
+  return RTB_OK;
+}
+
+static int copy_impl(rtb_ctx* ctx, void* dst, const void* src, size_t bytes, void* stream,
+                     cudaMemcpyKind kind, const char* what) {
+  RTB_CHECK_CTX(ctx);
+  if (bytes == 0) return RTB_OK;
+  if (!dst || !src) return set_error(RTB_E_INVALID, std::string(what) + ": null pointer");
+  DeviceGuard g(ctx->device);
+  cudaError_t e = cudaMemcpyAsync(dst, src, bytes, kind, pick_stream(ctx, stream));
+  if (e != cudaSuccess) return cuda_status(e, what);
+  return RTB_OK;
+}
+
+int rtb_memcpy_h2d(rtb_ctx* ctx, void* dst, const void* src, size_t bytes, void* stream) {
+  return copy_impl(ctx, dst, src, bytes, stream, cudaMemcpyHostToDevice, "rtb_memcpy_h2d");
+}
+int rtb_memcpy_d2h(rtb_ctx* ctx, void* dst, const void* src, size_t bytes, void* stream) {
+  return copy_impl(ctx, dst, src, bytes, stream, cudaMemcpyDeviceToHost, "rtb_memcpy_d2h");
+}
+int rtb_memcpy_d2d(rtb_ctx* ctx, void* dst, const void* src, size_t bytes, void* stream) {
+  return copy_impl(ctx, dst, src, bytes, stream, cudaMemcpyDeviceToDevice, "rtb_memcpy_d2d");
+}
+
+int rtb_memset_zero(rtb_ctx* ctx, void* dst, size_t bytes, void* stream) {
+  RTB_CHECK_CTX(ctx);
+  if (bytes == 0) return RTB_OK;
+  if (!dst) return set_error(RTB_E_INVALID, "rtb_memset_zero: null pointer");
+  DeviceGuard g(ctx->device);
+  cudaError_t e = cudaMemsetAsync(dst, 0, bytes, pick_stream(ctx, stream));
+  if (e != cudaSuccess) return cuda_status(e, "rtb_memset_zero");
+  return RTB_OK;
+}
+
+// ---------------------------------------------------------------- streams
+int rtb_stream_create(rtb_ctx* ctx, void** stream) {
+  RTB_CHECK_CTX(ctx);
+  if (!stream) return set_error(RTB_E_INVALID, "null stream out");
+  DeviceGuard g(ctx->device);
+  cudaStream_t s;
+  cudaError_t e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+  if (e != cudaSuccess) return cuda_status(e, "rtb_stream_create");
+  *stream = s;
+  return RTB_OK;
+}
+
+int rtb_stream_destroy(rtb_ctx* ctx, void* stream) {
+  RTB_CHECK_CTX(ctx);
+  if (!stream) return RTB_OK;
+  DeviceGuard g(ctx->device);
+  cudaError_t e = cudaStreamDestroy(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_status(e, "rtb_stream_destroy");
+  return RTB_OK;
+}
+
+int rtb_stream_synchronize(rtb_ctx* ctx, void* stream) {
+  RTB_CHECK_CTX(ctx);
+  DeviceGuard g(ctx->device);
+  cudaError_t e = cudaStreamSynchronize(pick_stream(ctx, stream));
+  if (e != cudaSuccess) return cuda_status(e, "rtb_stream_synchronize");
+  int h = 0;
+  e = cudaMemcpy(&h, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_status(e, "read error word");
+  if (h) {
+    cudaMemset(ctx->d_err, 0, sizeof(int));
+    char buf[96];
+    std::snprintf(buf, sizeof buf, "device-side bounded wait expired (code %d)", h);
+    return set_error(RTB_E_TIMEOUT, buf);
+  }
+  return RTB_OK;
+}
+
+// ---------------------------------------------------------------- GEMM
+static int resolve_precision(rtb_ctx* ctx, int precision, int* split3) {
+  if (precision == RTB_PREC_DEFAULT) precision = ctx->default_precision;
+  if (precision != RTB_PREC_3XTF32 && precision != RTB_PREC_TF32)
+    return set_error(RTB_E_INVALID, "precision must be RTB_PREC_3XTF32, RTB_PREC_TF32 or DEFAULT");
+  *split3 = precision == RTB_PREC_3XTF32 ? 1 : 0;
+  return RTB_OK;
+}
+
+static int check_act(int act, int* relu) {
+  if (act == RTB_ACT_NONE) { *relu = 0; return RTB_OK; }
+  if (act == RTB_ACT_RELU) { *relu = 1; return RTB_OK; }
+  if (act == RTB_ACT_SIGMOID || act == RTB_ACT_TANH)
+    return set_error(RTB_E_UNSUPPORTED, "only None/ReLU activations are fused on this path");
+  return set_error(RTB_E_INVALID, "unknown activation");
+}
+
+// One 2-D GEMM on the current device/stream (helper for single and batched).
+static int sgemm_one(rtb_ctx* ctx, int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
+                     int transA, const float* B, int64_t ldb, int transB, const float* bias,
+                     int relu, float* C, int64_t ldc, int split3, cudaStream_t s) {
+  if (M == 0 || N == 0) return RTB_OK;
+  if (K == 0) return launch_fill_rows(C, M, N, ldc, bias, relu, s);
+
+  GemmDesc d;
+  d.M = M; d.N = N; d.K = K;
+  d.C = C; d.ldc = ldc; d.bias = bias; d.relu = relu; d.split3 = split3;
+  float* wsA = nullptr;
+  float* wsB = nullptr;
+  int st = RTB_OK;
+
+  // A must be K-major, 16-byte aligned, row stride a multiple of 4 floats.
+  if (!transA && aligned16(A) && lda % 4 == 0) {
+    d.A = A; d.lda = lda;
+  } else {
+    const int64_t Kp = round_up(K, 4);
+    st = ws_alloc(ctx, (void**)&wsA, (size_t)(M * Kp) * 4, s);
+    if (st) return st;
+    st = transA ? launch_pack_kmajor(A, M, K, 1, lda, wsA, Kp, s)
+                : launch_pack_kmajor(A, M, K, lda, 1, wsA, Kp, s);
+    d.A = wsA; d.lda = Kp;
+  }
+  if (st == RTB_OK) {
+    if (!transB && aligned16(B) && ldb % 4 == 0) {
+      d.B = B; d.ldb = ldb; d.b_mn_major = 1;           // [K,N] row-major
+    } else if (transB && aligned16(B) && ldb % 4 == 0) {
+      d.B = B; d.ldb = ldb; d.b_mn_major = 0;           // [N,K] row-major
+    } else {
+      const int64_t Kp = round_up(K, 4);
+      st = ws_alloc(ctx, (void**)&wsB, (size_t)(N * Kp) * 4, s);
+      if (st == RTB_OK)
+        st = transB ? launch_pack_kmajor(B, N, K, ldb, 1, wsB, Kp, s)
+                    : launch_pack_kmajor(B, N, K, 1, ldb, wsB, Kp, s);
+      d.B = wsB; d.ldb = Kp; d.b_mn_major = 0;
+    }
+  }
+  if (st == RTB_OK) st = gemm_run(ctx, d, s);
+  ws_free(wsA, s);
+  ws_free(wsB, s);
+  return st;
+}
+
+static int check_gemm_args(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
+                           int transA, const float* B, int64_t ldb, int transB, float* C,
+                           int64_t ldc) {
+  if (M < 0 || N < 0 || K < 0) return set_error(RTB_E_INVALID, "negative dimension");
+  if (transA != 0 && transA != 1) return set_error(RTB_E_INVALID, "transA must be 0 or 1");
+  if (transB != 0 && transB != 1) return set_error(RTB_E_INVALID, "transB must be 0 or 1");
+  if (M == 0 || N == 0) return RTB_OK;
+  if (!C) return set_error(RTB_E_INVALID, "null C");
+  if (ldc < N) return set_error(RTB_E_INVALID, "ldc < N");
+  if (K == 0) return RTB_OK;
+  if (!A || !B) return set_error(RTB_E_INVALID, "null A or B");
+  if (lda < (transA ? M : K)) return set_error(RTB_E_INVALID, "lda too small");
+  if (ldb < (transB ? K : N)) return set_error(RTB_E_INVALID, "ldb too small");
+  return RTB_OK;
+}
+
+int rtb_sgemm(rtb_ctx* ctx, int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
+              int transA, const float* B, int64_t ldb, int transB, const float* bias, int act,
+              float* C, int64_t ldc, int precision, void* stream) {
+  RTB_CHECK_CTX(ctx);
+  int st = check_gemm_args(M, N, K, A, lda, transA, B, ldb, transB, C, ldc);
+  if (st) return st;
+  int relu = 0, split3 = 1;
+  if ((st = check_act(act, &relu))) return st;
+  if ((st = resolve_precision(ctx, precision, &split3))) return st;
+  DeviceGuard g(ctx->device);
+  return sgemm_one(ctx, M, N, K, A, lda, transA, B, ldb, transB, bias, relu, C, ldc, split3,
+                   pick_stream(ctx, stream));
+}
+
+int rtb_sgemm_batched(rtb_ctx* ctx, int64_t batch, int64_t M, int64_t N, int64_t K,
+                      const float* A, int64_t lda, int64_t strideA, int transA, const float* B,
+                      int64_t ldb, int64_t strideB, int transB, const float* bias, int act,
+                      float* C, int64_t ldc, int64_t strideC, int precision, void* stream) {
+  RTB_CHECK_CTX(ctx);
+  if (batch < 0) return set_error(RTB_E_INVALID, "negative batch");
+  int st = check_gemm_args(M, N, K, A, lda, transA, B, ldb, transB, C, ldc);
+  if (st) return st;
+  int relu = 0, split3 = 1;
+  if ((st = check_act(act, &relu))) return st;
+  if ((st = resolve_precision(ctx, precision, &split3))) return st;
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = pick_stream(ctx, stream);
+  for (int64_t b = 0; b < batch; ++b) {
+    st = sgemm_one(ctx, M, N, K, A ? A + b * strideA : nullptr, lda, transA,
+                   B ? B + b * strideB : nullptr, ldb, transB, bias, relu, C + b * strideC, ldc,
+                   split3, s);
+    if (st) return st;
+  }
+  return RTB_OK;
+}
+
+// ---------------------------------------------------------------- conv
+int64_t rtb_conv2d_packed_weight_size(int64_t Co, int64_t Ci, int64_t kh, int64_t kw) {
+  return Co * kh * kw * round_up(Ci, 4);
+}
+
+int rtb_conv2d_prepack_weight(rtb_ctx* ctx, int64_t Co, int64_t Ci, int64_t kh, int64_t kw,
+                              const float* w, float* w_packed, void* stream) {
+  RTB_CHECK_CTX(ctx);
+  if (Co <= 0 || Ci <= 0 || kh <= 0 || kw <= 0 || !w || !w_packed)
+    return set_error(RTB_E_INVALID, "prepack: bad arguments");
+  DeviceGuard g(ctx->device);
+  return launch_prepack_weight(w, Co, Ci, kh, kw, round_up(Ci, 4), w_packed,
+                               pick_stream(ctx, stream));
+}
+
+int rtb_nchw_to_nhwc_padded(rtb_ctx* ctx, int64_t N, int64_t C, int64_t H, int64_t W,
+                            const float* x, float* y, void* stream) {
+  RTB_CHECK_CTX(ctx);
+  if (N < 0 || C <= 0 || H < 0 || W < 0 || !x || !y)
+    return set_error(RTB_E_INVALID, "nchw_to_nhwc: bad arguments");
+  if (N == 0 || H == 0 || W == 0) return RTB_OK;
+  DeviceGuard g(ctx->device);
+  return launch_nchw_to_nhwc_padded(x, N, C, H, W, round_up(C, 4), y, pick_stream(ctx, stream));
+}
+
+static int conv_check(int64_t N, int64_t Ci, int64_t H, int64_t W, int64_t Co, int64_t kh,
+                      int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw, int64_t* Ho,
+                      int64_t* Wo) {
+  // ops::conv2d panics (rustorch-core/src/ops/conv.rs:747-764) on these.
+  if (N < 0 || Ci <= 0 || H <= 0 || W <= 0 || Co <= 0 || kh <= 0 || kw <= 0)
+    return set_error(RTB_E_INVALID, "Conv2d requires 4D tensors with positive sizes");
+  if (sh <= 0 || sw <= 0 || ph < 0 || pw < 0) return set_error(RTB_E_INVALID, "bad stride/padding");
+  if (H + 2 * ph < kh || W + 2 * pw < kw)
+    return set_error(RTB_E_INVALID, "kernel larger than padded input");
+  *Ho = (H + 2 * ph - kh) / sh + 1;
+  *Wo = (W + 2 * pw - kw) / sw + 1;
+  return RTB_OK;
+}
+
+static int conv_core(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, int64_t Co,
+                     int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw,
+                     int64_t Ho, int64_t Wo, const float* x_nhwc, const float* wp,
+                     const float* bias, const float* residual, int relu, float* y, int y_layout,
+                     int split3, cudaStream_t s) {
+  const int64_t Cp = round_up(Ci, 4);
+  const int64_t M = N * Ho * Wo;
+  if (M == 0) return RTB_OK;
+  if (M > INT32_MAX || N * H * W * Cp > ((int64_t)1 << 40))
+    return set_error(RTB_E_UNSUPPORTED, "conv: problem too large for one launch");
+  GemmDesc d;
+  d.M = M; d.N = Co; d.K = kh * kw * Cp;
+  d.B = wp; d.ldb = d.K; d.b_mn_major = 0;
+  d.C = y; d.bias = bias; d.residual = residual; d.relu = relu;
+  if (y_layout == RTB_LAYOUT_NHWC) {
+    d.out_mode = 0; d.ldc = Co; d.ldr = Co;
+  } else {
+    d.out_mode = 1; d.ldc = Co; d.hw = (int)(Ho * Wo);
+  }
+  d.gather = 1; d.x = x_nhwc;
+  d.H = (int)H; d.W = (int)W; d.Cp = (int)Cp; d.Ho = (int)Ho; d.Wo = (int)Wo;
+  d.R = (int)kh; d.S = (int)kw; d.sh = (int)sh; d.sw = (int)sw; d.ph = (int)ph; d.pw = (int)pw;
+  d.split3 = split3;
+  return gemm_run(ctx, d, s);
+}
+
+int rtb_conv2d_fwd_packed(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, int64_t Co,
+                          int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw,
+                          const float* x_nhwc_padded, const float* w_packed, const float* bias,
+                          const float* residual, int act, float* y, int y_layout, int precision,
+                          void* stream) {
+  RTB_CHECK_CTX(ctx);
+  int64_t Ho, Wo;
+  int st = conv_check(N, Ci, H, W, Co, kh, kw, sh, sw, ph, pw, &Ho, &Wo);
+  if (st) return st;
+  if (N == 0) return RTB_OK;
+  if (!x_nhwc_padded || !w_packed || !y) return set_error(RTB_E_INVALID, "conv: null pointer");
+  if (!aligned16(x_nhwc_padded) || !aligned16(w_packed))
+    return set_error(RTB_E_INVALID, "conv: packed input/weight must be 16-byte aligned");
+  if (y_layout != RTB_LAYOUT_NCHW && y_layout != RTB_LAYOUT_NHWC)
+    return set_error(RTB_E_INVALID, "conv: bad y_layout");
+  int relu = 0, split3 = 1;
+  if ((st = check_act(act, &relu))) return st;
+  if ((st = resolve_precision(ctx, precision, &split3))) return st;
+  DeviceGuard g(ctx->device);
+  return conv_core(ctx, N, Ci, H, W, Co, kh, kw, sh, sw, ph, pw, Ho, Wo, x_nhwc_padded, w_packed,
+                   bias, residual, relu, y, y_layout, split3, pick_stream(ctx, stream));
+}
+
+int rtb_conv2d_fwd(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, int64_t Co,
+                   int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw,
+                   const float* x, int x_layout, const float* w, const float* bias,
+                   const float* residual, int act, float* y, int y_layout, int precision,
+                   void* stream) {
+  RTB_CHECK_CTX(ctx);
+  int64_t Ho, Wo;
+  int st = conv_check(N, Ci, H, W, Co, kh, kw, sh, sw, ph, pw, &Ho, &Wo);
+  if (st) return st;
+  if (N == 0) return RTB_OK;
+  if (!x || !w || !y) return set_error(RTB_E_INVALID, "conv: null pointer");
+  if (x_layout != RTB_LAYOUT_NCHW && x_layout != RTB_LAYOUT_NHWC)
+    return set_error(RTB_E_INVALID, "conv: bad x_layout");
+  if (y_layout != RTB_LAYOUT_NCHW && y_layout != RTB_LAYOUT_NHWC)
+    return set_error(RTB_E_INVALID, "conv: bad y_layout");
+  int relu = 0, split3 = 1;
+  if ((st = check_act(act, &relu))) return st;
+  if ((st = resolve_precision(ctx, precision, &split3))) return st;
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = pick_stream(ctx, stream);
+  const int64_t Cp = round_up(Ci, 4);
+  float* xs = nullptr;
+  float* ws = nullptr;
+  const float* xin = x;
+  if (x_layout == RTB_LAYOUT_NCHW || Cp != Ci || !aligned16(x)) {
+    st = ws_alloc(ctx, (void**)&xs, (size_t)(N * H * W * Cp) * 4, s);
+    if (st) return st;
+    if (x_layout == RTB_LAYOUT_NCHW) {
+      st = launch_nchw_to_nhwc_padded(x, N, Ci, H, W, Cp, xs, s);
+    } else {
+      // NHWC with Ci % 4 != 0 or unaligned: repack rows of Ci into rows of Cp.
+      st = launch_pack_kmajor(x, N * H * W, Ci, Ci, 1, xs, Cp, s);
+    }
+    xin = xs;
+  }
+  if (st == RTB_OK) {
+    st = ws_alloc(ctx, (void**)&ws, (size_t)rtb_conv2d_packed_weight_size(Co, Ci, kh, kw) * 4, s);
+    if (st == RTB_OK) st = launch_prepack_weight(w, Co, Ci, kh, kw, Cp, ws, s);
+  }
+  if (st == RTB_OK)
+    st = conv_core(ctx, N, Ci, H, W, Co, kh, kw, sh, sw, ph, pw, Ho, Wo, xin, ws, bias, residual,
+                   relu, y, y_layout, split3, s);
+  ws_free(xs, s);
+  ws_free(ws, s);
+  return st;
+}
+
+// ---------------------------------------------------------------- small ops
+int rtb_max_pool2d(rtb_ctx* ctx, int64_t N, int64_t C, int64_t H, int64_t W, int64_t kh,
+                   int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw, const float* x,
+                   float* y, int layout, void* stream) {
+  RTB_CHECK_CTX(ctx);
+  if (N < 0 || C <= 0 || H <= 0 || W <= 0 || kh <= 0 || kw <= 0 || sh <= 0 || sw <= 0 || ph < 0 ||
+      pw < 0 || H + 2 * ph < kh || W + 2 * pw < kw)
+    return set_error(RTB_E_INVALID, "MaxPool2d requires 4D tensor (N, C, H, W)");
+  if (layout != RTB_LAYOUT_NCHW && layout != RTB_LAYOUT_NHWC)
+    return set_error(RTB_E_INVALID, "max_pool2d: bad layout");
+  if (N == 0) return RTB_OK;
+  if (!x || !y) return set_error(RTB_E_INVALID, "max_pool2d: null pointer");
+  DeviceGuard g(ctx->device);
+  return launch_max_pool2d(x, y, N, C, H, W, kh, kw, sh, sw, ph, pw, layout,
+                           pick_stream(ctx, stream));
+}
+
+int rtb_global_avg_pool(rtb_ctx* ctx, int64_t N, int64_t C, int64_t H, int64_t W, const float* x,
+                        float* y, int layout, void* stream) {
+  RTB_CHECK_CTX(ctx);
+  if (N < 0 || C <= 0 || H <= 0 || W <= 0) return set_error(RTB_E_INVALID, "avg_pool: bad shape");
+  if (layout != RTB_LAYOUT_NCHW && layout != RTB_LAYOUT_NHWC)
+    return set_error(RTB_E_INVALID, "avg_pool: bad layout");
+  if (N == 0) return RTB_OK;
+  if (!x || !y) return set_error(RTB_E_INVALID, "avg_pool: null pointer");
+  DeviceGuard g(ctx->device);
+  return launch_global_avg_pool(x, y, N, C, H * W, layout, pick_stream(ctx, stream));
+}
+
+int rtb_add(rtb_ctx* ctx, int64_t n, const float* a, const float* b, float* y, void* stream) {
+  RTB_CHECK_CTX(ctx);
+  if (n < 0) return set_error(RTB_E_INVALID, "add: negative size");
+  if (n == 0) return RTB_OK;
+  if (!a || !b || !y) return set_error(RTB_E_INVALID, "add: null pointer");
+  DeviceGuard g(ctx->device);
+  return launch_add(a, b, y, n, pick_stream(ctx, stream));
+}
+
+int rtb_relu(rtb_ctx* ctx, int64_t n, const float* x, float* y, void* stream) {
+  RTB_CHECK_CTX(ctx);
+  if (n < 0) return set_error(RTB_E_INVALID, "relu: negative size");
+  if (n == 0) return RTB_OK;
+  if (!x || !y) return set_error(RTB_E_INVALID, "relu: null pointer");
+  DeviceGuard g(ctx->device);
+  return launch_relu(x, y, n, pick_stream(ctx, stream));
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------- data
+// SplitMix64-based generator (documented in the header).  Same arithmetic as
+// the published spec: finaliser constants of SplitMix64, Box-Muller in double.
+static inline uint64_t sm_fin(uint64_t x) {
+  x ^= x >> 30;
+  x *= 0xBF58476D1CE4E5B9ULL;
+  x ^= x >> 27;
+  x *= 0x94D049BB133111EBULL;
+  x ^= x >> 31;
+  return x;
+}
+static inline uint64_t sm_key(uint64_t seed, uint64_t tid) {
+  return sm_fin(seed * 0x9E3779B97F4A7C15ULL + tid * 0xD1B54A32D192ED03ULL + 1ULL);
+}
+static inline uint64_t sm_draw(uint64_t key, uint64_t i) {
+  return sm_fin(i + key * 0x9E3779B97F4A7C15ULL);
+}
+
+template <class F>
+static void parallel_ranges(int64_t n, F f) {
+  unsigned nt = std::thread::hardware_concurrency();
+  if (nt == 0) nt = 1;
+  if (nt > 64) nt = 64;
+  if (n < (int64_t)1 << 16) nt = 1;
+  std::vector<std::thread> th;
+  const int64_t chunk = (n + nt - 1) / nt;
+  for (unsigned t = 0; t < nt; ++t) {
+    const int64_t a = (int64_t)t * chunk, b = a + chunk < n ? a + chunk : n;
+    if (a >= b) break;
+    th.emplace_back([=] { f(a, b); });
+  }
+  for (auto& x : th) x.join();
+}
+
+extern "C" {
+
+int rtb_fill_normal_host(float* out, int64_t n, uint64_t seed, uint64_t tensor_id, float mean,
+                         float std_dev) {
+  if (n < 0 || (n > 0 && !out)) return set_error(RTB_E_INVALID, "fill_normal: bad arguments");
+  const uint64_t key = sm_key(seed, tensor_id);
+  const int64_t npairs = (n + 1) / 2;
+  parallel_ranges(npairs, [=](int64_t a, int64_t b) {
+    for (int64_t j = a; j < b; ++j) {
+      const uint64_t d1 = sm_draw(key, (uint64_t)(2 * j)), d2 = sm_draw(key, (uint64_t)(2 * j + 1));
+      const double u1 = ((double)(d1 >> 11) + 0.5) * (1.0 / 9007199254740992.0);
+      const double u2 = ((double)(d2 >> 11) + 0.5) * (1.0 / 9007199254740992.0);
+      const double r = std::sqrt(-2.0 * std::log(u1));
+      const double t = 6.283185307179586476925286766559 * u2;
+      out[2 * j] = (float)((double)mean + (double)std_dev * r * std::cos(t));
+      if (2 * j + 1 < n) out[2 * j + 1] = (float)((double)mean + (double)std_dev * r * std::sin(t));
+    }
+  });
+  return RTB_OK;
+}
+
+int rtb_fill_uniform_host(float* out, int64_t n, uint64_t seed, uint64_t tensor_id, float lo,
+                          float hi) {
+  if (n < 0 || (n > 0 && !out)) return set_error(RTB_E_INVALID, "fill_uniform: bad arguments");
+  const uint64_t key = sm_key(seed, tensor_id);
+  parallel_ranges(n, [=](int64_t a, int64_t b) {
+    for (int64_t i = a; i < b; ++i) {
+      const uint64_t d = sm_draw(key, (uint64_t)i);
+      const double u = ((double)(d >> 40) + 0.5) * (1.0 / 16777216.0);
+      out[i] = (float)((double)lo + ((double)hi - (double)lo) * u);
+    }
+  });
+  return RTB_OK;
+}
+
+}  // extern "C"

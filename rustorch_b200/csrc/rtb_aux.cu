@@ -1,0 +1,303 @@
+// Small device kernels around the contraction engine: operand packing,
+// layout conversion, max/avg pooling, elementwise ops, N-split repacking.
+// These are HBM-bound byte movers; grids are sized in multiples of the SM
+// count by the CUDA occupancy rules (256-thread blocks, grid-stride loops).
+#include <cfloat>
+
+#include "rtb_internal.h"
+
+namespace rtb {
+
+namespace {
+
+constexpr int kThreads = 256;
+
+inline int grid_for(int64_t n, int per_thread = 1) {
+  int64_t blocks = (n / per_thread + kThreads - 1) / kThreads;
+  if (blocks < 1) blocks = 1;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  return (int)blocks;
+}
+
+inline int launch_check(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? RTB_OK : cuda_status(e, what);
+}
+
+// dst[r, k] = src[r*rs + k*cs] for k < K, 0 for K <= k < Kp.  32x32 tiles
+// through shared memory so both the strided read and the row write coalesce.
+__global__ void pack_kmajor_kernel(const float* __restrict__ src, int64_t rows, int64_t K,
+                                   int64_t rs, int64_t cs, float* __restrict__ dst, int64_t Kp) {
+  __shared__ float tile[32][33];
+  const int64_t r0 = (int64_t)blockIdx.y * 32, k0 = (int64_t)blockIdx.x * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+  const bool k_fast = (cs == 1);
+  for (int i = ty; i < 32; i += 8) {
+    int64_t r, k;
+    if (k_fast) { r = r0 + i; k = k0 + tx; }
+    else        { r = r0 + tx; k = k0 + i; }
+    float v = 0.0f;
+    if (r < rows && k < K) v = src[r * rs + k * cs];
+    if (k_fast) tile[i][tx] = v; else tile[tx][i] = v;
+  }
+  __syncthreads();
+  for (int i = ty; i < 32; i += 8) {
+    const int64_t r = r0 + i, k = k0 + tx;
+    if (r < rows && k < Kp) dst[r * Kp + k] = tile[i][tx];
+  }
+}
+
+__global__ void fill_rows_kernel(float* C, int64_t M, int64_t N, int64_t ldc,
+                                 const float* bias, int relu) {
+  const int64_t total = M * N;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / N, n = i - m * N;
+    float v = bias ? bias[n] : 0.0f;
+    if (relu) v = fmaxf(v, 0.0f);
+    C[m * ldc + n] = v;
+  }
+}
+
+// NCHW -> NHWC with channel stride Cp (zero pad).  Tiled transpose per image:
+// tile of 32 pixels x 32 channels.
+__global__ void nchw_to_nhwc_kernel(const float* __restrict__ x, int64_t C, int64_t HW,
+                                    int64_t Cp, float* __restrict__ y) {
+  __shared__ float tile[32][33];
+  const int64_t img = blockIdx.z;
+  const int64_t p0 = (int64_t)blockIdx.x * 32, c0 = (int64_t)blockIdx.y * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  const float* xi = x + img * C * HW;
+  for (int i = ty; i < 32; i += 8) {
+    const int64_t c = c0 + i, p = p0 + tx;
+    tile[i][tx] = (c < C && p < HW) ? xi[c * HW + p] : 0.0f;
+  }
+  __syncthreads();
+  float* yi = y + img * HW * Cp;
+  for (int i = ty; i < 32; i += 8) {
+    const int64_t p = p0 + i, c = c0 + tx;
+    if (p < HW && c < Cp) yi[p * Cp + c] = tile[tx][i];
+  }
+}
+
+// NHWC [N, HW, C] -> NCHW [N, C, HW].
+__global__ void nhwc_to_nchw_kernel(const float* __restrict__ x, int64_t C, int64_t HW,
+                                    float* __restrict__ y) {
+  __shared__ float tile[32][33];
+  const int64_t img = blockIdx.z;
+  const int64_t p0 = (int64_t)blockIdx.x * 32, c0 = (int64_t)blockIdx.y * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  const float* xi = x + img * HW * C;
+  for (int i = ty; i < 32; i += 8) {
+    const int64_t p = p0 + i, c = c0 + tx;
+    tile[i][tx] = (c < C && p < HW) ? xi[p * C + c] : 0.0f;
+  }
+  __syncthreads();
+  float* yi = y + img * C * HW;
+  for (int i = ty; i < 32; i += 8) {
+    const int64_t c = c0 + i, p = p0 + tx;
+    if (c < C && p < HW) yi[c * HW + p] = tile[tx][i];
+  }
+}
+
+// w [Co, Ci, kh, kw] -> wp [Co, kh*kw*Cp] with k = (r*kw + s)*Cp + ci.
+__global__ void prepack_weight_kernel(const float* __restrict__ w, int64_t Co, int64_t Ci,
+                                      int64_t kh, int64_t kw, int64_t Cp, float* __restrict__ wp) {
+  const int64_t Kw = kh * kw * Cp;
+  const int64_t total = Co * Kw;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t co = i / Kw, k = i - co * Kw;
+    const int64_t tap = k / Cp, ci = k - tap * Cp;
+    const int64_t r = tap / kw, s = tap - r * kw;
+    wp[i] = ci < Ci ? w[((co * Ci + ci) * kh + r) * kw + s] : 0.0f;
+  }
+}
+
+// ops::max_pool2d semantics (-inf init, padding skipped, strict >).
+__global__ void max_pool_nchw_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t N,
+                                     int64_t C, int64_t H, int64_t W, int64_t Ho, int64_t Wo,
+                                     int kh, int kw, int sh, int sw, int ph, int pw) {
+  const int64_t total = N * C * Ho * Wo;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t ow = i % Wo, oh = (i / Wo) % Ho, nc = i / (Wo * Ho);
+    const float* xp = x + nc * H * W;
+    float m = -INFINITY;
+    for (int r = 0; r < kh; ++r) {
+      const int64_t hh = oh * sh - ph + r;
+      if (hh < 0 || hh >= H) continue;
+      for (int s = 0; s < kw; ++s) {
+        const int64_t ww = ow * sw - pw + s;
+        if (ww < 0 || ww >= W) continue;
+        const float v = xp[hh * W + ww];
+        if (v > m) m = v;
+      }
+    }
+    y[i] = m;
+  }
+}
+
+// NHWC variant, channel-contiguous (one thread per output element, C fastest).
+__global__ void max_pool_nhwc_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t N,
+                                     int64_t C, int64_t H, int64_t W, int64_t Ho, int64_t Wo,
+                                     int kh, int kw, int sh, int sw, int ph, int pw) {
+  const int64_t total = N * Ho * Wo * C;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t c = i % C, ow = (i / C) % Wo, oh = (i / (C * Wo)) % Ho, n = i / (C * Wo * Ho);
+    float m = -INFINITY;
+    for (int r = 0; r < kh; ++r) {
+      const int64_t hh = oh * sh - ph + r;
+      if (hh < 0 || hh >= H) continue;
+      for (int s = 0; s < kw; ++s) {
+        const int64_t ww = ow * sw - pw + s;
+        if (ww < 0 || ww >= W) continue;
+        const float v = x[((n * H + hh) * W + ww) * C + c];
+        if (v > m) m = v;
+      }
+    }
+    y[i] = m;
+  }
+}
+
+// Global average pool: one warp per (n, c) for NCHW (contiguous HW run);
+// NHWC: one thread per (n, c) striding over pixels (coalesced across c).
+__global__ void avg_pool_nchw_kernel(const float* __restrict__ x, float* __restrict__ y,
+                                     int64_t NC, int64_t HW) {
+  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= NC) return;
+  const float* xp = x + warp * HW;
+  double s = 0.0;
+  for (int64_t j = lane; j < HW; j += 32) s += (double)xp[j];
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) y[warp] = (float)(s / (double)HW);
+}
+
+__global__ void avg_pool_nhwc_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t N,
+                                     int64_t C, int64_t HW) {
+  const int64_t total = N * C;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t n = i / C, c = i - n * C;
+    const float* xp = x + n * HW * C + c;
+    double s = 0.0;
+    for (int64_t j = 0; j < HW; ++j) s += (double)xp[j * C];
+    y[i] = (float)(s / (double)HW);
+  }
+}
+
+__global__ void add_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                           float* __restrict__ y, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    y[i] = a[i] + b[i];
+}
+
+// Rust f32::max(x, 0.0): NaN -> 0.
+__global__ void relu_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = x[i];
+    y[i] = (v > 0.0f) ? v : 0.0f;
+  }
+}
+
+// parts [P, M, Nl] -> C [M, P*Nl].
+__global__ void unsplit_cols_kernel(const float* __restrict__ parts, float* __restrict__ C,
+                                    int64_t P, int64_t M, int64_t Nl) {
+  const int64_t N = P * Nl, total = M * N;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / N, n = i - m * N;
+    const int64_t pr = n / Nl, j = n - pr * Nl;
+    C[i] = parts[(pr * M + m) * Nl + j];
+  }
+}
+
+}  // namespace
+
+int launch_pack_kmajor(const float* src, int64_t rows, int64_t k, int64_t rs, int64_t cs,
+                       float* dst, int64_t kp, cudaStream_t s) {
+  dim3 grid((unsigned)((kp + 31) / 32), (unsigned)((rows + 31) / 32));
+  if (grid.y > 65535) return set_error(RTB_E_UNSUPPORTED, "pack: too many rows");
+  pack_kmajor_kernel<<<grid, dim3(32, 8), 0, s>>>(src, rows, k, rs, cs, dst, kp);
+  return launch_check("pack_kmajor");
+}
+
+int launch_fill_rows(float* C, int64_t M, int64_t N, int64_t ldc, const float* bias, int relu,
+                     cudaStream_t s) {
+  fill_rows_kernel<<<grid_for(M * N), kThreads, 0, s>>>(C, M, N, ldc, bias, relu);
+  return launch_check("fill_rows");
+}
+
+int launch_nchw_to_nhwc_padded(const float* x, int64_t N, int64_t C, int64_t H, int64_t W,
+                               int64_t Cp, float* y, cudaStream_t s) {
+  const int64_t HW = H * W;
+  dim3 grid((unsigned)((HW + 31) / 32), (unsigned)((Cp + 31) / 32), (unsigned)N);
+  if (N > 65535 || grid.y > 65535) return set_error(RTB_E_UNSUPPORTED, "nchw_to_nhwc: too large");
+  nchw_to_nhwc_kernel<<<grid, dim3(32, 8), 0, s>>>(x, C, HW, Cp, y);
+  return launch_check("nchw_to_nhwc");
+}
+
+int launch_nhwc_to_nchw(const float* x, float* y, int64_t N, int64_t C, int64_t HW,
+                        cudaStream_t s) {
+  dim3 grid((unsigned)((HW + 31) / 32), (unsigned)((C + 31) / 32), (unsigned)N);
+  if (N > 65535 || grid.y > 65535) return set_error(RTB_E_UNSUPPORTED, "nhwc_to_nchw: too large");
+  nhwc_to_nchw_kernel<<<grid, dim3(32, 8), 0, s>>>(x, C, HW, y);
+  return launch_check("nhwc_to_nchw");
+}
+
+int launch_prepack_weight(const float* w, int64_t Co, int64_t Ci, int64_t kh, int64_t kw,
+                          int64_t Cp, float* wp, cudaStream_t s) {
+  prepack_weight_kernel<<<grid_for(Co * kh * kw * Cp), kThreads, 0, s>>>(w, Co, Ci, kh, kw, Cp,
+                                                                          wp);
+  return launch_check("prepack_weight");
+}
+
+int launch_max_pool2d(const float* x, float* y, int64_t N, int64_t C, int64_t H, int64_t W,
+                      int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw,
+                      int layout, cudaStream_t s) {
+  const int64_t Ho = (H + 2 * ph - kh) / sh + 1, Wo = (W + 2 * pw - kw) / sw + 1;
+  const int64_t total = N * C * Ho * Wo;
+  if (layout == RTB_LAYOUT_NCHW)
+    max_pool_nchw_kernel<<<grid_for(total), kThreads, 0, s>>>(x, y, N, C, H, W, Ho, Wo, (int)kh,
+                                                             (int)kw, (int)sh, (int)sw, (int)ph,
+                                                             (int)pw);
+  else
+    max_pool_nhwc_kernel<<<grid_for(total), kThreads, 0, s>>>(x, y, N, C, H, W, Ho, Wo, (int)kh,
+                                                             (int)kw, (int)sh, (int)sw, (int)ph,
+                                                             (int)pw);
+  return launch_check("max_pool2d");
+}
+
+int launch_global_avg_pool(const float* x, float* y, int64_t N, int64_t C, int64_t HW, int layout,
+                           cudaStream_t s) {
+  if (layout == RTB_LAYOUT_NCHW) {
+    const int64_t threads = N * C * 32;
+    avg_pool_nchw_kernel<<<(unsigned)((threads + kThreads - 1) / kThreads), kThreads, 0, s>>>(
+        x, y, N * C, HW);
+  } else {
+    avg_pool_nhwc_kernel<<<grid_for(N * C), kThreads, 0, s>>>(x, y, N, C, HW);
+  }
+  return launch_check("global_avg_pool");
+}
+
+int launch_add(const float* a, const float* b, float* y, int64_t n, cudaStream_t s) {
+  add_kernel<<<grid_for(n), kThreads, 0, s>>>(a, b, y, n);
+  return launch_check("add");
+}
+
+int launch_relu(const float* x, float* y, int64_t n, cudaStream_t s) {
+  relu_kernel<<<grid_for(n), kThreads, 0, s>>>(x, y, n);
+  return launch_check("relu");
+}
+
+int launch_unsplit_cols(const float* parts, float* C, int64_t P, int64_t M, int64_t Nl,
+                        cudaStream_t s) {
+  unsplit_cols_kernel<<<grid_for(P * M * Nl), kThreads, 0, s>>>(parts, C, P, M, Nl);
+  return launch_check("unsplit_cols");
+}
+
+}  // namespace rtb

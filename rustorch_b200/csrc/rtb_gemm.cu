@@ -1,0 +1,133 @@
+// Instantiation and launch of the tcgen05 GEMM engine (rtb_gemm.cuh).
+#include <cstdlib>
+#include <mutex>
+
+#include "rtb_gemm.cuh"
+#include "rtb_internal.h"
+
+namespace rtb {
+
+namespace {
+
+template <int BN, bool SPLIT, bool GATHER, int B_MN>
+int launch_variant(rtb_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB,
+                   const GemmParams& p, cudaStream_t stream) {
+  using Cfg = GemmCfg<BN, SPLIT>;
+  using Roles = GemmRoles<SPLIT, GATHER>;
+  auto kern = rtb_gemm_kernel<BN, SPLIT, GATHER, B_MN>;
+  // The attribute is per function and per device; setting it is idempotent
+  // and cheap, so it is set on every launch (covers multi-device processes).
+  cudaError_t e =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemm smem)");
+  const int tiles = p.tiles_m * p.tiles_n;
+  const int grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
+  kern<<<grid, Roles::kThreads, Cfg::kSmemBytes, stream>>>(tmA, tmB, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_status(e, "gemm kernel launch");
+  return RTB_OK;
+}
+
+template <int BN>
+int launch_bn(rtb_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p,
+              const GemmDesc& d, cudaStream_t s) {
+  if (d.gather) {
+    return d.split3 ? launch_variant<BN, true, true, 0>(ctx, tmA, tmB, p, s)
+                    : launch_variant<BN, false, true, 0>(ctx, tmA, tmB, p, s);
+  }
+  if (d.b_mn_major)
+    return d.split3 ? launch_variant<BN, true, false, 1>(ctx, tmA, tmB, p, s)
+                    : launch_variant<BN, false, false, 1>(ctx, tmA, tmB, p, s);
+  return d.split3 ? launch_variant<BN, true, false, 0>(ctx, tmA, tmB, p, s)
+                  : launch_variant<BN, false, false, 0>(ctx, tmA, tmB, p, s);
+}
+
+int env_int(const char* name, int dflt) {
+  const char* v = std::getenv(name);
+  return v ? std::atoi(v) : dflt;
+}
+
+// Column-tile width: the widest tile that still fills every SM once; narrower
+// tiles for small problems (more CTAs), 3xTF32 caps at 128 so the smem ring
+// keeps three stages.
+int pick_bn(rtb_ctx* ctx, const GemmDesc& d) {
+  static const int forced = env_int("RTB_GEMM_BN", 0);
+  if (forced == 64 || forced == 128 || forced == 256) return forced;
+  const int64_t tm = (d.M + kBM - 1) / kBM;
+  const int cands_split[2] = {128, 64};
+  const int cands_fast[3] = {256, 128, 64};
+  const int* c = d.split3 ? cands_split : cands_fast;
+  const int nc = d.split3 ? 2 : 3;
+  for (int i = 0; i < nc; ++i) {
+    const int64_t tiles = tm * ((d.N + c[i] - 1) / c[i]);
+    if (tiles >= ctx->sm_count) return c[i];
+  }
+  return 64;
+}
+
+}  // namespace
+
+int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
+  if (d.M <= 0 || d.N <= 0 || d.K <= 0) return set_error(RTB_E_INVALID, "gemm_run: empty problem");
+  if (d.M > INT32_MAX || d.N > INT32_MAX || d.K > INT32_MAX)
+    return set_error(RTB_E_UNSUPPORTED, "gemm_run: dimension exceeds 2^31-1");
+  const int bn = d.bn ? d.bn : pick_bn(ctx, d);
+
+  CUtensorMap tmA, tmB;
+  int st;
+  if (d.gather) {
+    // A is gathered by the kernel; give the unused map a valid encoding.
+    st = make_tmap_2d(&tmA, d.B, (uint64_t)d.K, (uint64_t)d.N, (uint64_t)d.ldb, kBK, 64);
+  } else {
+    st = make_tmap_2d(&tmA, d.A, (uint64_t)d.K, (uint64_t)d.M, (uint64_t)d.lda, kBK, kBM);
+  }
+  if (st != RTB_OK) return st;
+  if (d.b_mn_major)
+    st = make_tmap_2d(&tmB, d.B, (uint64_t)d.N, (uint64_t)d.K, (uint64_t)d.ldb, 32, kBK);
+  else
+    st = make_tmap_2d(&tmB, d.B, (uint64_t)d.K, (uint64_t)d.N, (uint64_t)d.ldb, kBK, (uint32_t)bn);
+  if (st != RTB_OK) return st;
+
+  GemmParams p{};
+  p.M = (int)d.M;
+  p.N = (int)d.N;
+  p.K = (int)d.K;
+  p.num_kb = (int)((d.K + kBK - 1) / kBK);
+  p.tiles_m = (int)((d.M + kBM - 1) / kBM);
+  p.tiles_n = (int)((d.N + bn - 1) / bn);
+  p.group_m = p.tiles_m < 16 ? p.tiles_m : 16;
+  p.C = d.C;
+  p.ldc = d.ldc;
+  p.bias = d.bias;
+  p.residual = d.residual;
+  p.ldr = d.ldr;
+  p.relu = d.relu;
+  p.out_mode = d.out_mode;
+  p.hw = d.hw;
+  auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+  p.vec_ok = (d.out_mode == 0) && al16(d.C) && (d.ldc % 4 == 0) && (!d.bias || al16(d.bias)) &&
+             (!d.residual || (al16(d.residual) && d.ldr % 4 == 0));
+  p.x = d.x;
+  p.H = d.H;
+  p.W = d.W;
+  p.Cp = d.Cp;
+  p.Ho = d.Ho;
+  p.Wo = d.Wo;
+  p.R = d.R;
+  p.S = d.S;
+  p.sh = d.sh;
+  p.sw = d.sw;
+  p.ph = d.ph;
+  p.pw = d.pw;
+  p.err = ctx->d_err;
+  p.timeout_ns = ctx->timeout_ns;
+
+  switch (bn) {
+    case 64: return launch_bn<64>(ctx, tmA, tmB, p, d, stream);
+    case 128: return launch_bn<128>(ctx, tmA, tmB, p, d, stream);
+    case 256: return launch_bn<256>(ctx, tmA, tmB, p, d, stream);
+    default: return set_error(RTB_E_INVALID, "gemm_run: bad tile width");
+  }
+}
+
+}  // namespace rtb

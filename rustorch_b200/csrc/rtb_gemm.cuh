@@ -1,0 +1,458 @@
+// Persistent, warp-specialised tcgen05 GEMM / implicit-GEMM conv for sm_100a.
+//
+//   C[M,N] = act( A[M,K] . B[K,N] + bias[N] + residual[M,N] )
+//
+// Tiles: BM=128 rows x BN (64/128/256) columns, k-blocks of BK=32 fp32 (one
+// 128-byte swizzle atom).  Roles (warp index):
+//   0        TMA producer: A (unless gathered) and B tiles -> smem ring
+//   1        TMEM allocator + single-thread UMMA issuer (kind::tf32, M=128)
+//   2..5     epilogue: TMEM -> registers -> bias/residual/ReLU -> global
+//   6..9     (3xTF32 only) converters: split each fp32 tile in smem into a
+//            TF32 "hi" part (in place, round-to-nearest) and the exact fp32
+//            remainder "lo" (separate plane); UMMA then accumulates
+//            hi*hi + hi*lo + lo*hi (split-precision TF32, Ootomo & Yokota 2022)
+//   next 4   (conv only) im2col gather: 16-byte cp.async of NHWC input rows
+//            into the swizzled A tile, zero-filling padding taps
+// The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
+// of tile i overlaps the mainloop of tile i+1.
+//
+// Layouts in shared memory (all 128B-swizzled, 1024-byte aligned):
+//   A tile, K-major:  row r (M) at r*128 B, 32 fp32 of K per row.
+//   B tile, K-major:  same with BN rows (B given as [N,K], e.g. Linear.weight).
+//   B tile, MN-major: BN/32 boxes of 32 K-rows x 128 B (32 N values), 4 KB each
+//                     (B given as [K,N] row-major, e.g. Tensor::matmul's rhs).
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "rtb_ptx.cuh"
+
+namespace rtb {
+
+constexpr int kBM = 128;
+constexpr int kBK = 32;                      // fp32 elements per k-block (128 B)
+constexpr int kABytes = kBM * kBK * 4;       // 16 KB
+constexpr int kSmemLimit = 232448;           // 227 KB dynamic shared memory per CTA
+constexpr int kSmemReserve = 2048;           // barriers + alignment slack
+
+struct GemmParams {
+  int M, N, K;
+  int num_kb;            // ceil(K / 32)
+  int tiles_m, tiles_n;
+  int group_m;           // raster: tiles grouped by this many M-tiles
+  // output / epilogue
+  float* C;
+  int64_t ldc;
+  const float* bias;     // [N] or null
+  const float* residual; // same indexing as C, or null
+  int64_t ldr;
+  int relu;
+  int out_mode;          // 0: C[m*ldc+n]; 1: NCHW scatter, m=(img,pix), C[(img*N+n)*hw+pix]
+  int hw;                // Ho*Wo for out_mode 1
+  int vec_ok;            // 16-byte aligned C/residual/bias with ldc, ldr % 4 == 0
+  // implicit-GEMM conv (A gathered from NHWC input with Cp channels, Cp % 4 == 0)
+  const float* x;
+  int H, W, Cp, Ho, Wo, R, S, sh, sw, ph, pw;
+  // failure reporting
+  int* err;
+  unsigned long long timeout_ns;
+};
+
+template <int BN, bool SPLIT>
+struct GemmCfg {
+  static constexpr int kBBytes = BN * kBK * 4;
+  static constexpr int kStageBytes = (kABytes + kBBytes) * (SPLIT ? 2 : 1);
+  static constexpr int kStagesRaw = (kSmemLimit - kSmemReserve) / kStageBytes;
+  static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kSmemReserve;
+  static constexpr int kTmemCols = 2 * BN;  // 128/256/512: power of two >= 32
+  static_assert(kStages >= 2, "need at least two pipeline stages");
+  static_assert(BN == 64 || BN == 128 || BN == 256, "BN must be 64, 128 or 256");
+};
+
+template <bool SPLIT, bool GATHER>
+struct GemmRoles {
+  static constexpr int kWarpTma = 0;
+  static constexpr int kWarpMma = 1;
+  static constexpr int kWarpEpi = 2;                        // 4 warps
+  static constexpr int kWarpConv = 6;                       // 4 warps if SPLIT
+  static constexpr int kWarpGather = 6 + (SPLIT ? 4 : 0);   // 4 warps if GATHER
+  static constexpr int kWarps = 6 + (SPLIT ? 4 : 0) + (GATHER ? 4 : 0);
+  static constexpr int kThreads = kWarps * 32;
+};
+
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int group_m, int& tm,
+                                            int& tn) {
+  const int group_size = group_m * tiles_n;
+  const int g = t / group_size;
+  const int first_m = g * group_m;
+  int gm = tiles_m - first_m;
+  gm = gm < group_m ? gm : group_m;
+  const int r = t - g * group_size;
+  tm = first_m + r % gm;
+  tn = r / gm;
+}
+
+__device__ __forceinline__ float4 tf32_hi4(float4 v) {
+  float4 h;
+  uint32_t a, b, c, d;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(a) : "f"(v.x));
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(b) : "f"(v.y));
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(c) : "f"(v.z));
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(d) : "f"(v.w));
+  h.x = __uint_as_float(a);
+  h.y = __uint_as_float(b);
+  h.z = __uint_as_float(c);
+  h.w = __uint_as_float(d);
+  return h;
+}
+
+// Epilogue for one thread's row m and 32 consecutive columns n0..n0+31.
+__device__ __forceinline__ void epilogue_store32(const GemmParams& p, int m, int n0,
+                                                 const uint32_t (&r)[32]) {
+  if (m >= p.M) return;
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+  const bool full = (n0 + 32 <= p.N);
+  if (p.out_mode == 0) {
+    float* crow = p.C + (int64_t)m * p.ldc;
+    const float* rrow = p.residual ? p.residual + (int64_t)m * p.ldr : nullptr;
+    if (full && p.vec_ok) {
+      if (p.bias) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          const float4 b = __ldg(reinterpret_cast<const float4*>(p.bias + n0 + j));
+          v[j] += b.x; v[j + 1] += b.y; v[j + 2] += b.z; v[j + 3] += b.w;
+        }
+      }
+      if (rrow) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          const float4 q = __ldg(reinterpret_cast<const float4*>(rrow + n0 + j));
+          v[j] += q.x; v[j + 1] += q.y; v[j + 2] += q.z; v[j + 3] += q.w;
+        }
+      }
+      if (p.relu) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.0f);
+      }
+#pragma unroll
+      for (int j = 0; j < 32; j += 4)
+        *reinterpret_cast<float4*>(crow + n0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int n = n0 + j;
+        if (n < p.N) {
+          float o = v[j];
+          if (p.bias) o += __ldg(p.bias + n);
+          if (rrow) o += __ldg(rrow + n);
+          if (p.relu) o = fmaxf(o, 0.0f);
+          crow[n] = o;
+        }
+      }
+    }
+  } else {
+    const int img = m / p.hw;
+    const int pix = m - img * p.hw;
+    const int64_t base = (int64_t)img * p.N * p.hw + pix;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int n = n0 + j;
+      if (n < p.N) {
+        const int64_t off = base + (int64_t)n * p.hw;
+        float o = v[j];
+        if (p.bias) o += __ldg(p.bias + n);
+        if (p.residual) o += __ldg(p.residual + off);
+        if (p.relu) o = fmaxf(o, 0.0f);
+        p.C[off] = o;
+      }
+    }
+  }
+}
+
+// B_MN: 0 = B is K-major ([N,K] in memory), 1 = MN-major ([K,N] row-major).
+template <int BN, bool SPLIT, bool GATHER, int B_MN>
+__global__ void __launch_bounds__(GemmRoles<SPLIT, GATHER>::kThreads, 1)
+    rtb_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const GemmParams p) {
+  using Cfg = GemmCfg<BN, SPLIT>;
+  using Roles = GemmRoles<SPLIT, GATHER>;
+  constexpr int S = Cfg::kStages;
+  constexpr int kBBytes = Cfg::kBBytes;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sA = base;                                  // S x 16 KB
+  uint8_t* sB = sA + S * kABytes;                      // S x BN*128
+  uint8_t* sAlo = sB + S * kBBytes;                    // SPLIT: S x 16 KB
+  uint8_t* sBlo = sAlo + (SPLIT ? S * kABytes : 0);    // SPLIT: S x BN*128
+  uint8_t* tail = sBlo + (SPLIT ? S * kBBytes : 0);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(tail);
+  uint64_t* conv_bar = full_bar + S;
+  uint64_t* empty_bar = conv_bar + S;
+  uint64_t* tfull_bar = empty_bar + S;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_tiles = p.tiles_m * p.tiles_n;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full_bar[s], 1 + (GATHER ? 128 : 0));
+      mbar_init(&conv_bar[s], 128);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], 128);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == Roles::kWarpTma && lane == 0) {
+    if (!GATHER) tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == Roles::kWarpMma) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == Roles::kWarpTma) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      const uint32_t tx = (GATHER ? 0 : kABytes) + kBBytes;
+      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+        int tm, tn;
+        tile_coords(t, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait_bounded(&empty_bar[s], ph ^ 1, abort_flag, p.err, DEV_TIMEOUT_EMPTY,
+                                 p.timeout_ns))
+            break;
+          mbar_arrive_expect_tx(&full_bar[s], tx);
+          if (!GATHER) tma_load_2d(sA + s * kABytes, &tmA, &full_bar[s], kb * kBK, tm * kBM);
+          if (B_MN == 0) {
+            tma_load_2d(sB + s * kBBytes, &tmB, &full_bar[s], kb * kBK, tn * BN);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 32; ++j)
+              tma_load_2d(sB + s * kBBytes + j * 4096, &tmB, &full_bar[s], tn * BN + j * 32,
+                          kb * kBK);
+          }
+          if (++s == S) { s = 0; ph ^= 1; }
+        }
+      }
+    }
+  } else if (warp == Roles::kWarpMma) {
+    // ------------------------------------------------------------ UMMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_tf32(kBM, BN, 0, B_MN);
+      int s = 0;
+      uint32_t ph = 0;
+      int it = 0;
+      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x, ++it) {
+        const int b = it & 1;
+        const uint32_t use = (uint32_t)(it >> 1);
+        if (!mbar_wait_bounded(&tempty_bar[b], (use & 1) ^ 1, abort_flag, p.err,
+                               DEV_TIMEOUT_TMEM_EMPTY, p.timeout_ns))
+          break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(b * BN);
+        bool ok = true;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          uint64_t* ready = SPLIT ? &conv_bar[s] : &full_bar[s];
+          if (!mbar_wait_bounded(ready, ph, abort_flag, p.err,
+                                 SPLIT ? DEV_TIMEOUT_CONV : DEV_TIMEOUT_FULL, p.timeout_ns)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + s * kABytes);
+          const uint32_t b_addr = smem_u32(sB + s * kBBytes);
+          const uint32_t alo_addr = smem_u32(sAlo + s * kABytes);
+          const uint32_t blo_addr = smem_u32(sBlo + s * kBBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 8; ++k) {
+            // A K-major: +32 B per 8-element k step inside the 128 B swizzle row.
+            const uint64_t da = umma_desc_sw128(a_addr + k * 32, 16, 1024);
+            const uint64_t db = B_MN == 0 ? umma_desc_sw128(b_addr + k * 32, 16, 1024)
+                                          : umma_desc_sw128(b_addr + k * 1024, 4096, 1024);
+            const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+            umma_tf32(d_tmem, da, db, idesc, acc);
+            if (SPLIT) {
+              const uint64_t dal = umma_desc_sw128(alo_addr + k * 32, 16, 1024);
+              const uint64_t dbl = B_MN == 0 ? umma_desc_sw128(blo_addr + k * 32, 16, 1024)
+                                             : umma_desc_sw128(blo_addr + k * 1024, 4096, 1024);
+              umma_tf32(d_tmem, da, dbl, idesc, 1u);
+              umma_tf32(d_tmem, dal, db, idesc, 1u);
+            }
+          }
+          umma_commit(&empty_bar[s]);
+          if (++s == S) { s = 0; ph ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit(&tfull_bar[b]);
+      }
+    }
+  } else if (warp >= Roles::kWarpEpi && warp < Roles::kWarpEpi + 4) {
+    // ------------------------------------------------------------ epilogue
+    const int lane_base = 32 * (warp & 3);
+    const int row = lane_base + lane;
+    int it = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
+      int tm, tn;
+      tile_coords(t, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
+      const int b = it & 1;
+      const uint32_t use = (uint32_t)(it >> 1);
+      // tcgen05.ld is .sync.aligned: the whole warp must agree on the outcome.
+      int ok = 0;
+      if (lane == 0)
+        ok = mbar_wait_bounded(&tfull_bar[b], use & 1, abort_flag, p.err, DEV_TIMEOUT_TMEM_FULL,
+                               p.timeout_ns);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      const int m = tm * kBM + row;
+      const uint32_t taddr = tmem_base + ((uint32_t)lane_base << 16) + (uint32_t)(b * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(taddr + (uint32_t)c, r);
+        tmem_ld_wait();
+        if (c + 32 == BN) {
+          tc_fence_before();
+          mbar_arrive(&tempty_bar[b]);
+        }
+        epilogue_store32(p, m, tn * BN + c, r);
+      }
+    }
+  } else if (SPLIT && warp >= Roles::kWarpConv && warp < Roles::kWarpConv + 4) {
+    // ------------------------------------------------------------ converters
+    const int ct = threadIdx.x - Roles::kWarpConv * 32;  // 0..127
+    int s = 0;
+    uint32_t ph = 0;
+    for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+      bool ok = true;
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        if (!mbar_wait_bounded(&full_bar[s], ph, abort_flag, p.err, DEV_TIMEOUT_LOADED,
+                               p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        float4* a = reinterpret_cast<float4*>(sA + s * kABytes);
+        float4* alo = reinterpret_cast<float4*>(sAlo + s * kABytes);
+#pragma unroll 4
+        for (int i = ct; i < kABytes / 16; i += 128) {
+          const float4 v = a[i];
+          const float4 h = tf32_hi4(v);
+          a[i] = h;
+          alo[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+        }
+        float4* bb = reinterpret_cast<float4*>(sB + s * kBBytes);
+        float4* blo = reinterpret_cast<float4*>(sBlo + s * kBBytes);
+#pragma unroll 4
+        for (int i = ct; i < kBBytes / 16; i += 128) {
+          const float4 v = bb[i];
+          const float4 h = tf32_hi4(v);
+          bb[i] = h;
+          blo[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&conv_bar[s]);
+        if (++s == S) { s = 0; ph ^= 1; }
+      }
+      if (!ok) break;
+    }
+  } else if (GATHER && warp >= Roles::kWarpGather && warp < Roles::kWarpGather + 4) {
+    // ------------------------------------------------------------ im2col gather
+    constexpr int LAG = (S - 1) < 2 ? (S - 1) : 2;  // cp.async groups kept in flight
+    const int r = threadIdx.x - Roles::kWarpGather * 32;  // tile row 0..127
+    const int swz = r & 7;
+    const int Ktot = p.R * p.S * p.Cp;
+    const int HoWo = p.Ho * p.Wo;
+    int s = 0;
+    uint32_t ph = 0;
+    int pend_s[3] = {0, 0, 0};  // ring of stages whose arrive is deferred
+    int npend = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < num_tiles && ok && !*abort_flag; t += gridDim.x) {
+      int tm, tn;
+      tile_coords(t, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
+      const int m = tm * kBM + r;
+      const bool mvalid = m < p.M;
+      const int img = mvalid ? m / HoWo : 0;
+      const int rem = mvalid ? m - img * HoWo : 0;
+      const int oh = rem / p.Wo;
+      const int ow = rem - oh * p.Wo;
+      const int ih0 = oh * p.sh - p.ph;
+      const int iw0 = ow * p.sw - p.pw;
+      const float* ximg = p.x + (int64_t)img * p.H * p.W * p.Cp;
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        if (!mbar_wait_bounded(&empty_bar[s], ph ^ 1, abort_flag, p.err, DEV_TIMEOUT_EMPTY,
+                               p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        uint8_t* dst_row = sA + s * kABytes + r * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const int k = kb * kBK + c * 4;
+          const int tap = k / p.Cp;
+          const int ci = k - tap * p.Cp;
+          const int rr = tap / p.S;
+          const int ss = tap - rr * p.S;
+          const int ih = ih0 + rr, iw = iw0 + ss;
+          const bool v = mvalid && k < Ktot && ih >= 0 && ih < p.H && iw >= 0 && iw < p.W;
+          const float* src = v ? ximg + ((int64_t)ih * p.W + iw) * p.Cp + ci : p.x;
+          cp_async_16(dst_row + ((c ^ swz) << 4), src, v ? 16u : 0u);
+        }
+        cp_async_commit();
+        pend_s[npend++] = s;
+        if (npend > LAG) {
+          if (LAG == 2) cp_async_wait<2>();
+          else if (LAG == 1) cp_async_wait<1>();
+          else cp_async_wait<0>();
+          fence_proxy_async_smem();
+          mbar_arrive(&full_bar[pend_s[0]]);
+          for (int i = 1; i < npend; ++i) pend_s[i - 1] = pend_s[i];
+          --npend;
+        }
+        if (++s == S) { s = 0; ph ^= 1; }
+      }
+    }
+    cp_async_wait<0>();
+    fence_proxy_async_smem();
+    for (int i = 0; i < npend; ++i) mbar_arrive(&full_bar[pend_s[i]]);
+  }
+
+  // ------------------------------------------------------------ teardown
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag) {
+    // Give in-flight TMA / cp.async copies time to land before the CTA's
+    // shared memory is released (bounded: ~1 ms).
+    const uint64_t t0 = globaltimer_ns();
+    while (globaltimer_ns() - t0 < 1000000ull) __nanosleep(1000);
+    __syncthreads();
+  }
+  if (warp == Roles::kWarpMma) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+}  // namespace rtb

@@ -1,0 +1,106 @@
+// Internal declarations shared by the C-ABI implementation files.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <mutex>
+#include <string>
+
+#include "../../include/rustorch_b200.h"
+
+struct rtb_ctx {
+  int device = 0;
+  int sm_count = 0;
+  int cc_major = 0, cc_minor = 0;
+  size_t total_mem = 0;
+  cudaStream_t stream = nullptr;  // the context's own stream (non-blocking)
+  int* d_err = nullptr;           // device error word (bounded-wait timeouts)
+  uint64_t timeout_ns = 2000000000ull;
+  int default_precision = RTB_PREC_3XTF32;
+};
+
+namespace rtb {
+
+// Records `msg` as this thread's last error and returns `status`.
+int set_error(int status, const std::string& msg);
+int cuda_status(cudaError_t e, const char* what);
+
+inline cudaStream_t pick_stream(rtb_ctx* ctx, void* stream) {
+  return stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+}
+
+// RAII guard making ctx->device current for the calling thread.
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+// 2-D fp32 tensor map (innermost dim0 contiguous, row stride in elements).
+int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1,
+                 uint64_t row_stride_elems, uint32_t box0, uint32_t box1);
+
+// What the GEMM engine computes; see rtb_gemm.cuh (GemmParams) for the epilogue.
+struct GemmDesc {
+  int64_t M = 0, N = 0, K = 0;
+  // A: K-major [M, K] with row stride lda (GATHER: unused; see conv fields)
+  const float* A = nullptr;
+  int64_t lda = 0;
+  // B: b_mn_major=0 -> [N, K] row stride ldb; 1 -> [K, N] row stride ldb
+  const float* B = nullptr;
+  int64_t ldb = 0;
+  int b_mn_major = 0;
+  // epilogue
+  float* C = nullptr;
+  int64_t ldc = 0;
+  const float* bias = nullptr;
+  const float* residual = nullptr;
+  int64_t ldr = 0;
+  int relu = 0;
+  int out_mode = 0;  // 0 row-major, 1 NCHW scatter
+  int hw = 0;
+  // conv gather
+  int gather = 0;
+  const float* x = nullptr;
+  int H = 0, W = 0, Cp = 0, Ho = 0, Wo = 0, R = 0, S = 0, sh = 1, sw = 1, ph = 0, pw = 0;
+  int split3 = 1;     // 3xTF32 (1) or TF32 (0)
+  int bn = 0;         // 0 = heuristic
+};
+
+// Validated launch of the tcgen05 engine (A/B already TMA-compatible).
+int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream);
+
+// Aux kernels (rtb_aux.cu).
+int launch_pack_kmajor(const float* src, int64_t rows, int64_t k, int64_t rs, int64_t cs,
+                       float* dst, int64_t kp, cudaStream_t s);
+int launch_fill_rows(float* C, int64_t M, int64_t N, int64_t ldc, const float* bias, int relu,
+                     cudaStream_t s);
+int launch_nchw_to_nhwc_padded(const float* x, int64_t N, int64_t C, int64_t H, int64_t W,
+                               int64_t Cp, float* y, cudaStream_t s);
+int launch_prepack_weight(const float* w, int64_t Co, int64_t Ci, int64_t kh, int64_t kw,
+                          int64_t Cp, float* wp, cudaStream_t s);
+int launch_max_pool2d(const float* x, float* y, int64_t N, int64_t C, int64_t H, int64_t W,
+                      int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw,
+                      int layout, cudaStream_t s);
+int launch_global_avg_pool(const float* x, float* y, int64_t N, int64_t C, int64_t HW, int layout,
+                           cudaStream_t s);
+int launch_add(const float* a, const float* b, float* y, int64_t n, cudaStream_t s);
+int launch_relu(const float* x, float* y, int64_t n, cudaStream_t s);
+int launch_unsplit_cols(const float* parts, float* C, int64_t P, int64_t M, int64_t Nl,
+                        cudaStream_t s);
+int launch_nhwc_to_nchw(const float* x, float* y, int64_t N, int64_t C, int64_t HW,
+                        cudaStream_t s);
+
+// Stream-ordered workspace.
+int ws_alloc(rtb_ctx* ctx, void** p, size_t bytes, cudaStream_t s);
+void ws_free(void* p, cudaStream_t s);
+
+}  // namespace rtb

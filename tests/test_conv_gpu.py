@@ -1,0 +1,138 @@
+"""Conv2d (+bias, +residual, +ReLU) parity on the B200: the implicit-GEMM
+tcgen05 kernels against the oracle's restatement of ops::conv2d /
+nn::Conv2d::forward, and the pooling kernels against ops::max_pool2d."""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+TOL = {0: 1e-5, 1: 5e-3}
+
+
+def _dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def _host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def test_kat_conv2d(gpu, kats):
+    k = kats["conv2d_3x3_k2"]
+    x = np.array(k["x"], np.float32).reshape(k["x_shape"])
+    w = np.array(k["w"], np.float32).reshape(k["w_shape"])
+    for prec in (0, 1):
+        y = _host(gpu.conv2d_fwd(_dev(x), _dev(w), stride=tuple(k["stride"]),
+                                 padding=tuple(k["padding"]), precision=prec))
+        assert np.max(np.abs(y.reshape(-1) - np.array(k["expected"]))) < k["abs_tol"]
+
+
+def test_kat_jit_conv_relu_ones(gpu, kats):
+    k = kats["jit_conv2d_relu_ones"]
+    x = torch.full(k["x_shape"], k["x_fill"], device="cuda")
+    w = torch.full(k["w_shape"], k["w_fill"], device="cuda")
+    y = _host(gpu.conv2d_fwd(x, w, act=gpu.ACT_RELU))
+    assert list(y.shape) == k["out_shape"]
+    assert abs(y.reshape(-1)[0] - k["expected_first"]) < k["abs_tol"]
+
+
+def test_kat_bench_conv_fill(gpu, kats):
+    k = kats["bench_conv2d_fill"]
+    x = torch.full(k["x_shape"], k["x_fill"], device="cuda")
+    w = torch.full(k["w_shape"], k["w_fill"], device="cuda")
+    y = _host(gpu.conv2d_fwd(x, w, stride=tuple(k["stride"]), padding=tuple(k["padding"])))
+    interior = y[:, :, 1:-1, 1:-1]
+    assert np.max(np.abs(interior / k["expected_interior"] - 1.0)) < k["rel_tol"]
+
+
+def _cfg2_inputs(orc):
+    """Conv2d+bias+ReLU, ResNet-50 stage-2 3x3 layer: x [32,128,28,28] ~ N(0,1),
+    w Kaiming-normal std sqrt(2/1152), b ~ U(-0.1, 0.1), seed 1."""
+    x = orc.normal((32, 128, 28, 28), 1, 0)
+    w = orc.normal((128, 128, 3, 3), 1, 1, 0.0, float(np.sqrt(2.0 / (128 * 9))))
+    b = orc.uniform((128,), 1, 2, -0.1, 0.1)
+    return x, w, b
+
+
+@pytest.mark.parametrize("prec", [0, 1])
+def test_conv_bias_relu_resnet50_layer(gpu, orc, prec):
+    x, w, b = _cfg2_inputs(orc)
+    pre = orc.conv2d_f64(x, w, (1, 1), (1, 1)) + b.astype(np.float64)[None, :, None, None]
+    y = _host(gpu.conv2d_fwd(_dev(x), _dev(w), _dev(b), (1, 1), (1, 1), act=gpu.ACT_RELU,
+                             precision=prec))
+    assert orc.rel_frob(y, np.maximum(pre, 0)) <= TOL[prec]
+    mask = np.abs(pre) >= 1e-5
+    assert np.array_equal((y > 0)[mask], (pre > 0)[mask])
+    if prec == 0:
+        # the reference's own CPU path (im2col + parallel core, f32) on the same inputs
+        y32, _ = orc.conv2d_bias_relu(x, w, b, (1, 1), (1, 1))
+        assert orc.rel_frob(y, y32.astype(np.float64)) <= 2e-5
+
+
+@pytest.mark.parametrize("shape,wshape,stride,pad", [
+    ((2, 3, 224, 224), (64, 3, 7, 7), (2, 2), (3, 3)),      # ResNet stem, Ci=3 -> padded to 4
+    ((4, 64, 56, 56), (64, 64, 3, 3), (1, 1), (1, 1)),
+    ((4, 64, 56, 56), (128, 64, 3, 3), (2, 2), (1, 1)),
+    ((4, 64, 56, 56), (128, 64, 1, 1), (2, 2), (0, 0)),     # downsample 1x1 s2
+    ((2, 256, 14, 14), (256, 256, 3, 3), (1, 1), (1, 1)),
+    ((2, 512, 7, 7), (512, 512, 3, 3), (1, 1), (1, 1)),
+    ((3, 5, 9, 11), (7, 5, 3, 2), (1, 2), (2, 0)),          # odd everything
+    ((1, 36, 5, 5), (10, 36, 5, 5), (1, 1), (0, 0)),        # K-blocks straddle taps
+])
+@pytest.mark.parametrize("prec", [0, 1])
+def test_conv_shapes(gpu, orc, shape, wshape, stride, pad, prec):
+    x = orc.normal(shape, 5, 1)
+    w = orc.normal(wshape, 5, 2, 0.0, float(np.sqrt(2.0 / np.prod(wshape[1:]))))
+    ref = orc.conv2d_f64(x, w, stride, pad)
+    y = _host(gpu.conv2d_fwd(_dev(x), _dev(w), None, stride, pad, precision=prec))
+    assert y.shape == ref.shape
+    assert orc.rel_frob(y, ref) <= TOL[prec]
+
+
+def test_conv_nhwc_residual(gpu, orc):
+    """NHWC in/out with a residual and ReLU (a ResNet basic-block tail)."""
+    x = orc.normal((2, 16, 16, 64), 6, 1)       # NHWC
+    w = orc.normal((64, 64, 3, 3), 6, 2, 0.0, 0.06)
+    b = orc.uniform((64,), 6, 3, -0.1, 0.1)
+    r = orc.normal((2, 16, 16, 64), 6, 4)       # NHWC residual
+    xn = np.ascontiguousarray(x.transpose(0, 3, 1, 2))
+    pre = orc.conv2d_f64(xn, w, (1, 1), (1, 1)) + b.astype(np.float64)[None, :, None, None]
+    pre = pre.transpose(0, 2, 3, 1) + r.astype(np.float64)
+    y = _host(gpu.conv2d_fwd(_dev(x), _dev(w), _dev(b), (1, 1), (1, 1), residual=_dev(r),
+                             act=gpu.ACT_RELU, x_layout=gpu.LAYOUT_NHWC, y_layout=gpu.LAYOUT_NHWC))
+    assert orc.rel_frob(y, np.maximum(pre, 0)) <= 1e-5
+
+
+def test_conv_errors(gpu):
+    x = torch.ones((1, 3, 8, 8), device="cuda")
+    with pytest.raises(ValueError, match="must match input channels"):
+        gpu.conv2d_fwd(x, torch.ones((4, 2, 3, 3), device="cuda"))
+    with pytest.raises(gpu.RtbError) as e:
+        gpu.conv2d_fwd(x, torch.ones((4, 3, 9, 9), device="cuda"))
+    assert e.value.status == 1
+
+
+def test_max_pool_bit_exact(gpu, orc):
+    x = orc.normal((2, 64, 112, 112), 8, 1)
+    ref = orc.max_pool2d(x, (3, 3), (2, 2), (1, 1))
+    y = _host(gpu.max_pool2d(_dev(x)))
+    np.testing.assert_array_equal(y, ref)
+    yh = _host(gpu.max_pool2d(_dev(x.transpose(0, 2, 3, 1)), layout=gpu.LAYOUT_NHWC))
+    np.testing.assert_array_equal(yh.transpose(0, 3, 1, 2), ref)
+
+
+def test_global_avg_pool(gpu, orc):
+    x = orc.normal((4, 512, 7, 7), 8, 2)
+    ref = orc.global_avg_pool(x)
+    np.testing.assert_allclose(_host(gpu.global_avg_pool(_dev(x))), ref, rtol=1e-6, atol=1e-7)
+    yh = _host(gpu.global_avg_pool(_dev(x.transpose(0, 2, 3, 1)), layout=gpu.LAYOUT_NHWC))
+    np.testing.assert_allclose(yh, ref, rtol=1e-6, atol=1e-7)
+
+
+def test_add_relu(gpu, orc):
+    a = orc.normal((1000,), 9, 1)
+    b = orc.normal((1000,), 9, 2)
+    np.testing.assert_array_equal(_host(gpu.add(_dev(a), _dev(b))), a + b)
+    np.testing.assert_array_equal(_host(gpu.relu(_dev(a))), orc.relu(a))

@@ -1,0 +1,177 @@
+"""GEMM parity on the B200: the tcgen05 kernels (through the C ABI) against the
+oracle's restatement of the reference's CPU matmul, on seeded inputs.
+
+Tolerances (relative Frobenius error against the f64-accumulated oracle):
+3xTF32 <= 1e-5, TF32 <= 5e-3.  ReLU zero patterns must agree wherever the
+f64 pre-activation satisfies |x| >= 1e-5."""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+TOL = {0: 1e-5, 1: 5e-3}  # PREC_3XTF32, PREC_TF32
+
+
+def _dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def _host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def _relu_pattern_ok(y, pre64):
+    mask = np.abs(pre64) >= 1e-5
+    return np.array_equal((y > 0)[mask], (pre64 > 0)[mask])
+
+
+def test_kat_matmul_2x2(gpu, kats):
+    k = kats["matmul_2x2"]
+    a = np.array(k["a"], np.float32).reshape(k["a_shape"])
+    b = np.array(k["b"], np.float32).reshape(k["b_shape"])
+    for prec in (0, 1):
+        c = _host(gpu.sgemm(_dev(a), _dev(b), precision=prec))
+        assert np.max(np.abs(c.reshape(-1) - np.array(k["expected"]))) < k["abs_tol"]
+
+
+def test_kat_bench_ones(gpu, kats):
+    k = kats["bench_matmul_ones"]
+    a = torch.ones((k["m"], k["k"]), device="cuda")
+    b = torch.ones((k["k"], k["n"]), device="cuda")
+    for prec in (0, 1):
+        c = _host(gpu.sgemm(a, b, precision=prec))
+        assert np.all(c == k["expected_all"])
+
+
+@pytest.mark.parametrize("prec", [0, 1])
+def test_gemm_1024_seed0(gpu, orc, prec):
+    """The 1024^3 f32 matmul workload (A, B ~ N(0,1), seed 0)."""
+    a = orc.normal((1024, 1024), 0, 0)
+    b = orc.normal((1024, 1024), 0, 1)
+    ref = orc.matmul_f64(a, b)
+    c = _host(gpu.sgemm(_dev(a), _dev(b), precision=prec))
+    err = orc.rel_frob(c, ref)
+    assert err <= TOL[prec], err
+    # and against the f32 restatement of the reference's own kernel
+    c32, choice = orc.matmul(a, b)
+    assert choice == 0
+    assert orc.rel_frob(c, c32.astype(np.float64)) <= 2 * TOL[prec]
+
+
+@pytest.mark.parametrize("m,n,k", [
+    (1, 1, 1), (3, 5, 7), (17, 33, 65), (128, 128, 32), (129, 257, 31), (200, 1000, 512),
+    (64, 64, 2048), (300, 96, 100), (1, 4096, 256), (2048, 8, 64), (513, 130, 1027)])
+@pytest.mark.parametrize("prec", [0, 1])
+def test_gemm_shapes(gpu, orc, m, n, k, prec):
+    a = orc.normal((m, k), 7, 1)
+    b = orc.normal((k, n), 7, 2)
+    ref = orc.matmul_f64(a, b)
+    c = _host(gpu.sgemm(_dev(a), _dev(b), precision=prec))
+    assert c.shape == (m, n)
+    assert orc.rel_frob(c, ref) <= TOL[prec]
+
+
+@pytest.mark.parametrize("prec", [0, 1])
+def test_linear_transposed_weight_bias_relu(gpu, orc, prec):
+    """nn::Linear: x.matmul(w.t()) + b with ReLU; w.t() is passed as a
+    transposed view (K-major B) without a copy."""
+    x = orc.normal((333, 256), 2, 1)
+    w = orc.uniform((500, 256), 2, 2, -0.1, 0.1)
+    b = orc.uniform((500,), 2, 3, -0.1, 0.1)
+    pre = orc.matmul_f64(x, np.ascontiguousarray(w.T)) + b.astype(np.float64)
+    wt = _dev(w).t()
+    assert wt.stride(0) == 1
+    y = _host(gpu.sgemm(_dev(x), wt, bias=_dev(b), act=gpu.ACT_RELU, precision=prec))
+    assert orc.rel_frob(y, np.maximum(pre, 0)) <= TOL[prec]
+    assert _relu_pattern_ok(y, pre)
+    ref32 = orc.linear(x, w, b, relu=True)
+    assert orc.rel_frob(y, ref32.astype(np.float64)) <= 2 * TOL[prec] + 1e-6
+
+
+def test_matmul_fused_none_bias(gpu, orc):
+    a = orc.normal((100, 70), 3, 1)
+    b = orc.normal((70, 60), 3, 2)
+    bias = orc.normal((60,), 3, 3)
+    ref = orc.matmul_f64(a, b) + bias.astype(np.float64)
+    y = _host(gpu.sgemm(_dev(a), _dev(b), bias=_dev(bias)))
+    assert orc.rel_frob(y, ref) <= 1e-5
+    y32 = orc.matmul_fused(a, b, bias, 0)
+    assert orc.rel_frob(y32, ref) <= 1e-6
+
+
+def test_transposed_a_and_strided(gpu, orc):
+    a = orc.normal((96, 80), 9, 1)
+    b = orc.normal((80, 72), 9, 2)
+    ref = orc.matmul_f64(a, b)
+    at = _dev(np.ascontiguousarray(a.T)).t()          # stride (1, 96): transA path
+    c = _host(gpu.sgemm(at, _dev(b)))
+    assert orc.rel_frob(c, ref) <= 1e-5
+    big = _dev(np.pad(a, ((0, 0), (0, 3))))[:, :80]   # lda = 83: unaligned -> packed
+    c = _host(gpu.sgemm(big, _dev(b)))
+    assert orc.rel_frob(c, ref) <= 1e-5
+
+
+def test_k_zero_gives_bias(gpu):
+    a = torch.empty((5, 0), device="cuda")
+    b = torch.empty((0, 7), device="cuda")
+    bias = torch.arange(7, dtype=torch.float32, device="cuda") - 3
+    c = _host(gpu.sgemm(a, b, bias=bias, act=gpu.ACT_RELU))
+    assert np.array_equal(c, np.tile(np.maximum(np.arange(7) - 3, 0), (5, 1)).astype(np.float32))
+    c = _host(gpu.sgemm(a, b))
+    assert np.all(c == 0)
+
+
+def test_empty_m_n(gpu):
+    a = torch.empty((0, 4), device="cuda")
+    b = torch.ones((4, 3), device="cuda")
+    assert gpu.sgemm(a, b).shape == (0, 3)
+
+
+def test_errors(gpu):
+    a = torch.ones((4, 3), device="cuda")
+    with pytest.raises(ValueError, match="Matmul dimension mismatch"):
+        gpu.sgemm(a, torch.ones((4, 3), device="cuda"))
+    with pytest.raises(ValueError, match="Matmul only supports 2D"):
+        gpu.sgemm(torch.ones((2, 2, 2), device="cuda"), a)
+    with pytest.raises(gpu.RtbError) as e:
+        gpu.sgemm(a, torch.ones((3, 4), device="cuda"), act=gpu.ACT_SIGMOID)
+    assert e.value.status == 5
+
+
+@pytest.mark.parametrize("prec", [0, 1])
+def test_batched(gpu, orc, prec):
+    a = orc.normal((3, 65, 40), 5, 1)
+    b = orc.normal((3, 40, 33), 5, 2)
+    c = _host(gpu.sgemm_batched(_dev(a), _dev(b), precision=prec))
+    for i in range(3):
+        assert orc.rel_frob(c[i], orc.matmul_f64(a[i], b[i])) <= TOL[prec]
+
+
+def test_skinny_8192_sampled(gpu, orc):
+    """Skinny M=16 with N=K=8192 at full size; checked on sampled entries
+    against f64 dot products (a full f64 GEMM would take minutes on the CPU)."""
+    a = orc.normal((16, 8192), 4, 1)
+    b = orc.normal((8192, 8192), 4, 2)
+    c = _host(gpu.sgemm(_dev(a), _dev(b)))
+    rng = np.random.default_rng(0)
+    rows = rng.integers(0, 16, 4096)
+    cols = rng.integers(0, 8192, 4096)
+    ref = orc.matmul_f64_sampled(a, b, rows, cols)
+    assert orc.rel_frob(c[rows, cols], ref) <= 1e-5
+
+
+def test_square_4096_sampled_and_linearity(gpu, orc):
+    a = orc.normal((4096, 4096), 4, 3)
+    b = orc.normal((4096, 4096), 4, 4)
+    da, db = _dev(a), _dev(b)
+    c = gpu.sgemm(da, db)
+    rng = np.random.default_rng(1)
+    rows = rng.integers(0, 4096, 4096)
+    cols = rng.integers(0, 4096, 4096)
+    ref = orc.matmul_f64_sampled(a, b, rows, cols)
+    assert orc.rel_frob(_host(c)[rows, cols], ref) <= 1e-5
+    # linearity: A.(2B) == 2(A.B) exactly (scaling by 2 is exact in every split)
+    c2 = gpu.sgemm(da, db * 2)
+    assert torch.equal(c2, c * 2)

@@ -1,0 +1,149 @@
+"""The oracle pinned to the reference's own known-answer tests and checked
+against an independent float64 computation (CPU only)."""
+import numpy as np
+import pytest
+import torch
+
+
+def test_kat_matmul_2x2(orc, kats):
+    k = kats["matmul_2x2"]
+    a = np.array(k["a"], np.float32).reshape(k["a_shape"])
+    b = np.array(k["b"], np.float32).reshape(k["b_shape"])
+    c, choice = orc.matmul(a, b)
+    assert choice == 0  # 2x2 is below the parallel-core thresholds -> sgemm
+    assert np.max(np.abs(c.reshape(-1) - np.array(k["expected"]))) < k["abs_tol"]
+    pc = orc.matmul_parallel_core(a, b)
+    assert np.max(np.abs(pc.reshape(-1) - np.array(k["expected"]))) < k["abs_tol"]
+
+
+def test_kat_conv2d(orc, kats):
+    k = kats["conv2d_3x3_k2"]
+    x = np.array(k["x"], np.float32).reshape(k["x_shape"])
+    w = np.array(k["w"], np.float32).reshape(k["w_shape"])
+    y, choice = orc.conv2d(x, w, tuple(k["stride"]), tuple(k["padding"]))
+    assert choice == 0  # work < 65536 -> direct f64 path
+    assert np.max(np.abs(y.reshape(-1) - np.array(k["expected"]))) < k["abs_tol"]
+    yi = np.empty_like(y)
+    # the im2col path must agree on the same case
+    yi = orc.conv2d_direct(x, w, tuple(k["stride"]), tuple(k["padding"]))
+    np.testing.assert_array_equal(yi, y)
+
+
+def test_kat_jit_conv_relu(orc, kats):
+    k = kats["jit_conv2d_relu_ones"]
+    x = np.full(k["x_shape"], k["x_fill"], np.float32)
+    w = np.full(k["w_shape"], k["w_fill"], np.float32)
+    y, _ = orc.conv2d_bias_relu(x, w, None, tuple(k["stride"]), tuple(k["padding"]))
+    assert list(y.shape) == k["out_shape"]
+    assert abs(y.reshape(-1)[0] - k["expected_first"]) < k["abs_tol"]
+
+
+def test_kat_bench_matmul_ones(orc, kats):
+    k = kats["bench_matmul_ones"]
+    a = np.full((k["m"], k["k"]), k["a_fill"], np.float32)
+    b = np.full((k["k"], k["n"]), k["b_fill"], np.float32)
+    c, _ = orc.matmul(a, b)
+    assert np.all(c == k["expected_all"])
+
+
+def test_kat_bench_conv_fill(orc, kats):
+    k = kats["bench_conv2d_fill"]
+    x = np.full(k["x_shape"], k["x_fill"], np.float32)
+    w = np.full(k["w_shape"], k["w_fill"], np.float32)
+    y, choice = orc.conv2d(x, w, tuple(k["stride"]), tuple(k["padding"]))
+    assert choice == 1  # im2col; k = 144 < 256 -> sgemm
+    interior = y[:, :, 1:-1, 1:-1]
+    assert np.max(np.abs(interior / k["expected_interior"] - 1.0)) < k["rel_tol"]
+
+
+def test_kat_deterministic_unit(orc, kats):
+    k = kats["deterministic_unit"]
+    got = [orc.unit(i, k["seed"]) for i in k["idx"]]
+    assert got == [np.float32(v) for v in k["expected"]]
+
+
+def test_auto_dispatch_rule(orc):
+    # should_use_parallel_auto: m >= 128 && k >= 256 && n <= 128
+    assert orc.lib().orc_matmul_auto_parallel(25088, 1152, 128) == 1  # conv cfg im2col GEMM
+    assert orc.lib().orc_matmul_auto_parallel(1024, 1024, 1024) == 0
+    assert orc.lib().orc_matmul_auto_parallel(127, 1024, 64) == 0
+    assert orc.lib().orc_matmul_auto_parallel(128, 255, 64) == 0
+
+
+def _np_parallel_core(a, b, bias=None):
+    """Independent restatement of matmul_cpu_parallel_core in numpy float32
+    (separate multiply and add, sequential over k, unrolled by 8 like the
+    reference: the order of additions is identical)."""
+    m, k = a.shape
+    n = b.shape[1]
+    s = np.tile(bias.astype(np.float32), (m, 1)) if bias is not None else np.zeros((m, n), np.float32)
+    for p in range(k):
+        s = (s + (a[:, p:p + 1] * b[p:p + 1, :]).astype(np.float32)).astype(np.float32)
+    return s
+
+
+def test_parallel_core_bit_exact(orc):
+    rng = np.random.default_rng(5)
+    a = rng.standard_normal((9, 37)).astype(np.float32)
+    b = rng.standard_normal((37, 11)).astype(np.float32)
+    bias = rng.standard_normal(11).astype(np.float32)
+    np.testing.assert_array_equal(orc.matmul_parallel_core(a, b), _np_parallel_core(a, b))
+    np.testing.assert_array_equal(orc.matmul_parallel_core(a, b, bias), _np_parallel_core(a, b, bias))
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 1, 1), (7, 300, 5), (130, 257, 64), (64, 600, 200)])
+def test_matmul_vs_f64(orc, m, k, n):
+    a = orc.normal((m, k), 11, 1)
+    b = orc.normal((k, n), 11, 2)
+    ref = torch.from_numpy(a).double() @ torch.from_numpy(b).double()
+    c, _ = orc.matmul(a, b)
+    assert orc.rel_frob(c, ref.numpy()) < 1e-6
+    c64 = orc.matmul_f64(a, b)
+    np.testing.assert_allclose(c64, ref.numpy(), rtol=1e-12, atol=1e-12)
+    rows = np.array([0, m - 1]), np.array([n - 1, 0])
+    np.testing.assert_allclose(orc.matmul_f64_sampled(a, b, *rows), ref.numpy()[rows], rtol=1e-12)
+
+
+@pytest.mark.parametrize("shape,wshape,stride,pad", [
+    ((2, 3, 9, 7), (4, 3, 3, 3), (1, 1), (1, 1)),
+    ((1, 5, 11, 11), (6, 5, 3, 3), (2, 2), (1, 1)),
+    ((2, 4, 8, 8), (3, 4, 1, 1), (2, 2), (0, 0)),
+    ((1, 3, 15, 13), (2, 3, 7, 7), (2, 2), (3, 3)),
+    ((2, 16, 6, 6), (8, 16, 3, 3), (1, 1), (0, 2)),
+])
+def test_conv_vs_torch_f64(orc, shape, wshape, stride, pad):
+    x = orc.normal(shape, 3, 1)
+    w = orc.normal(wshape, 3, 2)
+    ref = torch.nn.functional.conv2d(torch.from_numpy(x).double(), torch.from_numpy(w).double(),
+                                     stride=stride, padding=pad).numpy()
+    y, _ = orc.conv2d(x, w, stride, pad)
+    assert orc.rel_frob(y, ref) < 1e-6
+    np.testing.assert_allclose(orc.conv2d_f64(x, w, stride, pad), ref, rtol=1e-10, atol=1e-10)
+    np.testing.assert_allclose(orc.conv2d_direct(x, w, stride, pad), ref, rtol=1e-6, atol=1e-6)
+
+
+def test_pooling_vs_torch(orc):
+    x = orc.normal((2, 3, 13, 11), 4, 1)
+    y = orc.max_pool2d(x, (3, 3), (2, 2), (1, 1))
+    ref = torch.nn.functional.max_pool2d(torch.from_numpy(x), 3, 2, 1).numpy()
+    np.testing.assert_array_equal(y, ref)
+    g = orc.global_avg_pool(x)
+    np.testing.assert_allclose(g, x.astype(np.float64).mean(axis=(2, 3)), rtol=1e-6)
+
+
+def test_relu_nan_and_bias(orc):
+    x = np.array([-1.0, 0.0, 2.0, np.nan], np.float32)
+    np.testing.assert_array_equal(orc.relu(x), np.array([0, 0, 2, 0], np.float32))
+    y = np.zeros((1, 2, 2, 2), np.float32)
+    out = orc.add_bias_nchw(y, np.array([1.0, -2.0], np.float32))
+    assert np.all(out[0, 0] == 1.0) and np.all(out[0, 1] == -2.0)
+
+
+def test_prng_distribution(orc):
+    z = orc.normal((200000,), 0, 0)
+    assert abs(float(z.mean())) < 0.01 and abs(float(z.std()) - 1.0) < 0.01
+    u = orc.uniform((200000,), 1, 3, -0.1, 0.1)
+    assert u.min() >= -0.1 and u.max() <= 0.1 and abs(float(u.mean())) < 1e-3
+    # deterministic and keyed by (seed, tensor id)
+    np.testing.assert_array_equal(orc.normal((17,), 4, 2), orc.normal((17,), 4, 2))
+    assert not np.array_equal(orc.normal((17,), 4, 2), orc.normal((17,), 4, 3))
