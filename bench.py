@@ -34,6 +34,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 L2_BYTES = 126 * 1024 * 1024
+PRECISION = [0]  # rtb precision enum used by every workload call (0 = 3xTF32, 1 = TF32)
+MMAS_PER_MAC = [3]
 
 
 # ------------------------------------------------------------------ helpers
@@ -49,54 +51,68 @@ def _peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+    """SM clock and clock-event (throttle) reasons sampled through NVML every
+    ~1 ms by a background thread while the timed region runs (the timed
+    regions here are milliseconds long, below nvidia-smi's 200 ms cadence)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "sw_power_cap": 0x4, "sw_thermal_slowdown": 0x20,
+               "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80}
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
+    def __init__(self, torch_dev):
         self.rows = []
-        self.proc = None
+        self.h = None
+        self.stop = threading.Event()
+        try:
+            import pynvml
+            self.nv = pynvml
+            pynvml.nvmlInit()
+            import torch
+            pr = torch.cuda.get_device_properties(torch_dev)
+            bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            try:
+                self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+            except Exception:
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(torch_dev.index or 0)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # NVML unavailable: report unsampled
+            self.err = str(e)
+            self.h = None
+
+    def sample(self):
+        if self.h is None:
+            return
+        try:
+            sm = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
+            try:
+                rs = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            except AttributeError:
+                rs = self.nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+            self.rows.append((sm, rs))
+        except Exception:
+            pass
+
+    def _run(self):
+        while not self.stop.is_set():
+            self.sample()
+            time.sleep(0.001)
 
     def __enter__(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
-        except (OSError, FileNotFoundError):
-            self.proc = None
+        self.sample()
+        self.t = threading.Thread(target=self._run, daemon=True)
+        self.t.start()
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                self.rows.append(parts)
-
     def __exit__(self, *a):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        self.stop.set()
+        self.t.join(timeout=2)
+        self.sample()
 
     def summary(self):
         if not self.rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows for i in range(4)
-                          if r[5 + i].lower().startswith("active")})
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(self.rows)}
+        reasons = sorted({n for _, rs in self.rows for n, bit in self.REASONS.items() if rs & bit})
+        return {"sm_mhz": statistics.median(r[0] for r in self.rows), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.rows), "source": "nvml"}
 
 
 def _dist_env():
@@ -144,7 +160,7 @@ class ConvWorkload:
         rb.call("rtb_conv2d_fwd", ctx.handle, self.N, self.C, self.H, self.W, self.Co, 3, 3, 1, 1, 1,
                 1, ctypes.c_void_p(x.data_ptr()), rb.LAYOUT_NCHW,
                 ctypes.c_void_p(self.w.data_ptr()), ctypes.c_void_p(self.b.data_ptr()), None,
-                rb.ACT_RELU, ctypes.c_void_p(y.data_ptr()), rb.LAYOUT_NCHW, rb.PREC_3XTF32, stream)
+                rb.ACT_RELU, ctypes.c_void_p(y.data_ptr()), rb.LAYOUT_NCHW, PRECISION[0], stream)
 
     # dominant kernel alone (NHWC input + prepacked weight), for the roofline
     def kernel_setup(self):
@@ -171,7 +187,7 @@ class ConvWorkload:
                 1, 1, 1, 1, ctypes.c_void_p(self.xh[k].data_ptr()),
                 ctypes.c_void_p(self.wp.data_ptr()), ctypes.c_void_p(self.b.data_ptr()), None,
                 rb.ACT_RELU, ctypes.c_void_p(self.ys[k].data_ptr()), rb.LAYOUT_NCHW,
-                rb.PREC_3XTF32, stream)
+                PRECISION[0], stream)
 
     def e2e_setup(self):
         rb, torch = self.rb, self.torch
@@ -203,7 +219,7 @@ class ConvWorkload:
         rb.call("rtb_conv2d_fwd", ctx.handle, self.N, self.C, self.H, self.W, self.Co, 3, 3, 1, 1, 1,
                 1, ctypes.c_void_p(self.dx.data_ptr()), rb.LAYOUT_NCHW,
                 ctypes.c_void_p(self.dw.data_ptr()), ctypes.c_void_p(self.db.data_ptr()), None,
-                rb.ACT_RELU, ctypes.c_void_p(y.data_ptr()), rb.LAYOUT_NCHW, rb.PREC_3XTF32, stream)
+                rb.ACT_RELU, ctypes.c_void_p(y.data_ptr()), rb.LAYOUT_NCHW, PRECISION[0], stream)
         p, nb = self.pinned["y"]
         rb.call("rtb_memcpy_d2h", ctx.handle, p, ctypes.c_void_p(y.data_ptr()), nb, stream)
 
@@ -260,9 +276,10 @@ class GemmWorkload:
     def step(self):
         k = self.i % self.nsets
         self.i += 1
-        self.rb.sgemm(self.as_[k], self.bs[k], out=self.cs[k], precision=self.rb.PREC_3XTF32)
+        self.rb.sgemm(self.as_[k], self.bs[k], out=self.cs[k], precision=PRECISION[0])
 
-    kernel_setup = lambda self: None  # noqa: E731
+    def kernel_setup(self):
+        pass
 
     def kernel_step(self):
         self.step()
@@ -292,7 +309,7 @@ class GemmWorkload:
         n = self.n
         rb.call("rtb_sgemm", ctx.handle, n, n, n, ctypes.c_void_p(a.data_ptr()), n, 0,
                 ctypes.c_void_p(b.data_ptr()), n, 0, None, rb.ACT_NONE,
-                ctypes.c_void_p(c.data_ptr()), n, rb.PREC_3XTF32, stream)
+                ctypes.c_void_p(c.data_ptr()), n, PRECISION[0], stream)
         p, nb = self.pinned["c"]
         rb.call("rtb_memcpy_d2h", ctx.handle, p, ctypes.c_void_p(c.data_ptr()), nb, stream)
 
@@ -329,9 +346,16 @@ WORKLOADS = {
 
 
 # ------------------------------------------------------------------ timing
-def _time_steps(torch, fn, steps, warmup, dev, dist=None):
-    for _ in range(warmup):
+def _time_steps(torch, fn, steps, warmup, dev, dist=None, min_warm_s=0.3):
+    # At least `warmup` steps, and at least min_warm_s of work so the SM
+    # clocks have left their idle state before the timed region starts.
+    t0 = time.perf_counter()
+    n = 0
+    while n < warmup or time.perf_counter() - t0 < min_warm_s:
         fn()
+        n += 1
+        if n % 16 == 0:
+            torch.cuda.synchronize(dev)
     torch.cuda.synchronize(dev)
     if dist is not None:
         dist.barrier()
@@ -372,7 +396,7 @@ def run_ours(args):
     wl = WORKLOADS[args.workload](rb, torch, dev)
     peaks = _peaks()
 
-    with ClockSampler(local) as clk:
+    with ClockSampler(dev) as clk:
         ms = _time_steps(torch, wl.step, args.steps, args.warmup, dev, dist)
     ms_per_step = ms / args.steps
     value = world * wl.flops * args.steps / (ms / 1e3) / 1e12
@@ -382,7 +406,7 @@ def run_ours(args):
     kms = _time_steps(torch, wl.kernel_step, args.steps, max(3, args.warmup), dev, None)
     k_tflops = wl.flops * args.steps / (kms / 1e3) / 1e12
     tf32_peak = peaks["bf16_tflops"] / 2.0
-    roof_peak = tf32_peak / 3.0  # 3xTF32: three tensor-core MMAs per algorithmic MAC
+    roof_peak = tf32_peak / MMAS_PER_MAC[0]  # 3xTF32: three tensor-core MMAs per algorithmic MAC
 
     # end to end through the C ABI with host buffers
     wl.e2e_setup()
@@ -397,18 +421,19 @@ def run_ours(args):
     if rank == 0:
         cpu_val, sample = wl.cpu_sample(os.cpu_count())
         line = {
-            "metric": f"{wl.name} TFLOP/s (3xTF32, fp32 in/out)",
+            "metric": f"{wl.name} TFLOP/s ({args.precision.upper()}, fp32 in/out)",
             "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32 (3xTF32 tensor-core split)",
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 (3xTF32 tensor-core split)" if PRECISION[0] == 0 else "f32 (TF32 tensor core)",
             "data": "synthetic (SplitMix64/Box-Muller, seeded)",
             "config": dict(wl.config, parallelism=f"replicas x{world}"),
             "roofline": {"bound": "tensor", "achieved": round(k_tflops, 3),
                          "peak": round(roof_peak, 3), "unit": "TFLOP/s",
                          "frac": round(k_tflops / roof_peak, 4), "traffic": None,
                          "peak_basis": f"{peaks['basis']} bf16 {peaks['bf16_tflops']} TFLOP/s "
-                                       f"/ 2 (TF32 rate) / 3 (3xTF32 MMAs per MAC)",
-                         "tensor_pipe_frac": round(3 * k_tflops / tf32_peak, 4),
+                                       f"/ 2 (TF32 rate) / {MMAS_PER_MAC[0]} (MMAs per MAC)",
+                         "tensor_pipe_frac": round(MMAS_PER_MAC[0] * k_tflops / tf32_peak, 4),
                          "kernel_ms": round(kms / args.steps, 5)},
             "cpu_baseline": {"value": round(cpu_val, 6), "unit": "TFLOP/s",
                              "cores": os.cpu_count(), "kind": "port", "sample": sample},
@@ -424,22 +449,16 @@ def run_ours(args):
 
 
 def run_reference(args):
+    """The reference's CPU path (oracle restatement; the Rust reference cannot
+    be built here) on the box's host cores, on a bounded sample per step."""
     rank, world, _ = _dist_env()
     if rank != 0:
         return
-    import torch  # noqa: F401  (device-free; the reference arm is CPU-only)
-    import rustorch_b200 as rb
-
-    class _Dummy:
-        index = 0
     threads = os.cpu_count()
-    wl_cls = {"conv": ConvWorkload, "gemm1024": None, "gemm8192": None}
-    # Build the workload description without touching a GPU.
     if args.workload == "conv":
         wl = ConvWorkload.__new__(ConvWorkload)
         wl.N, wl.C, wl.H, wl.W, wl.Co = 32, 128, 28, 28, 128
         wl.flops = 2.0 * wl.N * wl.H * wl.W * wl.Co * wl.C * 9
-        wl.name = ConvWorkload.name
         cfg = {"workload": "conv2d+bias+relu ResNet-50 stage-2 3x3", "input": [32, 128, 28, 28],
                "weight": [128, 128, 3, 3], "stride": 1, "pad": 1, "seed": 1}
     else:
@@ -447,19 +466,17 @@ def run_reference(args):
         wl = GemmWorkload.__new__(GemmWorkload)
         wl.n, wl.seed, wl.flops, wl.name = n, (0 if n == 1024 else 4), 2.0 * n ** 3, f"sgemm_{n}"
         cfg = {"workload": f"f32 matmul {n}x{n}x{n}", "seed": wl.seed}
-    vals = []
-    samples = []
-    for _ in range(args.warmup):
-        pass
+    vals, samples = [], []
     t0 = time.perf_counter()
     for _ in range(max(1, args.steps)):
-        v, s = wl.cpu_sample(threads)
+        v, smp = wl.cpu_sample(threads)
         vals.append(v)
-        samples.append(s)
+        samples.append(smp)
         if time.perf_counter() - t0 > 120:
             break
     v = statistics.median(vals)
-    line = {"impl": "reference", "metric": f"{wl.name} TFLOP/s (3xTF32, fp32 in/out)",
+    line = {"impl": "reference",
+            "metric": f"{wl.name} TFLOP/s ({args.precision.upper()}, fp32 in/out)",
             "value": round(v, 6), "unit": "TFLOP/s", "n_gpus": world, "steps": len(vals),
             "warmup": args.warmup, "higher_is_better": True, "vs_baseline": None,
             "dtype": "f32", "data": "synthetic (SplitMix64/Box-Muller, seeded)", "config": cfg,
@@ -467,7 +484,7 @@ def run_reference(args):
                              "kind": "port", "sample": samples[0]},
             "e2e": {"value": round(v, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},
-            "note": "reference CPU path restated in C (Rust toolchain unavailable)"}
+            "note": "reference CPU path restated in C (no Rust toolchain to build the reference)"}
     print(json.dumps(line), flush=True)
 
 
@@ -478,9 +495,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="conv", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--precision", default="3xtf32", choices=["3xtf32", "tf32"])
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    PRECISION[0] = 1 if args.precision == "tf32" else 0
+    MMAS_PER_MAC[0] = 1 if args.precision == "tf32" else 3
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -2,8 +2,9 @@
  * rustorch_b200 — C ABI of the B200 (sm_100a) dense-contraction backend for
  * RusTorch.  Plain pointers and sizes only; every function returns an int
  * status (RTB_OK = 0).  Device pointers are CUDA device addresses on the
- * context's device; `stream` is a cudaStream_t (NULL = the context's own
- * stream).  All compute entry points are asynchronous and stream-ordered like
+ * context's device; `stream` is a cudaStream_t (NULL = the legacy default
+ * stream, as in the CUDA runtime; rtb_context_stream gives the context's own
+ * non-blocking stream).  All compute entry points are asynchronous and stream-ordered like
  * cuBLAS: errors detected on the host (bad shapes, launch failures) are
  * returned immediately; a device-side bounded wait that expired is reported by
  * the next rtb_stream_synchronize / rtb_device_error on that context.
@@ -88,6 +89,8 @@ int rtb_memcpy_d2d(rtb_ctx* ctx, void* dst, const void* src, size_t bytes, void*
 int rtb_memset_zero(rtb_ctx* ctx, void* dst, size_t bytes, void* stream);
 
 /* ---------------------------------------------------------------- streams */
+/* The context's own non-blocking stream (created by rtb_init). */
+int rtb_context_stream(rtb_ctx* ctx, void** stream);
 int rtb_stream_create(rtb_ctx* ctx, void** stream);
 int rtb_stream_destroy(rtb_ctx* ctx, void* stream);
 /* Synchronise `stream`, then report a device-side timeout if one occurred. */

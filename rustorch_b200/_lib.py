@@ -50,6 +50,7 @@ SIGNATURES = {
     "rtb_memcpy_d2h": (_i, [_p, _p, _p, _sz, _p]),
     "rtb_memcpy_d2d": (_i, [_p, _p, _p, _sz, _p]),
     "rtb_memset_zero": (_i, [_p, _p, _sz, _p]),
+    "rtb_context_stream": (_i, [_p, _pp]),
     "rtb_stream_create": (_i, [_p, _pp]),
     "rtb_stream_destroy": (_i, [_p, _p]),
     "rtb_stream_synchronize": (_i, [_p, _p]),

@@ -50,7 +50,7 @@ static EncodeTiledFn get_encode_tiled() {
 }
 
 int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1,
-                 uint64_t row_stride_elems, uint32_t box0, uint32_t box1) {
+                 uint64_t row_stride_elems, uint32_t box0, uint32_t box1, bool atom32) {
   EncodeTiledFn enc = get_encode_tiled();
   if (!enc) return set_error(RTB_E_CUDA, "cuTensorMapEncodeTiled unavailable");
   if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (row_stride_elems * 4) % 16 != 0)
@@ -60,13 +60,61 @@ int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim
   const cuuint32_t box[2] = {box0, box1};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides,
-                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     char buf[160];
     snprintf(buf, sizeof buf, "cuTensorMapEncodeTiled failed (%d): dims %llu x %llu stride %llu",
              (int)r, (unsigned long long)dim0, (unsigned long long)dim1,
              (unsigned long long)row_stride_elems);
+    return set_error(RTB_E_CUDA, buf);
+  }
+  return RTB_OK;
+}
+
+typedef CUresult (*EncodeIm2colFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const int*, const int*,
+                                   cuuint32_t, cuuint32_t, const cuuint32_t*,
+                                   CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeIm2colFn get_encode_im2col() {
+  static EncodeIm2colFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeIm2colFn>(p);
+  });
+  return fn;
+}
+
+int make_tmap_im2col(CUtensorMap* map, const void* x, int N, int H, int W, int Cp, int R, int S,
+                     int sh, int sw, int ph, int pw, uint32_t channels_per_pixel,
+                     uint32_t pixels_per_column) {
+  EncodeIm2colFn enc = get_encode_im2col();
+  if (!enc) return set_error(RTB_E_CUDA, "cuTensorMapEncodeIm2col unavailable");
+  if ((reinterpret_cast<uintptr_t>(x) & 15u) != 0 || (Cp * 4) % 16 != 0)
+    return set_error(RTB_E_INVALID, "im2col map: base must be 16-byte aligned, Cp % 4 == 0");
+  const cuuint64_t dims[4] = {(cuuint64_t)Cp, (cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)N};
+  const cuuint64_t strides[3] = {(cuuint64_t)Cp * 4, (cuuint64_t)W * Cp * 4,
+                                 (cuuint64_t)H * W * Cp * 4};
+  // Bounding box of the traversal in (W, H): from -pad to (size-1 + pad - (filter-1)),
+  // so the traversal visits exactly the Wo x Ho top-left tap positions.
+  const int lower[2] = {-pw, -ph};
+  const int upper[2] = {pw - (S - 1), ph - (R - 1)};
+  const cuuint32_t estr[4] = {1, (cuuint32_t)sw, (cuuint32_t)sh, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void*>(x), dims, strides,
+                   lower, upper, channels_per_pixel, pixels_per_column, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[160];
+    snprintf(buf, sizeof buf, "cuTensorMapEncodeIm2col failed (%d)", (int)r);
     return set_error(RTB_E_CUDA, buf);
   }
   return RTB_OK;
@@ -286,6 +334,13 @@ int rtb_memset_zero(rtb_ctx* ctx, void* dst, size_t bytes, void* stream) {
 }
 
 // ---------------------------------------------------------------- streams
+int rtb_context_stream(rtb_ctx* ctx, void** stream) {
+  RTB_CHECK_CTX(ctx);
+  if (!stream) return set_error(RTB_E_INVALID, "null stream out");
+  *stream = ctx->stream;
+  return RTB_OK;
+}
+
 int rtb_stream_create(rtb_ctx* ctx, void** stream) {
   RTB_CHECK_CTX(ctx);
   if (!stream) return set_error(RTB_E_INVALID, "null stream out");
@@ -495,7 +550,15 @@ static int conv_core(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, 
   } else {
     d.out_mode = 1; d.ldc = Co; d.hw = (int)(Ho * Wo);
   }
-  d.gather = 1; d.x = x_nhwc;
+  // TMA im2col when every k-block is a single filter tap (Cp % 32 == 0), the
+  // corners fit the map's signed 8-bit range, and the tensor is not tiny;
+  // otherwise the cp.async gather producer.
+  const bool im2col_ok = (Cp % 32 == 0) && pw <= 127 && ph <= 127 && (kw - 1 - pw) <= 128 &&
+                         (kh - 1 - ph) <= 128 && N * H * W * Cp * 4 >= (int64_t)(256 << 10) &&
+                         std::getenv("RTB_CONV_GATHER") == nullptr;
+  d.gather = im2col_ok ? 2 : 1;
+  d.x = x_nhwc;
+  d.Nimg = (int)N;
   d.H = (int)H; d.W = (int)W; d.Cp = (int)Cp; d.Ho = (int)Ho; d.Wo = (int)Wo;
   d.R = (int)kh; d.S = (int)kw; d.sh = (int)sh; d.sw = (int)sw; d.ph = (int)ph; d.pw = (int)pw;
   d.split3 = split3;

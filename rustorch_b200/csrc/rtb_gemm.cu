@@ -9,12 +9,12 @@ namespace rtb {
 
 namespace {
 
-template <int BN, bool SPLIT, bool GATHER, int B_MN>
+template <int BN, bool SPLIT, int A_MODE, int B_MN>
 int launch_variant(rtb_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB,
                    const GemmParams& p, cudaStream_t stream) {
   using Cfg = GemmCfg<BN, SPLIT>;
-  using Roles = GemmRoles<SPLIT, GATHER>;
-  auto kern = rtb_gemm_kernel<BN, SPLIT, GATHER, B_MN>;
+  using Roles = GemmRoles<SPLIT, A_MODE == 1>;
+  auto kern = rtb_gemm_kernel<BN, SPLIT, A_MODE, B_MN>;
   // The attribute is per function and per device; setting it is idempotent
   // and cheap, so it is set on every launch (covers multi-device processes).
   cudaError_t e =
@@ -28,18 +28,24 @@ int launch_variant(rtb_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB,
   return RTB_OK;
 }
 
+template <int BN, bool SPLIT>
+int launch_prec(rtb_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p,
+                const GemmDesc& d, cudaStream_t s) {
+  if (d.gather == 1) return launch_variant<BN, SPLIT, 1, 0>(ctx, tmA, tmB, p, s);
+  if (d.gather == 2) return launch_variant<BN, SPLIT, 2, 0>(ctx, tmA, tmB, p, s);
+  if (d.b_mn_major) return launch_variant<BN, SPLIT, 0, 1>(ctx, tmA, tmB, p, s);
+  return launch_variant<BN, SPLIT, 0, 0>(ctx, tmA, tmB, p, s);
+}
+
 template <int BN>
 int launch_bn(rtb_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p,
               const GemmDesc& d, cudaStream_t s) {
-  if (d.gather) {
-    return d.split3 ? launch_variant<BN, true, true, 0>(ctx, tmA, tmB, p, s)
-                    : launch_variant<BN, false, true, 0>(ctx, tmA, tmB, p, s);
+  if (!d.split3) return launch_prec<BN, false>(ctx, tmA, tmB, p, d, s);
+  if constexpr (BN <= 128) {
+    return launch_prec<BN, true>(ctx, tmA, tmB, p, d, s);
+  } else {
+    return set_error(RTB_E_INVALID, "3xTF32 tiles are at most 128 columns wide");
   }
-  if (d.b_mn_major)
-    return d.split3 ? launch_variant<BN, true, false, 1>(ctx, tmA, tmB, p, s)
-                    : launch_variant<BN, false, false, 1>(ctx, tmA, tmB, p, s);
-  return d.split3 ? launch_variant<BN, true, false, 0>(ctx, tmA, tmB, p, s)
-                  : launch_variant<BN, false, false, 0>(ctx, tmA, tmB, p, s);
 }
 
 int env_int(const char* name, int dflt) {
@@ -52,7 +58,7 @@ int env_int(const char* name, int dflt) {
 // keeps three stages.
 int pick_bn(rtb_ctx* ctx, const GemmDesc& d) {
   static const int forced = env_int("RTB_GEMM_BN", 0);
-  if (forced == 64 || forced == 128 || forced == 256) return forced;
+  if (forced == 64 || forced == 128 || (forced == 256 && !d.split3)) return forced;
   const int64_t tm = (d.M + kBM - 1) / kBM;
   const int cands_split[2] = {128, 64};
   const int cands_fast[3] = {256, 128, 64};
@@ -75,17 +81,21 @@ int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
 
   CUtensorMap tmA, tmB;
   int st;
-  if (d.gather) {
+  if (d.gather == 1) {
     // A is gathered by the kernel; give the unused map a valid encoding.
-    st = make_tmap_2d(&tmA, d.B, (uint64_t)d.K, (uint64_t)d.N, (uint64_t)d.ldb, kBK, 64);
+    st = make_tmap_2d(&tmA, d.B, (uint64_t)d.K, (uint64_t)d.N, (uint64_t)d.ldb, kBK, 64, false);
+  } else if (d.gather == 2) {
+    st = make_tmap_im2col(&tmA, d.x, d.Nimg, d.H, d.W, d.Cp, d.R, d.S, d.sh, d.sw, d.ph, d.pw,
+                          kBK, kBM);
   } else {
-    st = make_tmap_2d(&tmA, d.A, (uint64_t)d.K, (uint64_t)d.M, (uint64_t)d.lda, kBK, kBM);
+    st = make_tmap_2d(&tmA, d.A, (uint64_t)d.K, (uint64_t)d.M, (uint64_t)d.lda, kBK, kBM, false);
   }
   if (st != RTB_OK) return st;
-  if (d.b_mn_major)
-    st = make_tmap_2d(&tmB, d.B, (uint64_t)d.N, (uint64_t)d.K, (uint64_t)d.ldb, 32, kBK);
+  if (d.b_mn_major)  // MN-major TF32 tiles use the 32-byte-atom 128B swizzle
+    st = make_tmap_2d(&tmB, d.B, (uint64_t)d.N, (uint64_t)d.K, (uint64_t)d.ldb, 32, kBK, true);
   else
-    st = make_tmap_2d(&tmB, d.B, (uint64_t)d.K, (uint64_t)d.N, (uint64_t)d.ldb, kBK, (uint32_t)bn);
+    st = make_tmap_2d(&tmB, d.B, (uint64_t)d.K, (uint64_t)d.N, (uint64_t)d.ldb, kBK, (uint32_t)bn,
+                      false);
   if (st != RTB_OK) return st;
 
   GemmParams p{};
@@ -93,6 +103,17 @@ int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
   p.N = (int)d.N;
   p.K = (int)d.K;
   p.num_kb = (int)((d.K + kBK - 1) / kBK);
+  static const int kb_acc_env = env_int("RTB_KB_PER_ACC", 0);
+  p.kb_per_acc = d.split3 ? (kb_acc_env > 0 ? kb_acc_env : 4) : p.num_kb;
+  // L2 prefetch measured no gain on B200 (the ring already hides the latency):
+  // off unless RTB_PREFETCH_KB asks for it.
+  static const int pf_env = env_int("RTB_PREFETCH_KB", 0);
+  p.prefetch_kb = pf_env > 0 ? pf_env : 0;
+  // The tensor core truncates fp32 operands to TF32 (pinned by a GPU test), so
+  // the raw tile already is the "hi" part; RTB_SPLIT_TRUNC=0 selects the
+  // round-to-nearest hi written back in place instead.
+  static const int trunc_env = env_int("RTB_SPLIT_TRUNC", 1);
+  p.split_trunc = trunc_env != 0;
   p.tiles_m = (int)((d.M + kBM - 1) / kBM);
   p.tiles_n = (int)((d.N + bn - 1) / bn);
   p.group_m = p.tiles_m < 16 ? p.tiles_m : 16;

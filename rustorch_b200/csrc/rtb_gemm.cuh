@@ -11,10 +11,21 @@
 //            TF32 "hi" part (in place, round-to-nearest) and the exact fp32
 //            remainder "lo" (separate plane); UMMA then accumulates
 //            hi*hi + hi*lo + lo*hi (split-precision TF32, Ootomo & Yokota 2022)
-//   next 4   (conv only) im2col gather: 16-byte cp.async of NHWC input rows
-//            into the swizzled A tile, zero-filling padding taps
+//   next 4   (conv, A_MODE 1) im2col gather: 16-byte cp.async of NHWC input
+//            rows into the swizzled A tile, zero-filling padding taps
+// A operand modes: 0 = tiled TMA of a K-major matrix; 1 = cp.async im2col
+// gather (any Cp % 4 == 0); 2 = TMA im2col (Cp % 32 == 0: every k-block is one
+// filter tap x 32 channels, fetched by one bulk tensor copy per k-block).
 // The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
 // of tile i overlaps the mainloop of tile i+1.
+//
+// Accumulator promotion (3xTF32): the tensor core's internal accumulation does
+// not round every addition to nearest fp32, so its error grows linearly with
+// the length of the accumulation chain.  The MMA issuer therefore restarts the
+// TMEM accumulator every `kb_per_acc` k-blocks (one "accumulation unit"), and
+// the epilogue warps add each unit's partial sum into an fp32 running sum kept
+// in a third TMEM buffer (round-to-nearest adds on the CUDA cores), emitting
+// the tile after its last unit.  TF32 mode uses one unit per tile.
 //
 // Layouts in shared memory (all 128B-swizzled, 1024-byte aligned):
 //   A tile, K-major:  row r (M) at r*128 B, 32 fp32 of K per row.
@@ -39,6 +50,11 @@ constexpr int kSmemReserve = 2048;           // barriers + alignment slack
 struct GemmParams {
   int M, N, K;
   int num_kb;            // ceil(K / 32)
+  int kb_per_acc;        // k-blocks accumulated on the tensor core before promotion
+  int prefetch_kb;       // L2 prefetch distance in k-blocks (0 = off)
+  int split_trunc;       // 3xTF32 hi part: 1 = the tensor core's own truncation of the
+                         // raw fp32 (lo = x - trunc(x)); 0 = round-to-nearest hi
+                         // written back in place
   int tiles_m, tiles_n;
   int group_m;           // raster: tiles grouped by this many M-tiles
   // output / epilogue
@@ -66,13 +82,17 @@ struct GemmCfg {
   static constexpr int kStagesRaw = (kSmemLimit - kSmemReserve) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
   static constexpr int kSmemBytes = kStages * kStageBytes + kSmemReserve;
-  static constexpr int kTmemCols = 2 * BN;  // 128/256/512: power of two >= 32
+  // TMEM: two partial-sum buffers (double buffering) + with 3xTF32 one fp32
+  // running sum the epilogue warps promote the partials into.
+  static constexpr int kTmemNeed = (SPLIT ? 3 : 2) * BN;
+  static constexpr int kTmemCols = kTmemNeed <= 128 ? 128 : (kTmemNeed <= 256 ? 256 : 512);
+  static_assert(kTmemNeed <= 512, "3xTF32 needs BN <= 128 (three BN-column TMEM buffers)");
   static_assert(kStages >= 2, "need at least two pipeline stages");
   static_assert(BN == 64 || BN == 128 || BN == 256, "BN must be 64, 128 or 256");
 };
 
 template <bool SPLIT, bool GATHER>
-struct GemmRoles {
+struct GemmRoles {  // GATHER: the cp.async im2col producer warps are present
   static constexpr int kWarpTma = 0;
   static constexpr int kWarpMma = 1;
   static constexpr int kWarpEpi = 2;                        // 4 warps
@@ -106,6 +126,16 @@ __device__ __forceinline__ float4 tf32_hi4(float4 v) {
   h.z = __uint_as_float(c);
   h.w = __uint_as_float(d);
   return h;
+}
+
+// x - trunc_tf32(x): the exact remainder below the 10 explicit mantissa bits a
+// TF32 operand keeps when the low 13 bits of the fp32 pattern are dropped.
+__device__ __forceinline__ float4 tf32_trunc_rem4(float4 v) {
+  const float hx = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
+  const float hy = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
+  const float hz = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
+  const float hw = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+  return make_float4(v.x - hx, v.y - hy, v.z - hz, v.w - hw);
 }
 
 // Epilogue for one thread's row m and 32 consecutive columns n0..n0+31.
@@ -174,10 +204,12 @@ __device__ __forceinline__ void epilogue_store32(const GemmParams& p, int m, int
 }
 
 // B_MN: 0 = B is K-major ([N,K] in memory), 1 = MN-major ([K,N] row-major).
-template <int BN, bool SPLIT, bool GATHER, int B_MN>
-__global__ void __launch_bounds__(GemmRoles<SPLIT, GATHER>::kThreads, 1)
+template <int BN, bool SPLIT, int A_MODE, int B_MN>
+__global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
     rtb_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const GemmParams p) {
+  constexpr bool GATHER = (A_MODE == 1);
+  constexpr bool IM2COL = (A_MODE == 2);
   using Cfg = GemmCfg<BN, SPLIT>;
   using Roles = GemmRoles<SPLIT, GATHER>;
   constexpr int S = Cfg::kStages;
@@ -217,7 +249,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, GATHER>::kThreads, 1)
     fence_mbar_init();
   }
   if (warp == Roles::kWarpTma && lane == 0) {
-    if (!GATHER) tma_prefetch_desc(&tmA);
+    if (!GATHER) tma_prefetch_desc(&tmA);  // tiled or im2col map
     tma_prefetch_desc(&tmB);
   }
   if (warp == Roles::kWarpMma) {
@@ -235,15 +267,49 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, GATHER>::kThreads, 1)
       int s = 0;
       uint32_t ph = 0;
       const uint32_t tx = (GATHER ? 0 : kABytes) + kBBytes;
+      const int HoWo = p.Ho * p.Wo;
       for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
         int tm, tn;
         tile_coords(t, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
+        // TMA im2col: input position of the tile's first output pixel.
+        int a_w = 0, a_h = 0, a_n = 0;
+        if (IM2COL) {
+          const int m0 = tm * kBM;
+          a_n = m0 / HoWo;
+          const int rem = m0 - a_n * HoWo;
+          const int oh = rem / p.Wo;
+          a_h = oh * p.sh - p.ph;
+          a_w = (rem - oh * p.Wo) * p.sw - p.pw;
+        }
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!mbar_wait_bounded(&empty_bar[s], ph ^ 1, abort_flag, p.err, DEV_TIMEOUT_EMPTY,
                                  p.timeout_ns))
             break;
           mbar_arrive_expect_tx(&full_bar[s], tx);
-          if (!GATHER) tma_load_2d(sA + s * kABytes, &tmA, &full_bar[s], kb * kBK, tm * kBM);
+          // Warm L2 for a k-block `prefetch_kb` ahead (hides DRAM latency beyond
+          // what the shared-memory ring can cover).
+          const int kp = kb + p.prefetch_kb;
+          if (p.prefetch_kb > 0 && kp < p.num_kb) {
+            if (A_MODE == 0) {
+              tma_prefetch_2d(&tmA, kp * kBK, tm * kBM);
+              if (B_MN == 0) tma_prefetch_2d(&tmB, kp * kBK, tn * BN);
+            } else if (IM2COL) {
+              const int k0 = kp * kBK, tap = k0 / p.Cp, rr = tap / p.S;
+              tma_prefetch_im2col_4d(&tmA, k0 - tap * p.Cp, a_w, a_h, a_n,
+                                     (uint16_t)(tap - rr * p.S), (uint16_t)rr);
+            }
+          }
+          if (A_MODE == 0) {
+            tma_load_2d(sA + s * kABytes, &tmA, &full_bar[s], kb * kBK, tm * kBM);
+          } else if (IM2COL) {
+            const int k0 = kb * kBK;
+            const int tap = k0 / p.Cp;           // one filter tap per k-block (Cp % 32 == 0)
+            const int c0 = k0 - tap * p.Cp;
+            const int rr = tap / p.S;
+            const int ss = tap - rr * p.S;
+            tma_load_im2col_4d(sA + s * kABytes, &tmA, &full_bar[s], c0, a_w, a_h, a_n,
+                               (uint16_t)ss, (uint16_t)rr);
+          }
           if (B_MN == 0) {
             tma_load_2d(sB + s * kBBytes, &tmB, &full_bar[s], kb * kBK, tn * BN);
           } else {
@@ -262,81 +328,118 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, GATHER>::kThreads, 1)
       constexpr uint32_t idesc = umma_idesc_tf32(kBM, BN, 0, B_MN);
       int s = 0;
       uint32_t ph = 0;
-      int it = 0;
-      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x, ++it) {
-        const int b = it & 1;
-        const uint32_t use = (uint32_t)(it >> 1);
-        if (!mbar_wait_bounded(&tempty_bar[b], (use & 1) ^ 1, abort_flag, p.err,
-                               DEV_TIMEOUT_TMEM_EMPTY, p.timeout_ns))
-          break;
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(b * BN);
-        bool ok = true;
-        for (int kb = 0; kb < p.num_kb; ++kb) {
-          uint64_t* ready = SPLIT ? &conv_bar[s] : &full_bar[s];
-          if (!mbar_wait_bounded(ready, ph, abort_flag, p.err,
-                                 SPLIT ? DEV_TIMEOUT_CONV : DEV_TIMEOUT_FULL, p.timeout_ns)) {
+      int g = 0;  // accumulation-unit counter (selects the TMEM partial buffer)
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok && !*abort_flag; t += gridDim.x) {
+        for (int kb0 = 0; kb0 < p.num_kb && ok; kb0 += p.kb_per_acc, ++g) {
+          const int b = g & 1;
+          const uint32_t use = (uint32_t)(g >> 1);
+          if (!mbar_wait_bounded(&tempty_bar[b], (use & 1) ^ 1, abort_flag, p.err,
+                                 DEV_TIMEOUT_TMEM_EMPTY, p.timeout_ns)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(sA + s * kABytes);
-          const uint32_t b_addr = smem_u32(sB + s * kBBytes);
-          const uint32_t alo_addr = smem_u32(sAlo + s * kABytes);
-          const uint32_t blo_addr = smem_u32(sBlo + s * kBBytes);
-#pragma unroll
-          for (int k = 0; k < kBK / 8; ++k) {
-            // A K-major: +32 B per 8-element k step inside the 128 B swizzle row.
-            const uint64_t da = umma_desc_sw128(a_addr + k * 32, 16, 1024);
-            const uint64_t db = B_MN == 0 ? umma_desc_sw128(b_addr + k * 32, 16, 1024)
-                                          : umma_desc_sw128(b_addr + k * 1024, 4096, 1024);
-            const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
-            umma_tf32(d_tmem, da, db, idesc, acc);
-            if (SPLIT) {
-              const uint64_t dal = umma_desc_sw128(alo_addr + k * 32, 16, 1024);
-              const uint64_t dbl = B_MN == 0 ? umma_desc_sw128(blo_addr + k * 32, 16, 1024)
-                                             : umma_desc_sw128(blo_addr + k * 1024, 4096, 1024);
-              umma_tf32(d_tmem, da, dbl, idesc, 1u);
-              umma_tf32(d_tmem, dal, db, idesc, 1u);
+          const uint32_t d_tmem = tmem_base + (uint32_t)(b * BN);
+          const int kend = (kb0 + p.kb_per_acc) < p.num_kb ? (kb0 + p.kb_per_acc) : p.num_kb;
+          for (int kb = kb0; kb < kend; ++kb) {
+            uint64_t* ready = SPLIT ? &conv_bar[s] : &full_bar[s];
+            if (!mbar_wait_bounded(ready, ph, abort_flag, p.err,
+                                   SPLIT ? DEV_TIMEOUT_CONV : DEV_TIMEOUT_FULL, p.timeout_ns)) {
+              ok = false;
+              break;
             }
+            tc_fence_after();
+            // cp.async-gathered A (TF32 mode has no converter pass): make the
+            // generic-proxy writes visible to the tensor core's async proxy.
+            if (GATHER && !SPLIT) fence_proxy_async_smem();
+            const uint32_t a_addr = smem_u32(sA + s * kABytes);
+            const uint32_t b_addr = smem_u32(sB + s * kBBytes);
+            const uint32_t alo_addr = smem_u32(sAlo + s * kABytes);
+            const uint32_t blo_addr = smem_u32(sBlo + s * kBBytes);
+#pragma unroll
+            for (int k = 0; k < kBK / 8; ++k) {
+              // A (K-major, SW128): +32 B per 8-element k step inside the 128 B row.
+              // B MN-major (SW128 with 32 B atoms): +1024 B = 8 K-rows per k step;
+              // LBO = 4096 B between 32-column boxes, SBO = 512 B per 4 K-rows.
+              const uint64_t da = umma_desc(a_addr + k * 32, 16, 1024, kLayoutSW128);
+              const uint64_t db =
+                  B_MN == 0 ? umma_desc(b_addr + k * 32, 16, 1024, kLayoutSW128)
+                            : umma_desc(b_addr + k * 1024, 4096, 512, kLayoutSW128Base32B);
+              const uint32_t acc = (kb > kb0 || k > 0) ? 1u : 0u;
+              if (SPLIT) {
+                const uint64_t dal = umma_desc(alo_addr + k * 32, 16, 1024, kLayoutSW128);
+                const uint64_t dbl =
+                    B_MN == 0 ? umma_desc(blo_addr + k * 32, 16, 1024, kLayoutSW128)
+                              : umma_desc(blo_addr + k * 1024, 4096, 512, kLayoutSW128Base32B);
+                // small cross terms first, then hi*hi
+                umma_tf32(d_tmem, da, dbl, idesc, acc);
+                umma_tf32(d_tmem, dal, db, idesc, 1u);
+                umma_tf32(d_tmem, da, db, idesc, 1u);
+              } else {
+                umma_tf32(d_tmem, da, db, idesc, acc);
+              }
+            }
+            umma_commit(&empty_bar[s]);
+            if (++s == S) { s = 0; ph ^= 1; }
           }
-          umma_commit(&empty_bar[s]);
-          if (++s == S) { s = 0; ph ^= 1; }
+          if (!ok) break;
+          umma_commit(&tfull_bar[b]);
         }
-        if (!ok) break;
-        umma_commit(&tfull_bar[b]);
       }
     }
   } else if (warp >= Roles::kWarpEpi && warp < Roles::kWarpEpi + 4) {
     // ------------------------------------------------------------ epilogue
     const int lane_base = 32 * (warp & 3);
     const int row = lane_base + lane;
-    int it = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
+    const uint32_t t_lane = tmem_base + ((uint32_t)lane_base << 16);
+    const uint32_t t_run = t_lane + (uint32_t)(2 * BN);  // fp32 running sum (3xTF32)
+    const int units = (p.num_kb + p.kb_per_acc - 1) / p.kb_per_acc;
+    int g = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
       int tm, tn;
       tile_coords(t, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
-      const int b = it & 1;
-      const uint32_t use = (uint32_t)(it >> 1);
-      // tcgen05.ld is .sync.aligned: the whole warp must agree on the outcome.
-      int ok = 0;
-      if (lane == 0)
-        ok = mbar_wait_bounded(&tfull_bar[b], use & 1, abort_flag, p.err, DEV_TIMEOUT_TMEM_FULL,
-                               p.timeout_ns);
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
-      tc_fence_after();
       const int m = tm * kBM + row;
-      const uint32_t taddr = tmem_base + ((uint32_t)lane_base << 16) + (uint32_t)(b * BN);
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(taddr + (uint32_t)c, r);
-        tmem_ld_wait();
-        if (c + 32 == BN) {
-          tc_fence_before();
-          mbar_arrive(&tempty_bar[b]);
+      for (int u = 0; u < units; ++u, ++g) {
+        const int b = g & 1;
+        const uint32_t use = (uint32_t)(g >> 1);
+        // tcgen05.ld is .sync.aligned: the whole warp must agree on the outcome.
+        int got = 0;
+        if (lane == 0)
+          got = mbar_wait_bounded(&tfull_bar[b], use & 1, abort_flag, p.err,
+                                  DEV_TIMEOUT_TMEM_FULL, p.timeout_ns);
+        got = __shfl_sync(0xffffffffu, got, 0);
+        if (!got) {
+          ok = false;
+          break;
         }
-        epilogue_store32(p, m, tn * BN + c, r);
+        tc_fence_after();
+        const bool last = (u + 1 == units);
+        const uint32_t t_part = t_lane + (uint32_t)(b * BN);
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_part + (uint32_t)c, r);
+          tmem_ld_wait();
+          if (SPLIT && u > 0) {
+            uint32_t q[32];
+            tmem_ld_32x32b_x32(t_run + (uint32_t)c, q);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(q[j]));
+          }
+          if (c + 32 == BN) {
+            tc_fence_before();
+            mbar_arrive(&tempty_bar[b]);  // partial buffer b may be overwritten now
+          }
+          if (SPLIT && !last)
+            tmem_st_32x32b_x32(t_run + (uint32_t)c, r);
+          else
+            epilogue_store32(p, m, tn * BN + c, r);
+        }
+        if (SPLIT && !last) tmem_st_wait();
       }
     }
   } else if (SPLIT && warp >= Roles::kWarpConv && warp < Roles::kWarpConv + 4) {
@@ -354,21 +457,29 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, GATHER>::kThreads, 1)
         }
         float4* a = reinterpret_cast<float4*>(sA + s * kABytes);
         float4* alo = reinterpret_cast<float4*>(sAlo + s * kABytes);
-#pragma unroll 4
-        for (int i = ct; i < kABytes / 16; i += 128) {
-          const float4 v = a[i];
-          const float4 h = tf32_hi4(v);
-          a[i] = h;
-          alo[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
-        }
         float4* bb = reinterpret_cast<float4*>(sB + s * kBBytes);
         float4* blo = reinterpret_cast<float4*>(sBlo + s * kBBytes);
+        if (p.split_trunc) {
+          // hi = the tensor core's truncation of the raw value (left in place)
 #pragma unroll 4
-        for (int i = ct; i < kBBytes / 16; i += 128) {
-          const float4 v = bb[i];
-          const float4 h = tf32_hi4(v);
-          bb[i] = h;
-          blo[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+          for (int i = ct; i < kABytes / 16; i += 128) alo[i] = tf32_trunc_rem4(a[i]);
+#pragma unroll 4
+          for (int i = ct; i < kBBytes / 16; i += 128) blo[i] = tf32_trunc_rem4(bb[i]);
+        } else {
+#pragma unroll 4
+          for (int i = ct; i < kABytes / 16; i += 128) {
+            const float4 v = a[i];
+            const float4 h = tf32_hi4(v);
+            a[i] = h;
+            alo[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+          }
+#pragma unroll 4
+          for (int i = ct; i < kBBytes / 16; i += 128) {
+            const float4 v = bb[i];
+            const float4 h = tf32_hi4(v);
+            bb[i] = h;
+            blo[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+          }
         }
         fence_proxy_async_smem();
         mbar_arrive(&conv_bar[s]);
@@ -378,15 +489,15 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, GATHER>::kThreads, 1)
     }
   } else if (GATHER && warp >= Roles::kWarpGather && warp < Roles::kWarpGather + 4) {
     // ------------------------------------------------------------ im2col gather
-    constexpr int LAG = (S - 1) < 2 ? (S - 1) : 2;  // cp.async groups kept in flight
+    // Each thread owns one row (output pixel) of the A tile: 8 x 16-byte
+    // cp.async per k-block into the swizzled row, then an asynchronous
+    // arrive on the stage's full barrier when its copies land.
     const int r = threadIdx.x - Roles::kWarpGather * 32;  // tile row 0..127
     const int swz = r & 7;
     const int Ktot = p.R * p.S * p.Cp;
     const int HoWo = p.Ho * p.Wo;
     int s = 0;
     uint32_t ph = 0;
-    int pend_s[3] = {0, 0, 0};  // ring of stages whose arrive is deferred
-    int npend = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < num_tiles && ok && !*abort_flag; t += gridDim.x) {
       int tm, tn;
@@ -400,6 +511,9 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, GATHER>::kThreads, 1)
       const int ih0 = oh * p.sh - p.ph;
       const int iw0 = ow * p.sw - p.pw;
       const float* ximg = p.x + (int64_t)img * p.H * p.W * p.Cp;
+      // (tap, channel) of the first 16-byte chunk of the k-block, advanced
+      // incrementally (Cp % 4 == 0, so a chunk never straddles a tap).
+      int tap = 0, ci = 0;
       for (int kb = 0; kb < p.num_kb; ++kb) {
         if (!mbar_wait_bounded(&empty_bar[s], ph ^ 1, abort_flag, p.err, DEV_TIMEOUT_EMPTY,
                                p.timeout_ns)) {
@@ -410,32 +524,20 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, GATHER>::kThreads, 1)
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           const int k = kb * kBK + c * 4;
-          const int tap = k / p.Cp;
-          const int ci = k - tap * p.Cp;
           const int rr = tap / p.S;
           const int ss = tap - rr * p.S;
           const int ih = ih0 + rr, iw = iw0 + ss;
           const bool v = mvalid && k < Ktot && ih >= 0 && ih < p.H && iw >= 0 && iw < p.W;
           const float* src = v ? ximg + ((int64_t)ih * p.W + iw) * p.Cp + ci : p.x;
           cp_async_16(dst_row + ((c ^ swz) << 4), src, v ? 16u : 0u);
+          ci += 4;
+          if (ci == p.Cp) { ci = 0; ++tap; }
         }
-        cp_async_commit();
-        pend_s[npend++] = s;
-        if (npend > LAG) {
-          if (LAG == 2) cp_async_wait<2>();
-          else if (LAG == 1) cp_async_wait<1>();
-          else cp_async_wait<0>();
-          fence_proxy_async_smem();
-          mbar_arrive(&full_bar[pend_s[0]]);
-          for (int i = 1; i < npend; ++i) pend_s[i - 1] = pend_s[i];
-          --npend;
-        }
+        cp_async_mbar_arrive_noinc(&full_bar[s]);
         if (++s == S) { s = 0; ph ^= 1; }
       }
     }
     cp_async_wait<0>();
-    fence_proxy_async_smem();
-    for (int i = 0; i < npend; ++i) mbar_arrive(&full_bar[pend_s[i]]);
   }
 
   // ------------------------------------------------------------ teardown

@@ -14,7 +14,7 @@ struct rtb_ctx {
   int sm_count = 0;
   int cc_major = 0, cc_minor = 0;
   size_t total_mem = 0;
-  cudaStream_t stream = nullptr;  // the context's own stream (non-blocking)
+  cudaStream_t stream = nullptr;  // the context's own non-blocking stream (rtb_context_stream)
   int* d_err = nullptr;           // device error word (bounded-wait timeouts)
   uint64_t timeout_ns = 2000000000ull;
   int default_precision = RTB_PREC_3XTF32;
@@ -26,8 +26,12 @@ namespace rtb {
 int set_error(int status, const std::string& msg);
 int cuda_status(cudaError_t e, const char* what);
 
+// NULL is the legacy default stream, as everywhere in the CUDA runtime (and
+// what torch's default stream handle is), so work on it orders with other
+// libraries' work on that stream.
 inline cudaStream_t pick_stream(rtb_ctx* ctx, void* stream) {
-  return stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  (void)ctx;
+  return static_cast<cudaStream_t>(stream);
 }
 
 // RAII guard making ctx->device current for the calling thread.
@@ -44,9 +48,17 @@ struct DeviceGuard {
   }
 };
 
-// 2-D fp32 tensor map (innermost dim0 contiguous, row stride in elements).
+// 2-D fp32 tensor map (innermost dim0 contiguous, row stride in elements),
+// 128-byte swizzle with 16-byte atoms, or 32-byte atoms when atom32 is set.
 int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1,
-                 uint64_t row_stride_elems, uint32_t box0, uint32_t box1);
+                 uint64_t row_stride_elems, uint32_t box0, uint32_t box1, bool atom32);
+
+// 4-D im2col map over an NHWC tensor [N, H, W, Cp] for a forward conv with
+// filter R x S, stride (sh, sw), padding (ph, pw): channels_per_pixel x
+// pixels_per_column boxes, 128-byte swizzle.
+int make_tmap_im2col(CUtensorMap* map, const void* x, int N, int H, int W, int Cp, int R, int S,
+                     int sh, int sw, int ph, int pw, uint32_t channels_per_pixel,
+                     uint32_t pixels_per_column);
 
 // What the GEMM engine computes; see rtb_gemm.cuh (GemmParams) for the epilogue.
 struct GemmDesc {
@@ -67,9 +79,10 @@ struct GemmDesc {
   int relu = 0;
   int out_mode = 0;  // 0 row-major, 1 NCHW scatter
   int hw = 0;
-  // conv gather
+  // conv A producer: 0 = none (A is a matrix), 1 = cp.async gather, 2 = TMA im2col
   int gather = 0;
   const float* x = nullptr;
+  int Nimg = 0;
   int H = 0, W = 0, Cp = 0, Ho = 0, Wo = 0, R = 0, S = 0, sh = 1, sw = 1, ph = 0, pw = 0;
   int split3 = 1;     // 3xTF32 (1) or TF32 (0)
   int bn = 0;         // 0 = heuristic

@@ -103,6 +103,39 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// 4-D im2col load over an NHWC tensor map (dims C, W, H, N): loads the map's
+// pixelsPerColumn output pixels starting at input position (w, h) of image n
+// (traversing W, then H, then N inside the map's bounding box), each shifted
+// by the filter tap (off_w, off_h), with the map's channelsPerPixel channels
+// starting at c.  Out-of-image taps read as zero.
+__device__ __forceinline__ void tma_load_im2col_4d(void* smem_dst, const CUtensorMap* map,
+                                                   uint64_t* bar, int32_t c, int32_t w, int32_t h,
+                                                   int32_t n, uint16_t off_w, uint16_t off_h) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6], {%7, %8};" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c), "r"(w), "r"(h), "r"(n), "r"(smem_u32(bar)),
+      "h"(off_w), "h"(off_h)
+      : "memory");
+}
+
+// L2 prefetch of a tile (no shared-memory destination, no completion).
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int32_t c0, int32_t c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_im2col_4d(const CUtensorMap* map, int32_t c,
+                                                       int32_t w, int32_t h, int32_t n,
+                                                       uint16_t off_w, uint16_t off_h) {
+  asm volatile(
+      "cp.async.bulk.prefetch.tensor.4d.L2.global.im2col [%0, {%1, %2, %3, %4}], {%5, %6};" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(c), "r"(w), "r"(h), "r"(n), "h"(off_w), "h"(off_h)
+      : "memory");
+}
+
 // ----------------------------------------------------------------- cp.async
 // 16-byte global->shared copy; src_bytes = 0 writes 16 zero bytes (padding).
 __device__ __forceinline__ void cp_async_16(void* smem_dst, const void* gsrc, uint32_t src_bytes) {
@@ -116,6 +149,12 @@ __device__ __forceinline__ void cp_async_commit() {
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// Arrive on `bar` once all of this thread's prior cp.async copies have landed
+// (.noinc: the arrival counts toward the barrier's expected count).
+__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
 }
 
 // Generic-proxy shared-memory writes -> visible to the async proxy (UMMA/TMA).
@@ -181,18 +220,42 @@ __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// 32 registers per thread -> 32 lanes x 32 columns of TMEM (inverse of the load).
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 // ----------------------------------------------------------------- descriptors
-// UMMA shared-memory matrix descriptor (sm_100 "version 1"), 128-byte swizzle.
+// UMMA shared-memory matrix descriptor (sm_100 "version 1").
 // Field layout: start>>4 [0,14), LBO>>4 [16,30), SBO>>4 [32,46), version [46,48)=1,
-// base offset [49,52)=0, LBO mode [52]=0, layout type [61,64)=2 (SWIZZLE_128B).
-__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr, uint32_t lbo_bytes,
-                                                    uint32_t sbo_bytes) {
+// base offset [49,52)=0, LBO mode [52]=0, layout type [61,64).
+// Layout types used here:
+//   2 = SWIZZLE_128B (16-byte chunks XOR row%8; K-major tiles, 8-row atoms)
+//   1 = SWIZZLE_128B_BASE32B (32-byte chunks XOR row%4; the only layout the
+//       MMA accepts for MN-major TF32 operands; 4-row atoms)
+constexpr uint32_t kLayoutSW128 = 2;
+constexpr uint32_t kLayoutSW128Base32B = 1;
+
+__device__ __forceinline__ uint64_t umma_desc(uint32_t smem_addr, uint32_t lbo_bytes,
+                                              uint32_t sbo_bytes, uint32_t layout_type) {
   uint64_t d = 0;
   d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
   d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
   d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
   d |= (uint64_t)1 << 46;
-  d |= (uint64_t)2 << 61;
+  d |= (uint64_t)layout_type << 61;
   return d;
 }
 

@@ -22,8 +22,9 @@ def _host(t):
     return t.cpu().numpy()
 
 
-def _relu_pattern_ok(y, pre64):
-    mask = np.abs(pre64) >= 1e-5
+def _relu_pattern_ok(y, pre64, prec=0):
+    band = 1e-5 if prec == 0 else 1e-2 * float(np.sqrt(np.mean(pre64 * pre64)))
+    mask = np.abs(pre64) >= band
     return np.array_equal((y > 0)[mask], (pre64 > 0)[mask])
 
 
@@ -85,7 +86,7 @@ def test_linear_transposed_weight_bias_relu(gpu, orc, prec):
     assert wt.stride(0) == 1
     y = _host(gpu.sgemm(_dev(x), wt, bias=_dev(b), act=gpu.ACT_RELU, precision=prec))
     assert orc.rel_frob(y, np.maximum(pre, 0)) <= TOL[prec]
-    assert _relu_pattern_ok(y, pre)
+    assert _relu_pattern_ok(y, pre, prec)
     ref32 = orc.linear(x, w, b, relu=True)
     assert orc.rel_frob(y, ref32.astype(np.float64)) <= 2 * TOL[prec] + 1e-6
 
@@ -175,3 +176,20 @@ def test_square_4096_sampled_and_linearity(gpu, orc):
     # linearity: A.(2B) == 2(A.B) exactly (scaling by 2 is exact in every split)
     c2 = gpu.sgemm(da, db * 2)
     assert torch.equal(c2, c * 2)
+
+
+def test_tf32_operand_truncation(gpu):
+    """The 3xTF32 split relies on how the tensor core turns an fp32 operand
+    into TF32: it keeps the top 10 explicit mantissa bits and drops the low 13
+    (round toward zero).  x = 1 + 0.75 * 2^-10 is 1.0 truncated, 1 + 2^-10
+    rounded; the product with 1.0 shows which one the hardware used."""
+    x = 1.0 + 2.0 ** -11 + 2.0 ** -12
+    for sign in (1.0, -1.0):
+        a = torch.tensor([[sign * x]], device="cuda")
+        one = torch.ones((1, 1), device="cuda")
+        ca = _host(gpu.sgemm(a, one, precision=gpu.PREC_TF32))[0, 0]
+        cb = _host(gpu.sgemm(one, a, precision=gpu.PREC_TF32))[0, 0]
+        assert ca == sign * 1.0 and cb == sign * 1.0, (ca, cb)
+        # and 3xTF32 recovers the full fp32 value
+        c3 = _host(gpu.sgemm(a, one, precision=gpu.PREC_3XTF32))[0, 0]
+        assert c3 == np.float32(sign * x), c3
