@@ -147,6 +147,22 @@ int rtb_conv2d_fwd_packed(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_
                           const float* x_nhwc_padded, const float* w_packed, const float* bias,
                           const float* residual, int act, float* y, int y_layout, int precision,
                           void* stream);
+/* rtb_conv2d_fwd for callers that cannot allocate device memory (no
+ * counterpart in the reference: RusTorch's CPU conv allocates freely).  Same
+ * arguments and results as rtb_conv2d_fwd, but the scratch it needs (the
+ * channel-padded NHWC input copy and the repacked weight) lives in a 16 MiB
+ * array compiled into the library, so the call allocates nothing; a request
+ * whose scratch would exceed 16 MiB returns RTB_E_INVALID.  Every GPU that
+ * loads the library holds the 16 MiB until process exit.  All calls on a
+ * device share the array: calls that overlap on the GPU race and must be
+ * ordered by the caller.  The first call on each device looks up the array's
+ * address (once per device) and should come before any stream capture. */
+int rtb_conv2d_fwd_noalloc(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, int64_t Co,
+                           int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw,
+                           const float* x, int x_layout, const float* w, const float* bias,
+                           const float* residual, int act, float* y, int y_layout, int precision,
+                           void* stream);
+
 /* NCHW [N,C,H,W] -> NHWC with channel stride Cp = roundup(C,4), zero padded. */
 int rtb_nchw_to_nhwc_padded(rtb_ctx* ctx, int64_t N, int64_t C, int64_t H, int64_t W,
                             const float* x, float* y, void* stream);

@@ -1,0 +1,109 @@
+// rtb_conv2d_fwd_noalloc: the Conv2d(+bias, +residual, +ReLU) forward of
+// rtb_conv2d_fwd for callers that cannot allocate device memory.
+//
+// Some callers cannot call cudaMalloc (or any allocator) on the path that
+// runs a conv: a host framework that owns the GPU's memory through its own
+// allocator and counts every other allocation against a fixed budget, or a
+// latency-critical loop where an allocation call may block on device-wide
+// synchronisation.  rtb_conv2d_fwd needs scratch memory for the channel-padded
+// NHWC copy of the input and the repacked weight, which it takes from the
+// stream-ordered pool.  This variant takes that scratch from a fixed array
+// compiled into the library instead, so the call itself allocates nothing.
+//
+// The scratch is a file-scope __device__ array of kNoAllocScratchBytes
+// (16 MiB).  Every GPU that loads this library holds those 16 MiB until the
+// process exits.  All calls on a device share the one array:
+//   - calls that overlap on the GPU (different streams, or different host
+//     threads without ordering) race on it and corrupt each other's results;
+//     callers must order them (same stream, or events);
+//   - the array keeps the previous call's contents; every byte a call reads is
+//     first written by that call (the padding channels and padding taps are
+//     written as zeros by the packing kernels), so nothing needs clearing.
+// The first call on each device looks up the array's device address with
+// cudaGetSymbolAddress while that device is current (once per device); that
+// first call should come before any stream capture.
+#include <cstdint>
+#include <mutex>
+
+#include "rtb_internal.h"
+
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;  // 16 MiB
+
+// Host code never touches this array directly: its name in host code is only
+// a handle for cudaGetSymbolAddress, not a device address.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+std::mutex g_mu;
+void* g_addr[kMaxDevices] = {nullptr};
+
+// Device address of the scratch array on `device` (which must be current).
+int scratch_address(int device, void** out) {
+  if (device < 0 || device >= kMaxDevices)
+    return rtb::set_error(RTB_E_UNSUPPORTED, "conv2d_fwd_noalloc: device index too large");
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_addr[device]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return rtb::cuda_status(e, "conv2d_fwd_noalloc: cudaGetSymbolAddress");
+    g_addr[device] = p;
+  }
+  *out = g_addr[device];
+  return RTB_OK;
+}
+
+inline int64_t round_up64(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+}  // namespace
+
+extern "C" {
+
+int rtb_conv2d_fwd_noalloc(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, int64_t Co,
+                           int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw,
+                           const float* x, int x_layout, const float* w, const float* bias,
+                           const float* residual, int act, float* y, int y_layout, int precision,
+                           void* stream) {
+  if (!ctx) return rtb::set_error(RTB_E_INVALID, "null rtb_ctx");
+  if (N < 0 || Ci <= 0 || H <= 0 || W <= 0 || Co <= 0 || kh <= 0 || kw <= 0 || sh <= 0 ||
+      sw <= 0 || ph < 0 || pw < 0 || H + 2 * ph < kh || W + 2 * pw < kw)
+    return rtb::set_error(RTB_E_INVALID, "conv2d_fwd_noalloc: bad shape, stride or padding");
+  if (x_layout != RTB_LAYOUT_NCHW && x_layout != RTB_LAYOUT_NHWC)
+    return rtb::set_error(RTB_E_INVALID, "conv2d_fwd_noalloc: bad x_layout");
+  if (N == 0) return RTB_OK;
+  if (!x || !w || !y) return rtb::set_error(RTB_E_INVALID, "conv2d_fwd_noalloc: null pointer");
+
+  const int64_t Cp = round_up64(Ci, 4);
+  const bool x_direct = x_layout == RTB_LAYOUT_NHWC && Cp == Ci &&
+                        (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
+  const int64_t x_bytes = x_direct ? 0 : round_up64(N * H * W * Cp * 4, 256);
+  const int64_t w_bytes = Co * kh * kw * Cp * 4;
+  if (x_bytes + w_bytes > (int64_t)kNoAllocScratchBytes)
+    return rtb::set_error(
+        RTB_E_INVALID,
+        "conv2d_fwd_noalloc: padded input + packed weight need more than the 16 MiB scratch "
+        "(use rtb_conv2d_fwd)");
+
+  rtb::DeviceGuard g(ctx->device);
+  void* base = nullptr;
+  int st = scratch_address(ctx->device, &base);
+  if (st) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  float* xs = x_direct ? nullptr : static_cast<float*>(base);
+  float* wp = reinterpret_cast<float*>(static_cast<unsigned char*>(base) + x_bytes);
+
+  if (!x_direct) {
+    st = x_layout == RTB_LAYOUT_NCHW ? rtb::launch_nchw_to_nhwc_padded(x, N, Ci, H, W, Cp, xs, s)
+                                     : rtb::launch_pack_kmajor(x, N * H * W, Ci, Ci, 1, xs, Cp, s);
+    if (st) return st;
+  }
+  st = rtb::launch_prepack_weight(w, Co, Ci, kh, kw, Cp, wp, s);
+  if (st) return st;
+  return rtb_conv2d_fwd_packed(ctx, N, Ci, H, W, Co, kh, kw, sh, sw, ph, pw,
+                               x_direct ? x : xs, wp, bias, residual, act, y, y_layout, precision,
+                               stream);
+}
+
+}  // extern "C"
