@@ -74,6 +74,14 @@ const char* rtb_status_string(int status);
 int rtb_last_error(char* buf, size_t len);
 /* Wall-clock limit for every device-side wait (default 2 s). */
 int rtb_set_timeout_ns(rtb_ctx* ctx, uint64_t ns);
+/* Diagnostics: record a per-CTA timeline of the contraction kernels
+ * (%globaltimer ns stamps; 20 per CTA: start, end, and for each of the CTA's
+ * first 3 tiles the producer's first issue, the MMA's first ready k-block,
+ * the MMA's last commit, the epilogue seeing the first and the last
+ * accumulation unit, and the epilogue's completion) into `buf`, a device
+ * buffer of `capacity` 64-bit words; a launch whose grid needs more is not
+ * traced.  capacity = 0 turns tracing off. */
+int rtb_set_kernel_trace(rtb_ctx* ctx, uint64_t* buf, int64_t capacity);
 /* Read and clear the device error word (synchronises the context's device).
  * *code receives 0 or the device error code; returns RTB_E_TIMEOUT if set. */
 int rtb_device_error(rtb_ctx* ctx, int* code);

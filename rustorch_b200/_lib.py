@@ -42,6 +42,7 @@ SIGNATURES = {
     "rtb_last_error": (_i, [ctypes.c_char_p, _sz]),
     "rtb_set_timeout_ns": (_i, [_p, _u64]),
     "rtb_device_error": (_i, [_p, ctypes.POINTER(_i)]),
+    "rtb_set_kernel_trace": (_i, [_p, _p, _i64]),
     "rtb_malloc": (_i, [_p, _pp, _sz, _p]),
     "rtb_free": (_i, [_p, _p, _p]),
     "rtb_host_alloc": (_i, [_p, _pp, _sz]),

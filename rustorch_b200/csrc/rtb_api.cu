@@ -248,6 +248,14 @@ int rtb_set_timeout_ns(rtb_ctx* ctx, uint64_t ns) {
   return RTB_OK;
 }
 
+int rtb_set_kernel_trace(rtb_ctx* ctx, uint64_t* buf, int64_t capacity) {
+  RTB_CHECK_CTX(ctx);
+  if (capacity < 0 || (capacity > 0 && !buf)) return set_error(RTB_E_INVALID, "bad trace buffer");
+  ctx->trace = reinterpret_cast<unsigned long long*>(capacity ? buf : nullptr);
+  ctx->trace_capacity = capacity;
+  return RTB_OK;
+}
+
 int rtb_device_error(rtb_ctx* ctx, int* code) {
   RTB_CHECK_CTX(ctx);
   DeviceGuard g(ctx->device);

@@ -1,5 +1,6 @@
 // Instantiation and launch of the tcgen05 GEMM engine (rtb_gemm.cuh).
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "rtb_gemm.cuh"
@@ -11,7 +12,7 @@ namespace {
 
 template <int BN, bool SPLIT, int A_MODE, int B_MN>
 int launch_variant(rtb_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB,
-                   const GemmParams& p, cudaStream_t stream) {
+                   const CUtensorMap& tmC, const GemmParams& p, cudaStream_t stream) {
   using Cfg = GemmCfg<BN, SPLIT>;
   using Roles = GemmRoles<SPLIT, A_MODE == 1>;
   auto kern = rtb_gemm_kernel<BN, SPLIT, A_MODE, B_MN>;
@@ -22,27 +23,27 @@ int launch_variant(rtb_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB,
   if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemm smem)");
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
-  kern<<<grid, Roles::kThreads, Cfg::kSmemBytes, stream>>>(tmA, tmB, p);
+  kern<<<grid, Roles::kThreads, Cfg::kSmemBytes, stream>>>(tmA, tmB, tmC, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_status(e, "gemm kernel launch");
   return RTB_OK;
 }
 
 template <int BN, bool SPLIT>
-int launch_prec(rtb_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p,
-                const GemmDesc& d, cudaStream_t s) {
-  if (d.gather == 1) return launch_variant<BN, SPLIT, 1, 0>(ctx, tmA, tmB, p, s);
-  if (d.gather == 2) return launch_variant<BN, SPLIT, 2, 0>(ctx, tmA, tmB, p, s);
-  if (d.b_mn_major) return launch_variant<BN, SPLIT, 0, 1>(ctx, tmA, tmB, p, s);
-  return launch_variant<BN, SPLIT, 0, 0>(ctx, tmA, tmB, p, s);
+int launch_prec(rtb_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB,
+                const CUtensorMap& tmC, const GemmParams& p, const GemmDesc& d, cudaStream_t s) {
+  if (d.gather == 1) return launch_variant<BN, SPLIT, 1, 0>(ctx, tmA, tmB, tmC, p, s);
+  if (d.gather == 2) return launch_variant<BN, SPLIT, 2, 0>(ctx, tmA, tmB, tmC, p, s);
+  if (d.b_mn_major) return launch_variant<BN, SPLIT, 0, 1>(ctx, tmA, tmB, tmC, p, s);
+  return launch_variant<BN, SPLIT, 0, 0>(ctx, tmA, tmB, tmC, p, s);
 }
 
 template <int BN>
-int launch_bn(rtb_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p,
-              const GemmDesc& d, cudaStream_t s) {
-  if (!d.split3) return launch_prec<BN, false>(ctx, tmA, tmB, p, d, s);
+int launch_bn(rtb_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB,
+              const CUtensorMap& tmC, const GemmParams& p, const GemmDesc& d, cudaStream_t s) {
+  if (!d.split3) return launch_prec<BN, false>(ctx, tmA, tmB, tmC, p, d, s);
   if constexpr (BN <= 128) {
-    return launch_prec<BN, true>(ctx, tmA, tmB, p, d, s);
+    return launch_prec<BN, true>(ctx, tmA, tmB, tmC, p, d, s);
   } else {
     return set_error(RTB_E_INVALID, "3xTF32 tiles are at most 128 columns wide");
   }
@@ -128,6 +129,16 @@ int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
   auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
   p.vec_ok = (d.out_mode == 0) && al16(d.C) && (d.ldc % 4 == 0) && (!d.bias || al16(d.bias)) &&
              (!d.residual || (al16(d.residual) && d.ldr % 4 == 0));
+  p.vec4_nchw = (d.out_mode == 1) && al16(d.C) && (!d.residual || al16(d.residual));
+  // Row-major C leaves through TMA stores when the tensor map can describe it.
+  CUtensorMap tmC;
+  std::memset(&tmC, 0, sizeof tmC);
+  p.c_tma = 0;
+  if (d.out_mode == 0 && al16(d.C) && d.ldc % 4 == 0) {
+    if (make_tmap_2d(&tmC, d.C, (uint64_t)d.N, (uint64_t)d.M, (uint64_t)d.ldc, 32, kBM, false) ==
+        RTB_OK)
+      p.c_tma = 1;
+  }
   p.x = d.x;
   p.H = d.H;
   p.W = d.W;
@@ -142,11 +153,16 @@ int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
   p.pw = d.pw;
   p.err = ctx->d_err;
   p.timeout_ns = ctx->timeout_ns;
+  {
+    const int64_t tiles = (int64_t)p.tiles_m * p.tiles_n;
+    const int64_t grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
+    p.trace = (ctx->trace && ctx->trace_capacity >= grid * kTraceSlots) ? ctx->trace : nullptr;
+  }
 
   switch (bn) {
-    case 64: return launch_bn<64>(ctx, tmA, tmB, p, d, stream);
-    case 128: return launch_bn<128>(ctx, tmA, tmB, p, d, stream);
-    case 256: return launch_bn<256>(ctx, tmA, tmB, p, d, stream);
+    case 64: return launch_bn<64>(ctx, tmA, tmB, tmC, p, d, stream);
+    case 128: return launch_bn<128>(ctx, tmA, tmB, tmC, p, d, stream);
+    case 256: return launch_bn<256>(ctx, tmA, tmB, tmC, p, d, stream);
     default: return set_error(RTB_E_INVALID, "gemm_run: bad tile width");
   }
 }

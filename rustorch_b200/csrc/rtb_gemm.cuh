@@ -46,6 +46,8 @@ constexpr int kBK = 32;                      // fp32 elements per k-block (128 B
 constexpr int kABytes = kBM * kBK * 4;       // 16 KB
 constexpr int kSmemLimit = 232448;           // 227 KB dynamic shared memory per CTA
 constexpr int kSmemReserve = 2048;           // barriers + alignment slack
+constexpr int kOutChunkBytes = kBM * 32 * 4;  // one 128 x 32 fp32 output chunk (16 KB)
+constexpr int kOutBytes = 2 * kOutChunkBytes; // double-buffered epilogue staging
 
 struct GemmParams {
   int M, N, K;
@@ -67,21 +69,35 @@ struct GemmParams {
   int out_mode;          // 0: C[m*ldc+n]; 1: NCHW scatter, m=(img,pix), C[(img*N+n)*hw+pix]
   int hw;                // Ho*Wo for out_mode 1
   int vec_ok;            // 16-byte aligned C/residual/bias with ldc, ldr % 4 == 0
+  int c_tma;             // out_mode 0 with a TMA-storable C (tmC valid)
+  int vec4_nchw;         // out_mode 1: C and residual 16-byte aligned
   // implicit-GEMM conv (A gathered from NHWC input with Cp channels, Cp % 4 == 0)
   const float* x;
   int H, W, Cp, Ho, Wo, R, S, sh, sw, ph, pw;
   // failure reporting
   int* err;
   unsigned long long timeout_ns;
+  // optional timeline trace: per CTA kTraceSlots globaltimer stamps (null = off)
+  unsigned long long* trace;
 };
+
+// Trace slot layout per CTA (first kTraceTiles tiles of the CTA):
+//   0 start, 1 end, then per tile j at 2+6j: producer first issue, MMA first
+//   k-block ready, MMA last commit, epilogue sees the first accumulation unit,
+//   epilogue sees the last unit, epilogue done.
+constexpr int kTraceTiles = 3;
+constexpr int kTraceSlots = 2 + 6 * kTraceTiles;
+__device__ __forceinline__ void trace_stamp(const GemmParams& p, int slot) {
+  if (p.trace) p.trace[(size_t)blockIdx.x * kTraceSlots + slot] = globaltimer_ns();
+}
 
 template <int BN, bool SPLIT>
 struct GemmCfg {
   static constexpr int kBBytes = BN * kBK * 4;
   static constexpr int kStageBytes = (kABytes + kBBytes) * (SPLIT ? 2 : 1);
-  static constexpr int kStagesRaw = (kSmemLimit - kSmemReserve) / kStageBytes;
+  static constexpr int kStagesRaw = (kSmemLimit - kSmemReserve - kOutBytes) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
-  static constexpr int kSmemBytes = kStages * kStageBytes + kSmemReserve;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kOutBytes + kSmemReserve;
   // TMEM: two partial-sum buffers (double buffering) + with 3xTF32 one fp32
   // running sum the epilogue warps promote the partials into.
   static constexpr int kTmemNeed = (SPLIT ? 3 : 2) * BN;
@@ -203,11 +219,113 @@ __device__ __forceinline__ void epilogue_store32(const GemmParams& p, int m, int
   }
 }
 
+// Row-major epilogue via TMA store: bias, residual and ReLU in registers, then
+// this thread's row (32 fp32) into the 128 x 32 staging chunk, 128-byte
+// swizzled (16-byte unit j of row r at position j ^ (r % 8)) to match the
+// store map and keep the 8-thread phases of the writes conflict-free.
+__device__ __forceinline__ void epilogue_stage_rowmajor(const GemmParams& p, uint8_t* buf, int row,
+                                                        int n0, int m, const uint32_t (&r)[32]) {
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+  const bool full = (n0 + 32 <= p.N) && p.vec_ok;
+  if (p.bias) {
+    if (full) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        const float4 b = __ldg(reinterpret_cast<const float4*>(p.bias + n0 + j));
+        v[j] += b.x; v[j + 1] += b.y; v[j + 2] += b.z; v[j + 3] += b.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (n0 + j < p.N) v[j] += __ldg(p.bias + n0 + j);
+    }
+  }
+  if (p.residual && m < p.M) {
+    const float* rrow = p.residual + (int64_t)m * p.ldr;
+    if (full) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        const float4 q = __ldg(reinterpret_cast<const float4*>(rrow + n0 + j));
+        v[j] += q.x; v[j + 1] += q.y; v[j + 2] += q.z; v[j + 3] += q.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (n0 + j < p.N) v[j] += __ldg(rrow + n0 + j);
+    }
+  }
+  if (p.relu) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.0f);
+  }
+  float4* rowp = reinterpret_cast<float4*>(buf + row * 128);
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    rowp[j ^ (row & 7)] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+}
+
+// NCHW epilogue: transpose the 128-pixel x 32-channel chunk through shared
+// memory ([32 channels][128 pixels]), then each thread writes 4 consecutive
+// pixels of one channel with a 16-byte store (a warp covers 512 contiguous
+// bytes of a channel plane), adding the NCHW residual and applying ReLU there.
+__device__ __forceinline__ void epilogue_nchw_chunk(const GemmParams& p, float* buf, int row,
+                                                    int et, int m0, int n0,
+                                                    const uint32_t (&r)[32]) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    float v = __uint_as_float(r[j]);
+    if (p.bias && n0 + j < p.N) v += __ldg(p.bias + n0 + j);
+    buf[j * kBM + row] = v;
+  }
+  named_bar_sync(1, 128);
+  const bool vec = (p.hw % 4 == 0) && p.vec4_nchw;
+#pragma unroll 2
+  for (int i = et; i < 32 * (kBM / 4); i += 128) {
+    const int ch = i >> 5;         // channel within the chunk
+    const int q = i & 31;          // 4-pixel group
+    const int n = n0 + ch;
+    const int m = m0 + 4 * q;
+    if (n >= p.N || m >= p.M) continue;
+    const float4 s4 = *reinterpret_cast<const float4*>(buf + ch * kBM + 4 * q);
+    const int img = m / p.hw;
+    const int pix = m - img * p.hw;
+    const int64_t off = ((int64_t)img * p.N + n) * p.hw + pix;
+    if (vec && m + 3 < p.M) {
+      float4 o = s4;
+      if (p.residual) {
+        const float4 q4 = __ldg(reinterpret_cast<const float4*>(p.residual + off));
+        o.x += q4.x; o.y += q4.y; o.z += q4.z; o.w += q4.w;
+      }
+      if (p.relu) {
+        o.x = fmaxf(o.x, 0.f); o.y = fmaxf(o.y, 0.f); o.z = fmaxf(o.z, 0.f); o.w = fmaxf(o.w, 0.f);
+      }
+      *reinterpret_cast<float4*>(p.C + off) = o;
+    } else {
+      const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int me = m + e;
+        if (me >= p.M) break;
+        const int im = me / p.hw;
+        const int px = me - im * p.hw;
+        const int64_t o1 = ((int64_t)im * p.N + n) * p.hw + px;
+        float o = sv[e];
+        if (p.residual) o += __ldg(p.residual + o1);
+        if (p.relu) o = fmaxf(o, 0.f);
+        p.C[o1] = o;
+      }
+    }
+  }
+  named_bar_sync(1, 128);
+}
+
 // B_MN: 0 = B is K-major ([N,K] in memory), 1 = MN-major ([K,N] row-major).
 template <int BN, bool SPLIT, int A_MODE, int B_MN>
 __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
     rtb_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const GemmParams p) {
+                    const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
   constexpr bool GATHER = (A_MODE == 1);
   constexpr bool IM2COL = (A_MODE == 2);
   using Cfg = GemmCfg<BN, SPLIT>;
@@ -222,7 +340,8 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
   uint8_t* sB = sA + S * kABytes;                      // S x BN*128
   uint8_t* sAlo = sB + S * kBBytes;                    // SPLIT: S x 16 KB
   uint8_t* sBlo = sAlo + (SPLIT ? S * kABytes : 0);    // SPLIT: S x BN*128
-  uint8_t* tail = sBlo + (SPLIT ? S * kBBytes : 0);
+  uint8_t* sOut = sBlo + (SPLIT ? S * kBBytes : 0);    // 2 x 16 KB epilogue staging
+  uint8_t* tail = sOut + kOutBytes;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(tail);
   uint64_t* conv_bar = full_bar + S;
   uint64_t* empty_bar = conv_bar + S;
@@ -251,6 +370,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
   if (warp == Roles::kWarpTma && lane == 0) {
     if (!GATHER) tma_prefetch_desc(&tmA);  // tiled or im2col map
     tma_prefetch_desc(&tmB);
+    if (p.c_tma) tma_prefetch_desc(&tmC);
   }
   if (warp == Roles::kWarpMma) {
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
@@ -260,6 +380,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x == 0) trace_stamp(p, 0);
 
   if (warp == Roles::kWarpTma) {
     // ------------------------------------------------------------ TMA producer
@@ -281,10 +402,12 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
           a_h = oh * p.sh - p.ph;
           a_w = (rem - oh * p.Wo) * p.sw - p.pw;
         }
+        const int tj = (t - (int)blockIdx.x) / (int)gridDim.x;
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!mbar_wait_bounded(&empty_bar[s], ph ^ 1, abort_flag, p.err, DEV_TIMEOUT_EMPTY,
                                  p.timeout_ns))
             break;
+          if (kb == 0 && tj < kTraceTiles) trace_stamp(p, 2 + 6 * tj);
           mbar_arrive_expect_tx(&full_bar[s], tx);
           // Warm L2 for a k-block `prefetch_kb` ahead (hides DRAM latency beyond
           // what the shared-memory ring can cover).
@@ -349,6 +472,10 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
               ok = false;
               break;
             }
+            {
+              const int tj = (t - (int)blockIdx.x) / (int)gridDim.x;
+              if (kb == 0 && tj < kTraceTiles) trace_stamp(p, 3 + 6 * tj);
+            }
             tc_fence_after();
             // cp.async-gathered A (TF32 mode has no converter pass): make the
             // generic-proxy writes visible to the tensor core's async proxy.
@@ -385,6 +512,10 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
           }
           if (!ok) break;
           umma_commit(&tfull_bar[b]);
+          {
+            const int tj = (t - (int)blockIdx.x) / (int)gridDim.x;
+            if (kb0 + p.kb_per_acc >= p.num_kb && tj < kTraceTiles) trace_stamp(p, 4 + 6 * tj);
+          }
         }
       }
     }
@@ -395,6 +526,8 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
     const uint32_t t_lane = tmem_base + ((uint32_t)lane_base << 16);
     const uint32_t t_run = t_lane + (uint32_t)(2 * BN);  // fp32 running sum (3xTF32)
     const int units = (p.num_kb + p.kb_per_acc - 1) / p.kb_per_acc;
+    const int et = threadIdx.x - Roles::kWarpEpi * 32;  // 0..127 within the epilogue group
+    int chunk = 0;  // staging-buffer sequence number
     int g = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
@@ -416,6 +549,13 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
         }
         tc_fence_after();
         const bool last = (u + 1 == units);
+        if (warp == Roles::kWarpEpi && lane == 0) {
+          const int tj = (t - (int)blockIdx.x) / (int)gridDim.x;
+          if (tj < kTraceTiles) {
+            if (u == 0) trace_stamp(p, 5 + 6 * tj);
+            if (last) trace_stamp(p, 6 + 6 * tj);
+          }
+        }
         const uint32_t t_part = t_lane + (uint32_t)(b * BN);
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
@@ -434,14 +574,36 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
             tc_fence_before();
             mbar_arrive(&tempty_bar[b]);  // partial buffer b may be overwritten now
           }
-          if (SPLIT && !last)
+          if (SPLIT && !last) {
             tmem_st_32x32b_x32(t_run + (uint32_t)c, r);
-          else
+          } else if (p.c_tma) {
+            epilogue_stage_rowmajor(p, sOut + (chunk & 1) * kOutChunkBytes, row, tn * BN + c, m, r);
+            fence_proxy_async_smem();
+            named_bar_sync(1, 128);
+            if (et == 0) {
+              tma_store_2d(&tmC, sOut + (chunk & 1) * kOutChunkBytes, tn * BN + c, tm * kBM);
+              bulk_commit_group();
+              bulk_wait_group_read<1>();  // the buffer used next is free again
+            }
+            named_bar_sync(1, 128);
+            ++chunk;
+          } else if (p.out_mode == 1) {
+            float* buf = reinterpret_cast<float*>(sOut + (chunk & 1) * kOutChunkBytes);
+            epilogue_nchw_chunk(p, buf, row, et, tm * kBM, tn * BN + c, r);
+            ++chunk;
+          } else {
             epilogue_store32(p, m, tn * BN + c, r);
+          }
         }
         if (SPLIT && !last) tmem_st_wait();
       }
+      {
+        const int tj = (t - (int)blockIdx.x) / (int)gridDim.x;
+        if (ok && warp == Roles::kWarpEpi && lane == 0 && tj < kTraceTiles)
+          trace_stamp(p, 7 + 6 * tj);
+      }
     }
+    if (p.c_tma && et == 0) bulk_wait_group<0>();  // all output stores complete
   } else if (SPLIT && warp >= Roles::kWarpConv && warp < Roles::kWarpConv + 4) {
     // ------------------------------------------------------------ converters
     const int ct = threadIdx.x - Roles::kWarpConv * 32;  // 0..127
@@ -555,6 +717,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::kTmemCols);
   }
+  if (threadIdx.x == 0) trace_stamp(p, 1);
 }
 
 }  // namespace rtb

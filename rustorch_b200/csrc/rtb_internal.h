@@ -18,6 +18,8 @@ struct rtb_ctx {
   int* d_err = nullptr;           // device error word (bounded-wait timeouts)
   uint64_t timeout_ns = 2000000000ull;
   int default_precision = RTB_PREC_3XTF32;
+  unsigned long long* trace = nullptr;  // kernel timeline trace buffer (diagnostics)
+  int64_t trace_capacity = 0;           // in 64-bit stamps
 };
 
 namespace rtb {
