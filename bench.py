@@ -30,6 +30,8 @@ import sys
 import threading
 import time
 
+import numpy as np
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
@@ -338,10 +340,219 @@ class GemmWorkload:
                                                 f"single-threaded blocked sgemm, {reps} calls")
 
 
+class ResNet18Workload:
+    """ResNet-18 forward, B=256 images per GPU (batch-sharded, no communication)."""
+    name = "resnet18_fwd"
+
+    def __init__(self, rb, torch, dev, batch=256):
+        self.rb, self.torch, self.dev = rb, torch, dev
+        self.B = batch
+        self.h = ctypes.c_void_p()
+        rb.call("rtb_resnet18_create", dev.index or 0, 3, PRECISION[0], ctypes.byref(self.h))
+        self.flops_img = rb.lib().rtb_resnet18_flops_per_image(self.h)
+        self.flops = float(self.flops_img * self.B)
+        x = rb.fill_normal((self.B, 3, 224, 224), 3, 1000)
+        self.host = {"x": x}
+        self.x = torch.from_numpy(x).to(dev)          # 154 MB > L2
+        self.logits = torch.empty((self.B, 1000), device=dev)
+        self.config = {"workload": "ResNet-18 forward (BN folded), fp32",
+                       "batch_per_gpu": self.B, "input": [self.B, 3, 224, 224], "seed": 3,
+                       "flops_per_image": self.flops_img,
+                       "l2": "inputs larger than L2 (154 MB per batch)"}
+        self.launches_per_step = 24  # layout, 20 convs, max pool, avg pool, fc
+        self.unit = "img/s"
+
+    def _fwd(self, x):
+        stream = ctypes.c_void_p(self.torch.cuda.current_stream(self.dev).cuda_stream)
+        self.rb.call("rtb_resnet18_forward", self.h, self.B, ctypes.c_void_p(x.data_ptr()),
+                     ctypes.c_void_p(self.logits.data_ptr()), stream)
+
+    def step(self):
+        self._fwd(self.x)
+
+    def kernel_setup(self):
+        pass
+
+    def kernel_step(self):
+        self._fwd(self.x)
+
+    def e2e_setup(self):
+        rb = self.rb
+        ctx = rb.get_context(self.dev.index or 0)
+        x = self.host["x"]
+        self.px = ctypes.c_void_p()
+        rb.call("rtb_host_alloc", ctx.handle, ctypes.byref(self.px), x.nbytes)
+        ctypes.memmove(self.px, x.ctypes.data, x.nbytes)
+        self.py = ctypes.c_void_p()
+        rb.call("rtb_host_alloc", ctx.handle, ctypes.byref(self.py), self.B * 1000 * 4)
+        self.dx = self.torch.empty_like(self.x)
+        self.h2d_bytes = x.nbytes
+        self.d2h_bytes = self.B * 1000 * 4
+
+    def e2e_step(self):
+        rb = self.rb
+        ctx = rb.get_context(self.dev.index or 0)
+        stream = ctypes.c_void_p(self.torch.cuda.current_stream(self.dev).cuda_stream)
+        rb.call("rtb_memcpy_h2d", ctx.handle, ctypes.c_void_p(self.dx.data_ptr()), self.px,
+                self.h2d_bytes, stream)
+        self._fwd(self.dx)
+        rb.call("rtb_memcpy_d2h", ctx.handle, self.py, ctypes.c_void_p(self.logits.data_ptr()),
+                self.d2h_bytes, stream)
+
+    def e2e_teardown(self):
+        ctx = self.rb.get_context(self.dev.index or 0)
+        self.rb.call("rtb_host_free", ctx.handle, self.px)
+        self.rb.call("rtb_host_free", ctx.handle, self.py)
+
+    def cpu_sample(self, threads):
+        """The reference's CPU ops (conv2d auto path, bias, relu, max_pool2d,
+        add, avg pool, Linear) composed into ResNet-18, on one image."""
+        from oracle import oracle as orc
+        convs = []
+        specs = [(3, 64, 7, 2, 3)]
+        cin = 64
+        for st, co in enumerate([64, 128, 256, 512]):
+            for blk in range(2):
+                down = st > 0 and blk == 0
+                specs += [(cin, co, 3, 2 if down else 1, 1), (co, co, 3, 1, 1)]
+                if down:
+                    specs.append((cin, co, 1, 2, 0))
+                cin = co
+        for i, (ci, co, k, s, p) in enumerate(specs):
+            convs.append((orc.normal((co, ci, k, k), 3, i, 0.0, math.sqrt(2.0 / (ci * k * k))),
+                          np.zeros(co, np.float32), s, p))
+        fc_w = orc.uniform((1000, 512), 3, 100, -1 / math.sqrt(512), 1 / math.sqrt(512))
+        fc_b = orc.uniform((1000,), 3, 101, -1 / math.sqrt(512), 1 / math.sqrt(512))
+        x = orc.normal((1, 3, 224, 224), 3, 1000)
+
+        def conv(t, i, relu, res=None):
+            w, b, s, p = convs[i]
+            y, _ = orc.conv2d(t, w, (s, s), (p, p), threads)
+            y = orc.add_bias_nchw(y, b)
+            if res is not None:
+                y = y + res
+            return orc.relu(y) if relu else y
+
+        def forward(t):
+            t = orc.max_pool2d(conv(t, 0, True), (3, 3), (2, 2), (1, 1))
+            i = 1
+            for st in range(4):
+                for blk in range(2):
+                    down = st > 0 and blk == 0
+                    a = conv(t, i, True)
+                    ident = conv(t, i + 2, False) if down else t
+                    t = conv(a, i + 1, True, ident)
+                    i += 3 if down else 2
+            return orc.linear(orc.global_avg_pool(t), fc_w, fc_b)
+
+        t0 = time.perf_counter()
+        reps = 0
+        while reps < 1 or (time.perf_counter() - t0 < 10.0 and reps < 5):
+            forward(x)
+            reps += 1
+        dt = (time.perf_counter() - t0) / reps
+        return 1.0 / dt, f"1 image per forward (reference CPU ops composed), {reps} forwards"
+
+
+class MlpWorkload:
+    """3-layer MLP forward: X [4096,1024] -> 4096 -> 4096 -> 1024, Linear+ReLU
+    after the first two layers (bias and ReLU fused in the GEMM epilogue)."""
+    name = "mlp3_fwd"
+
+    def __init__(self, rb, torch, dev):
+        self.rb, self.torch, self.dev = rb, torch, dev
+        self.dims = [1024, 4096, 4096, 1024]
+        self.M = 4096
+        self.flops = float(sum(2 * self.M * self.dims[i] * self.dims[i + 1] for i in range(3)))
+        gain = math.sqrt(2.0)
+        self.host = {"x": rb.fill_normal((self.M, 1024), 2, 0)}
+        self.ws, self.bs = [], []
+        for i in range(3):
+            fan_in = self.dims[i]
+            bound = math.sqrt(3.0) * gain / math.sqrt(fan_in)
+            w = rb.fill_uniform((self.dims[i + 1], fan_in), 2, 1 + i, -bound, bound)
+            self.host[f"w{i}"] = w
+            self.ws.append(torch.from_numpy(w).to(dev))
+            self.bs.append(torch.zeros(self.dims[i + 1], device=dev))
+        self.x = torch.from_numpy(self.host["x"]).to(dev)
+        self.h = [torch.empty((self.M, d), device=dev) for d in self.dims[1:]]
+        self.config = {"workload": "3-layer MLP forward 4096x(1024->4096->4096->1024)",
+                       "seed": 2, "l2": "operands + activations larger than L2 (~370 MB)"}
+        self.launches_per_step = 3
+        self.unit = "TFLOP/s"
+
+    def _fwd(self, x):
+        rb = self.rb
+        a = x
+        for i in range(3):
+            rb.sgemm(a, self.ws[i].t(), bias=self.bs[i], act=rb.ACT_RELU if i < 2 else rb.ACT_NONE,
+                     precision=PRECISION[0], out=self.h[i])
+            a = self.h[i]
+
+    def step(self):
+        self._fwd(self.x)
+
+    def kernel_setup(self):
+        pass
+
+    def kernel_step(self):
+        self._fwd(self.x)
+
+    def e2e_setup(self):
+        rb = self.rb
+        ctx = rb.get_context(self.dev.index or 0)
+        x = self.host["x"]
+        self.px = ctypes.c_void_p()
+        rb.call("rtb_host_alloc", ctx.handle, ctypes.byref(self.px), x.nbytes)
+        ctypes.memmove(self.px, x.ctypes.data, x.nbytes)
+        self.py = ctypes.c_void_p()
+        rb.call("rtb_host_alloc", ctx.handle, ctypes.byref(self.py), self.M * 1024 * 4)
+        self.dx = self.torch.empty_like(self.x)
+        self.h2d_bytes = x.nbytes
+        self.d2h_bytes = self.M * 1024 * 4
+
+    def e2e_step(self):
+        rb = self.rb
+        ctx = rb.get_context(self.dev.index or 0)
+        stream = ctypes.c_void_p(self.torch.cuda.current_stream(self.dev).cuda_stream)
+        rb.call("rtb_memcpy_h2d", ctx.handle, ctypes.c_void_p(self.dx.data_ptr()), self.px,
+                self.h2d_bytes, stream)
+        self._fwd(self.dx)
+        rb.call("rtb_memcpy_d2h", ctx.handle, self.py, ctypes.c_void_p(self.h[2].data_ptr()),
+                self.d2h_bytes, stream)
+
+    def e2e_teardown(self):
+        ctx = self.rb.get_context(self.dev.index or 0)
+        self.rb.call("rtb_host_free", ctx.handle, self.px)
+        self.rb.call("rtb_host_free", ctx.handle, self.py)
+
+    def cpu_sample(self, threads):
+        """nn::Linear x3 on the reference's CPU path for a 64-row sample."""
+        from oracle import oracle as orc
+        rows = 64
+        x = orc.normal((self.M, 1024), 2, 0)[:rows]
+        ws = []
+        for i in range(3):
+            bound = math.sqrt(3.0) * math.sqrt(2.0) / math.sqrt(self.dims[i])
+            ws.append(orc.uniform((self.dims[i + 1], self.dims[i]), 2, 1 + i, -bound, bound))
+        t0 = time.perf_counter()
+        reps = 0
+        while reps < 1 or (time.perf_counter() - t0 < 10.0 and reps < 10):
+            a = x
+            for i in range(3):
+                a = orc.linear(a, ws[i], np.zeros(self.dims[i + 1], np.float32), relu=i < 2,
+                               threads=threads)
+            reps += 1
+        dt = (time.perf_counter() - t0) / reps
+        return self.flops * rows / self.M / dt / 1e12, f"{rows} of 4096 rows, {reps} passes"
+
+
 WORKLOADS = {
     "conv": lambda rb, torch, dev: ConvWorkload(rb, torch, dev),
     "gemm1024": lambda rb, torch, dev: GemmWorkload(rb, torch, dev, 1024, 0),
     "gemm8192": lambda rb, torch, dev: GemmWorkload(rb, torch, dev, 8192, 4),
+    "resnet18": lambda rb, torch, dev: ResNet18Workload(rb, torch, dev),
+    "mlp": lambda rb, torch, dev: MlpWorkload(rb, torch, dev),
 }
 
 
@@ -396,10 +607,18 @@ def run_ours(args):
     wl = WORKLOADS[args.workload](rb, torch, dev)
     peaks = _peaks()
 
+    unit = getattr(wl, "unit", "TFLOP/s")
+
+    def rate(total_ms, ranks):
+        # whole-job throughput in the workload's unit over `ranks` GPUs
+        if unit == "img/s":
+            return ranks * wl.B * args.steps / (total_ms / 1e3)
+        return ranks * wl.flops * args.steps / (total_ms / 1e3) / 1e12
+
     with ClockSampler(dev) as clk:
         ms = _time_steps(torch, wl.step, args.steps, args.warmup, dev, dist)
     ms_per_step = ms / args.steps
-    value = world * wl.flops * args.steps / (ms / 1e3) / 1e12
+    value = rate(ms, world)
 
     # dominant kernel alone, CUDA events on its launch stream
     wl.kernel_setup()
@@ -412,7 +631,7 @@ def run_ours(args):
     wl.e2e_setup()
     ems = _time_steps(torch, wl.e2e_step, args.steps, max(3, args.warmup), dev, dist)
     wl.e2e_teardown()
-    e2e = world * wl.flops * args.steps / (ems / 1e3) / 1e12
+    e2e = rate(ems, world)
 
     err = rb.get_context(local).device_error()
     if err:
@@ -420,14 +639,16 @@ def run_ours(args):
 
     if rank == 0:
         cpu_val, sample = wl.cpu_sample(os.cpu_count())
+        par = (f"batch-sharded x{world} (no collective)" if unit == "img/s"
+               else f"replicas x{world}")
         line = {
-            "metric": f"{wl.name} TFLOP/s ({args.precision.upper()}, fp32 in/out)",
-            "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "metric": f"{wl.name} {unit} ({args.precision.upper()}, fp32 in/out)",
+            "value": round(value, 3), "unit": unit, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None,
             "dtype": "f32 (3xTF32 tensor-core split)" if PRECISION[0] == 0 else "f32 (TF32 tensor core)",
             "data": "synthetic (SplitMix64/Box-Muller, seeded)",
-            "config": dict(wl.config, parallelism=f"replicas x{world}"),
+            "config": dict(wl.config, parallelism=par),
             "roofline": {"bound": "tensor", "achieved": round(k_tflops, 3),
                          "peak": round(roof_peak, 3), "unit": "TFLOP/s",
                          "frac": round(k_tflops / roof_peak, 4), "traffic": None,
@@ -435,9 +656,9 @@ def run_ours(args):
                                        f"/ 2 (TF32 rate) / {MMAS_PER_MAC[0]} (MMAs per MAC)",
                          "tensor_pipe_frac": round(MMAS_PER_MAC[0] * k_tflops / tf32_peak, 4),
                          "kernel_ms": round(kms / args.steps, 5)},
-            "cpu_baseline": {"value": round(cpu_val, 6), "unit": "TFLOP/s",
+            "cpu_baseline": {"value": round(cpu_val, 6), "unit": unit,
                              "cores": os.cpu_count(), "kind": "port", "sample": sample},
-            "e2e": {"value": round(e2e, 3), "unit": "TFLOP/s",
+            "e2e": {"value": round(e2e, 3), "unit": unit,
                     "h2d_bytes_per_step": wl.h2d_bytes, "d2h_bytes_per_step": wl.d2h_bytes},
             "gpu_launches": wl.launches_per_step * args.steps,
             "clocks": clk.summary(),
@@ -455,17 +676,32 @@ def run_reference(args):
     if rank != 0:
         return
     threads = os.cpu_count()
+    # Workload descriptions only (no GPU): cpu_sample needs the sizes.
     if args.workload == "conv":
         wl = ConvWorkload.__new__(ConvWorkload)
         wl.N, wl.C, wl.H, wl.W, wl.Co = 32, 128, 28, 28, 128
         wl.flops = 2.0 * wl.N * wl.H * wl.W * wl.Co * wl.C * 9
         cfg = {"workload": "conv2d+bias+relu ResNet-50 stage-2 3x3", "input": [32, 128, 28, 28],
                "weight": [128, 128, 3, 3], "stride": 1, "pad": 1, "seed": 1}
+        unit = "TFLOP/s"
+    elif args.workload == "resnet18":
+        wl = ResNet18Workload.__new__(ResNet18Workload)
+        wl.B = 256
+        cfg = {"workload": "ResNet-18 forward (BN folded), fp32", "batch_per_gpu": 256, "seed": 3}
+        unit = "img/s"
+    elif args.workload == "mlp":
+        wl = MlpWorkload.__new__(MlpWorkload)
+        wl.dims, wl.M = [1024, 4096, 4096, 1024], 4096
+        wl.flops = float(sum(2 * wl.M * wl.dims[i] * wl.dims[i + 1] for i in range(3)))
+        cfg = {"workload": "3-layer MLP forward 4096x(1024->4096->4096->1024)", "seed": 2}
+        unit = "TFLOP/s"
     else:
         n = 1024 if args.workload == "gemm1024" else 8192
         wl = GemmWorkload.__new__(GemmWorkload)
         wl.n, wl.seed, wl.flops, wl.name = n, (0 if n == 1024 else 4), 2.0 * n ** 3, f"sgemm_{n}"
         cfg = {"workload": f"f32 matmul {n}x{n}x{n}", "seed": wl.seed}
+        unit = "TFLOP/s"
+    name = getattr(wl, "name", args.workload)
     vals, samples = [], []
     t0 = time.perf_counter()
     for _ in range(max(1, args.steps)):
@@ -476,13 +712,13 @@ def run_reference(args):
             break
     v = statistics.median(vals)
     line = {"impl": "reference",
-            "metric": f"{wl.name} TFLOP/s ({args.precision.upper()}, fp32 in/out)",
-            "value": round(v, 6), "unit": "TFLOP/s", "n_gpus": world, "steps": len(vals),
+            "metric": f"{name} {unit} ({args.precision.upper()}, fp32 in/out)",
+            "value": round(v, 6), "unit": unit, "n_gpus": world, "steps": len(vals),
             "warmup": args.warmup, "higher_is_better": True, "vs_baseline": None,
             "dtype": "f32", "data": "synthetic (SplitMix64/Box-Muller, seeded)", "config": cfg,
-            "cpu_baseline": {"value": round(v, 6), "unit": "TFLOP/s", "cores": threads,
+            "cpu_baseline": {"value": round(v, 6), "unit": unit, "cores": threads,
                              "kind": "port", "sample": samples[0]},
-            "e2e": {"value": round(v, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+            "e2e": {"value": round(v, 6), "unit": unit, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},
             "note": "reference CPU path restated in C (no Rust toolchain to build the reference)"}
     print(json.dumps(line), flush=True)

@@ -186,6 +186,13 @@ int rtb_global_avg_pool(rtb_ctx* ctx, int64_t N, int64_t C, int64_t H, int64_t W
 /* Elementwise: y = a + b (ops::add same shape), y = max(x, 0) (ops::relu). */
 int rtb_add(rtb_ctx* ctx, int64_t n, const float* a, const float* b, float* y, void* stream);
 int rtb_relu(rtb_ctx* ctx, int64_t n, const float* x, float* y, void* stream);
+/* y = a op b (op 0 = add, 1 = mul) over an n-d output `shape` (1..8 dims,
+ * row-major y) with per-operand element strides, 0 for broadcast dimensions:
+ * ops::add / ops::mul with broadcasting (rustorch-core/src/ops.rs:223-291,
+ * rustorch-core/src/broadcast.rs:23-136). */
+int rtb_elementwise_broadcast(rtb_ctx* ctx, int op, int ndim, const int64_t* shape,
+                              const float* a, const int64_t* a_strides, const float* b,
+                              const int64_t* b_strides, float* y, void* stream);
 
 /* ---------------------------------------------------------------- data */
 /* The documented synthetic-input generator: SplitMix64 stream keyed by

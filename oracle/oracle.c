@@ -138,38 +138,87 @@ static float* orc_contig2d(const float* src, int64_t rows, int64_t cols, int64_t
 
 /* matrixmultiply::sgemm restatement (call site rustorch-core/src/ops.rs:1099-1114,
  * alpha=1, beta=0, C row-major with ldc=n).  C[i,j] = sum over KC=256 k-blocks,
- * left to right, of fma-chains over the block.  Tiled MRxNR for speed; the
- * per-element order is independent of the tiling.  Rows [r0, r1) only, so the
- * all-cores variant can split rows without changing numerics. */
+ * left to right, of fma-chains over the block.  Packed MRxNR = 8x8 register
+ * blocking with an AVX2/FMA microkernel (one 8-wide accumulator per row, an FMA
+ * per k step), as the crate's x86 FMA kernel does; the per-element summation
+ * order is independent of the tiling.  Rows [r0, r1) only, so the all-cores
+ * variant can split rows without changing numerics. */
+#if defined(__AVX2__) && defined(__FMA__)
+#include <immintrin.h>
+#endif
+#define ORC_MC 64
+#define ORC_NC 512
 static void orc_sgemm_rows(int64_t r0, int64_t r1, int64_t k, int64_t n, const float* A, int64_t rsa,
                            int64_t csa, const float* B, int64_t rsb, int64_t csb, float* C) {
-  float* bpack = (float*)malloc((size_t)ORC_KC * ORC_NR * sizeof(float));
-  for (int64_t j0 = 0; j0 < n; j0 += ORC_NR) {
-    const int64_t nj = (n - j0) < ORC_NR ? (n - j0) : ORC_NR;
+  float* bpack = (float*)aligned_alloc(64, (size_t)ORC_KC * ORC_NC * sizeof(float));
+  float* apack = (float*)aligned_alloc(64, (size_t)ORC_KC * ORC_MC * sizeof(float));
+  for (int64_t j1 = 0; j1 < n; j1 += ORC_NC) {
+    const int64_t nc = (n - j1) < ORC_NC ? (n - j1) : ORC_NC;
+    const int64_t npan = (nc + ORC_NR - 1) / ORC_NR;
     for (int64_t k0 = 0; k0 < k; k0 += ORC_KC) {
       const int64_t kb = (k - k0) < ORC_KC ? (k - k0) : ORC_KC;
-      for (int64_t p = 0; p < kb; ++p)
-        for (int64_t jj = 0; jj < ORC_NR; ++jj)
-          bpack[p * ORC_NR + jj] = jj < nj ? B[(k0 + p) * rsb + (j0 + jj) * csb] : 0.0f;
-      for (int64_t i0 = r0; i0 < r1; i0 += ORC_MR) {
-        const int64_t mi = (r1 - i0) < ORC_MR ? (r1 - i0) : ORC_MR;
-        float acc[ORC_MR][ORC_NR];
-        memset(acc, 0, sizeof(acc));
-        for (int64_t p = 0; p < kb; ++p) {
-          const float* bp = bpack + p * ORC_NR;
-          for (int64_t ii = 0; ii < ORC_MR; ++ii) {
-            const float a = ii < mi ? A[(i0 + ii) * rsa + (k0 + p) * csa] : 0.0f;
-            for (int64_t jj = 0; jj < ORC_NR; ++jj) acc[ii][jj] = fmaf(a, bp[jj], acc[ii][jj]);
+      /* B[k0:k0+kb, j1:j1+nc] -> panels of NR columns, p-major inside a panel */
+      for (int64_t jp = 0; jp < npan; ++jp)
+        for (int64_t p = 0; p < kb; ++p)
+          for (int64_t jj = 0; jj < ORC_NR; ++jj) {
+            const int64_t j = j1 + jp * ORC_NR + jj;
+            bpack[(jp * kb + p) * ORC_NR + jj] = j < j1 + nc ? B[(k0 + p) * rsb + j * csb] : 0.0f;
+          }
+      for (int64_t i1 = r0; i1 < r1; i1 += ORC_MC) {
+        const int64_t mc = (r1 - i1) < ORC_MC ? (r1 - i1) : ORC_MC;
+        const int64_t mpan = (mc + ORC_MR - 1) / ORC_MR;
+        for (int64_t ip = 0; ip < mpan; ++ip)
+          for (int64_t p = 0; p < kb; ++p)
+            for (int64_t ii = 0; ii < ORC_MR; ++ii) {
+              const int64_t i = i1 + ip * ORC_MR + ii;
+              apack[(ip * kb + p) * ORC_MR + ii] = i < i1 + mc ? A[i * rsa + (k0 + p) * csa] : 0.0f;
+            }
+        for (int64_t jp = 0; jp < npan; ++jp) {
+          const float* bp0 = bpack + jp * kb * ORC_NR;
+          const int64_t j0 = j1 + jp * ORC_NR;
+          const int64_t nj = (j1 + nc - j0) < ORC_NR ? (j1 + nc - j0) : ORC_NR;
+          for (int64_t ip = 0; ip < mpan; ++ip) {
+            const float* ap0 = apack + ip * kb * ORC_MR;
+            const int64_t i0 = i1 + ip * ORC_MR;
+            const int64_t mi = (i1 + mc - i0) < ORC_MR ? (i1 + mc - i0) : ORC_MR;
+            float acc[ORC_MR][ORC_NR] __attribute__((aligned(32)));
+#if defined(__AVX2__) && defined(__FMA__)
+            __m256 c0 = _mm256_setzero_ps(), c1 = c0, c2 = c0, c3 = c0, c4 = c0, c5 = c0,
+                   c6 = c0, c7 = c0;
+            for (int64_t p = 0; p < kb; ++p) {
+              const __m256 bv = _mm256_load_ps(bp0 + p * ORC_NR);
+              const float* ap = ap0 + p * ORC_MR;
+              c0 = _mm256_fmadd_ps(_mm256_broadcast_ss(ap + 0), bv, c0);
+              c1 = _mm256_fmadd_ps(_mm256_broadcast_ss(ap + 1), bv, c1);
+              c2 = _mm256_fmadd_ps(_mm256_broadcast_ss(ap + 2), bv, c2);
+              c3 = _mm256_fmadd_ps(_mm256_broadcast_ss(ap + 3), bv, c3);
+              c4 = _mm256_fmadd_ps(_mm256_broadcast_ss(ap + 4), bv, c4);
+              c5 = _mm256_fmadd_ps(_mm256_broadcast_ss(ap + 5), bv, c5);
+              c6 = _mm256_fmadd_ps(_mm256_broadcast_ss(ap + 6), bv, c6);
+              c7 = _mm256_fmadd_ps(_mm256_broadcast_ss(ap + 7), bv, c7);
+            }
+            _mm256_store_ps(acc[0], c0); _mm256_store_ps(acc[1], c1);
+            _mm256_store_ps(acc[2], c2); _mm256_store_ps(acc[3], c3);
+            _mm256_store_ps(acc[4], c4); _mm256_store_ps(acc[5], c5);
+            _mm256_store_ps(acc[6], c6); _mm256_store_ps(acc[7], c7);
+#else
+            memset(acc, 0, sizeof(acc));
+            for (int64_t p = 0; p < kb; ++p)
+              for (int64_t ii = 0; ii < ORC_MR; ++ii)
+                for (int64_t jj = 0; jj < ORC_NR; ++jj)
+                  acc[ii][jj] = fmaf(ap0[p * ORC_MR + ii], bp0[p * ORC_NR + jj], acc[ii][jj]);
+#endif
+            for (int64_t ii = 0; ii < mi; ++ii)
+              for (int64_t jj = 0; jj < nj; ++jj) {
+                float* c = &C[(i0 + ii) * n + (j0 + jj)];
+                *c = (k0 == 0) ? acc[ii][jj] : (*c + acc[ii][jj]);
+              }
           }
         }
-        for (int64_t ii = 0; ii < mi; ++ii)
-          for (int64_t jj = 0; jj < nj; ++jj) {
-            float* c = &C[(i0 + ii) * n + (j0 + jj)];
-            *c = (k0 == 0) ? acc[ii][jj] : (*c + acc[ii][jj]);
-          }
       }
     }
   }
+  free(apack);
   free(bpack);
 }
 

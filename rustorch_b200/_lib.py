@@ -68,12 +68,20 @@ SIGNATURES = {
     "rtb_global_avg_pool": (_i, [_p] + [_i64] * 4 + [_p, _p, _i, _p]),
     "rtb_add": (_i, [_p, _i64, _p, _p, _p, _p]),
     "rtb_relu": (_i, [_p, _i64, _p, _p, _p]),
+    "rtb_elementwise_broadcast": (_i, [_p, _i, _i, _p, _p, _p, _p, _p, _p, _p]),
     "rtb_fill_normal_host": (_i, [_p, _i64, _u64, _u64, _f, _f]),
     "rtb_fill_uniform_host": (_i, [_p, _i64, _u64, _u64, _f, _f]),
     "rtb_nccl_unique_id": (_i, [_p]),
     "rtb_nccl_comm_init": (_i, [_p, _p, _i, _i, _pp]),
     "rtb_nccl_comm_destroy": (_i, [_p]),
     "rtb_sgemm_nsplit_allgather": (_i, [_p, _p, _i64, _i64, _i64, _p, _p, _p, _p, _i, _p]),
+    # include/rustorch_b200_vision.h
+    "rtb_resnet18_create": (_i, [_i, _u64, _i, _pp]),
+    "rtb_resnet18_destroy": (_i, [_p]),
+    "rtb_resnet18_forward": (_i, [_p, _i64, _p, _p, _p]),
+    "rtb_resnet18_num_params": (_i64, [_p]),
+    "rtb_resnet18_get_param": (_i, [_p, _i64, _p, ctypes.POINTER(_i64)]),
+    "rtb_resnet18_flops_per_image": (_i64, [_p]),
 }
 
 _lib = None

@@ -2,7 +2,7 @@
 
     python -m rustorch_b200.build [--force] [--verbose]
 
-Each csrc/*.cu compiles to _build/*.o in parallel, then links into
+Each csrc/*.cu and csrc/*.cpp compiles to _build/*.o in parallel, then links into
 rustorch_b200/librustorch_b200.so (NCCL is dlopen'ed at first use).  The library is
 rebuilt only when a source or header is newer than it.
 """
@@ -33,7 +33,7 @@ def _nvcc() -> str:
 
 
 def _sources():
-    return sorted(glob.glob(os.path.join(CSRC, "*.cu")))
+    return sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cpp")))
 
 
 def _deps():
@@ -49,7 +49,7 @@ def needs_build() -> bool:
 
 
 def _compile(src: str, verbose: bool) -> str:
-    obj = os.path.join(BUILD, os.path.basename(src)[:-3] + ".o")
+    obj = os.path.join(BUILD, os.path.basename(src).rsplit(".", 1)[0] + ".o")
     cmd = [_nvcc()] + NVCC_FLAGS + ["-c", src, "-o", obj]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")

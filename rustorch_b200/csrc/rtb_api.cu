@@ -681,6 +681,22 @@ int rtb_add(rtb_ctx* ctx, int64_t n, const float* a, const float* b, float* y, v
   return launch_add(a, b, y, n, pick_stream(ctx, stream));
 }
 
+int rtb_elementwise_broadcast(rtb_ctx* ctx, int op, int ndim, const int64_t* shape,
+                              const float* a, const int64_t* a_strides, const float* b,
+                              const int64_t* b_strides, float* y, void* stream) {
+  RTB_CHECK_CTX(ctx);
+  if (op != 0 && op != 1) return set_error(RTB_E_INVALID, "elementwise: op must be 0 (add) or 1 (mul)");
+  if (!shape || !a_strides || !b_strides) return set_error(RTB_E_INVALID, "elementwise: null shape");
+  for (int k = 0; k < ndim; ++k)
+    if (shape[k] < 0) return set_error(RTB_E_INVALID, "elementwise: negative extent");
+  int64_t n = 1;
+  for (int k = 0; k < ndim; ++k) n *= shape[k];
+  if (n == 0) return RTB_OK;
+  if (!a || !b || !y) return set_error(RTB_E_INVALID, "elementwise: null pointer");
+  DeviceGuard g(ctx->device);
+  return launch_broadcast(op, ndim, shape, a, a_strides, b, b_strides, y, pick_stream(ctx, stream));
+}
+
 int rtb_relu(rtb_ctx* ctx, int64_t n, const float* x, float* y, void* stream) {
   RTB_CHECK_CTX(ctx);
   if (n < 0) return set_error(RTB_E_INVALID, "relu: negative size");

@@ -204,6 +204,32 @@ __global__ void relu_kernel(const float* __restrict__ x, float* __restrict__ y, 
   }
 }
 
+// y[i] = a[.] op b[.] over an n-d output shape with per-operand element
+// strides (0 for a broadcast dimension), as ops::add / ops::mul do through
+// Tensor::expand (rustorch-core/src/broadcast.rs:23-136).
+struct BcastDesc {
+  int ndim;
+  int64_t shape[8];
+  int64_t sa[8];
+  int64_t sb[8];
+};
+
+__global__ void bcast_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                             float* __restrict__ y, int64_t n, BcastDesc d, int op) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t rem = i, oa = 0, ob = 0;
+    for (int k = d.ndim - 1; k >= 0; --k) {
+      const int64_t c = rem % d.shape[k];
+      rem /= d.shape[k];
+      oa += c * d.sa[k];
+      ob += c * d.sb[k];
+    }
+    const float x = a[oa], z = b[ob];
+    y[i] = op == 0 ? x + z : x * z;
+  }
+}
+
 // parts [P, M, Nl] -> C [M, P*Nl].
 __global__ void unsplit_cols_kernel(const float* __restrict__ parts, float* __restrict__ C,
                                     int64_t P, int64_t M, int64_t Nl) {
@@ -292,6 +318,24 @@ int launch_add(const float* a, const float* b, float* y, int64_t n, cudaStream_t
 int launch_relu(const float* x, float* y, int64_t n, cudaStream_t s) {
   relu_kernel<<<grid_for(n), kThreads, 0, s>>>(x, y, n);
   return launch_check("relu");
+}
+
+int launch_broadcast(int op, int ndim, const int64_t* shape, const float* a,
+                     const int64_t* sa, const float* b, const int64_t* sb, float* y,
+                     cudaStream_t s) {
+  if (ndim < 1 || ndim > 8) return set_error(RTB_E_UNSUPPORTED, "broadcast: 1..8 dimensions");
+  BcastDesc d;
+  d.ndim = ndim;
+  int64_t n = 1;
+  for (int k = 0; k < ndim; ++k) {
+    d.shape[k] = shape[k];
+    d.sa[k] = sa[k];
+    d.sb[k] = sb[k];
+    n *= shape[k];
+  }
+  if (n == 0) return RTB_OK;
+  bcast_kernel<<<grid_for(n), kThreads, 0, s>>>(a, b, y, n, d, op);
+  return launch_check("broadcast elementwise");
 }
 
 int launch_unsplit_cols(const float* parts, float* C, int64_t P, int64_t M, int64_t Nl,

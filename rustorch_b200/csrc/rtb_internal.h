@@ -109,6 +109,9 @@ int launch_global_avg_pool(const float* x, float* y, int64_t N, int64_t C, int64
                            cudaStream_t s);
 int launch_add(const float* a, const float* b, float* y, int64_t n, cudaStream_t s);
 int launch_relu(const float* x, float* y, int64_t n, cudaStream_t s);
+int launch_broadcast(int op, int ndim, const int64_t* shape, const float* a,
+                     const int64_t* sa, const float* b, const int64_t* sb, float* y,
+                     cudaStream_t s);
 int launch_unsplit_cols(const float* parts, float* C, int64_t P, int64_t M, int64_t Nl,
                         cudaStream_t s);
 int launch_nhwc_to_nchw(const float* x, float* y, int64_t N, int64_t C, int64_t HW,

@@ -1,0 +1,212 @@
+// The reference's own tests, restated against the C++ mirror of its API
+// (include/rustorch_b200.hpp) running on the B200 backend:
+//   rustorch-core/tests/autograd_test.rs:40-57   matmul 2x2 forward
+//   rustorch-core/tests/autograd_test.rs:86-99   conv2d 3x3 / 2x2 forward
+//   rustorch-core/examples/jit_demo.rs:21-88     Conv2d -> Relu fusion and execution
+// plus the panics the reference raises and the Conv2d -> Add -> Relu fusion.
+//
+// Usage: test_reference_api [--cpu-only]
+//   --cpu-only runs only the checks that need no GPU (graph rewriting, panics
+//   raised before any device work).  Prints "KAT <name> v0 v1 ..." lines that
+//   the pytest wrapper compares with tests/golden/reference_kat.json, and
+//   "PASS/FAIL <name>"; exit status = number of failures.
+#include <rustorch_b200.hpp>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <functional>
+#include <string>
+#include <vector>
+
+using namespace rustorch;
+
+static int g_fail = 0;
+
+static void run(const char* name, const std::function<void()>& fn) {
+  try {
+    fn();
+    std::printf("PASS %s\n", name);
+  } catch (const std::exception& e) {
+    std::printf("FAIL %s: %s\n", name, e.what());
+    ++g_fail;
+  }
+}
+
+static void expect(bool ok, const std::string& msg) {
+  if (!ok) throw std::runtime_error(msg);
+}
+
+static void expect_panic(const std::function<void()>& fn, const std::string& text) {
+  try {
+    fn();
+  } catch (const Panic& p) {
+    expect(std::string(p.what()).find(text) != std::string::npos,
+           std::string("panic message '") + p.what() + "' lacks '" + text + "'");
+    return;
+  }
+  throw std::runtime_error("expected a panic containing '" + text + "'");
+}
+
+static void kat(const char* name, const std::vector<float>& v) {
+  std::printf("KAT %s", name);
+  for (float x : v) std::printf(" %.9g", x);
+  std::printf("\n");
+}
+
+static void graph_tests() {
+  run("jit_fuse_conv_relu_rewrite", [] {
+    jit::Graph g;
+    size_t in = g.add_input({1, 1, 4, 4});
+    size_t w = g.add_input({1, 1, 3, 3});
+    size_t c = g.add_node(jit::NodeType::Conv2d(in, w, {1, 1}, {0, 0}), {1, 1, 2, 2});
+    size_t r = g.add_node(jit::NodeType::Relu(c), {1, 1, 2, 2});
+    g.outputs.push_back(r);
+    jit::Optimizer::optimize(g);
+    expect(g.nodes.size() == 3, "fused graph should have 3 nodes");
+    expect(g.nodes[2].op.op == jit::Op::Conv2dRelu, "Conv2dRelu node missing");
+    expect(g.outputs[0] == 2, "output not remapped to the fused node");
+  });
+  run("jit_fuse_conv_bias_relu_rewrite", [] {
+    jit::Graph g;
+    size_t in = g.add_input({1, 2, 5, 5});
+    size_t w = g.add_input({3, 2, 3, 3});
+    size_t b = g.add_input({1, 3, 1, 1});
+    size_t c = g.add_node(jit::NodeType::Conv2d(in, w, {1, 1}, {1, 1}), {1, 3, 5, 5});
+    size_t a = g.add_node(jit::NodeType::Add(c, b), {1, 3, 5, 5});
+    size_t r = g.add_node(jit::NodeType::Relu(a), {1, 3, 5, 5});
+    g.outputs.push_back(r);
+    jit::Optimizer::optimize(g);
+    expect(g.nodes.size() == 4, "fused graph should have 4 nodes");
+    expect(g.nodes[3].op.op == jit::Op::Conv2dBiasRelu, "Conv2dBiasRelu node missing");
+    expect(g.nodes[3].op.c == b, "bias operand not kept");
+  });
+  run("jit_no_fusion_when_relu_not_next", [] {
+    jit::Graph g;
+    size_t in = g.add_input({1, 1, 4, 4});
+    size_t w = g.add_input({1, 1, 3, 3});
+    size_t c = g.add_node(jit::NodeType::Conv2d(in, w, {1, 1}, {0, 0}), {1, 1, 2, 2});
+    size_t m = g.add_node(jit::NodeType::Mul(c, c), {1, 1, 2, 2});
+    size_t r = g.add_node(jit::NodeType::Relu(c), {1, 1, 2, 2});
+    g.outputs.push_back(m);
+    g.outputs.push_back(r);
+    jit::Optimizer::optimize(g);
+    expect(g.nodes.size() == 5, "no node should be fused");
+  });
+  run("panics_without_device_work", [] {
+    expect_panic([] { Tensor::new_({1, 2, 3}, {2, 2}); }, "does not match shape");
+    Tensor a = Tensor::new_({1, 2, 3, 4, 5, 6, 7, 8}, {2, 2, 2});
+    Tensor b = Tensor::new_({1, 2, 3, 4}, {2, 2});
+    expect_panic([&] { ops::matmul(a, b); }, "Matmul only supports 2D");
+    Tensor c = Tensor::new_({1, 2, 3, 4, 5, 6}, {2, 3});
+    expect_panic([&] { ops::matmul(c, c); }, "Matmul dimension mismatch");
+    expect_panic([&] { ops::conv2d(b, b, {1, 1}, {0, 0}); }, "Conv2d requires 4D tensors");
+    Tensor x = Tensor::zeros({1, 3, 8, 8});
+    Tensor w = Tensor::zeros({4, 2, 3, 3});
+    expect_panic([&] { ops::conv2d(x, w, {1, 1}, {0, 0}); }, "must match input channels");
+    expect_panic([&] { ops::max_pool2d(b, {2, 2}, {2, 2}, {0, 0}); }, "MaxPool2d requires 4D");
+  });
+}
+
+static void device_tests() {
+  run("test_matmul_forward_precision_under_1e6", [] {
+    Tensor a = Tensor::new_({1.0, 2.0, 3.0, 4.0}, {2, 2});
+    Tensor b = Tensor::new_({5.0, 6.0, 7.0, 8.0}, {2, 2});
+    Tensor c = a.matmul(b);
+    expect(c.device().kind == Device::Cpu, "CPU inputs must give a CPU result");
+    std::vector<float> got = c.data();
+    kat("matmul_2x2", got);
+    const float expected[4] = {19.0f, 22.0f, 43.0f, 50.0f};
+    for (int i = 0; i < 4; ++i)
+      expect(std::fabs(got[i] - expected[i]) < 1e-6f, "matmul value " + std::to_string(i));
+  });
+  run("test_conv2d_forward_precision_under_1e6", [] {
+    Tensor input = Tensor::new_({1, 2, 3, 4, 5, 6, 7, 8, 9}, {1, 1, 3, 3});
+    Tensor weight = Tensor::new_({1.0, 0.0, 0.0, -1.0}, {1, 1, 2, 2});
+    Tensor out = ops::conv2d(input, weight, {1, 1}, {0, 0});
+    std::vector<float> got = out.data();
+    kat("conv2d_3x3_k2", got);
+    for (int i = 0; i < 4; ++i) expect(std::fabs(got[i] + 4.0f) < 1e-6f, "conv value");
+  });
+  run("jit_demo_conv2d_relu_ones", [] {
+    jit::Graph g;
+    size_t in = g.add_input({1, 1, 4, 4});
+    size_t w = g.add_input({1, 1, 3, 3});
+    size_t c = g.add_node(jit::NodeType::Conv2d(in, w, {1, 1}, {0, 0}), {1, 1, 2, 2});
+    size_t r = g.add_node(jit::NodeType::Relu(c), {1, 1, 2, 2});
+    g.outputs.push_back(r);
+    jit::Optimizer::optimize(g);
+    auto res = jit::Executor::run(g, {Tensor::ones({1, 1, 4, 4}), Tensor::ones({1, 1, 3, 3})});
+    std::vector<float> got = res[0].data();
+    kat("jit_conv2d_relu_ones", got);
+    expect(res[0].shape() == std::vector<size_t>({1, 1, 2, 2}), "output shape");
+    expect(std::fabs(got[0] - 9.0f) < 1e-5f, "fused conv of ones should be 9");
+  });
+  run("jit_conv_bias_relu_matches_unfused", [] {
+    const Device d = Device::cuda(0);
+    Tensor x = Tensor::randn({2, 8, 9, 9}, 7, 1, 0.f, 1.f, d);
+    Tensor w = Tensor::randn({16, 8, 3, 3}, 7, 2, 0.f, 0.1f, d);
+    Tensor b = Tensor::randn({1, 16, 1, 1}, 7, 3, 0.f, 0.1f, d);
+    auto build = [&](bool fuse) {
+      jit::Graph g;
+      size_t in = g.add_input(x.shape());
+      size_t wi = g.add_weight(w);
+      size_t bi = g.add_weight(b);
+      size_t c = g.add_node(jit::NodeType::Conv2d(in, wi, {1, 1}, {1, 1}), {2, 16, 9, 9});
+      size_t a = g.add_node(jit::NodeType::Add(c, bi), {2, 16, 9, 9});
+      size_t r = g.add_node(jit::NodeType::Relu(a), {2, 16, 9, 9});
+      g.outputs.push_back(r);
+      if (fuse) jit::Optimizer::optimize(g);
+      return g;
+    };
+    jit::Graph gf = build(true), gu = build(false);
+    expect(gf.nodes.size() < gu.nodes.size(), "fusion did not fire");
+    std::vector<float> yf = jit::Executor::run(gf, {x})[0].to_cpu().data();
+    std::vector<float> yu = jit::Executor::run(gu, {x})[0].to_cpu().data();
+    double num = 0, den = 0;
+    for (size_t i = 0; i < yf.size(); ++i) {
+      num += (double)(yf[i] - yu[i]) * (yf[i] - yu[i]);
+      den += (double)yu[i] * yu[i];
+    }
+    expect(std::sqrt(num / den) < 1e-6, "fused and unfused results differ");
+  });
+  run("nn_linear_and_conv2d_modules", [] {
+    nn::Linear lin(6, 5, 11, Device::cuda(0));
+    Tensor x = Tensor::randn({4, 6}, 11, 9, 0.f, 1.f, Device::cuda(0));
+    Tensor y = lin.forward(x).to_cpu();
+    Tensor ref = x.matmul(lin.weight.t()).add(*lin.bias).to_cpu();
+    std::vector<float> a = y.data(), b = ref.data();
+    for (size_t i = 0; i < a.size(); ++i) expect(std::fabs(a[i] - b[i]) < 1e-5f, "linear");
+    nn::Conv2d conv(2, 3, {3, 3}, {1, 1}, {1, 1});
+    Tensor img = Tensor::ones({1, 2, 4, 4});
+    std::vector<float> o = conv.forward(img).data();
+    // interior: 2 channels * 9 taps * 0.01 = 0.18; corner sees 2 * 4 taps
+    expect(std::fabs(o[5] - 0.18f) < 1e-6f, "conv interior");
+    expect(std::fabs(o[0] - 0.08f) < 1e-6f, "conv corner");
+  });
+  run("device_data_panics", [] {
+    Tensor t = Tensor::ones({2, 2}, Device::cuda(0));
+    expect_panic([&] { t.data(); }, "only supported on CPU tensors");
+    expect_panic([&] { ops::add(t, Tensor::ones({2, 2})); }, "different devices");
+  });
+  run("broadcast_add_and_views", [] {
+    Tensor a = Tensor::new_({1, 2, 3, 4, 5, 6}, {2, 3});
+    Tensor b = Tensor::new_({10, 20, 30}, {3});
+    std::vector<float> s = a.add(b).data();
+    const float e[6] = {11, 22, 33, 14, 25, 36};
+    for (int i = 0; i < 6; ++i) expect(s[i] == e[i], "broadcast add");
+    std::vector<float> tc = a.to_cuda().t().contiguous().to_cpu().data();
+    const float te[6] = {1, 4, 2, 5, 3, 6};
+    for (int i = 0; i < 6; ++i) expect(tc[i] == te[i], "transpose contiguous on device");
+    std::vector<float> mm = a.t().matmul(a).data();  // 3x2 . 2x3 through a transposed view
+    expect(mm.size() == 9 && mm[0] == 17.0f && mm[8] == 45.0f, "transposed-view matmul");
+  });
+}
+
+int main(int argc, char** argv) {
+  const bool cpu_only = argc > 1 && std::strcmp(argv[1], "--cpu-only") == 0;
+  graph_tests();
+  if (!cpu_only) device_tests();
+  std::printf("%d failure(s)\n", g_fail);
+  return g_fail;
+}

@@ -21,9 +21,14 @@ def rb():
 
 
 def _header_functions():
-    src = open(os.path.join(ROOT, "include", "rustorch_b200.h")).read()
-    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
-    return sorted(set(re.findall(r"\b(rtb_[a-z0-9_]+)\s*\(", src)))
+    """Every rtb_* function declared in the C headers include/*.h."""
+    names = set()
+    inc = os.path.join(ROOT, "include")
+    for f in sorted(os.listdir(inc)):
+        if f.endswith(".h"):
+            src = re.sub(r"/\*.*?\*/", "", open(os.path.join(inc, f)).read(), flags=re.S)
+            names |= set(re.findall(r"\b(rtb_[a-z0-9_]+)\s*\(", src))
+    return sorted(names)
 
 
 def test_header_symbols_exported(rb):
