@@ -82,6 +82,13 @@ int rtb_set_timeout_ns(rtb_ctx* ctx, uint64_t ns);
  * buffer of `capacity` 64-bit words; a launch whose grid needs more is not
  * traced.  capacity = 0 turns tracing off. */
 int rtb_set_kernel_trace(rtb_ctx* ctx, uint64_t* buf, int64_t capacity);
+/* Failure-detection probe: launches a kernel whose single bounded wait can
+ * never be satisfied; after timeout_ns (1 us .. 1 s) the wait gives up,
+ * records device error code 8 and the kernel returns.  The next
+ * rtb_stream_synchronize / rtb_device_error then reports RTB_E_TIMEOUT, and
+ * the context stays usable.  Exercises the timeout path every kernel's waits
+ * use, without faulting or hanging the GPU. */
+int rtb_debug_wait_probe(rtb_ctx* ctx, uint64_t timeout_ns, void* stream);
 /* Read and clear the device error word (synchronises the context's device).
  * *code receives 0 or the device error code; returns RTB_E_TIMEOUT if set. */
 int rtb_device_error(rtb_ctx* ctx, int* code);

@@ -43,6 +43,7 @@ SIGNATURES = {
     "rtb_set_timeout_ns": (_i, [_p, _u64]),
     "rtb_device_error": (_i, [_p, ctypes.POINTER(_i)]),
     "rtb_set_kernel_trace": (_i, [_p, _p, _i64]),
+    "rtb_debug_wait_probe": (_i, [_p, _u64, _p]),
     "rtb_malloc": (_i, [_p, _pp, _sz, _p]),
     "rtb_free": (_i, [_p, _p, _p]),
     "rtb_host_alloc": (_i, [_p, _pp, _sz]),

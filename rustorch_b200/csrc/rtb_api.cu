@@ -26,6 +26,7 @@ int set_error(int status, const std::string& msg) {
 
 int cuda_status(cudaError_t e, const char* what) {
   const int st = (e == cudaErrorMemoryAllocation) ? RTB_E_OOM : RTB_E_CUDA;
+  (void)cudaGetLastError();  // consume it so a later launch check does not see it again
   return set_error(st, std::string(what) + ": " + cudaGetErrorString(e));
 }
 
@@ -254,6 +255,14 @@ int rtb_set_kernel_trace(rtb_ctx* ctx, uint64_t* buf, int64_t capacity) {
   ctx->trace = reinterpret_cast<unsigned long long*>(capacity ? buf : nullptr);
   ctx->trace_capacity = capacity;
   return RTB_OK;
+}
+
+int rtb_debug_wait_probe(rtb_ctx* ctx, uint64_t timeout_ns, void* stream) {
+  RTB_CHECK_CTX(ctx);
+  if (timeout_ns < 1000ull || timeout_ns > 1000000000ull)
+    return set_error(RTB_E_INVALID, "wait probe: timeout must be in [1 us, 1 s]");
+  DeviceGuard g(ctx->device);
+  return launch_wait_probe(ctx->d_err, timeout_ns, pick_stream(ctx, stream));
 }
 
 int rtb_device_error(rtb_ctx* ctx, int* code) {

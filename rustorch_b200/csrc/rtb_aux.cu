@@ -5,6 +5,7 @@
 #include <cfloat>
 
 #include "rtb_internal.h"
+#include "rtb_ptx.cuh"
 
 namespace rtb {
 
@@ -80,6 +81,22 @@ __global__ void nchw_to_nhwc_kernel(const float* __restrict__ x, int64_t C, int6
   }
 }
 
+// Small-channel variant (C <= 4, Cp == 4): one thread per pixel reads its C
+// channel values (coalesced across threads within each plane) and writes one
+// 16-byte NHWC pixel.
+__global__ void nchw_to_nhwc_c4_kernel(const float* __restrict__ x, int C, int HW, int64_t npix,
+                                       float4* __restrict__ y) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < npix;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t img = i / HW;
+    const int p = (int)(i - img * HW);
+    const float* xi = x + img * C * HW + p;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int c = 0; c < C; ++c) v[c] = __ldg(xi + (int64_t)c * HW);
+    y[i] = make_float4(v[0], v[1], v[2], v[3]);
+  }
+}
+
 // NHWC [N, HW, C] -> NCHW [N, C, HW].
 __global__ void nhwc_to_nchw_kernel(const float* __restrict__ x, int64_t C, int64_t HW,
                                     float* __restrict__ y) {
@@ -138,7 +155,37 @@ __global__ void max_pool_nchw_kernel(const float* __restrict__ x, float* __restr
   }
 }
 
-// NHWC variant, channel-contiguous (one thread per output element, C fastest).
+// NHWC variant: one thread per output pixel and 4 consecutive channels
+// (16-byte loads/stores, C % 4 == 0), 32-bit index math.
+__global__ void max_pool_nhwc4_kernel(const float4* __restrict__ x, float4* __restrict__ y,
+                                      int N, int C4, int H, int W, int Ho, int Wo, int kh, int kw,
+                                      int sh, int sw, int ph, int pw) {
+  const int total = N * Ho * Wo * C4;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int c = i % C4;
+    const int pix = i / C4;
+    const int ow = pix % Wo;
+    const int oh = (pix / Wo) % Ho;
+    const int n = pix / (Wo * Ho);
+    float4 m = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+    for (int r = 0; r < kh; ++r) {
+      const int hh = oh * sh - ph + r;
+      if (hh < 0 || hh >= H) continue;
+      for (int s = 0; s < kw; ++s) {
+        const int ww = ow * sw - pw + s;
+        if (ww < 0 || ww >= W) continue;
+        const float4 v = __ldg(x + ((size_t)(n * H + hh) * W + ww) * C4 + c);
+        if (v.x > m.x) m.x = v.x;
+        if (v.y > m.y) m.y = v.y;
+        if (v.z > m.z) m.z = v.z;
+        if (v.w > m.w) m.w = v.w;
+      }
+    }
+    y[i] = m;
+  }
+}
+
+// Generic NHWC fallback (any C), one thread per output element.
 __global__ void max_pool_nhwc_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t N,
                                      int64_t C, int64_t H, int64_t W, int64_t Ho, int64_t Wo,
                                      int kh, int kw, int sh, int sw, int ph, int pw) {
@@ -230,6 +277,25 @@ __global__ void bcast_kernel(const float* __restrict__ a, const float* __restric
   }
 }
 
+// Failure-detection probe: one thread waits, with the library's bounded wait,
+// on an mbarrier that nothing ever arrives on; the wait expires after
+// timeout_ns, records DEV_TIMEOUT_PROBE in the error word and the kernel
+// returns normally (no trap, no hang).
+__global__ void wait_probe_kernel(int* err, unsigned long long timeout_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0)
+    mbar_wait_bounded(&bar, 0, reinterpret_cast<volatile int*>(&abort_flag), err,
+                      DEV_TIMEOUT_PROBE, timeout_ns);
+  __syncthreads();
+}
+
 // parts [P, M, Nl] -> C [M, P*Nl].
 __global__ void unsplit_cols_kernel(const float* __restrict__ parts, float* __restrict__ C,
                                     int64_t P, int64_t M, int64_t Nl) {
@@ -248,12 +314,14 @@ int launch_pack_kmajor(const float* src, int64_t rows, int64_t k, int64_t rs, in
                        float* dst, int64_t kp, cudaStream_t s) {
   dim3 grid((unsigned)((kp + 31) / 32), (unsigned)((rows + 31) / 32));
   if (grid.y > 65535) return set_error(RTB_E_UNSUPPORTED, "pack: too many rows");
+  clear_stale_cuda_error();
   pack_kmajor_kernel<<<grid, dim3(32, 8), 0, s>>>(src, rows, k, rs, cs, dst, kp);
   return launch_check("pack_kmajor");
 }
 
 int launch_fill_rows(float* C, int64_t M, int64_t N, int64_t ldc, const float* bias, int relu,
                      cudaStream_t s) {
+  clear_stale_cuda_error();
   fill_rows_kernel<<<grid_for(M * N), kThreads, 0, s>>>(C, M, N, ldc, bias, relu);
   return launch_check("fill_rows");
 }
@@ -261,8 +329,15 @@ int launch_fill_rows(float* C, int64_t M, int64_t N, int64_t ldc, const float* b
 int launch_nchw_to_nhwc_padded(const float* x, int64_t N, int64_t C, int64_t H, int64_t W,
                                int64_t Cp, float* y, cudaStream_t s) {
   const int64_t HW = H * W;
+  if (Cp == 4 && HW < INT32_MAX && (reinterpret_cast<uintptr_t>(y) & 15u) == 0) {
+    clear_stale_cuda_error();
+    nchw_to_nhwc_c4_kernel<<<grid_for(N * HW), kThreads, 0, s>>>(x, (int)C, (int)HW, N * HW,
+                                                                 reinterpret_cast<float4*>(y));
+    return launch_check("nchw_to_nhwc (C<=4)");
+  }
   dim3 grid((unsigned)((HW + 31) / 32), (unsigned)((Cp + 31) / 32), (unsigned)N);
   if (N > 65535 || grid.y > 65535) return set_error(RTB_E_UNSUPPORTED, "nchw_to_nhwc: too large");
+  clear_stale_cuda_error();
   nchw_to_nhwc_kernel<<<grid, dim3(32, 8), 0, s>>>(x, C, HW, Cp, y);
   return launch_check("nchw_to_nhwc");
 }
@@ -271,12 +346,14 @@ int launch_nhwc_to_nchw(const float* x, float* y, int64_t N, int64_t C, int64_t 
                         cudaStream_t s) {
   dim3 grid((unsigned)((HW + 31) / 32), (unsigned)((C + 31) / 32), (unsigned)N);
   if (N > 65535 || grid.y > 65535) return set_error(RTB_E_UNSUPPORTED, "nhwc_to_nchw: too large");
+  clear_stale_cuda_error();
   nhwc_to_nchw_kernel<<<grid, dim3(32, 8), 0, s>>>(x, C, HW, y);
   return launch_check("nhwc_to_nchw");
 }
 
 int launch_prepack_weight(const float* w, int64_t Co, int64_t Ci, int64_t kh, int64_t kw,
                           int64_t Cp, float* wp, cudaStream_t s) {
+  clear_stale_cuda_error();
   prepack_weight_kernel<<<grid_for(Co * kh * kw * Cp), kThreads, 0, s>>>(w, Co, Ci, kh, kw, Cp,
                                                                           wp);
   return launch_check("prepack_weight");
@@ -287,10 +364,16 @@ int launch_max_pool2d(const float* x, float* y, int64_t N, int64_t C, int64_t H,
                       int layout, cudaStream_t s) {
   const int64_t Ho = (H + 2 * ph - kh) / sh + 1, Wo = (W + 2 * pw - kw) / sw + 1;
   const int64_t total = N * C * Ho * Wo;
+  clear_stale_cuda_error();
   if (layout == RTB_LAYOUT_NCHW)
     max_pool_nchw_kernel<<<grid_for(total), kThreads, 0, s>>>(x, y, N, C, H, W, Ho, Wo, (int)kh,
                                                              (int)kw, (int)sh, (int)sw, (int)ph,
                                                              (int)pw);
+  else if (C % 4 == 0 && total / 4 < INT32_MAX && N * H * W * C < INT32_MAX * 4LL &&
+           (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0)
+    max_pool_nhwc4_kernel<<<grid_for(total / 4), kThreads, 0, s>>>(
+        reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(y), (int)N, (int)(C / 4),
+        (int)H, (int)W, (int)Ho, (int)Wo, (int)kh, (int)kw, (int)sh, (int)sw, (int)ph, (int)pw);
   else
     max_pool_nhwc_kernel<<<grid_for(total), kThreads, 0, s>>>(x, y, N, C, H, W, Ho, Wo, (int)kh,
                                                              (int)kw, (int)sh, (int)sw, (int)ph,
@@ -302,20 +385,24 @@ int launch_global_avg_pool(const float* x, float* y, int64_t N, int64_t C, int64
                            cudaStream_t s) {
   if (layout == RTB_LAYOUT_NCHW) {
     const int64_t threads = N * C * 32;
+    clear_stale_cuda_error();
     avg_pool_nchw_kernel<<<(unsigned)((threads + kThreads - 1) / kThreads), kThreads, 0, s>>>(
         x, y, N * C, HW);
   } else {
+    clear_stale_cuda_error();
     avg_pool_nhwc_kernel<<<grid_for(N * C), kThreads, 0, s>>>(x, y, N, C, HW);
   }
   return launch_check("global_avg_pool");
 }
 
 int launch_add(const float* a, const float* b, float* y, int64_t n, cudaStream_t s) {
+  clear_stale_cuda_error();
   add_kernel<<<grid_for(n), kThreads, 0, s>>>(a, b, y, n);
   return launch_check("add");
 }
 
 int launch_relu(const float* x, float* y, int64_t n, cudaStream_t s) {
+  clear_stale_cuda_error();
   relu_kernel<<<grid_for(n), kThreads, 0, s>>>(x, y, n);
   return launch_check("relu");
 }
@@ -334,12 +421,20 @@ int launch_broadcast(int op, int ndim, const int64_t* shape, const float* a,
     n *= shape[k];
   }
   if (n == 0) return RTB_OK;
+  clear_stale_cuda_error();
   bcast_kernel<<<grid_for(n), kThreads, 0, s>>>(a, b, y, n, d, op);
   return launch_check("broadcast elementwise");
 }
 
+int launch_wait_probe(int* err, uint64_t timeout_ns, cudaStream_t s) {
+  clear_stale_cuda_error();
+  wait_probe_kernel<<<1, 32, 0, s>>>(err, (unsigned long long)timeout_ns);
+  return launch_check("wait probe");
+}
+
 int launch_unsplit_cols(const float* parts, float* C, int64_t P, int64_t M, int64_t Nl,
                         cudaStream_t s) {
+  clear_stale_cuda_error();
   unsplit_cols_kernel<<<grid_for(P * M * Nl), kThreads, 0, s>>>(parts, C, P, M, Nl);
   return launch_check("unsplit_cols");
 }

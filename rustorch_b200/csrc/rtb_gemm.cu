@@ -23,6 +23,7 @@ int launch_variant(rtb_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB,
   if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemm smem)");
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
+  clear_stale_cuda_error();
   kern<<<grid, Roles::kThreads, Cfg::kSmemBytes, stream>>>(tmA, tmB, tmC, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_status(e, "gemm kernel launch");
@@ -66,6 +67,7 @@ int pick_bn(rtb_ctx* ctx, const GemmDesc& d) {
   const int* c = d.split3 ? cands_split : cands_fast;
   const int nc = d.split3 ? 2 : 3;
   for (int i = 0; i < nc; ++i) {
+    if (c[i] > 64 && d.N <= c[i] / 2) continue;  // half the tile (or more) would be padding
     const int64_t tiles = tm * ((d.N + c[i] - 1) / c[i]);
     if (tiles >= ctx->sm_count) return c[i];
   }

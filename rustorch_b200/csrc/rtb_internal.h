@@ -24,6 +24,11 @@ struct rtb_ctx {
 
 namespace rtb {
 
+// Clears the calling thread's CUDA "last error" (a non-sticky error left by an
+// earlier, already reported call, possibly another library's) so the check
+// after our own kernel launch sees only that launch's outcome.
+inline void clear_stale_cuda_error() { (void)cudaGetLastError(); }
+
 // Records `msg` as this thread's last error and returns `status`.
 int set_error(int status, const std::string& msg);
 int cuda_status(cudaError_t e, const char* what);
@@ -112,6 +117,7 @@ int launch_relu(const float* x, float* y, int64_t n, cudaStream_t s);
 int launch_broadcast(int op, int ndim, const int64_t* shape, const float* a,
                      const int64_t* sa, const float* b, const int64_t* sb, float* y,
                      cudaStream_t s);
+int launch_wait_probe(int* err, uint64_t timeout_ns, cudaStream_t s);
 int launch_unsplit_cols(const float* parts, float* C, int64_t P, int64_t M, int64_t Nl,
                         cudaStream_t s);
 int launch_nhwc_to_nchw(const float* x, float* y, int64_t N, int64_t C, int64_t HW,

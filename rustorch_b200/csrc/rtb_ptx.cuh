@@ -21,6 +21,7 @@ enum DevErr : int {
   DEV_TIMEOUT_TMEM_EMPTY = 5,// MMA issuer waited too long for a drained accumulator
   DEV_TIMEOUT_LOADED = 6,    // converter waited too long for a loaded stage
   DEV_BAD_CONFIG = 7,        // kernel launched with an inconsistent configuration
+  DEV_TIMEOUT_PROBE = 8,     // rtb_debug_wait_probe: the deliberately unsatisfied wait expired
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
