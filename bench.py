@@ -36,6 +36,14 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 L2_BYTES = 126 * 1024 * 1024
+
+# DRAM bytes (read + write) per launch of each workload's dominant kernel, from
+# one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum); the capture and
+# its command are summarised in the named profiles/ file.
+TRAFFIC = {
+    "conv": (13.51e6, "profiles/conv2d_bias_relu_r50s2_3x3.md"),
+    "gemm8192": (3.458e9, "profiles/sgemm_8192_3xtf32.md"),
+}
 PRECISION = [0]  # rtb precision enum used by every workload call (0 = 3xTF32, 1 = TF32)
 MMAS_PER_MAC = [3]
 
@@ -651,7 +659,9 @@ def run_ours(args):
             "config": dict(wl.config, parallelism=par),
             "roofline": {"bound": "tensor", "achieved": round(k_tflops, 3),
                          "peak": round(roof_peak, 3), "unit": "TFLOP/s",
-                         "frac": round(k_tflops / roof_peak, 4), "traffic": None,
+                         "frac": round(k_tflops / roof_peak, 4),
+                         "traffic": TRAFFIC.get(args.workload, (None,))[0],
+                         "traffic_source": TRAFFIC.get(args.workload, (None, None))[1],
                          "peak_basis": f"{peaks['basis']} bf16 {peaks['bf16_tflops']} TFLOP/s "
                                        f"/ 2 (TF32 rate) / {MMAS_PER_MAC[0]} (MMAs per MAC)",
                          "tensor_pipe_frac": round(MMAS_PER_MAC[0] * k_tflops / tf32_peak, 4),
