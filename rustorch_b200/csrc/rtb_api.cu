@@ -552,7 +552,7 @@ static int conv_core(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, 
                      int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw,
                      int64_t Ho, int64_t Wo, const float* x_nhwc, const float* wp,
                      const float* bias, const float* residual, int relu, float* y, int y_layout,
-                     int split3, cudaStream_t s) {
+                     int split3, cudaStream_t s, bool allow_workspace = true) {
   const int64_t Cp = round_up(Ci, 4);
   const int64_t M = N * Ho * Wo;
   if (M == 0) return RTB_OK;
@@ -579,14 +579,16 @@ static int conv_core(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, 
   d.H = (int)H; d.W = (int)W; d.Cp = (int)Cp; d.Ho = (int)Ho; d.Wo = (int)Wo;
   d.R = (int)kh; d.S = (int)kw; d.sh = (int)sh; d.sw = (int)sw; d.ph = (int)ph; d.pw = (int)pw;
   d.split3 = split3;
+  d.allow_workspace = allow_workspace ? 1 : 0;
   return gemm_run(ctx, d, s);
 }
 
-int rtb_conv2d_fwd_packed(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, int64_t Co,
-                          int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw,
-                          const float* x_nhwc_padded, const float* w_packed, const float* bias,
-                          const float* residual, int act, float* y, int y_layout, int precision,
-                          void* stream) {
+static int conv_packed_impl(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W,
+                            int64_t Co, int64_t kh, int64_t kw, int64_t sh, int64_t sw,
+                            int64_t ph, int64_t pw, const float* x_nhwc_padded,
+                            const float* w_packed, const float* bias, const float* residual,
+                            int act, float* y, int y_layout, int precision, void* stream,
+                            bool allow_workspace) {
   RTB_CHECK_CTX(ctx);
   int64_t Ho, Wo;
   int st = conv_check(N, Ci, H, W, Co, kh, kw, sh, sw, ph, pw, &Ho, &Wo);
@@ -602,7 +604,32 @@ int rtb_conv2d_fwd_packed(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_
   if ((st = resolve_precision(ctx, precision, &split3))) return st;
   DeviceGuard g(ctx->device);
   return conv_core(ctx, N, Ci, H, W, Co, kh, kw, sh, sw, ph, pw, Ho, Wo, x_nhwc_padded, w_packed,
-                   bias, residual, relu, y, y_layout, split3, pick_stream(ctx, stream));
+                   bias, residual, relu, y, y_layout, split3, pick_stream(ctx, stream),
+                   allow_workspace);
+}
+
+}  // extern "C"
+
+namespace rtb {
+int conv2d_fwd_packed_noalloc(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W,
+                              int64_t Co, int64_t kh, int64_t kw, int64_t sh, int64_t sw,
+                              int64_t ph, int64_t pw, const float* x_nhwc_padded,
+                              const float* w_packed, const float* bias, const float* residual,
+                              int act, float* y, int y_layout, int precision, void* stream) {
+  return conv_packed_impl(ctx, N, Ci, H, W, Co, kh, kw, sh, sw, ph, pw, x_nhwc_padded, w_packed,
+                          bias, residual, act, y, y_layout, precision, stream, false);
+}
+}  // namespace rtb
+
+extern "C" {
+
+int rtb_conv2d_fwd_packed(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, int64_t Co,
+                          int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw,
+                          const float* x_nhwc_padded, const float* w_packed, const float* bias,
+                          const float* residual, int act, float* y, int y_layout, int precision,
+                          void* stream) {
+  return conv_packed_impl(ctx, N, Ci, H, W, Co, kh, kw, sh, sw, ph, pw, x_nhwc_padded, w_packed,
+                          bias, residual, act, y, y_layout, precision, stream, true);
 }
 
 int rtb_conv2d_fwd(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, int64_t Co,

@@ -21,8 +21,7 @@ int launch_variant(rtb_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB,
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
   if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemm smem)");
-  const int tiles = p.tiles_m * p.tiles_n;
-  const int grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
+  const int grid = p.num_units < ctx->sm_count ? p.num_units : ctx->sm_count;
   clear_stale_cuda_error();
   kern<<<grid, Roles::kThreads, Cfg::kSmemBytes, stream>>>(tmA, tmB, tmC, p);
   e = cudaGetLastError();
@@ -155,18 +154,60 @@ int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
   p.pw = d.pw;
   p.err = ctx->d_err;
   p.timeout_ns = ctx->timeout_ns;
+
+  // Tail balancing: when the last wave of tiles would leave at least half of
+  // the SMs idle, its tiles are cut along K into split_k pieces that run on
+  // the otherwise idle SMs (e.g. 196 tiles on 148 SMs: 148 whole tiles, then
+  // 48 tiles x 3 pieces).  The pieces' partial tiles go through a stream-
+  // ordered workspace; RTB_TAIL_SPLIT=0 turns this off.
+  const int64_t tiles = (int64_t)p.tiles_m * p.tiles_n;
+  if (tiles > INT32_MAX / 8) return set_error(RTB_E_UNSUPPORTED, "gemm_run: too many tiles");
+  p.full_units = (int)tiles;
+  p.split_k = 1;
+  p.num_units = (int)tiles;
+  p.ws = nullptr;
+  p.ws_cnt = nullptr;
+  void* split_ws = nullptr;
+  static const int tail_env = env_int("RTB_TAIL_SPLIT", 1);
+  if (tail_env && d.allow_workspace) {
+    const int64_t G = ctx->sm_count;
+    const int64_t rem = tiles % G;
+    if (rem > 0 && rem * 2 <= G) {
+      int sk = (int)(G / rem);
+      if (sk > 8) sk = 8;
+      if (sk > p.num_kb / 2) sk = p.num_kb / 2;  // every piece keeps >= 2 k-blocks
+      if (sk >= 2) {
+        const size_t part_bytes = (size_t)rem * sk * bn * kBM * sizeof(float);
+        const size_t cnt_off = (part_bytes + 255) & ~size_t(255);
+        st = ws_alloc(ctx, &split_ws, cnt_off + (size_t)rem * sizeof(int), stream);
+        if (st != RTB_OK) return st;
+        cudaError_t e = cudaMemsetAsync(static_cast<char*>(split_ws) + cnt_off, 0,
+                                        (size_t)rem * sizeof(int), stream);
+        if (e != cudaSuccess) {
+          ws_free(split_ws, stream);
+          return cuda_status(e, "split counters memset");
+        }
+        p.full_units = (int)(tiles - rem);
+        p.split_k = sk;
+        p.num_units = (int)(tiles - rem + rem * sk);
+        p.ws = static_cast<float*>(split_ws);
+        p.ws_cnt = reinterpret_cast<int*>(static_cast<char*>(split_ws) + cnt_off);
+      }
+    }
+  }
   {
-    const int64_t tiles = (int64_t)p.tiles_m * p.tiles_n;
-    const int64_t grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
+    const int64_t grid = p.num_units < ctx->sm_count ? p.num_units : ctx->sm_count;
     p.trace = (ctx->trace && ctx->trace_capacity >= grid * kTraceSlots) ? ctx->trace : nullptr;
   }
 
   switch (bn) {
-    case 64: return launch_bn<64>(ctx, tmA, tmB, tmC, p, d, stream);
-    case 128: return launch_bn<128>(ctx, tmA, tmB, tmC, p, d, stream);
-    case 256: return launch_bn<256>(ctx, tmA, tmB, tmC, p, d, stream);
-    default: return set_error(RTB_E_INVALID, "gemm_run: bad tile width");
+    case 64: st = launch_bn<64>(ctx, tmA, tmB, tmC, p, d, stream); break;
+    case 128: st = launch_bn<128>(ctx, tmA, tmB, tmC, p, d, stream); break;
+    case 256: st = launch_bn<256>(ctx, tmA, tmB, tmC, p, d, stream); break;
+    default: st = set_error(RTB_E_INVALID, "gemm_run: bad tile width");
   }
+  ws_free(split_ws, stream);
+  return st;
 }
 
 }  // namespace rtb

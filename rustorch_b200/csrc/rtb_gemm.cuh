@@ -79,7 +79,46 @@ struct GemmParams {
   unsigned long long timeout_ns;
   // optional timeline trace: per CTA kTraceSlots globaltimer stamps (null = off)
   unsigned long long* trace;
+  // Work units (tail balancing).  Units [0, full_units) are whole tiles
+  // 0..full_units-1; the remaining tiles_m*tiles_n - full_units "tail" tiles
+  // are each cut into split_k pieces along K (consecutive k-block ranges),
+  // one unit per piece.  A piece leaves its fp32 partial tile in ws; the last
+  // piece of a tile to arrive (ws_cnt) sums the pieces in piece order and runs
+  // the epilogue, so the result does not depend on arrival order.
+  int full_units;
+  int split_k;           // 1 = no split
+  int num_units;
+  float* ws;             // [tail tile][piece][BN/32][8][128] float4
+  int* ws_cnt;           // [tail tile] arrival counters, zero at launch
 };
+
+struct WorkUnit {
+  int tile;
+  int kb0, kb1;  // k-block range [kb0, kb1)
+  int piece;     // -1 = whole tile
+  int slot;      // tail tile index (pieces only)
+};
+
+__device__ __forceinline__ WorkUnit work_unit(const GemmParams& p, int w) {
+  WorkUnit u;
+  if (w < p.full_units) {
+    u.tile = w;
+    u.kb0 = 0;
+    u.kb1 = p.num_kb;
+    u.piece = -1;
+    u.slot = -1;
+  } else {
+    const int j = w - p.full_units;
+    const int q = j / p.split_k;
+    const int piece = j - q * p.split_k;
+    u.tile = p.full_units + q;
+    u.kb0 = (int)((int64_t)piece * p.num_kb / p.split_k);
+    u.kb1 = (int)((int64_t)(piece + 1) * p.num_kb / p.split_k);
+    u.piece = piece;
+    u.slot = q;
+  }
+  return u;
+}
 
 // Trace slot layout per CTA (first kTraceTiles tiles of the CTA):
 //   0 start, 1 end, then per tile j at 2+6j: producer first issue, MMA first
@@ -349,10 +388,11 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
   uint64_t* tempty_bar = tfull_bar + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* fix_flag = abort_flag + 1;  // epilogue: this CTA sums a split tile
+  volatile int* epi_vote = abort_flag + 2;  // epilogue: per-warp wait outcome (4 ints)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int num_tiles = p.tiles_m * p.tiles_n;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -389,9 +429,10 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
       uint32_t ph = 0;
       const uint32_t tx = (GATHER ? 0 : kABytes) + kBBytes;
       const int HoWo = p.Ho * p.Wo;
-      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+      for (int w = blockIdx.x; w < p.num_units && !*abort_flag; w += gridDim.x) {
+        const WorkUnit u = work_unit(p, w);
         int tm, tn;
-        tile_coords(t, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
+        tile_coords(u.tile, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
         // TMA im2col: input position of the tile's first output pixel.
         int a_w = 0, a_h = 0, a_n = 0;
         if (IM2COL) {
@@ -402,17 +443,17 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
           a_h = oh * p.sh - p.ph;
           a_w = (rem - oh * p.Wo) * p.sw - p.pw;
         }
-        const int tj = (t - (int)blockIdx.x) / (int)gridDim.x;
-        for (int kb = 0; kb < p.num_kb; ++kb) {
+        const int tj = (w - (int)blockIdx.x) / (int)gridDim.x;
+        for (int kb = u.kb0; kb < u.kb1; ++kb) {
           if (!mbar_wait_bounded(&empty_bar[s], ph ^ 1, abort_flag, p.err, DEV_TIMEOUT_EMPTY,
                                  p.timeout_ns))
             break;
-          if (kb == 0 && tj < kTraceTiles) trace_stamp(p, 2 + 6 * tj);
+          if (kb == u.kb0 && tj < kTraceTiles) trace_stamp(p, 2 + 6 * tj);
           mbar_arrive_expect_tx(&full_bar[s], tx);
           // Warm L2 for a k-block `prefetch_kb` ahead (hides DRAM latency beyond
           // what the shared-memory ring can cover).
           const int kp = kb + p.prefetch_kb;
-          if (p.prefetch_kb > 0 && kp < p.num_kb) {
+          if (p.prefetch_kb > 0 && kp < u.kb1) {
             if (A_MODE == 0) {
               tma_prefetch_2d(&tmA, kp * kBK, tm * kBM);
               if (B_MN == 0) tma_prefetch_2d(&tmB, kp * kBK, tn * BN);
@@ -453,8 +494,10 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
       uint32_t ph = 0;
       int g = 0;  // accumulation-unit counter (selects the TMEM partial buffer)
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok && !*abort_flag; t += gridDim.x) {
-        for (int kb0 = 0; kb0 < p.num_kb && ok; kb0 += p.kb_per_acc, ++g) {
+      for (int w = blockIdx.x; w < p.num_units && ok && !*abort_flag; w += gridDim.x) {
+        const WorkUnit u = work_unit(p, w);
+        const int tj = (w - (int)blockIdx.x) / (int)gridDim.x;
+        for (int kb0 = u.kb0; kb0 < u.kb1 && ok; kb0 += p.kb_per_acc, ++g) {
           const int b = g & 1;
           const uint32_t use = (uint32_t)(g >> 1);
           if (!mbar_wait_bounded(&tempty_bar[b], (use & 1) ^ 1, abort_flag, p.err,
@@ -464,7 +507,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
           }
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + (uint32_t)(b * BN);
-          const int kend = (kb0 + p.kb_per_acc) < p.num_kb ? (kb0 + p.kb_per_acc) : p.num_kb;
+          const int kend = (kb0 + p.kb_per_acc) < u.kb1 ? (kb0 + p.kb_per_acc) : u.kb1;
           for (int kb = kb0; kb < kend; ++kb) {
             uint64_t* ready = SPLIT ? &conv_bar[s] : &full_bar[s];
             if (!mbar_wait_bounded(ready, ph, abort_flag, p.err,
@@ -472,10 +515,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
               ok = false;
               break;
             }
-            {
-              const int tj = (t - (int)blockIdx.x) / (int)gridDim.x;
-              if (kb == 0 && tj < kTraceTiles) trace_stamp(p, 3 + 6 * tj);
-            }
+            if (kb == u.kb0 && tj < kTraceTiles) trace_stamp(p, 3 + 6 * tj);
             tc_fence_after();
             // cp.async-gathered A (TF32 mode has no converter pass): make the
             // generic-proxy writes visible to the tensor core's async proxy.
@@ -512,10 +552,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
           }
           if (!ok) break;
           umma_commit(&tfull_bar[b]);
-          {
-            const int tj = (t - (int)blockIdx.x) / (int)gridDim.x;
-            if (kb0 + p.kb_per_acc >= p.num_kb && tj < kTraceTiles) trace_stamp(p, 4 + 6 * tj);
-          }
+          if (kb0 + p.kb_per_acc >= u.kb1 && tj < kTraceTiles) trace_stamp(p, 4 + 6 * tj);
         }
       }
     }
@@ -525,36 +562,63 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
     const int row = lane_base + lane;
     const uint32_t t_lane = tmem_base + ((uint32_t)lane_base << 16);
     const uint32_t t_run = t_lane + (uint32_t)(2 * BN);  // fp32 running sum (3xTF32)
-    const int units = (p.num_kb + p.kb_per_acc - 1) / p.kb_per_acc;
     const int et = threadIdx.x - Roles::kWarpEpi * 32;  // 0..127 within the epilogue group
     int chunk = 0;  // staging-buffer sequence number
     int g = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+    // One finished 128 x 32 chunk (this thread's row, columns n0..n0+31) to C.
+    auto emit = [&](int tm, int n0, int m, const uint32_t (&r)[32]) {
+      if (p.c_tma) {
+        epilogue_stage_rowmajor(p, sOut + (chunk & 1) * kOutChunkBytes, row, n0, m, r);
+        fence_proxy_async_smem();
+        named_bar_sync(1, 128);
+        if (et == 0) {
+          tma_store_2d(&tmC, sOut + (chunk & 1) * kOutChunkBytes, n0, tm * kBM);
+          bulk_commit_group();
+          bulk_wait_group_read<1>();  // the buffer used next is free again
+        }
+        named_bar_sync(1, 128);
+        ++chunk;
+      } else if (p.out_mode == 1) {
+        float* buf = reinterpret_cast<float*>(sOut + (chunk & 1) * kOutChunkBytes);
+        epilogue_nchw_chunk(p, buf, row, et, tm * kBM, n0, r);
+        ++chunk;
+      } else {
+        epilogue_store32(p, m, n0, r);
+      }
+    };
+    for (int w = blockIdx.x; w < p.num_units && ok; w += gridDim.x) {
+      const WorkUnit u = work_unit(p, w);
+      const int tj = (w - (int)blockIdx.x) / (int)gridDim.x;
       int tm, tn;
-      tile_coords(t, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
+      tile_coords(u.tile, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
       const int m = tm * kBM + row;
-      for (int u = 0; u < units; ++u, ++g) {
+      const bool piece = u.piece >= 0;
+      // this piece's partial tile in the workspace, as float4 [BN/32][8][128]
+      float4* wsp = piece ? reinterpret_cast<float4*>(p.ws) +
+                                ((size_t)u.slot * p.split_k + u.piece) * (size_t)(BN * kBM / 4)
+                          : nullptr;
+      const int units = (u.kb1 - u.kb0 + p.kb_per_acc - 1) / p.kb_per_acc;
+      for (int a = 0; a < units; ++a, ++g) {
         const int b = g & 1;
         const uint32_t use = (uint32_t)(g >> 1);
-        // tcgen05.ld is .sync.aligned: the whole warp must agree on the outcome.
-        int got = 0;
+        // tcgen05.ld is .sync.aligned and the staged stores meet at named
+        // barriers: all four warps take the same branch (vote through smem).
         if (lane == 0)
-          got = mbar_wait_bounded(&tfull_bar[b], use & 1, abort_flag, p.err,
-                                  DEV_TIMEOUT_TMEM_FULL, p.timeout_ns);
-        got = __shfl_sync(0xffffffffu, got, 0);
+          epi_vote[warp & 3] = mbar_wait_bounded(&tfull_bar[b], use & 1, abort_flag, p.err,
+                                                 DEV_TIMEOUT_TMEM_FULL, p.timeout_ns);
+        named_bar_sync(2, 128);
+        const bool got = epi_vote[0] && epi_vote[1] && epi_vote[2] && epi_vote[3];
+        named_bar_sync(2, 128);
         if (!got) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const bool last = (u + 1 == units);
-        if (warp == Roles::kWarpEpi && lane == 0) {
-          const int tj = (t - (int)blockIdx.x) / (int)gridDim.x;
-          if (tj < kTraceTiles) {
-            if (u == 0) trace_stamp(p, 5 + 6 * tj);
-            if (last) trace_stamp(p, 6 + 6 * tj);
-          }
+        const bool last = (a + 1 == units);
+        if (warp == Roles::kWarpEpi && lane == 0 && tj < kTraceTiles) {
+          if (a == 0) trace_stamp(p, 5 + 6 * tj);
+          if (last) trace_stamp(p, 6 + 6 * tj);
         }
         const uint32_t t_part = t_lane + (uint32_t)(b * BN);
 #pragma unroll 1
@@ -562,7 +626,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
           uint32_t r[32];
           tmem_ld_32x32b_x32(t_part + (uint32_t)c, r);
           tmem_ld_wait();
-          if (SPLIT && u > 0) {
+          if (SPLIT && a > 0) {
             uint32_t q[32];
             tmem_ld_32x32b_x32(t_run + (uint32_t)c, q);
             tmem_ld_wait();
@@ -576,32 +640,59 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
           }
           if (SPLIT && !last) {
             tmem_st_32x32b_x32(t_run + (uint32_t)c, r);
-          } else if (p.c_tma) {
-            epilogue_stage_rowmajor(p, sOut + (chunk & 1) * kOutChunkBytes, row, tn * BN + c, m, r);
-            fence_proxy_async_smem();
-            named_bar_sync(1, 128);
-            if (et == 0) {
-              tma_store_2d(&tmC, sOut + (chunk & 1) * kOutChunkBytes, tn * BN + c, tm * kBM);
-              bulk_commit_group();
-              bulk_wait_group_read<1>();  // the buffer used next is free again
-            }
-            named_bar_sync(1, 128);
-            ++chunk;
-          } else if (p.out_mode == 1) {
-            float* buf = reinterpret_cast<float*>(sOut + (chunk & 1) * kOutChunkBytes);
-            epilogue_nchw_chunk(p, buf, row, et, tm * kBM, tn * BN + c, r);
-            ++chunk;
+          } else if (piece) {
+            float4* dst = wsp + (size_t)(c / 32) * 8 * kBM + row;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              __stcg(dst + j * kBM, make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                                __uint_as_float(r[4 * j + 2]),
+                                                __uint_as_float(r[4 * j + 3])));
           } else {
-            epilogue_store32(p, m, tn * BN + c, r);
+            emit(tm, tn * BN + c, m, r);
           }
         }
         if (SPLIT && !last) tmem_st_wait();
       }
-      {
-        const int tj = (t - (int)blockIdx.x) / (int)gridDim.x;
-        if (ok && warp == Roles::kWarpEpi && lane == 0 && tj < kTraceTiles)
-          trace_stamp(p, 7 + 6 * tj);
+      if (ok && piece) {
+        // Publish this piece, count arrivals; the last piece sums all of them.
+        __threadfence();
+        named_bar_sync(1, 128);
+        if (et == 0) {
+          const int old = atomicAdd(p.ws_cnt + u.slot, 1);
+          *fix_flag = (old == p.split_k - 1);
+        }
+        named_bar_sync(1, 128);
+        if (*fix_flag) {
+          __threadfence();
+          const float4* src0 = reinterpret_cast<const float4*>(p.ws) +
+                               (size_t)u.slot * p.split_k * (size_t)(BN * kBM / 4);
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 32) {
+            float v[32];
+            const float4* s0 = src0 + (size_t)(c / 32) * 8 * kBM + row;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float4 q = __ldcg(s0 + j * kBM);
+              v[4 * j] = q.x; v[4 * j + 1] = q.y; v[4 * j + 2] = q.z; v[4 * j + 3] = q.w;
+            }
+#pragma unroll 1
+            for (int pc = 1; pc < p.split_k; ++pc) {
+              const float4* sp = s0 + (size_t)pc * (BN * kBM / 4);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float4 q = __ldcg(sp + j * kBM);
+                v[4 * j] += q.x; v[4 * j + 1] += q.y; v[4 * j + 2] += q.z; v[4 * j + 3] += q.w;
+              }
+            }
+            uint32_t r[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(v[j]);
+            emit(tm, tn * BN + c, m, r);
+          }
+        }
       }
+      if (ok && warp == Roles::kWarpEpi && lane == 0 && tj < kTraceTiles)
+        trace_stamp(p, 7 + 6 * tj);
     }
     if (p.c_tma && et == 0) bulk_wait_group<0>();  // all output stores complete
   } else if (SPLIT && warp >= Roles::kWarpConv && warp < Roles::kWarpConv + 4) {
@@ -609,9 +700,10 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
     const int ct = threadIdx.x - Roles::kWarpConv * 32;  // 0..127
     int s = 0;
     uint32_t ph = 0;
-    for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+    for (int w = blockIdx.x; w < p.num_units && !*abort_flag; w += gridDim.x) {
+      const WorkUnit u = work_unit(p, w);
       bool ok = true;
-      for (int kb = 0; kb < p.num_kb; ++kb) {
+      for (int kb = u.kb0; kb < u.kb1; ++kb) {
         if (!mbar_wait_bounded(&full_bar[s], ph, abort_flag, p.err, DEV_TIMEOUT_LOADED,
                                p.timeout_ns)) {
           ok = false;
@@ -661,9 +753,10 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
     int s = 0;
     uint32_t ph = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < num_tiles && ok && !*abort_flag; t += gridDim.x) {
+    for (int w = blockIdx.x; w < p.num_units && ok && !*abort_flag; w += gridDim.x) {
+      const WorkUnit u = work_unit(p, w);
       int tm, tn;
-      tile_coords(t, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
+      tile_coords(u.tile, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
       const int m = tm * kBM + r;
       const bool mvalid = m < p.M;
       const int img = mvalid ? m / HoWo : 0;
@@ -675,8 +768,9 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
       const float* ximg = p.x + (int64_t)img * p.H * p.W * p.Cp;
       // (tap, channel) of the first 16-byte chunk of the k-block, advanced
       // incrementally (Cp % 4 == 0, so a chunk never straddles a tap).
-      int tap = 0, ci = 0;
-      for (int kb = 0; kb < p.num_kb; ++kb) {
+      int tap = (u.kb0 * kBK) / p.Cp;
+      int ci = u.kb0 * kBK - tap * p.Cp;
+      for (int kb = u.kb0; kb < u.kb1; ++kb) {
         if (!mbar_wait_bounded(&empty_bar[s], ph ^ 1, abort_flag, p.err, DEV_TIMEOUT_EMPTY,
                                p.timeout_ns)) {
           ok = false;

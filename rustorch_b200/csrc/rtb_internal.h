@@ -93,6 +93,7 @@ struct GemmDesc {
   int H = 0, W = 0, Cp = 0, Ho = 0, Wo = 0, R = 0, S = 0, sh = 1, sw = 1, ph = 0, pw = 0;
   int split3 = 1;     // 3xTF32 (1) or TF32 (0)
   int bn = 0;         // 0 = heuristic
+  int allow_workspace = 1;  // 0: never allocate (tail balancing off)
 };
 
 // Validated launch of the tcgen05 engine (A/B already TMA-compatible).
@@ -122,6 +123,13 @@ int launch_unsplit_cols(const float* parts, float* C, int64_t P, int64_t M, int6
                         cudaStream_t s);
 int launch_nhwc_to_nchw(const float* x, float* y, int64_t N, int64_t C, int64_t HW,
                         cudaStream_t s);
+
+// rtb_conv2d_fwd_packed without any device allocation (rtb_noalloc.cu).
+int conv2d_fwd_packed_noalloc(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W,
+                              int64_t Co, int64_t kh, int64_t kw, int64_t sh, int64_t sw,
+                              int64_t ph, int64_t pw, const float* x_nhwc_padded,
+                              const float* w_packed, const float* bias, const float* residual,
+                              int act, float* y, int y_layout, int precision, void* stream);
 
 // Stream-ordered workspace.
 int ws_alloc(rtb_ctx* ctx, void** p, size_t bytes, cudaStream_t s);

@@ -101,9 +101,9 @@ int rtb_conv2d_fwd_noalloc(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64
   }
   st = rtb::launch_prepack_weight(w, Co, Ci, kh, kw, Cp, wp, s);
   if (st) return st;
-  return rtb_conv2d_fwd_packed(ctx, N, Ci, H, W, Co, kh, kw, sh, sw, ph, pw,
-                               x_direct ? x : xs, wp, bias, residual, act, y, y_layout, precision,
-                               stream);
+  return rtb::conv2d_fwd_packed_noalloc(ctx, N, Ci, H, W, Co, kh, kw, sh, sw, ph, pw,
+                                        x_direct ? x : xs, wp, bias, residual, act, y, y_layout,
+                                        precision, stream);
 }
 
 }  // extern "C"
