@@ -45,7 +45,7 @@ constexpr int kBM = 128;
 constexpr int kBK = 32;                      // fp32 elements per k-block (128 B)
 constexpr int kABytes = kBM * kBK * 4;       // 16 KB
 constexpr int kSmemLimit = 232448;           // 227 KB dynamic shared memory per CTA
-constexpr int kSmemReserve = 2048;           // barriers + alignment slack
+constexpr int kSmemReserve = 3072;           // bias staging (1 KB) + barriers + alignment slack
 constexpr int kOutChunkBytes = kBM * 32 * 4;  // one 128 x 32 fp32 output chunk (16 KB)
 constexpr int kOutBytes = 2 * kOutChunkBytes; // double-buffered epilogue staging
 
@@ -133,15 +133,22 @@ __device__ __forceinline__ void trace_stamp(const GemmParams& p, int slot) {
 template <int BN, bool SPLIT>
 struct GemmCfg {
   static constexpr int kBBytes = BN * kBK * 4;
-  static constexpr int kStageBytes = (kABytes + kBBytes) * (SPLIT ? 2 : 1);
+  // Shared-memory stage: A + B tiles; with 3xTF32 also B's low part (A's
+  // hi/lo parts go to TMEM instead, so the MMAs read only B from smem).
+  static constexpr int kStageBytes = kABytes + kBBytes * (SPLIT ? 2 : 1);
   static constexpr int kStagesRaw = (kSmemLimit - kSmemReserve - kOutBytes) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
   static constexpr int kSmemBytes = kStages * kStageBytes + kOutBytes + kSmemReserve;
-  // TMEM: two partial-sum buffers (double buffering) + with 3xTF32 one fp32
-  // running sum the epilogue warps promote the partials into.
-  static constexpr int kTmemNeed = (SPLIT ? 3 : 2) * BN;
+  // TMEM: two partial-sum buffers (double buffering); with 3xTF32 one fp32
+  // running sum the epilogue warps promote the partials into, then a ring of
+  // kAStages A k-blocks, each a 32-column hi part and a 32-column lo part.
+  static constexpr int kAccCols = (SPLIT ? 3 : 2) * BN;
+  static constexpr int kAStagesRaw = SPLIT ? (512 - kAccCols) / (2 * kBK) : 0;
+  static constexpr int kAStages = kAStagesRaw > 4 ? 4 : kAStagesRaw;
+  static constexpr int kTmemNeed = kAccCols + kAStages * 2 * kBK;
   static constexpr int kTmemCols = kTmemNeed <= 128 ? 128 : (kTmemNeed <= 256 ? 256 : 512);
-  static_assert(kTmemNeed <= 512, "3xTF32 needs BN <= 128 (three BN-column TMEM buffers)");
+  static_assert(kTmemNeed <= 512, "TMEM holds 512 columns");
+  static_assert(!SPLIT || kAStages >= 2, "3xTF32 needs BN <= 128 (two TMEM A stages)");
   static_assert(kStages >= 2, "need at least two pipeline stages");
   static_assert(BN == 64 || BN == 128 || BN == 256, "BN must be 64, 128 or 256");
 };
@@ -193,67 +200,50 @@ __device__ __forceinline__ float4 tf32_trunc_rem4(float4 v) {
   return make_float4(v.x - hx, v.y - hy, v.z - hz, v.w - hw);
 }
 
-// Epilogue for one thread's row m and 32 consecutive columns n0..n0+31.
+// The epilogue functions below take `sb`: the 32 bias values of the chunk,
+// staged once per tile in shared memory (zero past N), or null without bias.
+// Every global load of a chunk is issued before its first store, so loads are
+// not serialised behind stores the compiler cannot prove disjoint.
+
+// Row-major epilogue for one thread's row m and 32 consecutive columns n0..n0+31.
 __device__ __forceinline__ void epilogue_store32(const GemmParams& p, int m, int n0,
-                                                 const uint32_t (&r)[32]) {
+                                                 const uint32_t (&r)[32], const float* sb) {
   if (m >= p.M) return;
   float v[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-  const bool full = (n0 + 32 <= p.N);
-  if (p.out_mode == 0) {
-    float* crow = p.C + (int64_t)m * p.ldc;
-    const float* rrow = p.residual ? p.residual + (int64_t)m * p.ldr : nullptr;
-    if (full && p.vec_ok) {
-      if (p.bias) {
+  if (sb) {
 #pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-          const float4 b = __ldg(reinterpret_cast<const float4*>(p.bias + n0 + j));
-          v[j] += b.x; v[j + 1] += b.y; v[j + 2] += b.z; v[j + 3] += b.w;
-        }
-      }
-      if (rrow) {
+    for (int j = 0; j < 32; ++j) v[j] += sb[j];
+  }
+  float* crow = p.C + (int64_t)m * p.ldc;
+  const float* rrow = p.residual ? p.residual + (int64_t)m * p.ldr : nullptr;
+  if (n0 + 32 <= p.N && p.vec_ok) {
+    if (rrow) {
+      float4 q[8];
 #pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-          const float4 q = __ldg(reinterpret_cast<const float4*>(rrow + n0 + j));
-          v[j] += q.x; v[j + 1] += q.y; v[j + 2] += q.z; v[j + 3] += q.w;
-        }
-      }
-      if (p.relu) {
+      for (int j = 0; j < 8; ++j) q[j] = __ldg(reinterpret_cast<const float4*>(rrow + n0) + j);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.0f);
-      }
-#pragma unroll
-      for (int j = 0; j < 32; j += 4)
-        *reinterpret_cast<float4*>(crow + n0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int n = n0 + j;
-        if (n < p.N) {
-          float o = v[j];
-          if (p.bias) o += __ldg(p.bias + n);
-          if (rrow) o += __ldg(rrow + n);
-          if (p.relu) o = fmaxf(o, 0.0f);
-          crow[n] = o;
-        }
+      for (int j = 0; j < 8; ++j) {
+        v[4 * j] += q[j].x; v[4 * j + 1] += q[j].y; v[4 * j + 2] += q[j].z; v[4 * j + 3] += q[j].w;
       }
     }
+    if (p.relu) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.0f);
+    }
+#pragma unroll
+    for (int j = 0; j < 32; j += 4)
+      *reinterpret_cast<float4*>(crow + n0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
   } else {
-    const int img = m / p.hw;
-    const int pix = m - img * p.hw;
-    const int64_t base = (int64_t)img * p.N * p.hw + pix;
+    if (rrow) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (n0 + j < p.N) v[j] += __ldg(rrow + n0 + j);
+    }
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
-      const int n = n0 + j;
-      if (n < p.N) {
-        const int64_t off = base + (int64_t)n * p.hw;
-        float o = v[j];
-        if (p.bias) o += __ldg(p.bias + n);
-        if (p.residual) o += __ldg(p.residual + off);
-        if (p.relu) o = fmaxf(o, 0.0f);
-        p.C[off] = o;
-      }
+      if (n0 + j < p.N) crow[n0 + j] = p.relu ? fmaxf(v[j], 0.0f) : v[j];
     }
   }
 }
@@ -263,31 +253,24 @@ __device__ __forceinline__ void epilogue_store32(const GemmParams& p, int m, int
 // swizzled (16-byte unit j of row r at position j ^ (r % 8)) to match the
 // store map and keep the 8-thread phases of the writes conflict-free.
 __device__ __forceinline__ void epilogue_stage_rowmajor(const GemmParams& p, uint8_t* buf, int row,
-                                                        int n0, int m, const uint32_t (&r)[32]) {
+                                                        int n0, int m, const uint32_t (&r)[32],
+                                                        const float* sb) {
   float v[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-  const bool full = (n0 + 32 <= p.N) && p.vec_ok;
-  if (p.bias) {
-    if (full) {
+  if (sb) {
 #pragma unroll
-      for (int j = 0; j < 32; j += 4) {
-        const float4 b = __ldg(reinterpret_cast<const float4*>(p.bias + n0 + j));
-        v[j] += b.x; v[j + 1] += b.y; v[j + 2] += b.z; v[j + 3] += b.w;
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (n0 + j < p.N) v[j] += __ldg(p.bias + n0 + j);
-    }
+    for (int j = 0; j < 32; ++j) v[j] += sb[j];
   }
   if (p.residual && m < p.M) {
     const float* rrow = p.residual + (int64_t)m * p.ldr;
-    if (full) {
+    if (n0 + 32 <= p.N && p.vec_ok) {
+      float4 q[8];
 #pragma unroll
-      for (int j = 0; j < 32; j += 4) {
-        const float4 q = __ldg(reinterpret_cast<const float4*>(rrow + n0 + j));
-        v[j] += q.x; v[j + 1] += q.y; v[j + 2] += q.z; v[j + 3] += q.w;
+      for (int j = 0; j < 8; ++j) q[j] = __ldg(reinterpret_cast<const float4*>(rrow + n0) + j);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        v[4 * j] += q[j].x; v[4 * j + 1] += q[j].y; v[4 * j + 2] += q[j].z; v[4 * j + 3] += q[j].w;
       }
     } else {
 #pragma unroll
@@ -308,16 +291,13 @@ __device__ __forceinline__ void epilogue_stage_rowmajor(const GemmParams& p, uin
 // NCHW epilogue: transpose the 128-pixel x 32-channel chunk through shared
 // memory ([32 channels][128 pixels]), then each thread writes 4 consecutive
 // pixels of one channel with a 16-byte store (a warp covers 512 contiguous
-// bytes of a channel plane), adding the NCHW residual and applying ReLU there.
+// bytes of a channel plane), adding bias and the NCHW residual and applying
+// ReLU there.
 __device__ __forceinline__ void epilogue_nchw_chunk(const GemmParams& p, float* buf, int row,
                                                     int et, int m0, int n0,
-                                                    const uint32_t (&r)[32]) {
+                                                    const uint32_t (&r)[32], const float* sb) {
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    float v = __uint_as_float(r[j]);
-    if (p.bias && n0 + j < p.N) v += __ldg(p.bias + n0 + j);
-    buf[j * kBM + row] = v;
-  }
+  for (int j = 0; j < 32; ++j) buf[j * kBM + row] = __uint_as_float(r[j]);
   named_bar_sync(1, 128);
   const bool vec = (p.hw % 4 == 0) && p.vec4_nchw;
 #pragma unroll 2
@@ -327,12 +307,15 @@ __device__ __forceinline__ void epilogue_nchw_chunk(const GemmParams& p, float* 
     const int n = n0 + ch;
     const int m = m0 + 4 * q;
     if (n >= p.N || m >= p.M) continue;
-    const float4 s4 = *reinterpret_cast<const float4*>(buf + ch * kBM + 4 * q);
+    float4 o = *reinterpret_cast<const float4*>(buf + ch * kBM + 4 * q);
+    if (sb) {
+      const float bv = sb[ch];
+      o.x += bv; o.y += bv; o.z += bv; o.w += bv;
+    }
     const int img = m / p.hw;
     const int pix = m - img * p.hw;
     const int64_t off = ((int64_t)img * p.N + n) * p.hw + pix;
     if (vec && m + 3 < p.M) {
-      float4 o = s4;
       if (p.residual) {
         const float4 q4 = __ldg(reinterpret_cast<const float4*>(p.residual + off));
         o.x += q4.x; o.y += q4.y; o.z += q4.z; o.w += q4.w;
@@ -342,19 +325,27 @@ __device__ __forceinline__ void epilogue_nchw_chunk(const GemmParams& p, float* 
       }
       *reinterpret_cast<float4*>(p.C + off) = o;
     } else {
-      const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
+      float sv[4] = {o.x, o.y, o.z, o.w};
+      int64_t offs[4];
+      int cnt = 0;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int me = m + e;
-        if (me >= p.M) break;
-        const int im = me / p.hw;
-        const int px = me - im * p.hw;
-        const int64_t o1 = ((int64_t)im * p.N + n) * p.hw + px;
-        float o = sv[e];
-        if (p.residual) o += __ldg(p.residual + o1);
-        if (p.relu) o = fmaxf(o, 0.f);
-        p.C[o1] = o;
+        if (me < p.M) {
+          const int im = me / p.hw;
+          const int px = me - im * p.hw;
+          offs[e] = ((int64_t)im * p.N + n) * p.hw + px;
+          cnt = e + 1;
+        }
       }
+      if (p.residual) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (e < cnt) sv[e] += __ldg(p.residual + offs[e]);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (e < cnt) p.C[offs[e]] = p.relu ? fmaxf(sv[e], 0.f) : sv[e];
     }
   }
   named_bar_sync(1, 128);
@@ -375,18 +366,20 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
+  constexpr int kAS = SPLIT ? Cfg::kAStages : 1;
   uint8_t* sA = base;                                  // S x 16 KB
   uint8_t* sB = sA + S * kABytes;                      // S x BN*128
-  uint8_t* sAlo = sB + S * kBBytes;                    // SPLIT: S x 16 KB
-  uint8_t* sBlo = sAlo + (SPLIT ? S * kABytes : 0);    // SPLIT: S x BN*128
+  uint8_t* sBlo = sB + S * kBBytes;                    // SPLIT: S x BN*128
   uint8_t* sOut = sBlo + (SPLIT ? S * kBBytes : 0);    // 2 x 16 KB epilogue staging
   uint8_t* tail = sOut + kOutBytes;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(tail);
+  float* sBias = reinterpret_cast<float*>(tail);         // epilogue: the tile's BN bias values
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(tail + 1024);
   uint64_t* conv_bar = full_bar + S;
   uint64_t* empty_bar = conv_bar + S;
   uint64_t* tfull_bar = empty_bar + S;
   uint64_t* tempty_bar = tfull_bar + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+  uint64_t* aempty_bar = tempty_bar + 2;  // SPLIT: TMEM A stage consumed by the MMAs
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aempty_bar + kAS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* fix_flag = abort_flag + 1;  // epilogue: this CTA sums a split tile
   volatile int* epi_vote = abort_flag + 2;  // epilogue: per-warp wait outcome (4 ints)
@@ -404,6 +397,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
       mbar_init(&tfull_bar[b], 1);
       mbar_init(&tempty_bar[b], 128);
     }
+    for (int j = 0; j < kAS; ++j) mbar_init(&aempty_bar[j], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -493,6 +487,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
       int s = 0;
       uint32_t ph = 0;
       int g = 0;  // accumulation-unit counter (selects the TMEM partial buffer)
+      int ja = 0;  // TMEM A stage (3xTF32)
       bool ok = true;
       for (int w = blockIdx.x; w < p.num_units && ok && !*abort_flag; w += gridDim.x) {
         const WorkUnit u = work_unit(p, w);
@@ -522,32 +517,37 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
             if (GATHER && !SPLIT) fence_proxy_async_smem();
             const uint32_t a_addr = smem_u32(sA + s * kABytes);
             const uint32_t b_addr = smem_u32(sB + s * kBBytes);
-            const uint32_t alo_addr = smem_u32(sAlo + s * kABytes);
             const uint32_t blo_addr = smem_u32(sBlo + s * kBBytes);
+            // 3xTF32: A's hi / lo k-block in TMEM columns (lane 0 = tile row 0)
+            const uint32_t a_hi = tmem_base + (uint32_t)(Cfg::kAccCols + ja * 2 * kBK);
+            const uint32_t a_lo = a_hi + (uint32_t)kBK;
 #pragma unroll
             for (int k = 0; k < kBK / 8; ++k) {
               // A (K-major, SW128): +32 B per 8-element k step inside the 128 B row.
               // B MN-major (SW128 with 32 B atoms): +1024 B = 8 K-rows per k step;
               // LBO = 4096 B between 32-column boxes, SBO = 512 B per 4 K-rows.
-              const uint64_t da = umma_desc(a_addr + k * 32, 16, 1024, kLayoutSW128);
               const uint64_t db =
                   B_MN == 0 ? umma_desc(b_addr + k * 32, 16, 1024, kLayoutSW128)
                             : umma_desc(b_addr + k * 1024, 4096, 512, kLayoutSW128Base32B);
               const uint32_t acc = (kb > kb0 || k > 0) ? 1u : 0u;
               if (SPLIT) {
-                const uint64_t dal = umma_desc(alo_addr + k * 32, 16, 1024, kLayoutSW128);
                 const uint64_t dbl =
                     B_MN == 0 ? umma_desc(blo_addr + k * 32, 16, 1024, kLayoutSW128)
                               : umma_desc(blo_addr + k * 1024, 4096, 512, kLayoutSW128Base32B);
-                // small cross terms first, then hi*hi
-                umma_tf32(d_tmem, da, dbl, idesc, acc);
-                umma_tf32(d_tmem, dal, db, idesc, 1u);
-                umma_tf32(d_tmem, da, db, idesc, 1u);
+                // small cross terms first, then hi*hi; A from TMEM (8 columns per k step)
+                umma_tf32_ts(d_tmem, a_hi + k * 8, dbl, idesc, acc);
+                umma_tf32_ts(d_tmem, a_lo + k * 8, db, idesc, 1u);
+                umma_tf32_ts(d_tmem, a_hi + k * 8, db, idesc, 1u);
               } else {
+                const uint64_t da = umma_desc(a_addr + k * 32, 16, 1024, kLayoutSW128);
                 umma_tf32(d_tmem, da, db, idesc, acc);
               }
             }
             umma_commit(&empty_bar[s]);
+            if (SPLIT) {
+              umma_commit(&aempty_bar[ja]);
+              if (++ja == kAS) ja = 0;
+            }
             if (++s == S) { s = 0; ph ^= 1; }
           }
           if (!ok) break;
@@ -567,9 +567,11 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
     int g = 0;
     bool ok = true;
     // One finished 128 x 32 chunk (this thread's row, columns n0..n0+31) to C.
-    auto emit = [&](int tm, int n0, int m, const uint32_t (&r)[32]) {
+    auto emit = [&](int tm, int tn, int c, int m, const uint32_t (&r)[32]) {
+      const int n0 = tn * BN + c;
+      const float* sb = p.bias ? sBias + c : nullptr;
       if (p.c_tma) {
-        epilogue_stage_rowmajor(p, sOut + (chunk & 1) * kOutChunkBytes, row, n0, m, r);
+        epilogue_stage_rowmajor(p, sOut + (chunk & 1) * kOutChunkBytes, row, n0, m, r, sb);
         fence_proxy_async_smem();
         named_bar_sync(1, 128);
         if (et == 0) {
@@ -581,10 +583,10 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
         ++chunk;
       } else if (p.out_mode == 1) {
         float* buf = reinterpret_cast<float*>(sOut + (chunk & 1) * kOutChunkBytes);
-        epilogue_nchw_chunk(p, buf, row, et, tm * kBM, n0, r);
+        epilogue_nchw_chunk(p, buf, row, et, tm * kBM, n0, r, sb);
         ++chunk;
       } else {
-        epilogue_store32(p, m, n0, r);
+        epilogue_store32(p, m, n0, r, sb);
       }
     };
     for (int w = blockIdx.x; w < p.num_units && ok; w += gridDim.x) {
@@ -599,6 +601,16 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
                                 ((size_t)u.slot * p.split_k + u.piece) * (size_t)(BN * kBM / 4)
                           : nullptr;
       const int units = (u.kb1 - u.kb0 + p.kb_per_acc - 1) / p.kb_per_acc;
+      if (p.bias) {
+        // Stage the tile's bias once (the loads overlap the mainloop); the
+        // barrier keeps the previous tile's readers ahead of the overwrite,
+        // the vote barriers below publish the values.
+        named_bar_sync(2, 128);
+        for (int i = et; i < BN; i += 128) {
+          const int n = tn * BN + i;
+          sBias[i] = n < p.N ? __ldg(p.bias + n) : 0.0f;
+        }
+      }
       for (int a = 0; a < units; ++a, ++g) {
         const int b = g & 1;
         const uint32_t use = (uint32_t)(g >> 1);
@@ -648,7 +660,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
                                                 __uint_as_float(r[4 * j + 2]),
                                                 __uint_as_float(r[4 * j + 3])));
           } else {
-            emit(tm, tn * BN + c, m, r);
+            emit(tm, tn, c, m, r);
           }
         }
         if (SPLIT && !last) tmem_st_wait();
@@ -687,7 +699,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
             uint32_t r[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(v[j]);
-            emit(tm, tn * BN + c, m, r);
+            emit(tm, tn, c, m, r);
           }
         }
       }
@@ -697,36 +709,61 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
     if (p.c_tma && et == 0) bulk_wait_group<0>();  // all output stores complete
   } else if (SPLIT && warp >= Roles::kWarpConv && warp < Roles::kWarpConv + 4) {
     // ------------------------------------------------------------ converters
+    // Per k-block: thread = tile row (TMEM lane 32*(warp%4)+lane).  The A row
+    // (32 fp32, 128B-swizzled in smem) becomes hi = trunc_tf32(x) and
+    // lo = x - hi, stored as two 32-column blocks of the TMEM A stage; the B
+    // tile's low part goes to its smem plane (its hi part is the raw tile,
+    // truncated by the tensor core).
     const int ct = threadIdx.x - Roles::kWarpConv * 32;  // 0..127
+    const int lane_base = 32 * (warp & 3);
+    const int row = lane_base + lane;
+    const uint32_t t_lane = tmem_base + ((uint32_t)lane_base << 16);
     int s = 0;
     uint32_t ph = 0;
-    for (int w = blockIdx.x; w < p.num_units && !*abort_flag; w += gridDim.x) {
+    int ja = 0;
+    uint32_t pa = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < p.num_units && ok && !*abort_flag; w += gridDim.x) {
       const WorkUnit u = work_unit(p, w);
-      bool ok = true;
       for (int kb = u.kb0; kb < u.kb1; ++kb) {
-        if (!mbar_wait_bounded(&full_bar[s], ph, abort_flag, p.err, DEV_TIMEOUT_LOADED,
-                               p.timeout_ns)) {
+        // every lane waits (acquire for its own smem reads); tcgen05.st is
+        // .sync.aligned, so the warp proceeds only if all lanes got through
+        bool got = mbar_wait_bounded(&full_bar[s], ph, abort_flag, p.err, DEV_TIMEOUT_LOADED,
+                                     p.timeout_ns);
+        got = got && mbar_wait_bounded(&aempty_bar[ja], pa ^ 1, abort_flag, p.err,
+                                       DEV_TIMEOUT_TMEM_A, p.timeout_ns);
+        if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           break;
         }
-        float4* a = reinterpret_cast<float4*>(sA + s * kABytes);
-        float4* alo = reinterpret_cast<float4*>(sAlo + s * kABytes);
+        tc_fence_after();
+        const float4* arow = reinterpret_cast<const float4*>(sA + s * kABytes + row * 128);
+        uint32_t hi[32], lo[32];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 v = arow[j ^ (row & 7)];
+          const float x[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            uint32_t h;
+            if (p.split_trunc) {
+              h = __float_as_uint(x[e]) & 0xFFFFE000u;
+            } else {
+              asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x[e]));
+            }
+            hi[4 * j + e] = h;
+            lo[4 * j + e] = __float_as_uint(x[e] - __uint_as_float(h));
+          }
+        }
+        const uint32_t t_a = t_lane + (uint32_t)(Cfg::kAccCols + ja * 2 * kBK);
+        tmem_st_32x32b_x32(t_a, hi);
+        tmem_st_32x32b_x32(t_a + (uint32_t)kBK, lo);
         float4* bb = reinterpret_cast<float4*>(sB + s * kBBytes);
         float4* blo = reinterpret_cast<float4*>(sBlo + s * kBBytes);
         if (p.split_trunc) {
-          // hi = the tensor core's truncation of the raw value (left in place)
-#pragma unroll 4
-          for (int i = ct; i < kABytes / 16; i += 128) alo[i] = tf32_trunc_rem4(a[i]);
 #pragma unroll 4
           for (int i = ct; i < kBBytes / 16; i += 128) blo[i] = tf32_trunc_rem4(bb[i]);
         } else {
-#pragma unroll 4
-          for (int i = ct; i < kABytes / 16; i += 128) {
-            const float4 v = a[i];
-            const float4 h = tf32_hi4(v);
-            a[i] = h;
-            alo[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
-          }
 #pragma unroll 4
           for (int i = ct; i < kBBytes / 16; i += 128) {
             const float4 v = bb[i];
@@ -736,10 +773,12 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
           }
         }
         fence_proxy_async_smem();
+        tmem_st_wait();
+        tc_fence_before();
         mbar_arrive(&conv_bar[s]);
         if (++s == S) { s = 0; ph ^= 1; }
+        if (++ja == kAS) { ja = 0; pa ^= 1; }
       }
-      if (!ok) break;
     }
   } else if (GATHER && warp >= Roles::kWarpGather && warp < Roles::kWarpGather + 4) {
     // ------------------------------------------------------------ im2col gather

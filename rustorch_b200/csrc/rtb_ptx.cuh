@@ -22,6 +22,7 @@ enum DevErr : int {
   DEV_TIMEOUT_LOADED = 6,    // converter waited too long for a loaded stage
   DEV_BAD_CONFIG = 7,        // kernel launched with an inconsistent configuration
   DEV_TIMEOUT_PROBE = 8,     // rtb_debug_wait_probe: the deliberately unsatisfied wait expired
+  DEV_TIMEOUT_TMEM_A = 9,    // converter waited too long for a free TMEM A stage
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -220,6 +221,18 @@ __device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a_desc, uint
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// D (+)= A . B with A (M x 8 tf32, row i in TMEM lane i, one element per
+// 32-bit column) read from tensor memory and B from shared memory.
+__device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
