@@ -290,62 +290,84 @@ __device__ __forceinline__ void epilogue_stage_rowmajor(const GemmParams& p, uin
 
 // NCHW epilogue: transpose the 128-pixel x 32-channel chunk through shared
 // memory ([32 channels][128 pixels]), then each thread writes 4 consecutive
-// pixels of one channel with a 16-byte store (a warp covers 512 contiguous
-// bytes of a channel plane), adding bias and the NCHW residual and applying
-// ReLU there.
+// pixels of 8 channels with 16-byte stores (a warp covers 512 contiguous bytes
+// of one channel plane per store), adding bias and the NCHW residual and
+// applying ReLU there.  A thread keeps the same 4-pixel group (et % 32) for
+// all of its channels, so the pixel -> (image, offset) division happens once
+// per chunk, and the 8 loads are issued before the 8 stores.
 __device__ __forceinline__ void epilogue_nchw_chunk(const GemmParams& p, float* buf, int row,
                                                     int et, int m0, int n0,
                                                     const uint32_t (&r)[32], const float* sb) {
 #pragma unroll
   for (int j = 0; j < 32; ++j) buf[j * kBM + row] = __uint_as_float(r[j]);
   named_bar_sync(1, 128);
-  const bool vec = (p.hw % 4 == 0) && p.vec4_nchw;
-#pragma unroll 2
-  for (int i = et; i < 32 * (kBM / 4); i += 128) {
-    const int ch = i >> 5;         // channel within the chunk
-    const int q = i & 31;          // 4-pixel group
-    const int n = n0 + ch;
-    const int m = m0 + 4 * q;
-    if (n >= p.N || m >= p.M) continue;
-    float4 o = *reinterpret_cast<const float4*>(buf + ch * kBM + 4 * q);
-    if (sb) {
-      const float bv = sb[ch];
-      o.x += bv; o.y += bv; o.z += bv; o.w += bv;
-    }
-    const int img = m / p.hw;
-    const int pix = m - img * p.hw;
-    const int64_t off = ((int64_t)img * p.N + n) * p.hw + pix;
-    if (vec && m + 3 < p.M) {
-      if (p.residual) {
-        const float4 q4 = __ldg(reinterpret_cast<const float4*>(p.residual + off));
-        o.x += q4.x; o.y += q4.y; o.z += q4.z; o.w += q4.w;
+  const int q = et & 31;   // 4-pixel group
+  const int cw = et >> 5;  // channels cw, cw+4, ..., cw+28 of the chunk
+  const int m = m0 + 4 * q;
+  if (m < p.M) {
+    if ((p.hw % 4 == 0) && p.vec4_nchw && m + 3 < p.M) {
+      // the 4 pixels lie in one image
+      const int img = m / p.hw;
+      const int pix = m - img * p.hw;
+      const float* rbase =
+          p.residual ? p.residual + ((int64_t)img * p.N + n0) * p.hw + pix : nullptr;
+      float* cbase = p.C + ((int64_t)img * p.N + n0) * p.hw + pix;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {  // two halves of 4 channels: loads, then stores
+        float4 o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int ch = cw + 4 * (4 * h + k);
+          o[k] = *reinterpret_cast<const float4*>(buf + ch * kBM + 4 * q);
+          const float bv = sb ? sb[ch] : 0.0f;
+          o[k].x += bv; o[k].y += bv; o[k].z += bv; o[k].w += bv;
+          if (rbase && n0 + ch < p.N) {
+            const float4 r4 = __ldg(reinterpret_cast<const float4*>(rbase + (int64_t)ch * p.hw));
+            o[k].x += r4.x; o[k].y += r4.y; o[k].z += r4.z; o[k].w += r4.w;
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int ch = cw + 4 * (4 * h + k);
+          if (n0 + ch < p.N) {
+            float4 v = o[k];
+            if (p.relu) {
+              v.x = fmaxf(v.x, 0.f); v.y = fmaxf(v.y, 0.f); v.z = fmaxf(v.z, 0.f); v.w = fmaxf(v.w, 0.f);
+            }
+            *reinterpret_cast<float4*>(cbase + (int64_t)ch * p.hw) = v;
+          }
+        }
       }
-      if (p.relu) {
-        o.x = fmaxf(o.x, 0.f); o.y = fmaxf(o.y, 0.f); o.z = fmaxf(o.z, 0.f); o.w = fmaxf(o.w, 0.f);
-      }
-      *reinterpret_cast<float4*>(p.C + off) = o;
     } else {
-      float sv[4] = {o.x, o.y, o.z, o.w};
-      int64_t offs[4];
+      // general case: each of the 4 pixels resolved on its own
+      int64_t pb[4];
       int cnt = 0;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int me = m + e;
+        pb[e] = 0;
         if (me < p.M) {
           const int im = me / p.hw;
-          const int px = me - im * p.hw;
-          offs[e] = ((int64_t)im * p.N + n) * p.hw + px;
+          pb[e] = ((int64_t)im * p.N + n0) * p.hw + (me - im * p.hw);
           cnt = e + 1;
         }
       }
-      if (p.residual) {
+#pragma unroll 1
+      for (int k = 0; k < 8; ++k) {
+        const int ch = cw + 4 * k;
+        if (n0 + ch >= p.N) continue;
+        const float4 o = *reinterpret_cast<const float4*>(buf + ch * kBM + 4 * q);
+        const float bv = sb ? sb[ch] : 0.0f;
+        float sv[4] = {o.x + bv, o.y + bv, o.z + bv, o.w + bv};
+        if (p.residual) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (e < cnt) sv[e] += __ldg(p.residual + pb[e] + (int64_t)ch * p.hw);
+        }
 #pragma unroll
         for (int e = 0; e < 4; ++e)
-          if (e < cnt) sv[e] += __ldg(p.residual + offs[e]);
+          if (e < cnt) p.C[pb[e] + (int64_t)ch * p.hw] = p.relu ? fmaxf(sv[e], 0.f) : sv[e];
       }
-#pragma unroll
-      for (int e = 0; e < 4; ++e)
-        if (e < cnt) p.C[offs[e]] = p.relu ? fmaxf(sv[e], 0.f) : sv[e];
     }
   }
   named_bar_sync(1, 128);
@@ -633,6 +655,19 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
           if (last) trace_stamp(p, 6 + 6 * tj);
         }
         const uint32_t t_part = t_lane + (uint32_t)(b * BN);
+        // One finished chunk: a split piece's partial to the workspace, else to C.
+        auto out = [&](int c, const uint32_t (&r)[32]) {
+          if (piece) {
+            float4* dst = wsp + (size_t)(c / 32) * 8 * kBM + row;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              __stcg(dst + j * kBM, make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                                __uint_as_float(r[4 * j + 2]),
+                                                __uint_as_float(r[4 * j + 3])));
+          } else {
+            emit(tm, tn, c, m, r);
+          }
+        };
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
           uint32_t r[32];
@@ -650,20 +685,24 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
             tc_fence_before();
             mbar_arrive(&tempty_bar[b]);  // partial buffer b may be overwritten now
           }
-          if (SPLIT && !last) {
+          if (SPLIT) {
+            // running sum; after the last unit the finished tile, which leaves
+            // from there so the accumulator is not held during the stores
             tmem_st_32x32b_x32(t_run + (uint32_t)c, r);
-          } else if (piece) {
-            float4* dst = wsp + (size_t)(c / 32) * 8 * kBM + row;
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              __stcg(dst + j * kBM, make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                                __uint_as_float(r[4 * j + 2]),
-                                                __uint_as_float(r[4 * j + 3])));
           } else {
-            emit(tm, tn, c, m, r);
+            out(c, r);
           }
         }
-        if (SPLIT && !last) tmem_st_wait();
+        if (SPLIT) tmem_st_wait();
+        if (SPLIT && last) {
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 32) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(t_run + (uint32_t)c, r);
+            tmem_ld_wait();
+            out(c, r);
+          }
+        }
       }
       if (ok && piece) {
         // Publish this piece, count arrivals; the last piece sums all of them.
