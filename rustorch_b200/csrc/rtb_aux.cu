@@ -62,22 +62,59 @@ __global__ void fill_rows_kernel(float* C, int64_t M, int64_t N, int64_t ldc,
 
 // NCHW -> NHWC with channel stride Cp (zero pad).  Tiled transpose per image:
 // tile of 32 pixels x 32 channels.
-__global__ void nchw_to_nhwc_kernel(const float* __restrict__ x, int64_t C, int64_t HW,
-                                    int64_t Cp, float* __restrict__ y) {
-  __shared__ float tile[32][33];
-  const int64_t img = blockIdx.z;
-  const int64_t p0 = (int64_t)blockIdx.x * 32, c0 = (int64_t)blockIdx.y * 32;
-  const int tx = threadIdx.x, ty = threadIdx.y;
-  const float* xi = x + img * C * HW;
-  for (int i = ty; i < 32; i += 8) {
-    const int64_t c = c0 + i, p = p0 + tx;
-    tile[i][tx] = (c < C && p < HW) ? xi[c * HW + p] : 0.0f;
+// NCHW [N, C, HW] -> NHWC [N, HW, Cp] (channels >= C zero-filled).  A block
+// moves a 32-channel x 128-pixel tile (16 KB): each warp reads 512 contiguous
+// bytes of one channel plane (16-byte loads when HW % 4 == 0), the tile is
+// transposed through shared memory (row pitch 129: conflict-free), and each
+// warp writes 4 pixels x 32 channels as 16-byte stores.  32-bit index math
+// within an image.
+constexpr int kT2Pix = 128;
+__global__ void __launch_bounds__(256) nchw_to_nhwc_kernel(const float* __restrict__ x, int C,
+                                                            int HW, int Cp, int vec,
+                                                            int vec_out, float* __restrict__ y) {
+  __shared__ float tile[32][kT2Pix + 1];
+  const int p0 = blockIdx.x * kT2Pix, c0 = blockIdx.y * 32;
+  const float* xi = x + (int64_t)blockIdx.z * C * HW;
+  float* yi = y + (int64_t)blockIdx.z * HW * Cp;
+  const int t = threadIdx.x;
+  // load: 32 channels x 32 four-pixel groups, 4 per thread
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int idx = t + 256 * it;
+    const int cl = idx >> 5, g = idx & 31;
+    const int c = c0 + cl, p = p0 + 4 * g;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (c < C) {
+      const float* src = xi + (int64_t)c * HW + p;
+      if (vec && p + 3 < HW) {
+        const float4 q = __ldg(reinterpret_cast<const float4*>(src));
+        v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (p + e < HW) v[e] = __ldg(src + e);
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) tile[cl][4 * g + e] = v[e];
   }
   __syncthreads();
-  float* yi = y + img * HW * Cp;
-  for (int i = ty; i < 32; i += 8) {
-    const int64_t p = p0 + i, c = c0 + tx;
-    if (p < HW && c < Cp) yi[p * Cp + c] = tile[tx][i];
+  // store: 128 pixels x 8 four-channel groups, 4 per thread
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int idx = t + 256 * it;
+    const int pl = idx >> 3, cg = idx & 7;
+    const int p = p0 + pl, c = c0 + 4 * cg;
+    if (p >= HW || c >= Cp) continue;
+    float* dst = yi + (int64_t)p * Cp + c;
+    const float4 o = make_float4(tile[4 * cg][pl], tile[4 * cg + 1][pl], tile[4 * cg + 2][pl],
+                                 tile[4 * cg + 3][pl]);
+    if (vec_out && c + 3 < Cp) {
+      *reinterpret_cast<float4*>(dst) = o;  // y 16-byte aligned, Cp % 4 == 0
+    } else {
+      const float ov[4] = {o.x, o.y, o.z, o.w};
+      for (int e = 0; e < 4 && c + e < Cp; ++e) dst[e] = ov[e];
+    }
   }
 }
 
@@ -118,16 +155,30 @@ __global__ void nhwc_to_nchw_kernel(const float* __restrict__ x, int64_t C, int6
 }
 
 // w [Co, Ci, kh, kw] -> wp [Co, kh*kw*Cp] with k = (r*kw + s)*Cp + ci.
-__global__ void prepack_weight_kernel(const float* __restrict__ w, int64_t Co, int64_t Ci,
-                                      int64_t kh, int64_t kw, int64_t Cp, float* __restrict__ wp) {
-  const int64_t Kw = kh * kw * Cp;
-  const int64_t total = Co * Kw;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t co = i / Kw, k = i - co * Kw;
-    const int64_t tap = k / Cp, ci = k - tap * Cp;
-    const int64_t r = tap / kw, s = tap - r * kw;
-    wp[i] = ci < Ci ? w[((co * Ci + ci) * kh + r) * kw + s] : 0.0f;
+// One block per output channel: its Ci*kh*kw weights are read contiguously
+// into shared memory (when they fit), then written in (tap, ci) order.
+constexpr int kPrepackSmemFloats = 12288;  // 48 KB
+__global__ void __launch_bounds__(256) prepack_weight_kernel(const float* __restrict__ w, int Ci,
+                                                              int taps, int Cp,
+                                                              float* __restrict__ wp) {
+  __shared__ float sw[kPrepackSmemFloats];
+  const int co = blockIdx.x;
+  const int n_in = Ci * taps;
+  const float* src = w + (int64_t)co * n_in;
+  float* dst = wp + (int64_t)co * taps * Cp;
+  const int Kw = taps * Cp;
+  if (n_in <= kPrepackSmemFloats) {
+    for (int i = threadIdx.x; i < n_in; i += blockDim.x) sw[i] = __ldg(src + i);
+    __syncthreads();
+    for (int k = threadIdx.x; k < Kw; k += blockDim.x) {
+      const int tap = k / Cp, ci = k - tap * Cp;
+      dst[k] = ci < Ci ? sw[ci * taps + tap] : 0.0f;
+    }
+  } else {
+    for (int k = threadIdx.x; k < Kw; k += blockDim.x) {
+      const int tap = k / Cp, ci = k - tap * Cp;
+      dst[k] = ci < Ci ? __ldg(src + ci * taps + tap) : 0.0f;
+    }
   }
 }
 
@@ -335,10 +386,14 @@ int launch_nchw_to_nhwc_padded(const float* x, int64_t N, int64_t C, int64_t H, 
                                                                  reinterpret_cast<float4*>(y));
     return launch_check("nchw_to_nhwc (C<=4)");
   }
-  dim3 grid((unsigned)((HW + 31) / 32), (unsigned)((Cp + 31) / 32), (unsigned)N);
-  if (N > 65535 || grid.y > 65535) return set_error(RTB_E_UNSUPPORTED, "nchw_to_nhwc: too large");
+  if (HW > INT32_MAX || C > INT32_MAX || Cp > INT32_MAX || N > 65535)
+    return set_error(RTB_E_UNSUPPORTED, "nchw_to_nhwc: too large");
+  dim3 grid((unsigned)((HW + kT2Pix - 1) / kT2Pix), (unsigned)((Cp + 31) / 32), (unsigned)N);
+  if (grid.y > 65535) return set_error(RTB_E_UNSUPPORTED, "nchw_to_nhwc: too many channels");
+  const int vec = (HW % 4 == 0) && (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
+  const int vec_out = (Cp % 4 == 0) && (reinterpret_cast<uintptr_t>(y) & 15u) == 0;
   clear_stale_cuda_error();
-  nchw_to_nhwc_kernel<<<grid, dim3(32, 8), 0, s>>>(x, C, HW, Cp, y);
+  nchw_to_nhwc_kernel<<<grid, 256, 0, s>>>(x, (int)C, (int)HW, (int)Cp, vec, vec_out, y);
   return launch_check("nchw_to_nhwc");
 }
 
@@ -353,9 +408,11 @@ int launch_nhwc_to_nchw(const float* x, float* y, int64_t N, int64_t C, int64_t 
 
 int launch_prepack_weight(const float* w, int64_t Co, int64_t Ci, int64_t kh, int64_t kw,
                           int64_t Cp, float* wp, cudaStream_t s) {
+  const int64_t taps = kh * kw;
+  if (Co > INT32_MAX || Ci * taps > INT32_MAX || taps * Cp > INT32_MAX)
+    return set_error(RTB_E_UNSUPPORTED, "prepack_weight: too large");
   clear_stale_cuda_error();
-  prepack_weight_kernel<<<grid_for(Co * kh * kw * Cp), kThreads, 0, s>>>(w, Co, Ci, kh, kw, Cp,
-                                                                          wp);
+  prepack_weight_kernel<<<(unsigned)Co, 256, 0, s>>>(w, (int)Ci, (int)taps, (int)Cp, wp);
   return launch_check("prepack_weight");
 }
 

@@ -47,7 +47,6 @@ constexpr int kABytes = kBM * kBK * 4;       // 16 KB
 constexpr int kSmemLimit = 232448;           // 227 KB dynamic shared memory per CTA
 constexpr int kSmemReserve = 3072;           // bias staging (1 KB) + barriers + alignment slack
 constexpr int kOutChunkBytes = kBM * 32 * 4;  // one 128 x 32 fp32 output chunk (16 KB)
-constexpr int kOutBytes = 2 * kOutChunkBytes; // double-buffered epilogue staging
 
 struct GemmParams {
   int M, N, K;
@@ -133,18 +132,27 @@ __device__ __forceinline__ void trace_stamp(const GemmParams& p, int slot) {
 template <int BN, bool SPLIT>
 struct GemmCfg {
   static constexpr int kBBytes = BN * kBK * 4;
-  // Shared-memory stage: A + B tiles; with 3xTF32 also B's low part (A's
-  // hi/lo parts go to TMEM instead, so the MMAs read only B from smem).
-  static constexpr int kStageBytes = kABytes + kBBytes * (SPLIT ? 2 : 1);
-  static constexpr int kStagesRaw = (kSmemLimit - kSmemReserve - kOutBytes) / kStageBytes;
-  static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
-  static constexpr int kSmemBytes = kStages * kStageBytes + kOutBytes + kSmemReserve;
   // TMEM: two partial-sum buffers (double buffering); with 3xTF32 one fp32
   // running sum the epilogue warps promote the partials into, then a ring of
-  // kAStages A k-blocks, each a 32-column hi part and a 32-column lo part.
+  // kAStages converted k-blocks: A's 32-column hi and lo parts in TMEM, B's
+  // low part in a shared-memory slot (the MMAs read only B from smem).
   static constexpr int kAccCols = (SPLIT ? 3 : 2) * BN;
   static constexpr int kAStagesRaw = SPLIT ? (512 - kAccCols) / (2 * kBK) : 0;
   static constexpr int kAStages = kAStagesRaw > 4 ? 4 : kAStagesRaw;
+  static constexpr int kBloBytes = SPLIT ? kAStages * kBBytes : 0;
+  // Load ring stage: the raw A and B tiles (TMA).
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  // Epilogue staging: two 16 KB chunks alternate, unless dropping one gives
+  // the load ring another stage.
+  static constexpr int kRingBytes = kSmemLimit - kSmemReserve - kBloBytes;
+  static constexpr int kOutBufs =
+      (kRingBytes - kOutChunkBytes) / kStageBytes > (kRingBytes - 2 * kOutChunkBytes) / kStageBytes
+          ? 1 : 2;
+  static constexpr int kOutBytes = kOutBufs * kOutChunkBytes;
+  static constexpr int kStagesRaw = (kRingBytes - kOutBytes) / kStageBytes;
+  static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
+  static constexpr int kSmemBytes =
+      kStages * kStageBytes + kBloBytes + kOutBytes + kSmemReserve;
   static constexpr int kTmemNeed = kAccCols + kAStages * 2 * kBK;
   static constexpr int kTmemCols = kTmemNeed <= 128 ? 128 : (kTmemNeed <= 256 ? 256 : 512);
   static_assert(kTmemNeed <= 512, "TMEM holds 512 columns");
@@ -391,13 +399,13 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
   constexpr int kAS = SPLIT ? Cfg::kAStages : 1;
   uint8_t* sA = base;                                  // S x 16 KB
   uint8_t* sB = sA + S * kABytes;                      // S x BN*128
-  uint8_t* sBlo = sB + S * kBBytes;                    // SPLIT: S x BN*128
-  uint8_t* sOut = sBlo + (SPLIT ? S * kBBytes : 0);    // 2 x 16 KB epilogue staging
-  uint8_t* tail = sOut + kOutBytes;
+  uint8_t* sBlo = sB + S * kBBytes;                    // SPLIT: kAS x BN*128
+  uint8_t* sOut = sBlo + Cfg::kBloBytes;               // kOutBufs x 16 KB epilogue staging
+  uint8_t* tail = sOut + Cfg::kOutBytes;
   float* sBias = reinterpret_cast<float*>(tail);         // epilogue: the tile's BN bias values
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(tail + 1024);
-  uint64_t* conv_bar = full_bar + S;
-  uint64_t* empty_bar = conv_bar + S;
+  uint64_t* conv_bar = full_bar + S;                     // SPLIT: [kAS] converted k-block ready
+  uint64_t* empty_bar = conv_bar + kAS;
   uint64_t* tfull_bar = empty_bar + S;
   uint64_t* tempty_bar = tfull_bar + 2;
   uint64_t* aempty_bar = tempty_bar + 2;  // SPLIT: TMEM A stage consumed by the MMAs
@@ -412,14 +420,16 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full_bar[s], 1 + (GATHER ? 128 : 0));
-      mbar_init(&conv_bar[s], 128);
       mbar_init(&empty_bar[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull_bar[b], 1);
       mbar_init(&tempty_bar[b], 128);
     }
-    for (int j = 0; j < kAS; ++j) mbar_init(&aempty_bar[j], 1);
+    for (int j = 0; j < kAS; ++j) {
+      mbar_init(&conv_bar[j], 128);
+      mbar_init(&aempty_bar[j], 1);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -509,7 +519,8 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
       int s = 0;
       uint32_t ph = 0;
       int g = 0;  // accumulation-unit counter (selects the TMEM partial buffer)
-      int ja = 0;  // TMEM A stage (3xTF32)
+      int ja = 0;  // converted-k-block ring slot (3xTF32)
+      uint32_t pa = 0;
       bool ok = true;
       for (int w = blockIdx.x; w < p.num_units && ok && !*abort_flag; w += gridDim.x) {
         const WorkUnit u = work_unit(p, w);
@@ -526,8 +537,8 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
           const uint32_t d_tmem = tmem_base + (uint32_t)(b * BN);
           const int kend = (kb0 + p.kb_per_acc) < u.kb1 ? (kb0 + p.kb_per_acc) : u.kb1;
           for (int kb = kb0; kb < kend; ++kb) {
-            uint64_t* ready = SPLIT ? &conv_bar[s] : &full_bar[s];
-            if (!mbar_wait_bounded(ready, ph, abort_flag, p.err,
+            uint64_t* ready = SPLIT ? &conv_bar[ja] : &full_bar[s];
+            if (!mbar_wait_bounded(ready, SPLIT ? pa : ph, abort_flag, p.err,
                                    SPLIT ? DEV_TIMEOUT_CONV : DEV_TIMEOUT_FULL, p.timeout_ns)) {
               ok = false;
               break;
@@ -539,7 +550,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
             if (GATHER && !SPLIT) fence_proxy_async_smem();
             const uint32_t a_addr = smem_u32(sA + s * kABytes);
             const uint32_t b_addr = smem_u32(sB + s * kBBytes);
-            const uint32_t blo_addr = smem_u32(sBlo + s * kBBytes);
+            const uint32_t blo_addr = smem_u32(sBlo + ja * kBBytes);
             // 3xTF32: A's hi / lo k-block in TMEM columns (lane 0 = tile row 0)
             const uint32_t a_hi = tmem_base + (uint32_t)(Cfg::kAccCols + ja * 2 * kBK);
             const uint32_t a_lo = a_hi + (uint32_t)kBK;
@@ -568,7 +579,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
             umma_commit(&empty_bar[s]);
             if (SPLIT) {
               umma_commit(&aempty_bar[ja]);
-              if (++ja == kAS) ja = 0;
+              if (++ja == kAS) { ja = 0; pa ^= 1; }
             }
             if (++s == S) { s = 0; ph ^= 1; }
           }
@@ -593,18 +604,20 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
       const int n0 = tn * BN + c;
       const float* sb = p.bias ? sBias + c : nullptr;
       if (p.c_tma) {
-        epilogue_stage_rowmajor(p, sOut + (chunk & 1) * kOutChunkBytes, row, n0, m, r, sb);
+        uint8_t* stg = sOut + (chunk % Cfg::kOutBufs) * kOutChunkBytes;
+        epilogue_stage_rowmajor(p, stg, row, n0, m, r, sb);
         fence_proxy_async_smem();
         named_bar_sync(1, 128);
         if (et == 0) {
-          tma_store_2d(&tmC, sOut + (chunk & 1) * kOutChunkBytes, n0, tm * kBM);
+          tma_store_2d(&tmC, stg, n0, tm * kBM);
           bulk_commit_group();
-          bulk_wait_group_read<1>();  // the buffer used next is free again
+          // the buffer used next is free again
+          if (Cfg::kOutBufs == 2) bulk_wait_group_read<1>(); else bulk_wait_group_read<0>();
         }
         named_bar_sync(1, 128);
         ++chunk;
       } else if (p.out_mode == 1) {
-        float* buf = reinterpret_cast<float*>(sOut + (chunk & 1) * kOutChunkBytes);
+        float* buf = reinterpret_cast<float*>(sOut + (chunk % Cfg::kOutBufs) * kOutChunkBytes);
         epilogue_nchw_chunk(p, buf, row, et, tm * kBM, n0, r, sb);
         ++chunk;
       } else {
@@ -776,12 +789,21 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
           break;
         }
         tc_fence_after();
+        // All shared-memory loads first (A row and this thread's share of B),
+        // then the splits, so the converter's latency is one load round trip.
+        constexpr int kBPer = kBBytes / 16 / 128;  // float4 of B per thread
         const float4* arow = reinterpret_cast<const float4*>(sA + s * kABytes + row * 128);
+        float4* bb = reinterpret_cast<float4*>(sB + s * kBBytes);
+        float4* blo = reinterpret_cast<float4*>(sBlo + ja * kBBytes);
+        float4 av[8], bv[kBPer];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) av[j] = arow[j ^ (row & 7)];
+#pragma unroll
+        for (int i = 0; i < kBPer; ++i) bv[i] = bb[ct + 128 * i];
         uint32_t hi[32], lo[32];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const float4 v = arow[j ^ (row & 7)];
-          const float x[4] = {v.x, v.y, v.z, v.w};
+          const float x[4] = {av[j].x, av[j].y, av[j].z, av[j].w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             uint32_t h;
@@ -797,24 +819,22 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
         const uint32_t t_a = t_lane + (uint32_t)(Cfg::kAccCols + ja * 2 * kBK);
         tmem_st_32x32b_x32(t_a, hi);
         tmem_st_32x32b_x32(t_a + (uint32_t)kBK, lo);
-        float4* bb = reinterpret_cast<float4*>(sB + s * kBBytes);
-        float4* blo = reinterpret_cast<float4*>(sBlo + s * kBBytes);
         if (p.split_trunc) {
-#pragma unroll 4
-          for (int i = ct; i < kBBytes / 16; i += 128) blo[i] = tf32_trunc_rem4(bb[i]);
+#pragma unroll
+          for (int i = 0; i < kBPer; ++i) blo[ct + 128 * i] = tf32_trunc_rem4(bv[i]);
         } else {
-#pragma unroll 4
-          for (int i = ct; i < kBBytes / 16; i += 128) {
-            const float4 v = bb[i];
-            const float4 h = tf32_hi4(v);
-            bb[i] = h;
-            blo[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+#pragma unroll
+          for (int i = 0; i < kBPer; ++i) {
+            const float4 h = tf32_hi4(bv[i]);
+            bb[ct + 128 * i] = h;
+            blo[ct + 128 * i] =
+                make_float4(bv[i].x - h.x, bv[i].y - h.y, bv[i].z - h.z, bv[i].w - h.w);
           }
         }
         fence_proxy_async_smem();
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(&conv_bar[s]);
+        mbar_arrive(&conv_bar[ja]);
         if (++s == S) { s = 0; ph ^= 1; }
         if (++ja == kAS) { ja = 0; pa ^= 1; }
       }
