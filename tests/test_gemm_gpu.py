@@ -178,6 +178,18 @@ def test_square_4096_sampled_and_linearity(gpu, orc):
     assert torch.equal(c2, c * 2)
 
 
+@pytest.mark.parametrize("k", [1024, 16384])
+def test_all_positive_long_k(gpu, orc, k):
+    """All-positive operands (no cancellation) are the hardest case for the
+    tensor core's accumulation: the 3xTF32 error must stay under 1e-5 and must
+    not grow with K (the accumulator is promoted to fp32 at a fixed interval)."""
+    a = orc.uniform((256, k), 6, 1, 0.0, 1.0)
+    b = orc.uniform((k, 256), 6, 2, 0.0, 1.0)
+    ref = orc.matmul_f64(a, b)
+    c = _host(gpu.sgemm(_dev(a), _dev(b), precision=0))
+    assert orc.rel_frob(c, ref) <= 1e-5
+
+
 def test_tf32_operand_truncation(gpu):
     """The 3xTF32 split relies on how the tensor core turns an fp32 operand
     into TF32: it keeps the top 10 explicit mantissa bits and drops the low 13
