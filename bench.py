@@ -7,7 +7,13 @@ Workloads (default: conv):
             w [128,128,3,3] Kaiming-normal, b ~ U(-0.1,0.1), stride 1, pad 1, seed 1.
             One step = one reference-facing conv call (NCHW in/out).  Replicas at N>1.
   gemm1024  f32 matmul 1024^3, A, B ~ N(0,1), seed 0.  Replicas at N>1.
-  gemm8192  f32 matmul 8192^3, seed 4.  Replicas at N>1.
+  gemm2048, gemm4096, gemm8192, gemm16384
+            square f32 matmul sweep, seed 4.  2048/4096 replicas at N>1;
+            8192/16384 N-split across the GPUs + NCCL all-gather of C (strong
+            scaling: one problem per job).
+  gemm_m16, gemm_m64, gemm_m256
+            skinny f32 matmul M x 8192 x 8192, seed 4 (HBM-bound for M < 128:
+            roofline in GB/s).  Replicas at N>1.
   mlp       3-layer MLP forward, batch 4096, 1024->4096->4096->1024, seed 2.  Replicas.
 
 Timing: W warm-up steps, then K steps between barrier + synchronize, CUDA
@@ -260,53 +266,100 @@ class ConvWorkload:
                                    f"bias, ReLU), {reps} calls")
 
 
+# f32 matmul shapes (M, N, K, seed): the 1024^3 workload and the large-GEMM
+# sweep (square 2048..16384, skinny M = 16/64/256 with N = K = 8192).
+GEMM_SHAPES = {
+    "gemm1024": (1024, 1024, 1024, 0),
+    "gemm2048": (2048, 2048, 2048, 4),
+    "gemm4096": (4096, 4096, 4096, 4),
+    "gemm8192": (8192, 8192, 8192, 4),
+    "gemm16384": (16384, 16384, 16384, 4),
+    "gemm_m16": (16, 8192, 8192, 4),
+    "gemm_m64": (64, 8192, 8192, 4),
+    "gemm_m256": (256, 8192, 8192, 4),
+}
+
+
 class GemmWorkload:
-    def __init__(self, rb, torch, dev, n, seed):
+    """C = A . B, A [M,K] and B [K,N] ~ N(0,1).  Replicas at N>1, except square
+    problems of 8192 and up, which are N-split: every rank holds A and its
+    N/P columns of B, computes its block of C on the tensor cores, and the
+    blocks are all-gathered over NCCL (strong scaling, one problem per job)."""
+
+    def __init__(self, rb, torch, dev, m, n, k, seed, world=1, rank=0):
         self.rb, self.torch, self.dev = rb, torch, dev
-        self.n = n
-        self.seed = seed
-        self.name = f"sgemm_{n}"
-        self.flops = 2.0 * n ** 3
-        a = rb.fill_normal((n, n), seed, 0)
-        b = rb.fill_normal((n, n), seed, 1)
+        self.m, self.n, self.k, self.seed = m, n, k, seed
+        self.name = f"sgemm_{n}" if m == n == k else f"sgemm_{m}x{n}x{k}"
+        self.nsplit = world > 1 and m == n == k and n >= 8192 and n % world == 0
+        self.world, self.rank = world, rank
+        self.scaling = "strong" if self.nsplit else "weak"
+        self.flops = 2.0 * m * n * k                      # one step of the whole job
+        self.n_local = n // world if self.nsplit else n
+        self.kernel_flops = 2.0 * m * self.n_local * k    # the dominant kernel, per GPU
+        self.bytes = 4.0 * (m * k + k * n + m * n)        # algorithmic HBM bytes
+        # HBM-bound where the arithmetic intensity is below the 3xTF32 ridge
+        self.bound = "hbm" if self.flops / self.bytes < 46 else "tensor"
+        a = rb.fill_normal((m, k), seed, 0)
+        b = rb.fill_normal((k, n), seed, 1)
+        if self.nsplit:
+            c0 = rank * self.n_local
+            b = np.ascontiguousarray(b[:, c0:c0 + self.n_local])
         self.host = {"a": a, "b": b}
-        per = 3 * n * n * 4
-        self.nsets = max(1, int(math.ceil(2 * L2_BYTES / per))) if per < 2 * L2_BYTES else 1
-        self.nsets = min(self.nsets, 24)
+        per = 4 * (m * k + k * self.n_local + m * n)
+        self.nsets = 1 if (self.nsplit or per >= 2 * L2_BYTES) else min(
+            24, int(math.ceil(2 * L2_BYTES / per)))
         self.as_ = [torch.from_numpy(a).to(dev) for _ in range(self.nsets)]
         self.bs = [torch.from_numpy(b).to(dev) for _ in range(self.nsets)]
-        self.cs = [torch.empty((n, n), device=dev) for _ in range(self.nsets)]
+        self.cs = [torch.empty((m, n), device=dev) for _ in range(self.nsets)]
         self.i = 0
-        self.config = {"workload": f"f32 matmul {n}x{n}x{n}", "seed": seed,
+        if self.nsplit:
+            from rustorch_b200.dist import NsplitGemm
+            self.gemm = NsplitGemm(rb.get_context(dev.index or 0), world, rank)
+            self.parts = torch.empty((world, m, self.n_local), device=dev)
+            self.c_local = torch.empty((m, self.n_local), device=dev)
+        par = (f"N-split x{world}: A . B[:, cols(rank)] on each GPU + NCCL all-gather of C"
+               if self.nsplit else None)
+        self.config = {"workload": f"f32 matmul {m}x{n}x{k}", "seed": seed,
                        "layout": "row-major A[M,K], B[K,N]",
                        "l2": (f"rotating {self.nsets} operand sets" if self.nsets > 1 else
                               "operands larger than L2")}
-        self.launches_per_step = 1
+        if par:
+            self.config["parallelism_detail"] = par
+        # the all-gather and its repack are two more launches (NCCL + unsplit)
+        self.launches_per_step = 2 if self.nsplit else 1
 
     def step(self):
         k = self.i % self.nsets
         self.i += 1
-        self.rb.sgemm(self.as_[k], self.bs[k], out=self.cs[k], precision=PRECISION[0])
+        if self.nsplit:
+            self.gemm(self.as_[k], self.bs[k], precision=PRECISION[0], out=self.cs[k],
+                      parts=self.parts)
+        else:
+            self.rb.sgemm(self.as_[k], self.bs[k], out=self.cs[k], precision=PRECISION[0])
 
     def kernel_setup(self):
         pass
 
     def kernel_step(self):
-        self.step()
+        k = self.i % self.nsets
+        self.i += 1
+        out = self.c_local if self.nsplit else self.cs[k]
+        self.rb.sgemm(self.as_[k], self.bs[k], out=out, precision=PRECISION[0])
 
     def e2e_setup(self):
-        rb, torch = self.rb, self.torch
+        rb = self.rb
         ctx = rb.get_context(self.dev.index or 0)
         self.pinned = {}
-        for key, arr in list(self.host.items()) + [("c", None)]:
-            nb = self.n * self.n * 4
+        sizes = {"a": self.m * self.k * 4, "b": self.k * self.n_local * 4,
+                 "c": self.m * self.n * 4}
+        for key in ("a", "b", "c"):
             p = ctypes.c_void_p()
-            rb.call("rtb_host_alloc", ctx.handle, ctypes.byref(p), nb)
-            if arr is not None:
-                ctypes.memmove(p, arr.ctypes.data, nb)
-            self.pinned[key] = (p, nb)
-        self.h2d_bytes = 2 * self.n * self.n * 4
-        self.d2h_bytes = self.n * self.n * 4
+            rb.call("rtb_host_alloc", ctx.handle, ctypes.byref(p), sizes[key])
+            if key in self.host:
+                ctypes.memmove(p, self.host[key].ctypes.data, sizes[key])
+            self.pinned[key] = (p, sizes[key])
+        self.h2d_bytes = sizes["a"] + sizes["b"]
+        self.d2h_bytes = sizes["c"]
 
     def e2e_step(self):
         rb = self.rb
@@ -316,10 +369,13 @@ class GemmWorkload:
         for key, dst in (("a", a), ("b", b)):
             p, nb = self.pinned[key]
             rb.call("rtb_memcpy_h2d", ctx.handle, ctypes.c_void_p(dst.data_ptr()), p, nb, stream)
-        n = self.n
-        rb.call("rtb_sgemm", ctx.handle, n, n, n, ctypes.c_void_p(a.data_ptr()), n, 0,
-                ctypes.c_void_p(b.data_ptr()), n, 0, None, rb.ACT_NONE,
-                ctypes.c_void_p(c.data_ptr()), n, PRECISION[0], stream)
+        if self.nsplit:
+            self.gemm(a, b, precision=PRECISION[0], out=c, parts=self.parts)
+        else:
+            rb.call("rtb_sgemm", ctx.handle, self.m, self.n, self.k,
+                    ctypes.c_void_p(a.data_ptr()), self.k, 0, ctypes.c_void_p(b.data_ptr()),
+                    self.n, 0, None, rb.ACT_NONE, ctypes.c_void_p(c.data_ptr()), self.n,
+                    PRECISION[0], stream)
         p, nb = self.pinned["c"]
         rb.call("rtb_memcpy_d2h", ctx.handle, p, ctypes.c_void_p(c.data_ptr()), nb, stream)
 
@@ -328,23 +384,27 @@ class GemmWorkload:
         for p, _ in self.pinned.values():
             self.rb.call("rtb_host_free", ctx.handle, p)
 
+    def close(self):
+        if self.nsplit:
+            self.gemm.close()
+
     def cpu_sample(self, threads):
         """matrixmultiply restatement (single-threaded, as the reference builds
         it) on a row sample of the same product."""
         from oracle import oracle as orc
-        n = self.n
-        a = orc.normal((n, n), self.seed, 0)
-        b = orc.normal((n, n), self.seed, 1)
-        rows = max(8, min(n, int(2e9 / (2 * n * n))))
+        m, n, k = self.m, self.n, self.k
+        rows = max(1, min(m, int(2e9 / (2 * n * k))))
+        a = orc.normal((rows, k), self.seed, 0)   # the first rows of A
+        b = orc.normal((k, n), self.seed, 1)
         t0 = time.perf_counter()
         reps = 0
         while True:
-            orc.sgemm_mm(a[:rows], b, threads=1)
+            orc.sgemm_mm(a, b, threads=1)
             reps += 1
             if time.perf_counter() - t0 > 10.0 or reps >= 10:
                 break
         dt = (time.perf_counter() - t0) / reps
-        return 2.0 * rows * n * n / dt / 1e12, (f"{rows} of {n} rows of A per call, "
+        return 2.0 * rows * n * k / dt / 1e12, (f"{rows} of {m} rows of A per call, "
                                                 f"single-threaded blocked sgemm, {reps} calls")
 
 
@@ -557,11 +617,20 @@ class MlpWorkload:
 
 WORKLOADS = {
     "conv": lambda rb, torch, dev: ConvWorkload(rb, torch, dev),
-    "gemm1024": lambda rb, torch, dev: GemmWorkload(rb, torch, dev, 1024, 0),
-    "gemm8192": lambda rb, torch, dev: GemmWorkload(rb, torch, dev, 8192, 4),
     "resnet18": lambda rb, torch, dev: ResNet18Workload(rb, torch, dev),
     "mlp": lambda rb, torch, dev: MlpWorkload(rb, torch, dev),
 }
+
+
+def _gemm_factory(m, n, k, seed):
+    def make(rb, torch, dev):
+        rank, world, _ = _dist_env()
+        return GemmWorkload(rb, torch, dev, m, n, k, seed, world, rank)
+    return make
+
+
+for _name, (_m, _n, _k, _seed) in GEMM_SHAPES.items():
+    WORKLOADS[_name] = _gemm_factory(_m, _n, _k, _seed)
 
 
 # ------------------------------------------------------------------ timing
@@ -616,12 +685,15 @@ def run_ours(args):
     peaks = _peaks()
 
     unit = getattr(wl, "unit", "TFLOP/s")
+    scaling = getattr(wl, "scaling", "weak")
 
     def rate(total_ms, ranks):
-        # whole-job throughput in the workload's unit over `ranks` GPUs
+        # whole-job throughput in the workload's unit over `ranks` GPUs; with
+        # strong scaling one step is one problem for the whole job
+        jobs = 1 if scaling == "strong" else ranks
         if unit == "img/s":
-            return ranks * wl.B * args.steps / (total_ms / 1e3)
-        return ranks * wl.flops * args.steps / (total_ms / 1e3) / 1e12
+            return jobs * wl.B * args.steps / (total_ms / 1e3)
+        return jobs * wl.flops * args.steps / (total_ms / 1e3) / 1e12
 
     with ClockSampler(dev) as clk:
         ms = _time_steps(torch, wl.step, args.steps, args.warmup, dev, dist)
@@ -631,9 +703,29 @@ def run_ours(args):
     # dominant kernel alone, CUDA events on its launch stream
     wl.kernel_setup()
     kms = _time_steps(torch, wl.kernel_step, args.steps, max(3, args.warmup), dev, None)
-    k_tflops = wl.flops * args.steps / (kms / 1e3) / 1e12
+    kflops = getattr(wl, "kernel_flops", wl.flops)
+    k_tflops = kflops * args.steps / (kms / 1e3) / 1e12
     tf32_peak = peaks["bf16_tflops"] / 2.0
     roof_peak = tf32_peak / MMAS_PER_MAC[0]  # 3xTF32: three tensor-core MMAs per algorithmic MAC
+    if getattr(wl, "bound", "tensor") == "hbm":
+        # below the ridge: bytes that must cross HBM per launch / launch time
+        k_gbs = wl.bytes * args.steps / (kms / 1e3) / 1e9
+        roofline = {"bound": "hbm", "achieved": round(k_gbs, 1), "peak": peaks["hbm_gbs"],
+                    "unit": "GB/s", "frac": round(k_gbs / peaks["hbm_gbs"], 4),
+                    "traffic": TRAFFIC.get(args.workload, (None,))[0],
+                    "peak_basis": f"{peaks['basis']} HBM copy {peaks['hbm_gbs']} GB/s",
+                    "algorithmic_bytes": wl.bytes, "kernel_tflops": round(k_tflops, 3),
+                    "kernel_ms": round(kms / args.steps, 5)}
+    else:
+        roofline = {"bound": "tensor", "achieved": round(k_tflops, 3),
+                    "peak": round(roof_peak, 3), "unit": "TFLOP/s",
+                    "frac": round(k_tflops / roof_peak, 4),
+                    "traffic": TRAFFIC.get(args.workload, (None,))[0],
+                    "traffic_source": TRAFFIC.get(args.workload, (None, None))[1],
+                    "peak_basis": f"{peaks['basis']} bf16 {peaks['bf16_tflops']} TFLOP/s "
+                                  f"/ 2 (TF32 rate) / {MMAS_PER_MAC[0]} (MMAs per MAC)",
+                    "tensor_pipe_frac": round(MMAS_PER_MAC[0] * k_tflops / tf32_peak, 4),
+                    "kernel_ms": round(kms / args.steps, 5)}
 
     # end to end through the C ABI with host buffers
     wl.e2e_setup()
@@ -647,25 +739,21 @@ def run_ours(args):
 
     if rank == 0:
         cpu_val, sample = wl.cpu_sample(os.cpu_count())
-        par = (f"batch-sharded x{world} (no collective)" if unit == "img/s"
-               else f"replicas x{world}")
+        if scaling == "strong":
+            par = f"N-split x{world} + NCCL all-gather"
+        elif unit == "img/s":
+            par = f"batch-sharded x{world} (no collective)"
+        else:
+            par = f"replicas x{world}"
         line = {
             "metric": f"{wl.name} {unit} ({args.precision.upper()}, fp32 in/out)",
             "value": round(value, 3), "unit": unit, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None,
+            "scaling": scaling, "vs_baseline": None,
             "dtype": "f32 (3xTF32 tensor-core split)" if PRECISION[0] == 0 else "f32 (TF32 tensor core)",
             "data": "synthetic (SplitMix64/Box-Muller, seeded)",
             "config": dict(wl.config, parallelism=par),
-            "roofline": {"bound": "tensor", "achieved": round(k_tflops, 3),
-                         "peak": round(roof_peak, 3), "unit": "TFLOP/s",
-                         "frac": round(k_tflops / roof_peak, 4),
-                         "traffic": TRAFFIC.get(args.workload, (None,))[0],
-                         "traffic_source": TRAFFIC.get(args.workload, (None, None))[1],
-                         "peak_basis": f"{peaks['basis']} bf16 {peaks['bf16_tflops']} TFLOP/s "
-                                       f"/ 2 (TF32 rate) / {MMAS_PER_MAC[0]} (MMAs per MAC)",
-                         "tensor_pipe_frac": round(MMAS_PER_MAC[0] * k_tflops / tf32_peak, 4),
-                         "kernel_ms": round(kms / args.steps, 5)},
+            "roofline": roofline,
             "cpu_baseline": {"value": round(cpu_val, 6), "unit": unit,
                              "cores": os.cpu_count(), "kind": "port", "sample": sample},
             "e2e": {"value": round(e2e, 3), "unit": unit,
@@ -674,6 +762,8 @@ def run_ours(args):
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)
+    if hasattr(wl, "close"):
+        wl.close()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -706,10 +796,11 @@ def run_reference(args):
         cfg = {"workload": "3-layer MLP forward 4096x(1024->4096->4096->1024)", "seed": 2}
         unit = "TFLOP/s"
     else:
-        n = 1024 if args.workload == "gemm1024" else 8192
+        m, n, k, seed = GEMM_SHAPES[args.workload]
         wl = GemmWorkload.__new__(GemmWorkload)
-        wl.n, wl.seed, wl.flops, wl.name = n, (0 if n == 1024 else 4), 2.0 * n ** 3, f"sgemm_{n}"
-        cfg = {"workload": f"f32 matmul {n}x{n}x{n}", "seed": wl.seed}
+        wl.m, wl.n, wl.k, wl.seed, wl.flops = m, n, k, seed, 2.0 * m * n * k
+        wl.name = f"sgemm_{n}" if m == n == k else f"sgemm_{m}x{n}x{k}"
+        cfg = {"workload": f"f32 matmul {m}x{n}x{k}", "seed": seed}
         unit = "TFLOP/s"
     name = getattr(wl, "name", args.workload)
     vals, samples = [], []

@@ -35,12 +35,15 @@ def broadcast_id(group=None, make_id=None) -> bytes:
     import torch.distributed as dist
 
     rank = dist.get_rank(group)
-    buf = torch.zeros(128, dtype=torch.uint8)
+    # an NCCL group moves CUDA tensors only
+    dev = (torch.device("cuda", torch.cuda.current_device())
+           if dist.get_backend(group) == "nccl" else torch.device("cpu"))
+    buf = torch.zeros(128, dtype=torch.uint8, device=dev)
     if rank == 0:
         raw = make_id() if make_id else _nccl_unique_id()
-        buf = torch.frombuffer(bytearray(raw), dtype=torch.uint8).clone()
+        buf.copy_(torch.frombuffer(bytearray(raw), dtype=torch.uint8))
     dist.broadcast(buf, src=0, group=group)
-    return bytes(buf.tolist())
+    return bytes(buf.cpu().tolist())
 
 
 def _nccl_unique_id() -> bytes:
@@ -66,15 +69,17 @@ class NsplitGemm:
             call("rtb_nccl_comm_destroy", self.comm)
             self.comm = None
 
-    def __call__(self, a, b_local, precision: int = _lib.PREC_DEFAULT):
+    def __call__(self, a, b_local, precision: int = _lib.PREC_DEFAULT, out=None, parts=None):
         """a: [M,K] (replicated), b_local: [K, N/world] (this rank's columns),
-        both contiguous float32 CUDA tensors; returns C [M, N] on every rank."""
+        both contiguous float32 CUDA tensors; returns C [M, N] on every rank
+        (in `out` when given; `parts` is the [world, M, N/world] gather buffer)."""
         import torch
         M, K = a.shape
         nl = b_local.shape[1]
         N = nl * self.world
-        parts = torch.empty((self.world, M, nl), dtype=torch.float32, device=a.device)
-        c = torch.empty((M, N), dtype=torch.float32, device=a.device)
+        if parts is None:
+            parts = torch.empty((self.world, M, nl), dtype=torch.float32, device=a.device)
+        c = out if out is not None else torch.empty((M, N), dtype=torch.float32, device=a.device)
         stream = ctypes.c_void_p(torch.cuda.current_stream(a.device).cuda_stream)
         call("rtb_sgemm_nsplit_allgather", self.ctx.handle, self.comm, M, N, K,
              ctypes.c_void_p(a.data_ptr()), ctypes.c_void_p(b_local.data_ptr()),
