@@ -52,6 +52,12 @@ static EncodeTiledFn get_encode_tiled() {
 
 int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1,
                  uint64_t row_stride_elems, uint32_t box0, uint32_t box1, bool atom32) {
+  return make_tmap_2d_swz(map, base, dim0, dim1, row_stride_elems, box0, box1,
+                          atom32 ? kTmapSwizzle128Atom32 : kTmapSwizzle128);
+}
+
+int make_tmap_2d_swz(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1,
+                     uint64_t row_stride_elems, uint32_t box0, uint32_t box1, int swizzle) {
   EncodeTiledFn enc = get_encode_tiled();
   if (!enc) return set_error(RTB_E_CUDA, "cuTensorMapEncodeTiled unavailable");
   if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (row_stride_elems * 4) % 16 != 0)
@@ -62,7 +68,9 @@ int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides,
                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                   swizzle == kTmapSwizzle128Atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                   : swizzle == kTmapSwizzle128     ? CU_TENSOR_MAP_SWIZZLE_128B
+                                                    : CU_TENSOR_MAP_SWIZZLE_NONE,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     char buf[160];
@@ -451,7 +459,15 @@ static int sgemm_one(rtb_ctx* ctx, int64_t M, int64_t N, int64_t K, const float*
       d.B = wsB; d.ldb = Kp; d.b_mn_major = 0;
     }
   }
-  if (st == RTB_OK) st = gemm_run(ctx, d, s);
+  if (st == RTB_OK) {
+    // Few rows: a stream over B on the CUDA cores beats a padded 128-row
+    // tensor-core tile (RTB_SMALLM=0 turns the small-M path off).
+    static const bool smallm_on = [] {
+      const char* v = std::getenv("RTB_SMALLM");
+      return !(v && v[0] == '0');
+    }();
+    st = (smallm_on && M <= kSmallMMax) ? smallm_run(ctx, d, s) : gemm_run(ctx, d, s);
+  }
   ws_free(wsA, s);
   ws_free(wsB, s);
   return st;

@@ -208,21 +208,26 @@ __device__ __forceinline__ float4 tf32_trunc_rem4(float4 v) {
   return make_float4(v.x - hx, v.y - hy, v.z - hz, v.w - hw);
 }
 
-// The epilogue functions below take `sb`: the 32 bias values of the chunk,
-// staged once per tile in shared memory (zero past N), or null without bias.
+// The epilogue functions below take `sb`: the shared-window address of the
+// chunk's 32 bias values, staged once per tile (zero past N), used when
+// p.bias is set; shared memory is addressed through 32-bit shared-window
+// addresses (ld/st.shared) throughout.
 // Every global load of a chunk is issued before its first store, so loads are
 // not serialised behind stores the compiler cannot prove disjoint.
 
 // Row-major epilogue for one thread's row m and 32 consecutive columns n0..n0+31.
 __device__ __forceinline__ void epilogue_store32(const GemmParams& p, int m, int n0,
-                                                 const uint32_t (&r)[32], const float* sb) {
+                                                 const uint32_t (&r)[32], uint32_t sb) {
   if (m >= p.M) return;
   float v[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-  if (sb) {
+  if (p.bias) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] += sb[j];
+    for (int j = 0; j < 32; j += 4) {
+      const float4 b = lds128(sb + 4 * j);
+      v[j] += b.x; v[j + 1] += b.y; v[j + 2] += b.z; v[j + 3] += b.w;
+    }
   }
   float* crow = p.C + (int64_t)m * p.ldc;
   const float* rrow = p.residual ? p.residual + (int64_t)m * p.ldr : nullptr;
@@ -260,15 +265,18 @@ __device__ __forceinline__ void epilogue_store32(const GemmParams& p, int m, int
 // this thread's row (32 fp32) into the 128 x 32 staging chunk, 128-byte
 // swizzled (16-byte unit j of row r at position j ^ (r % 8)) to match the
 // store map and keep the 8-thread phases of the writes conflict-free.
-__device__ __forceinline__ void epilogue_stage_rowmajor(const GemmParams& p, uint8_t* buf, int row,
+__device__ __forceinline__ void epilogue_stage_rowmajor(const GemmParams& p, uint32_t buf, int row,
                                                         int n0, int m, const uint32_t (&r)[32],
-                                                        const float* sb) {
+                                                        uint32_t sb) {
   float v[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-  if (sb) {
+  if (p.bias) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] += sb[j];
+    for (int j = 0; j < 32; j += 4) {
+      const float4 b = lds128(sb + 4 * j);
+      v[j] += b.x; v[j + 1] += b.y; v[j + 2] += b.z; v[j + 3] += b.w;
+    }
   }
   if (p.residual && m < p.M) {
     const float* rrow = p.residual + (int64_t)m * p.ldr;
@@ -290,10 +298,10 @@ __device__ __forceinline__ void epilogue_stage_rowmajor(const GemmParams& p, uin
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.0f);
   }
-  float4* rowp = reinterpret_cast<float4*>(buf + row * 128);
+  const uint32_t rowp = buf + row * 128;
 #pragma unroll
   for (int j = 0; j < 8; ++j)
-    rowp[j ^ (row & 7)] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    sts128(rowp + ((j ^ (row & 7)) << 4), make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
 }
 
 // NCHW epilogue: transpose the 128-pixel x 32-channel chunk through shared
@@ -303,11 +311,11 @@ __device__ __forceinline__ void epilogue_stage_rowmajor(const GemmParams& p, uin
 // applying ReLU there.  A thread keeps the same 4-pixel group (et % 32) for
 // all of its channels, so the pixel -> (image, offset) division happens once
 // per chunk, and the 8 loads are issued before the 8 stores.
-__device__ __forceinline__ void epilogue_nchw_chunk(const GemmParams& p, float* buf, int row,
+__device__ __forceinline__ void epilogue_nchw_chunk(const GemmParams& p, uint32_t buf, int row,
                                                     int et, int m0, int n0,
-                                                    const uint32_t (&r)[32], const float* sb) {
+                                                    const uint32_t (&r)[32], uint32_t sb) {
 #pragma unroll
-  for (int j = 0; j < 32; ++j) buf[j * kBM + row] = __uint_as_float(r[j]);
+  for (int j = 0; j < 32; ++j) sts32(buf + (j * kBM + row) * 4, __uint_as_float(r[j]));
   named_bar_sync(1, 128);
   const int q = et & 31;   // 4-pixel group
   const int cw = et >> 5;  // channels cw, cw+4, ..., cw+28 of the chunk
@@ -326,8 +334,8 @@ __device__ __forceinline__ void epilogue_nchw_chunk(const GemmParams& p, float* 
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const int ch = cw + 4 * (4 * h + k);
-          o[k] = *reinterpret_cast<const float4*>(buf + ch * kBM + 4 * q);
-          const float bv = sb ? sb[ch] : 0.0f;
+          o[k] = lds128(buf + (ch * kBM + 4 * q) * 4);
+          const float bv = p.bias ? lds32(sb + ch * 4) : 0.0f;
           o[k].x += bv; o[k].y += bv; o[k].z += bv; o[k].w += bv;
           if (rbase && n0 + ch < p.N) {
             const float4 r4 = __ldg(reinterpret_cast<const float4*>(rbase + (int64_t)ch * p.hw));
@@ -364,8 +372,8 @@ __device__ __forceinline__ void epilogue_nchw_chunk(const GemmParams& p, float* 
       for (int k = 0; k < 8; ++k) {
         const int ch = cw + 4 * k;
         if (n0 + ch >= p.N) continue;
-        const float4 o = *reinterpret_cast<const float4*>(buf + ch * kBM + 4 * q);
-        const float bv = sb ? sb[ch] : 0.0f;
+        const float4 o = lds128(buf + (ch * kBM + 4 * q) * 4);
+        const float bv = p.bias ? lds32(sb + ch * 4) : 0.0f;
         float sv[4] = {o.x + bv, o.y + bv, o.z + bv, o.w + bv};
         if (p.residual) {
 #pragma unroll
@@ -602,10 +610,10 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
     // One finished 128 x 32 chunk (this thread's row, columns n0..n0+31) to C.
     auto emit = [&](int tm, int tn, int c, int m, const uint32_t (&r)[32]) {
       const int n0 = tn * BN + c;
-      const float* sb = p.bias ? sBias + c : nullptr;
+      const uint32_t sb = smem_u32(sBias) + 4 * c;
       if (p.c_tma) {
         uint8_t* stg = sOut + (chunk % Cfg::kOutBufs) * kOutChunkBytes;
-        epilogue_stage_rowmajor(p, stg, row, n0, m, r, sb);
+        epilogue_stage_rowmajor(p, smem_u32(stg), row, n0, m, r, sb);
         fence_proxy_async_smem();
         named_bar_sync(1, 128);
         if (et == 0) {
@@ -617,7 +625,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
         named_bar_sync(1, 128);
         ++chunk;
       } else if (p.out_mode == 1) {
-        float* buf = reinterpret_cast<float*>(sOut + (chunk % Cfg::kOutBufs) * kOutChunkBytes);
+        const uint32_t buf = smem_u32(sOut + (chunk % Cfg::kOutBufs) * kOutChunkBytes);
         epilogue_nchw_chunk(p, buf, row, et, tm * kBM, n0, r, sb);
         ++chunk;
       } else {
@@ -643,7 +651,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
         named_bar_sync(2, 128);
         for (int i = et; i < BN; i += 128) {
           const int n = tn * BN + i;
-          sBias[i] = n < p.N ? __ldg(p.bias + n) : 0.0f;
+          sts32(smem_u32(sBias) + 4 * i, n < p.N ? __ldg(p.bias + n) : 0.0f);
         }
       }
       for (int a = 0; a < units; ++a, ++g) {
@@ -792,14 +800,14 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
         // All shared-memory loads first (A row and this thread's share of B),
         // then the splits, so the converter's latency is one load round trip.
         constexpr int kBPer = kBBytes / 16 / 128;  // float4 of B per thread
-        const float4* arow = reinterpret_cast<const float4*>(sA + s * kABytes + row * 128);
-        float4* bb = reinterpret_cast<float4*>(sB + s * kBBytes);
-        float4* blo = reinterpret_cast<float4*>(sBlo + ja * kBBytes);
+        const uint32_t arow = smem_u32(sA + s * kABytes + row * 128);
+        const uint32_t bb = smem_u32(sB + s * kBBytes);
+        const uint32_t blo = smem_u32(sBlo + ja * kBBytes);
         float4 av[8], bv[kBPer];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) av[j] = arow[j ^ (row & 7)];
+        for (int j = 0; j < 8; ++j) av[j] = lds128(arow + ((j ^ (row & 7)) << 4));
 #pragma unroll
-        for (int i = 0; i < kBPer; ++i) bv[i] = bb[ct + 128 * i];
+        for (int i = 0; i < kBPer; ++i) bv[i] = lds128(bb + (ct + 128 * i) * 16);
         uint32_t hi[32], lo[32];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -821,14 +829,14 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
         tmem_st_32x32b_x32(t_a + (uint32_t)kBK, lo);
         if (p.split_trunc) {
 #pragma unroll
-          for (int i = 0; i < kBPer; ++i) blo[ct + 128 * i] = tf32_trunc_rem4(bv[i]);
+          for (int i = 0; i < kBPer; ++i) sts128(blo + (ct + 128 * i) * 16, tf32_trunc_rem4(bv[i]));
         } else {
 #pragma unroll
           for (int i = 0; i < kBPer; ++i) {
             const float4 h = tf32_hi4(bv[i]);
-            bb[ct + 128 * i] = h;
-            blo[ct + 128 * i] =
-                make_float4(bv[i].x - h.x, bv[i].y - h.y, bv[i].z - h.z, bv[i].w - h.w);
+            sts128(bb + (ct + 128 * i) * 16, h);
+            sts128(blo + (ct + 128 * i) * 16,
+                   make_float4(bv[i].x - h.x, bv[i].y - h.y, bv[i].z - h.z, bv[i].w - h.w));
           }
         }
         fence_proxy_async_smem();

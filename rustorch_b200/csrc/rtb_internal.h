@@ -59,6 +59,11 @@ struct DeviceGuard {
 // 128-byte swizzle with 16-byte atoms, or 32-byte atoms when atom32 is set.
 int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1,
                  uint64_t row_stride_elems, uint32_t box0, uint32_t box1, bool atom32);
+// Same with the shared-memory layout chosen explicitly (no swizzle allows an
+// inner box wider than 128 bytes).
+constexpr int kTmapSwizzleNone = 0, kTmapSwizzle128 = 1, kTmapSwizzle128Atom32 = 2;
+int make_tmap_2d_swz(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1,
+                     uint64_t row_stride_elems, uint32_t box0, uint32_t box1, int swizzle);
 
 // 4-D im2col map over an NHWC tensor [N, H, W, Cp] for a forward conv with
 // filter R x S, stride (sh, sw), padding (ph, pw): channels_per_pixel x
@@ -98,6 +103,13 @@ struct GemmDesc {
 
 // Validated launch of the tcgen05 engine (A/B already TMA-compatible).
 int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream);
+
+// Small-M path (M <= kSmallMMax, no conv producer): fp32 FMA on the CUDA cores
+// with B streamed once from HBM (rtb_smallm.cu).  Measured on B200 for
+// M x 8192 x 8192: 87 / 113 / 169 us at M = 1 / 16 / 32 against 186 us for the
+// 128-row tensor-core tile; at M = 48 and 64 the tensor path is faster.
+constexpr int64_t kSmallMMax = 32;
+int smallm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream);
 
 // Aux kernels (rtb_aux.cu).
 int launch_pack_kmajor(const float* src, int64_t rows, int64_t k, int64_t rs, int64_t cs,

@@ -196,12 +196,51 @@ def test_tf32_operand_truncation(gpu):
     (round toward zero).  x = 1 + 0.75 * 2^-10 is 1.0 truncated, 1 + 2^-10
     rounded; the product with 1.0 shows which one the hardware used."""
     x = 1.0 + 2.0 ** -11 + 2.0 ** -12
+    # 128 rows: above the small-M threshold, so the tensor-core path runs
     for sign in (1.0, -1.0):
-        a = torch.tensor([[sign * x]], device="cuda")
+        a = torch.full((128, 1), sign * x, device="cuda")
         one = torch.ones((1, 1), device="cuda")
-        ca = _host(gpu.sgemm(a, one, precision=gpu.PREC_TF32))[0, 0]
-        cb = _host(gpu.sgemm(one, a, precision=gpu.PREC_TF32))[0, 0]
-        assert ca == sign * 1.0 and cb == sign * 1.0, (ca, cb)
+        ca = _host(gpu.sgemm(a, one, precision=gpu.PREC_TF32))
+        cb = _host(gpu.sgemm(torch.ones((128, 1), device="cuda"), a[:1], precision=gpu.PREC_TF32))
+        assert np.all(ca == sign * 1.0) and np.all(cb == sign * 1.0), (ca[0], cb[0])
         # and 3xTF32 recovers the full fp32 value
-        c3 = _host(gpu.sgemm(a, one, precision=gpu.PREC_3XTF32))[0, 0]
-        assert c3 == np.float32(sign * x), c3
+        c3 = _host(gpu.sgemm(a, one, precision=gpu.PREC_3XTF32))
+        assert np.all(c3 == np.float32(sign * x)), c3[0]
+
+
+@pytest.mark.parametrize("m", [1, 7, 16, 17, 32, 33, 64])
+@pytest.mark.parametrize("n,k", [(1, 1), (100, 31), (257, 1000), (1024, 4096)])
+@pytest.mark.parametrize("trans_b", [0, 1])
+def test_small_m_path(gpu, orc, m, n, k, trans_b):
+    """M <= 32 runs the CUDA-core small-M path (exact fp32 FMAs, B streamed
+    once, K split across CTAs with an ordered fix-up); 33 and 64 check the
+    switch back to the tensor-core path: both B layouts (the matmul rhs [K,N]
+    and Linear's transposed weight view of [N,K]), bias and ReLU, ragged N
+    and K."""
+    a = orc.normal((m, k), 9, 1)
+    w = orc.normal((n, k), 9, 2) if trans_b else orc.normal((k, n), 9, 2)
+    b = w.T if trans_b else w
+    bias = orc.uniform((n,), 9, 3, -0.5, 0.5)
+    pre = orc.matmul_f64(a, np.ascontiguousarray(b)) + bias.astype(np.float64)
+    bd = _dev(w).t() if trans_b else _dev(w)
+    for prec in (0, 1):
+        y = _host(gpu.sgemm(_dev(a), bd, bias=_dev(bias), act=gpu.ACT_RELU, precision=prec))
+        ref = np.maximum(pre, 0.0)
+        tol_prec = 0 if m <= 32 else prec  # the small-M path is exact fp32 in both modes
+        assert orc.rel_frob(y, ref) <= TOL[tol_prec]
+        # outputs here are ~sqrt(K) in size: the 1e-5 zero band is scaled by
+        # their rms (it is written for the O(1) outputs of the workloads)
+        scale = max(1.0, float(np.sqrt(np.mean(pre * pre))))
+        assert _relu_pattern_ok(y / scale, pre / scale, tol_prec)
+
+
+@pytest.mark.parametrize("m", [16, 64])
+def test_small_m_skinny_8192(gpu, orc, m):
+    """The skinny M x 8192 x 8192 workloads (M=16 on the small-M path, M=64
+    on the tensor cores) against float64 on a sample of columns."""
+    a = orc.normal((m, 8192), 4, 0)
+    b = orc.normal((8192, 8192), 4, 1)
+    c = _host(gpu.sgemm(_dev(a), _dev(b)))
+    cols = np.random.default_rng(2).integers(0, 8192, 256)
+    ref = a.astype(np.float64) @ b[:, cols].astype(np.float64)
+    assert orc.rel_frob(c[:, cols], ref) <= TOL[0]
