@@ -47,8 +47,9 @@ L2_BYTES = 126 * 1024 * 1024
 # one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum); the capture and
 # its command are summarised in the named profiles/ file.
 TRAFFIC = {
-    "conv": (13.51e6, "profiles/conv2d_bias_relu_r50s2_3x3.md"),
-    "gemm8192": (3.458e9, "profiles/sgemm_8192_3xtf32.md"),
+    "conv": (13.52e6, "profiles/conv2d_bias_relu_r50s2_3x3.md"),
+    "gemm8192": (3.485e9, "profiles/sgemm_8192_3xtf32.md"),
+    "gemm_m16": (273.3e6, "profiles/sgemm_small_m16_8192.md"),
 }
 PRECISION = [0]  # rtb precision enum used by every workload call (0 = 3xTF32, 1 = TF32)
 MMAS_PER_MAC = [3]
@@ -713,6 +714,7 @@ def run_ours(args):
         roofline = {"bound": "hbm", "achieved": round(k_gbs, 1), "peak": peaks["hbm_gbs"],
                     "unit": "GB/s", "frac": round(k_gbs / peaks["hbm_gbs"], 4),
                     "traffic": TRAFFIC.get(args.workload, (None,))[0],
+                    "traffic_source": TRAFFIC.get(args.workload, (None, None))[1],
                     "peak_basis": f"{peaks['basis']} HBM copy {peaks['hbm_gbs']} GB/s",
                     "algorithmic_bytes": wl.bytes, "kernel_tflops": round(k_tflops, 3),
                     "kernel_ms": round(kms / args.steps, 5)}
