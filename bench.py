@@ -139,6 +139,47 @@ def _dist_env():
     return rank, world, local
 
 
+class E2EPipeline:
+    """Round-robin slots for the end-to-end measurement, each with its own CUDA
+    stream and its own device and pinned host buffers: step i runs its H2D
+    copies, its call and its D2H copy in order on slot i % depth, so one step's
+    upload overlaps the previous step's call and the one before's download
+    (PCIe is full duplex).  Every step still moves its own inputs and result."""
+
+    def __init__(self, torch, dev, depth):
+        self.torch, self.dev, self.depth = torch, dev, depth
+        self.streams = [torch.cuda.Stream(dev) for _ in range(depth)]
+        self.i = 0
+
+    def next(self):
+        k = self.i % self.depth
+        self.i += 1
+        return k, self.streams[k], ctypes.c_void_p(self.streams[k].cuda_stream)
+
+    def begin(self, ev):
+        for st in self.streams:
+            st.wait_event(ev)
+
+    def join(self, cur):
+        for st in self.streams:
+            e = self.torch.cuda.Event()
+            e.record(st)
+            cur.wait_event(e)
+
+
+def _pinned_copy(rb, ctx, arr):
+    p = ctypes.c_void_p()
+    rb.call("rtb_host_alloc", ctx.handle, ctypes.byref(p), arr.nbytes)
+    ctypes.memmove(p, arr.ctypes.data, arr.nbytes)
+    return p
+
+
+def _pinned_empty(rb, ctx, nbytes):
+    p = ctypes.c_void_p()
+    rb.call("rtb_host_alloc", ctx.handle, ctypes.byref(p), nbytes)
+    return p
+
+
 # ------------------------------------------------------------------ workloads
 class ConvWorkload:
     name = "conv2d_bias_relu_resnet50_3x3"
@@ -209,41 +250,43 @@ class ConvWorkload:
     def e2e_setup(self):
         rb, torch = self.rb, self.torch
         ctx = rb.get_context(self.dev.index or 0)
-        self.pinned = {}
-        for key, arr in self.host.items():
-            p = ctypes.c_void_p()
-            rb.call("rtb_host_alloc", ctx.handle, ctypes.byref(p), arr.nbytes)
-            ctypes.memmove(p, arr.ctypes.data, arr.nbytes)
-            self.pinned[key] = (p, arr.nbytes)
-        p = ctypes.c_void_p()
+        self.pipe = E2EPipeline(torch, self.dev, 3)
         ybytes = self.N * self.Co * self.H * self.W * 4
-        rb.call("rtb_host_alloc", ctx.handle, ctypes.byref(p), ybytes)
-        self.pinned["y"] = (p, ybytes)
-        self.dx = torch.empty((self.N, self.C, self.H, self.W), device=self.dev)
-        self.dw = torch.empty_like(self.w)
-        self.db = torch.empty_like(self.b)
-        self.h2d_bytes = sum(v[1] for k, v in self.pinned.items() if k != "y")
+        self.slots = []
+        for _ in range(self.pipe.depth):
+            slot = {key: (_pinned_copy(rb, ctx, arr), arr.nbytes) for key, arr in self.host.items()}
+            slot["y"] = (_pinned_empty(rb, ctx, ybytes), ybytes)
+            slot["dx"] = torch.empty((self.N, self.C, self.H, self.W), device=self.dev)
+            slot["dw"] = torch.empty_like(self.w)
+            slot["db"] = torch.empty_like(self.b)
+            slot["dy"] = torch.empty((self.N, self.Co, self.H, self.W), device=self.dev)
+            self.slots.append(slot)
+        self.h2d_bytes = sum(arr.nbytes for arr in self.host.values())
         self.d2h_bytes = ybytes
 
     def e2e_step(self):
         rb = self.rb
         ctx = rb.get_context(self.dev.index or 0)
-        stream = ctypes.c_void_p(self.torch.cuda.current_stream(self.dev).cuda_stream)
-        for key, dst in (("x", self.dx), ("w", self.dw), ("b", self.db)):
-            p, nb = self.pinned[key]
+        k, _, stream = self.pipe.next()
+        slot = self.slots[k]
+        for key, dst in (("x", slot["dx"]), ("w", slot["dw"]), ("b", slot["db"])):
+            p, nb = slot[key]
             rb.call("rtb_memcpy_h2d", ctx.handle, ctypes.c_void_p(dst.data_ptr()), p, nb, stream)
-        y = self.ys[0]
+        y = slot["dy"]
         rb.call("rtb_conv2d_fwd", ctx.handle, self.N, self.C, self.H, self.W, self.Co, 3, 3, 1, 1, 1,
-                1, ctypes.c_void_p(self.dx.data_ptr()), rb.LAYOUT_NCHW,
-                ctypes.c_void_p(self.dw.data_ptr()), ctypes.c_void_p(self.db.data_ptr()), None,
-                rb.ACT_RELU, ctypes.c_void_p(y.data_ptr()), rb.LAYOUT_NCHW, PRECISION[0], stream)
-        p, nb = self.pinned["y"]
+                1, ctypes.c_void_p(slot["dx"].data_ptr()), rb.LAYOUT_NCHW,
+                ctypes.c_void_p(slot["dw"].data_ptr()), ctypes.c_void_p(slot["db"].data_ptr()),
+                None, rb.ACT_RELU, ctypes.c_void_p(y.data_ptr()), rb.LAYOUT_NCHW, PRECISION[0],
+                stream)
+        p, nb = slot["y"]
         rb.call("rtb_memcpy_d2h", ctx.handle, p, ctypes.c_void_p(y.data_ptr()), nb, stream)
 
     def e2e_teardown(self):
         ctx = self.rb.get_context(self.dev.index or 0)
-        for p, _ in self.pinned.values():
-            self.rb.call("rtb_host_free", ctx.handle, p)
+        for slot in self.slots:
+            for key in ("x", "w", "b", "y"):
+                self.rb.call("rtb_host_free", ctx.handle, slot[key][0])
+        self.slots = []
 
     # CPU baseline: the reference's own CPU path (oracle restatement) on a sample
     def cpu_sample(self, threads):
@@ -348,42 +391,55 @@ class GemmWorkload:
         self.rb.sgemm(self.as_[k], self.bs[k], out=out, precision=PRECISION[0])
 
     def e2e_setup(self):
-        rb = self.rb
+        rb, torch = self.rb, self.torch
         ctx = rb.get_context(self.dev.index or 0)
-        self.pinned = {}
         sizes = {"a": self.m * self.k * 4, "b": self.k * self.n_local * 4,
                  "c": self.m * self.n * 4}
-        for key in ("a", "b", "c"):
-            p = ctypes.c_void_p()
-            rb.call("rtb_host_alloc", ctx.handle, ctypes.byref(p), sizes[key])
-            if key in self.host:
-                ctypes.memmove(p, self.host[key].ctypes.data, sizes[key])
-            self.pinned[key] = (p, sizes[key])
+        per_slot = sum(sizes.values())
+        # the N-split step holds NCCL calls, which stay on one stream in issue order
+        depth = 1 if self.nsplit else (3 if per_slot <= 256 * 2**20 else 2)
+        self.pipe = E2EPipeline(torch, self.dev, depth)
+        self.slots = []
+        for k in range(depth):
+            slot = {"a": (_pinned_copy(rb, ctx, self.host["a"]), sizes["a"]),
+                    "b": (_pinned_copy(rb, ctx, self.host["b"]), sizes["b"]),
+                    "c": (_pinned_empty(rb, ctx, sizes["c"]), sizes["c"])}
+            if k < self.nsets:  # device operands: reuse the rotating sets where they exist
+                slot["da"], slot["db"], slot["dc"] = self.as_[k], self.bs[k], self.cs[k]
+            else:
+                slot["da"] = torch.empty_like(self.as_[0])
+                slot["db"] = torch.empty_like(self.bs[0])
+                slot["dc"] = torch.empty_like(self.cs[0])
+            self.slots.append(slot)
         self.h2d_bytes = sizes["a"] + sizes["b"]
         self.d2h_bytes = sizes["c"]
 
     def e2e_step(self):
         rb = self.rb
         ctx = rb.get_context(self.dev.index or 0)
-        stream = ctypes.c_void_p(self.torch.cuda.current_stream(self.dev).cuda_stream)
-        a, b, c = self.as_[0], self.bs[0], self.cs[0]
+        k, st, stream = self.pipe.next()
+        slot = self.slots[k]
+        a, b, c = slot["da"], slot["db"], slot["dc"]
         for key, dst in (("a", a), ("b", b)):
-            p, nb = self.pinned[key]
+            p, nb = slot[key]
             rb.call("rtb_memcpy_h2d", ctx.handle, ctypes.c_void_p(dst.data_ptr()), p, nb, stream)
         if self.nsplit:
-            self.gemm(a, b, precision=PRECISION[0], out=c, parts=self.parts)
+            with self.torch.cuda.stream(st):
+                self.gemm(a, b, precision=PRECISION[0], out=c, parts=self.parts)
         else:
             rb.call("rtb_sgemm", ctx.handle, self.m, self.n, self.k,
                     ctypes.c_void_p(a.data_ptr()), self.k, 0, ctypes.c_void_p(b.data_ptr()),
-                    self.n, 0, None, rb.ACT_NONE, ctypes.c_void_p(c.data_ptr()), self.n,
+                    self.n_local, 0, None, rb.ACT_NONE, ctypes.c_void_p(c.data_ptr()), self.n,
                     PRECISION[0], stream)
-        p, nb = self.pinned["c"]
+        p, nb = slot["c"]
         rb.call("rtb_memcpy_d2h", ctx.handle, p, ctypes.c_void_p(c.data_ptr()), nb, stream)
 
     def e2e_teardown(self):
         ctx = self.rb.get_context(self.dev.index or 0)
-        for p, _ in self.pinned.values():
-            self.rb.call("rtb_host_free", ctx.handle, p)
+        for slot in self.slots:
+            for key in ("a", "b", "c"):
+                self.rb.call("rtb_host_free", ctx.handle, slot[key][0])
+        self.slots = []
 
     def close(self):
         if self.nsplit:
@@ -446,32 +502,46 @@ class ResNet18Workload:
         self._fwd(self.x)
 
     def e2e_setup(self):
-        rb = self.rb
+        rb, torch = self.rb, self.torch
         ctx = rb.get_context(self.dev.index or 0)
         x = self.host["x"]
-        self.px = ctypes.c_void_p()
-        rb.call("rtb_host_alloc", ctx.handle, ctypes.byref(self.px), x.nbytes)
-        ctypes.memmove(self.px, x.ctypes.data, x.nbytes)
-        self.py = ctypes.c_void_p()
-        rb.call("rtb_host_alloc", ctx.handle, ctypes.byref(self.py), self.B * 1000 * 4)
-        self.dx = self.torch.empty_like(self.x)
+        # two slots, each with its own model instance (a forward's activation
+        # buffers belong to its instance), same seed: identical weights
+        self.pipe = E2EPipeline(torch, self.dev, 2)
+        self.slots = []
+        for k in range(self.pipe.depth):
+            h = self.h
+            if k > 0:
+                h = ctypes.c_void_p()
+                rb.call("rtb_resnet18_create", self.dev.index or 0, 3, PRECISION[0],
+                        ctypes.byref(h))
+            self.slots.append({"h": h, "px": _pinned_copy(rb, ctx, x),
+                               "py": _pinned_empty(rb, ctx, self.B * 1000 * 4),
+                               "dx": torch.empty_like(self.x),
+                               "dy": torch.empty_like(self.logits)})
         self.h2d_bytes = x.nbytes
         self.d2h_bytes = self.B * 1000 * 4
 
     def e2e_step(self):
         rb = self.rb
         ctx = rb.get_context(self.dev.index or 0)
-        stream = ctypes.c_void_p(self.torch.cuda.current_stream(self.dev).cuda_stream)
-        rb.call("rtb_memcpy_h2d", ctx.handle, ctypes.c_void_p(self.dx.data_ptr()), self.px,
+        k, _, stream = self.pipe.next()
+        slot = self.slots[k]
+        rb.call("rtb_memcpy_h2d", ctx.handle, ctypes.c_void_p(slot["dx"].data_ptr()), slot["px"],
                 self.h2d_bytes, stream)
-        self._fwd(self.dx)
-        rb.call("rtb_memcpy_d2h", ctx.handle, self.py, ctypes.c_void_p(self.logits.data_ptr()),
+        rb.call("rtb_resnet18_forward", slot["h"], self.B, ctypes.c_void_p(slot["dx"].data_ptr()),
+                ctypes.c_void_p(slot["dy"].data_ptr()), stream)
+        rb.call("rtb_memcpy_d2h", ctx.handle, slot["py"], ctypes.c_void_p(slot["dy"].data_ptr()),
                 self.d2h_bytes, stream)
 
     def e2e_teardown(self):
         ctx = self.rb.get_context(self.dev.index or 0)
-        self.rb.call("rtb_host_free", ctx.handle, self.px)
-        self.rb.call("rtb_host_free", ctx.handle, self.py)
+        for k, slot in enumerate(self.slots):
+            self.rb.call("rtb_host_free", ctx.handle, slot["px"])
+            self.rb.call("rtb_host_free", ctx.handle, slot["py"])
+            if k > 0:
+                self.rb.call("rtb_resnet18_destroy", slot["h"])
+        self.slots = []
 
     def cpu_sample(self, threads):
         """The reference's CPU ops (conv2d auto path, bias, relu, max_pool2d,
@@ -550,13 +620,14 @@ class MlpWorkload:
         self.launches_per_step = 3
         self.unit = "TFLOP/s"
 
-    def _fwd(self, x):
+    def _fwd(self, x, h=None):
         rb = self.rb
+        h = self.h if h is None else h
         a = x
         for i in range(3):
             rb.sgemm(a, self.ws[i].t(), bias=self.bs[i], act=rb.ACT_RELU if i < 2 else rb.ACT_NONE,
-                     precision=PRECISION[0], out=self.h[i])
-            a = self.h[i]
+                     precision=PRECISION[0], out=h[i])
+            a = h[i]
 
     def step(self):
         self._fwd(self.x)
@@ -568,32 +639,37 @@ class MlpWorkload:
         self._fwd(self.x)
 
     def e2e_setup(self):
-        rb = self.rb
+        rb, torch = self.rb, self.torch
         ctx = rb.get_context(self.dev.index or 0)
         x = self.host["x"]
-        self.px = ctypes.c_void_p()
-        rb.call("rtb_host_alloc", ctx.handle, ctypes.byref(self.px), x.nbytes)
-        ctypes.memmove(self.px, x.ctypes.data, x.nbytes)
-        self.py = ctypes.c_void_p()
-        rb.call("rtb_host_alloc", ctx.handle, ctypes.byref(self.py), self.M * 1024 * 4)
-        self.dx = self.torch.empty_like(self.x)
+        self.pipe = E2EPipeline(torch, self.dev, 2)
+        self.slots = []
+        for k in range(self.pipe.depth):
+            h = self.h if k == 0 else [torch.empty_like(t) for t in self.h]
+            self.slots.append({"px": _pinned_copy(rb, ctx, x),
+                               "py": _pinned_empty(rb, ctx, self.M * 1024 * 4),
+                               "dx": torch.empty_like(self.x), "h": h})
         self.h2d_bytes = x.nbytes
         self.d2h_bytes = self.M * 1024 * 4
 
     def e2e_step(self):
         rb = self.rb
         ctx = rb.get_context(self.dev.index or 0)
-        stream = ctypes.c_void_p(self.torch.cuda.current_stream(self.dev).cuda_stream)
-        rb.call("rtb_memcpy_h2d", ctx.handle, ctypes.c_void_p(self.dx.data_ptr()), self.px,
+        k, st, stream = self.pipe.next()
+        slot = self.slots[k]
+        rb.call("rtb_memcpy_h2d", ctx.handle, ctypes.c_void_p(slot["dx"].data_ptr()), slot["px"],
                 self.h2d_bytes, stream)
-        self._fwd(self.dx)
-        rb.call("rtb_memcpy_d2h", ctx.handle, self.py, ctypes.c_void_p(self.h[2].data_ptr()),
+        with self.torch.cuda.stream(st):  # rb.sgemm launches on torch's current stream
+            self._fwd(slot["dx"], slot["h"])
+        rb.call("rtb_memcpy_d2h", ctx.handle, slot["py"], ctypes.c_void_p(slot["h"][2].data_ptr()),
                 self.d2h_bytes, stream)
 
     def e2e_teardown(self):
         ctx = self.rb.get_context(self.dev.index or 0)
-        self.rb.call("rtb_host_free", ctx.handle, self.px)
-        self.rb.call("rtb_host_free", ctx.handle, self.py)
+        for slot in self.slots:
+            self.rb.call("rtb_host_free", ctx.handle, slot["px"])
+            self.rb.call("rtb_host_free", ctx.handle, slot["py"])
+        self.slots = []
 
     def cpu_sample(self, threads):
         """nn::Linear x3 on the reference's CPU path for a 64-row sample."""
@@ -635,7 +711,7 @@ for _name, (_m, _n, _k, _seed) in GEMM_SHAPES.items():
 
 
 # ------------------------------------------------------------------ timing
-def _time_steps(torch, fn, steps, warmup, dev, dist=None, min_warm_s=0.3):
+def _time_steps(torch, fn, steps, warmup, dev, dist=None, min_warm_s=0.3, pipe=None):
     # At least `warmup` steps, and at least min_warm_s of work so the SM
     # clocks have left their idle state before the timed region starts.
     t0 = time.perf_counter()
@@ -653,8 +729,12 @@ def _time_steps(torch, fn, steps, warmup, dev, dist=None, min_warm_s=0.3):
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(s)
+    if pipe is not None:   # multi-stream steps start after e0 and finish before e1
+        pipe.begin(e0)
     for _ in range(steps):
         fn()
+    if pipe is not None:
+        pipe.join(s)
     e1.record(s)
     torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1)
@@ -731,7 +811,8 @@ def run_ours(args):
 
     # end to end through the C ABI with host buffers
     wl.e2e_setup()
-    ems = _time_steps(torch, wl.e2e_step, args.steps, max(3, args.warmup), dev, dist)
+    ems = _time_steps(torch, wl.e2e_step, args.steps, max(3, args.warmup), dev, dist,
+                      pipe=getattr(wl, "pipe", None))
     wl.e2e_teardown()
     e2e = rate(ems, world)
 

@@ -104,7 +104,7 @@ static EncodeIm2colFn get_encode_im2col() {
 
 int make_tmap_im2col(CUtensorMap* map, const void* x, int N, int H, int W, int Cp, int R, int S,
                      int sh, int sw, int ph, int pw, uint32_t channels_per_pixel,
-                     uint32_t pixels_per_column) {
+                     uint32_t pixels_per_column, bool swizzle128) {
   EncodeIm2colFn enc = get_encode_im2col();
   if (!enc) return set_error(RTB_E_CUDA, "cuTensorMapEncodeIm2col unavailable");
   if ((reinterpret_cast<uintptr_t>(x) & 15u) != 0 || (Cp * 4) % 16 != 0)
@@ -119,7 +119,8 @@ int make_tmap_im2col(CUtensorMap* map, const void* x, int N, int H, int W, int C
   const cuuint32_t estr[4] = {1, (cuuint32_t)sw, (cuuint32_t)sh, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void*>(x), dims, strides,
                    lower, upper, channels_per_pixel, pixels_per_column, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     char buf[160];
@@ -586,10 +587,16 @@ static int conv_core(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, 
   // TMA im2col when every k-block is a single filter tap (Cp % 32 == 0), the
   // corners fit the map's signed 8-bit range, and the tensor is not tiny;
   // otherwise the cp.async gather producer.
-  const bool im2col_ok = (Cp % 32 == 0) && pw <= 127 && ph <= 127 && (kw - 1 - pw) <= 128 &&
-                         (kh - 1 - ph) <= 128 && N * H * W * Cp * 4 >= (int64_t)(256 << 10) &&
-                         std::getenv("RTB_CONV_GATHER") == nullptr;
-  d.gather = im2col_ok ? 2 : 1;
+  const bool tma_ok = pw <= 127 && ph <= 127 && (kw - 1 - pw) <= 128 && (kh - 1 - ph) <= 128 &&
+                      N * H * W * Cp * 4 >= (int64_t)(256 << 10) &&
+                      std::getenv("RTB_CONV_GATHER") == nullptr;
+  // Cp in {8, 16}: several taps per k-block, each one TMA im2col box of Cp
+  // channels, read by the 3xTF32 converters.  Measured faster than the gather
+  // at Cp = 16 (52.6 vs 68.9 us) and 8 (39.9 vs 48.2 us, [64,Cp,56,56] 3x3);
+  // at Cp = 4 (the 3-channel stem) eight 2 KB boxes per k-block are slower
+  // than the gather (1492 vs 1214 us), so Cp = 4 keeps the gather.
+  const bool multitap_ok = split3 && (Cp == 8 || Cp == 16);
+  d.gather = (tma_ok && Cp % 32 == 0) ? 2 : ((tma_ok && multitap_ok) ? 3 : 1);
   d.x = x_nhwc;
   d.Nimg = (int)N;
   d.H = (int)H; d.W = (int)W; d.Cp = (int)Cp; d.Ho = (int)Ho; d.Wo = (int)Wo;

@@ -34,6 +34,10 @@ int launch_prec(rtb_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB,
                 const CUtensorMap& tmC, const GemmParams& p, const GemmDesc& d, cudaStream_t s) {
   if (d.gather == 1) return launch_variant<BN, SPLIT, 1, 0>(ctx, tmA, tmB, tmC, p, s);
   if (d.gather == 2) return launch_variant<BN, SPLIT, 2, 0>(ctx, tmA, tmB, tmC, p, s);
+  if (d.gather == 3) {
+    if constexpr (SPLIT) return launch_variant<BN, SPLIT, 3, 0>(ctx, tmA, tmB, tmC, p, s);
+    else return set_error(RTB_E_INVALID, "multi-tap im2col needs the 3xTF32 converters");
+  }
   if (d.b_mn_major) return launch_variant<BN, SPLIT, 0, 1>(ctx, tmA, tmB, tmC, p, s);
   return launch_variant<BN, SPLIT, 0, 0>(ctx, tmA, tmB, tmC, p, s);
 }
@@ -88,7 +92,10 @@ int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
     st = make_tmap_2d(&tmA, d.B, (uint64_t)d.K, (uint64_t)d.N, (uint64_t)d.ldb, kBK, 64, false);
   } else if (d.gather == 2) {
     st = make_tmap_im2col(&tmA, d.x, d.Nimg, d.H, d.W, d.Cp, d.R, d.S, d.sh, d.sw, d.ph, d.pw,
-                          kBK, kBM);
+                          kBK, kBM, true);
+  } else if (d.gather == 3) {  // one dense [128 pixels][Cp] box per filter tap
+    st = make_tmap_im2col(&tmA, d.x, d.Nimg, d.H, d.W, d.Cp, d.R, d.S, d.sh, d.sw, d.ph, d.pw,
+                          (uint32_t)d.Cp, kBM, false);
   } else {
     st = make_tmap_2d(&tmA, d.A, (uint64_t)d.K, (uint64_t)d.M, (uint64_t)d.lda, kBK, kBM, false);
   }

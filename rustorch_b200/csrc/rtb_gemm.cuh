@@ -395,7 +395,9 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
     rtb_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
   constexpr bool GATHER = (A_MODE == 1);
-  constexpr bool IM2COL = (A_MODE == 2);
+  constexpr bool IM2COL = (A_MODE == 2 || A_MODE == 3);
+  constexpr bool MULTITAP = (A_MODE == 3);
+  static_assert(!MULTITAP || SPLIT, "multi-tap im2col tiles are read by the 3xTF32 converters");
   using Cfg = GemmCfg<BN, SPLIT>;
   using Roles = GemmRoles<SPLIT, GATHER>;
   constexpr int S = Cfg::kStages;
@@ -483,7 +485,16 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
                                  p.timeout_ns))
             break;
           if (kb == u.kb0 && tj < kTraceTiles) trace_stamp(p, 2 + 6 * tj);
-          mbar_arrive_expect_tx(&full_bar[s], tx);
+          // multi-tap: 32 / Cp filter taps per k-block, the last k-block may
+          // hold fewer (no copy is issued for taps past R*S)
+          const int tpk = MULTITAP ? kBK / p.Cp : 1;
+          int ntaps = 0;
+          if (MULTITAP) {
+            ntaps = p.R * p.S - kb * tpk;
+            ntaps = ntaps < tpk ? ntaps : tpk;
+          }
+          mbar_arrive_expect_tx(&full_bar[s],
+                                MULTITAP ? (uint32_t)(ntaps * kBM * p.Cp * 4 + kBBytes) : tx);
           // Warm L2 for a k-block `prefetch_kb` ahead (hides DRAM latency beyond
           // what the shared-memory ring can cover).
           const int kp = kb + p.prefetch_kb;
@@ -491,7 +502,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
             if (A_MODE == 0) {
               tma_prefetch_2d(&tmA, kp * kBK, tm * kBM);
               if (B_MN == 0) tma_prefetch_2d(&tmB, kp * kBK, tn * BN);
-            } else if (IM2COL) {
+            } else if (IM2COL && !MULTITAP) {
               const int k0 = kp * kBK, tap = k0 / p.Cp, rr = tap / p.S;
               tma_prefetch_im2col_4d(&tmA, k0 - tap * p.Cp, a_w, a_h, a_n,
                                      (uint16_t)(tap - rr * p.S), (uint16_t)rr);
@@ -499,6 +510,15 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
           }
           if (A_MODE == 0) {
             tma_load_2d(sA + s * kABytes, &tmA, &full_bar[s], kb * kBK, tm * kBM);
+          } else if (MULTITAP) {
+            // tap j of the k-block -> dense [128 pixels][Cp] block j of the A tile
+            for (int j = 0; j < ntaps; ++j) {
+              const int tap = kb * tpk + j;
+              const int rr = tap / p.S;
+              const int ss = tap - rr * p.S;
+              tma_load_im2col_4d(sA + s * kABytes + j * (kBM * p.Cp * 4), &tmA, &full_bar[s], 0,
+                                 a_w, a_h, a_n, (uint16_t)ss, (uint16_t)rr);
+            }
           } else if (IM2COL) {
             const int k0 = kb * kBK;
             const int tap = k0 / p.Cp;           // one filter tap per k-block (Cp % 32 == 0)
@@ -804,8 +824,22 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
         const uint32_t bb = smem_u32(sB + s * kBBytes);
         const uint32_t blo = smem_u32(sBlo + ja * kBBytes);
         float4 av[8], bv[kBPer];
+        if (MULTITAP) {
+          // float4 q of the row = channels 4*qq.. of tap block j (dense rows of
+          // Cp floats); k-block columns past K = R*S*Cp are zero
+          const int l = p.Cp == 4 ? 0 : (p.Cp == 8 ? 1 : 2);  // log2(Cp / 4)
+          const uint32_t a0 = smem_u32(sA + s * kABytes) + row * p.Cp * 4;
+          const int kvalid = p.R * p.S * p.Cp - kb * kBK;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) av[j] = lds128(arow + ((j ^ (row & 7)) << 4));
+          for (int q = 0; q < 8; ++q) {
+            av[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (4 * q < kvalid)
+              av[q] = lds128(a0 + (q >> l) * (kBM * p.Cp * 4) + (q & ((1 << l) - 1)) * 16);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) av[j] = lds128(arow + ((j ^ (row & 7)) << 4));
+        }
 #pragma unroll
         for (int i = 0; i < kBPer; ++i) bv[i] = lds128(bb + (ct + 128 * i) * 16);
         uint32_t hi[32], lo[32];

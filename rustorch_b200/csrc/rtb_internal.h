@@ -67,10 +67,10 @@ int make_tmap_2d_swz(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t
 
 // 4-D im2col map over an NHWC tensor [N, H, W, Cp] for a forward conv with
 // filter R x S, stride (sh, sw), padding (ph, pw): channels_per_pixel x
-// pixels_per_column boxes, 128-byte swizzle.
+// pixels_per_column boxes, 128-byte swizzle or dense rows.
 int make_tmap_im2col(CUtensorMap* map, const void* x, int N, int H, int W, int Cp, int R, int S,
                      int sh, int sw, int ph, int pw, uint32_t channels_per_pixel,
-                     uint32_t pixels_per_column);
+                     uint32_t pixels_per_column, bool swizzle128);
 
 // What the GEMM engine computes; see rtb_gemm.cuh (GemmParams) for the epilogue.
 struct GemmDesc {
@@ -92,6 +92,8 @@ struct GemmDesc {
   int out_mode = 0;  // 0 row-major, 1 NCHW scatter
   int hw = 0;
   // conv A producer: 0 = none (A is a matrix), 1 = cp.async gather, 2 = TMA im2col
+  // (one tap x 32 channels per k-block), 3 = multi-tap TMA im2col (32 / Cp taps
+  // of Cp channels per k-block, Cp in {4, 8, 16}; 3xTF32 only; selected for 8, 16)
   int gather = 0;
   const float* x = nullptr;
   int Nimg = 0;

@@ -83,12 +83,16 @@ def test_conv_bias_relu_resnet50_layer(gpu, orc, prec):
     ((2, 512, 7, 7), (512, 512, 3, 3), (1, 1), (1, 1)),
     ((3, 5, 9, 11), (7, 5, 3, 2), (1, 2), (2, 0)),          # odd everything
     ((1, 36, 5, 5), (10, 36, 5, 5), (1, 1), (0, 0)),        # K-blocks straddle taps
+    ((8, 7, 40, 40), (16, 7, 3, 3), (1, 1), (1, 1)),        # Cp=8: 4 taps per k-block
+    ((4, 13, 48, 48), (32, 13, 5, 5), (2, 2), (2, 2)),      # Cp=16: 2 taps per k-block
 ])
 @pytest.mark.parametrize("prec", [0, 1])
 @pytest.mark.parametrize("producer", ["auto", "gather"])
 def test_conv_shapes(gpu, orc, shape, wshape, stride, pad, prec, producer, monkeypatch):
-    """producer=auto uses the TMA im2col path where Ci % 32 == 0 (the cp.async
-    gather otherwise); producer=gather forces the cp.async gather everywhere."""
+    """producer=auto uses the TMA im2col path where Ci % 32 == 0, the multi-tap
+    TMA im2col path (32 / Cp taps per k-block) for Cp in {8, 16} in 3xTF32
+    mode, and the cp.async gather otherwise; producer=gather forces the
+    cp.async gather everywhere."""
     if producer == "gather":
         monkeypatch.setenv("RTB_CONV_GATHER", "1")
     x = orc.normal(shape, 5, 1)
