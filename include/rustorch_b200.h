@@ -182,6 +182,28 @@ int rtb_conv2d_fwd_noalloc(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64
 int rtb_nchw_to_nhwc_padded(rtb_ctx* ctx, int64_t N, int64_t C, int64_t H, int64_t W,
                             const float* x, float* y, void* stream);
 
+/* ---------------------------------------------------------------- backward */
+/* MatmulBackward (rustorch-core/src/ops.rs:529-570) for C = A . B with A
+ * [M,K], B [K,N], dC [M,N], all row-major contiguous:
+ *   dA = dC . B^T  (grad_lhs = matmul(grad, rhs.t()))   when dA != NULL
+ *   dB = A^T . dC  (grad_rhs = matmul(lhs.t(), grad))   when dB != NULL
+ * accumulate != 0 adds into dA / dB (the reference's accumulate_grad) instead
+ * of overwriting.  Both products run on the same tensor-core engine. */
+int rtb_matmul_backward(rtb_ctx* ctx, int64_t M, int64_t N, int64_t K, const float* A,
+                        const float* B, const float* dC, float* dA, float* dB, int accumulate,
+                        int precision, void* stream);
+/* Conv2dBackward (rustorch-core/src/ops/conv.rs:336-736) for the NCHW conv of
+ * x [N,Ci,H,W] with w [Co,Ci,kh,kw] (stride, padding as in rtb_conv2d_fwd) and
+ * incoming gradient dy [N,Co,Ho,Wo]:
+ *   dx [N,Ci,H,W]     (conv2d_grad_input_*_core)   when dx != NULL
+ *   dw [Co,Ci,kh,kw]  (conv2d_grad_weight_*_core)  when dw != NULL
+ * accumulate != 0 adds into dx / dw.  grad_input needs padding <= kernel - 1
+ * (RTB_E_UNSUPPORTED otherwise). */
+int rtb_conv2d_backward(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, int64_t Co,
+                        int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw,
+                        const float* x, const float* w, const float* dy, float* dx, float* dw,
+                        int accumulate, int precision, void* stream);
+
 /* ---------------------------------------------------------------- small ops */
 /* ops::max_pool2d (rustorch-core/src/ops/pool.rs:115-191): -inf init, padding skipped. */
 int rtb_max_pool2d(rtb_ctx* ctx, int64_t N, int64_t C, int64_t H, int64_t W, int64_t kh,

@@ -509,6 +509,78 @@ ORC_API void orc_conv2d_f64(int64_t n, int64_t ci, int64_t h, int64_t w, int64_t
 }
 
 /* ------------------------------------------------------------------------ */
+/* Conv2dBackward (rustorch-core/src/ops/conv.rs:336-736)                     */
+/* ------------------------------------------------------------------------ */
+
+/* grad_input, restating conv2d_grad_input_direct_core (conv.rs:336-389): for
+ * every input element (b, ci, h, w), the f64 sum over the output positions
+ * whose window covers it, ho in [ceil((h+ph-kh+1)/sh), min(ho_n, (h+ph)/sh+1))
+ * with kh_idx = h + ph - ho*sh (same for w), and over co, of g * w.  Output in
+ * double (the reference casts this sum to f32). */
+ORC_API void orc_conv2d_grad_input_f64(int64_t n, int64_t ci, int64_t h, int64_t w, int64_t co,
+                                       int64_t kh, int64_t kw, int64_t sh, int64_t sw,
+                                       int64_t ph, int64_t pw, const float* gy, const float* wt,
+                                       double* gx, int nthreads) {
+  const int64_t ho_n = (h + 2 * ph - kh) / sh + 1;
+  const int64_t wo_n = (w + 2 * pw - kw) / sw + 1;
+  orc_set_threads(nthreads);
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int64_t b = 0; b < n; ++b)
+    for (int64_t c = 0; c < ci; ++c)
+      for (int64_t hh = 0; hh < h; ++hh)
+        for (int64_t ww = 0; ww < w; ++ww) {
+          double sum = 0.0;
+          const int64_t ho0 = hh + ph >= kh ? (hh + ph - kh + 1 + sh - 1) / sh : 0;
+          int64_t ho1 = (hh + ph) / sh + 1;
+          if (ho1 > ho_n) ho1 = ho_n;
+          for (int64_t oh = ho0; oh < ho1; ++oh) {
+            const int64_t r = hh + ph - oh * sh;
+            const int64_t wo0 = ww + pw >= kw ? (ww + pw - kw + 1 + sw - 1) / sw : 0;
+            int64_t wo1 = (ww + pw) / sw + 1;
+            if (wo1 > wo_n) wo1 = wo_n;
+            for (int64_t ow = wo0; ow < wo1; ++ow) {
+              const int64_t s = ww + pw - ow * sw;
+              for (int64_t c_o = 0; c_o < co; ++c_o)
+                sum += (double)gy[((b * co + c_o) * ho_n + oh) * wo_n + ow] *
+                       (double)wt[((c_o * ci + c) * kh + r) * kw + s];
+            }
+          }
+          gx[((b * ci + c) * h + hh) * w + ww] = sum;
+        }
+}
+
+/* grad_weight, restating conv2d_grad_weight_direct_core (conv.rs:455-502): for
+ * every weight (co, ci, r, s) the f64 sum over (b, ho, wo) of x * g, padding
+ * positions skipped.  Output in double. */
+ORC_API void orc_conv2d_grad_weight_f64(int64_t n, int64_t ci, int64_t h, int64_t w, int64_t co,
+                                        int64_t kh, int64_t kw, int64_t sh, int64_t sw,
+                                        int64_t ph, int64_t pw, const float* x, const float* gy,
+                                        double* gw, int nthreads) {
+  const int64_t ho_n = (h + 2 * ph - kh) / sh + 1;
+  const int64_t wo_n = (w + 2 * pw - kw) / sw + 1;
+  orc_set_threads(nthreads);
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int64_t c_o = 0; c_o < co; ++c_o)
+    for (int64_t c = 0; c < ci; ++c)
+      for (int64_t r = 0; r < kh; ++r)
+        for (int64_t s = 0; s < kw; ++s) {
+          double sum = 0.0;
+          for (int64_t b = 0; b < n; ++b)
+            for (int64_t oh = 0; oh < ho_n; ++oh) {
+              const int64_t hh = oh * sh + r - ph;
+              if (hh < 0 || hh >= h) continue;
+              const float* xr = x + ((b * ci + c) * h + hh) * w;
+              const float* gr = gy + ((b * co + c_o) * ho_n + oh) * wo_n;
+              for (int64_t ow = 0; ow < wo_n; ++ow) {
+                const int64_t ww = ow * sw + s - pw;
+                if (ww >= 0 && ww < w) sum += (double)xr[ww] * (double)gr[ow];
+              }
+            }
+          gw[((c_o * ci + c) * kh + r) * kw + s] = sum;
+        }
+}
+
+/* ------------------------------------------------------------------------ */
 /* Pooling                                                                   */
 /* ------------------------------------------------------------------------ */
 

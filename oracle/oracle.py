@@ -63,6 +63,8 @@ def lib():
         L.orc_conv2d.restype = ctypes.c_int
         L.orc_conv2d.argtypes = conv_args
         L.orc_conv2d_f64.argtypes = conv_args
+        L.orc_conv2d_grad_input_f64.argtypes = conv_args
+        L.orc_conv2d_grad_weight_f64.argtypes = conv_args
         L.orc_max_pool2d.argtypes = [_i64] * 10 + [_p, _p]
         L.orc_global_avg_pool.argtypes = [_i64] * 3 + [_p, _p]
         L.orc_rel_frob.restype = ctypes.c_double
@@ -261,6 +263,41 @@ def conv2d_f64(x, w, stride=(1, 1), padding=(0, 0), threads: int = 0) -> np.ndar
     lib().orc_conv2d_f64(n, ci, h, wd, co, kh, kw, sh, sw, ph, pw, _ptr(x), _ptr(w), _ptr(y),
                          threads)
     return y
+
+
+def conv2d_grad_input_f64(gy, w, x_shape, stride=(1, 1), padding=(0, 0), threads: int = 0):
+    """Conv2dBackward grad_input (rustorch-core/src/ops/conv.rs:336-389, the f64
+    direct core), float64 result; gy [N,Co,Ho,Wo], w [Co,Ci,kh,kw]."""
+    gy = _f32(gy)
+    w = _f32(w)
+    n, ci, h, wd = x_shape
+    co, _, kh, kw = w.shape
+    gx = np.empty((n, ci, h, wd), dtype=np.float64)
+    lib().orc_conv2d_grad_input_f64(n, ci, h, wd, co, kh, kw, stride[0], stride[1], padding[0],
+                                    padding[1], _ptr(gy), _ptr(w), _ptr(gx), threads)
+    return gx
+
+
+def conv2d_grad_weight_f64(x, gy, w_shape, stride=(1, 1), padding=(0, 0), threads: int = 0):
+    """Conv2dBackward grad_weight (rustorch-core/src/ops/conv.rs:455-502, the f64
+    direct core), float64 result; x [N,Ci,H,W], gy [N,Co,Ho,Wo]."""
+    x = _f32(x)
+    gy = _f32(gy)
+    n, ci, h, wd = x.shape
+    co, _, kh, kw = w_shape
+    gw = np.empty((co, ci, kh, kw), dtype=np.float64)
+    lib().orc_conv2d_grad_weight_f64(n, ci, h, wd, co, kh, kw, stride[0], stride[1], padding[0],
+                                     padding[1], _ptr(x), _ptr(gy), _ptr(gw), threads)
+    return gw
+
+
+def matmul_backward_f64(a, b, gc):
+    """MatmulBackward (rustorch-core/src/ops.rs:529-570): grad_lhs = grad . rhs^T,
+    grad_rhs = lhs^T . grad, in float64."""
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    gc = np.asarray(gc, np.float64)
+    return gc @ b.T, a.T @ gc
 
 
 def conv2d_bias_relu(x, w, b, stride=(1, 1), padding=(0, 0), relu_: bool = True, threads: int = 0):

@@ -22,7 +22,8 @@ from . import _lib
 from ._lib import (ACT_NONE, ACT_RELU, ACT_SIGMOID, ACT_TANH, LAYOUT_NCHW, LAYOUT_NHWC,
                    PREC_3XTF32, PREC_DEFAULT, PREC_TF32, RtbError, call, lib)
 
-__all__ = ["Context", "get_context", "sgemm", "sgemm_batched", "conv2d_fwd", "max_pool2d",
+__all__ = ["Context", "get_context", "sgemm", "sgemm_batched", "conv2d_fwd", "matmul_backward",
+           "conv2d_backward", "max_pool2d",
            "global_avg_pool", "add", "relu", "fill_normal", "fill_uniform", "RtbError",
            "ACT_NONE", "ACT_RELU", "ACT_SIGMOID", "ACT_TANH", "PREC_3XTF32", "PREC_TF32",
            "PREC_DEFAULT", "LAYOUT_NCHW", "LAYOUT_NHWC", "lib"]
@@ -184,6 +185,44 @@ def conv2d_fwd(x, w, bias=None, stride=(1, 1), padding=(0, 0), residual=None, ac
          padding[1], _ptr(x), x_layout, _ptr(w), _ptr(bias.contiguous() if bias is not None else None),
          _ptr(residual), act, _ptr(y), y_layout, precision, _stream_of(x))
     return y
+
+
+def matmul_backward(a, b, grad, need_a: bool = True, need_b: bool = True, out_a=None, out_b=None,
+                    accumulate: bool = False, precision: int = PREC_DEFAULT):
+    """MatmulBackward of c = a @ b: (grad @ b.T, a.T @ grad) for contiguous 2-D
+    float32 CUDA tensors; with accumulate the results are added to out_a/out_b."""
+    torch = _torch()
+    _check_f32_cuda(a, b, grad)
+    a, b, grad = a.contiguous(), b.contiguous(), grad.contiguous()
+    M, K = a.shape
+    N = b.shape[1]
+    if b.shape[0] != K or tuple(grad.shape) != (M, N):
+        raise ValueError("matmul_backward: shape mismatch")
+    da = (out_a if out_a is not None else torch.empty((M, K), dtype=torch.float32,
+                                                      device=a.device)) if need_a else None
+    db = (out_b if out_b is not None else torch.empty((K, N), dtype=torch.float32,
+                                                      device=a.device)) if need_b else None
+    ctx = get_context(_dev(a))
+    call("rtb_matmul_backward", ctx.handle, M, N, K, _ptr(a), _ptr(b), _ptr(grad), _ptr(da),
+         _ptr(db), int(accumulate), precision, _stream_of(a))
+    return da, db
+
+
+def conv2d_backward(x, w, grad, stride=(1, 1), padding=(0, 0), need_x: bool = True,
+                    need_w: bool = True, precision: int = PREC_DEFAULT):
+    """Conv2dBackward (NCHW): (grad wrt x, grad wrt w) of y = conv2d(x, w)."""
+    torch = _torch()
+    _check_f32_cuda(x, w, grad)
+    x, w, grad = x.contiguous(), w.contiguous(), grad.contiguous()
+    N, Ci, H, W = x.shape
+    Co, _, kh, kw = w.shape
+    dx = torch.empty_like(x) if need_x else None
+    dw = torch.empty_like(w) if need_w else None
+    ctx = get_context(_dev(x))
+    call("rtb_conv2d_backward", ctx.handle, N, Ci, H, W, Co, kh, kw, stride[0], stride[1],
+         padding[0], padding[1], _ptr(x), _ptr(w), _ptr(grad), _ptr(dx), _ptr(dw), 0, precision,
+         _stream_of(x))
+    return dx, dw
 
 
 def max_pool2d(x, kernel=(3, 3), stride=(2, 2), padding=(1, 1), layout: int = LAYOUT_NCHW):

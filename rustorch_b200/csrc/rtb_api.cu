@@ -422,15 +422,23 @@ static int check_act(int act, int* relu) {
 }
 
 // One 2-D GEMM on the current device/stream (helper for single and batched).
+// residual (optional, same indexing as C): C = act(A.B + bias + residual);
+// residual == C accumulates into C.
 static int sgemm_one(rtb_ctx* ctx, int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
                      int transA, const float* B, int64_t ldb, int transB, const float* bias,
-                     int relu, float* C, int64_t ldc, int split3, cudaStream_t s) {
+                     int relu, float* C, int64_t ldc, int split3, cudaStream_t s,
+                     const float* residual = nullptr) {
   if (M == 0 || N == 0) return RTB_OK;
-  if (K == 0) return launch_fill_rows(C, M, N, ldc, bias, relu, s);
+  if (K == 0) {
+    if (residual == C && !bias && !relu) return RTB_OK;  // C += 0
+    if (residual) return set_error(RTB_E_UNSUPPORTED, "K == 0 with a residual");
+    return launch_fill_rows(C, M, N, ldc, bias, relu, s);
+  }
 
   GemmDesc d;
   d.M = M; d.N = N; d.K = K;
   d.C = C; d.ldc = ldc; d.bias = bias; d.relu = relu; d.split3 = split3;
+  d.residual = residual; d.ldr = ldc;
   float* wsA = nullptr;
   float* wsB = nullptr;
   int st = RTB_OK;
@@ -467,7 +475,7 @@ static int sgemm_one(rtb_ctx* ctx, int64_t M, int64_t N, int64_t K, const float*
       const char* v = std::getenv("RTB_SMALLM");
       return !(v && v[0] == '0');
     }();
-    st = (smallm_on && M <= kSmallMMax) ? smallm_run(ctx, d, s) : gemm_run(ctx, d, s);
+    st = (smallm_on && M <= kSmallMMax && !residual) ? smallm_run(ctx, d, s) : gemm_run(ctx, d, s);
   }
   ws_free(wsA, s);
   ws_free(wsB, s);
@@ -700,6 +708,115 @@ int rtb_conv2d_fwd(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, in
   ws_free(xs, s);
   ws_free(ws, s);
   return st;
+}
+
+// ---------------------------------------------------------------- backward
+int rtb_matmul_backward(rtb_ctx* ctx, int64_t M, int64_t N, int64_t K, const float* A,
+                        const float* B, const float* dC, float* dA, float* dB, int accumulate,
+                        int precision, void* stream) {
+  RTB_CHECK_CTX(ctx);
+  if (M < 0 || N < 0 || K < 0) return set_error(RTB_E_INVALID, "negative dimension");
+  if ((dA && (!dC || !B)) || (dB && (!dC || !A)))
+    return set_error(RTB_E_INVALID, "matmul_backward: null operand");
+  int split3 = 1, st;
+  if ((st = resolve_precision(ctx, precision, &split3))) return st;
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = pick_stream(ctx, stream);
+  // grad_lhs = grad . rhs^T: [M,N] . [N,K]; rhs [K,N] row-major is the [N',K'] view
+  if (dA && M > 0 && K > 0) {
+    if (N == 0) {
+      if (!accumulate) {
+        cudaError_t e = cudaMemsetAsync(dA, 0, (size_t)(M * K) * 4, s);
+        if (e != cudaSuccess) return cuda_status(e, "matmul_backward memset");
+      }
+    } else if ((st = sgemm_one(ctx, M, K, N, dC, N, 0, B, N, 1, nullptr, 0, dA, K, split3, s,
+                               accumulate ? dA : nullptr))) {
+      return st;
+    }
+  }
+  // grad_rhs = lhs^T . grad: [K,M] . [M,N]
+  if (dB && K > 0 && N > 0) {
+    if (M == 0) {
+      if (!accumulate) {
+        cudaError_t e = cudaMemsetAsync(dB, 0, (size_t)(K * N) * 4, s);
+        if (e != cudaSuccess) return cuda_status(e, "matmul_backward memset");
+      }
+    } else if ((st = sgemm_one(ctx, K, N, M, A, K, 1, dC, N, 0, nullptr, 0, dB, N, split3, s,
+                               accumulate ? dB : nullptr))) {
+      return st;
+    }
+  }
+  return RTB_OK;
+}
+
+int rtb_conv2d_backward(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, int64_t Co,
+                        int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw,
+                        const float* x, const float* w, const float* dy, float* dx, float* dw,
+                        int accumulate, int precision, void* stream) {
+  RTB_CHECK_CTX(ctx);
+  int64_t Ho, Wo;
+  int st = conv_check(N, Ci, H, W, Co, kh, kw, sh, sw, ph, pw, &Ho, &Wo);
+  if (st) return st;
+  if (!dy || (dx && !w) || (dw && !x)) return set_error(RTB_E_INVALID, "conv_backward: null pointer");
+  int split3 = 1;
+  if ((st = resolve_precision(ctx, precision, &split3))) return st;
+  if (dx && (ph > kh - 1 || pw > kw - 1))
+    return set_error(RTB_E_UNSUPPORTED, "conv_backward: padding larger than kernel-1");
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = pick_stream(ctx, stream);
+  if (N == 0) return RTB_OK;
+
+  if (dx) {
+    // grad_input: conv (stride 1, padding k-1-p) of dy dilated by the stride
+    // (plus the rows/columns of x no window reaches) with the flipped filter.
+    const int64_t Cop = round_up(Co, 4);
+    const int64_t Hd = (Ho - 1) * sh + 1 + (H + 2 * ph - kh) % sh;
+    const int64_t Wd = (Wo - 1) * sw + 1 + (W + 2 * pw - kw) % sw;
+    const int64_t qh = kh - 1 - ph, qw = kw - 1 - pw;
+    if (Hd + 2 * qh - kh + 1 != H || Wd + 2 * qw - kw + 1 != W)
+      return set_error(RTB_E_INVALID, "conv_backward: inconsistent geometry");
+    float* dyd = nullptr;
+    float* wt = nullptr;
+    const size_t dyd_bytes = (size_t)(N * Hd * Wd * Cop) * 4;
+    st = ws_alloc(ctx, (void**)&dyd, dyd_bytes, s);
+    if (st == RTB_OK) {
+      cudaError_t e = cudaMemsetAsync(dyd, 0, dyd_bytes, s);
+      st = e == cudaSuccess ? RTB_OK : cuda_status(e, "conv_backward memset");
+    }
+    if (st == RTB_OK) st = launch_dilate_nchw_to_nhwc(dy, N, Co, Ho, Wo, sh, sw, Hd, Wd, Cop, dyd, s);
+    if (st == RTB_OK) st = ws_alloc(ctx, (void**)&wt, (size_t)(Ci * kh * kw * Cop) * 4, s);
+    if (st == RTB_OK) st = launch_prepack_flip(w, Co, Ci, kh, kw, Cop, wt, s);
+    if (st == RTB_OK)
+      st = conv_core(ctx, N, Co, Hd, Wd, Ci, kh, kw, 1, 1, qh, qw, H, W, dyd, wt, nullptr,
+                     accumulate ? dx : nullptr, 0, dx, RTB_LAYOUT_NCHW, split3, s);
+    ws_free(dyd, s);
+    ws_free(wt, s);
+    if (st) return st;
+  }
+  if (dw) {
+    // grad_weight = dy^T [Co, P] . im2col(x) [P, kh*kw*Cp], P = N*Ho*Wo
+    const int64_t Cp = round_up(Ci, 4);
+    const int64_t P = N * Ho * Wo;
+    const int64_t Pp = round_up(P, 4);
+    const int64_t Kp = kh * kw * Cp;
+    float *xh = nullptr, *col = nullptr, *dyt = nullptr, *dwp = nullptr;
+    st = ws_alloc(ctx, (void**)&xh, (size_t)(N * H * W * Cp) * 4, s);
+    if (st == RTB_OK) st = launch_nchw_to_nhwc_padded(x, N, Ci, H, W, Cp, xh, s);
+    if (st == RTB_OK) st = ws_alloc(ctx, (void**)&col, (size_t)(P * Kp) * 4, s);
+    if (st == RTB_OK) st = launch_im2col_nhwc(xh, N, H, W, Cp, Ho, Wo, kh, kw, sh, sw, ph, pw, col, s);
+    if (st == RTB_OK) st = ws_alloc(ctx, (void**)&dyt, (size_t)(Co * Pp) * 4, s);
+    if (st == RTB_OK) st = launch_nchw_to_cmajor(dy, N, Co, Ho * Wo, Pp, dyt, s);
+    if (st == RTB_OK) st = ws_alloc(ctx, (void**)&dwp, (size_t)(Co * Kp) * 4, s);
+    if (st == RTB_OK)
+      st = sgemm_one(ctx, Co, Kp, P, dyt, Pp, 0, col, Kp, 0, nullptr, 0, dwp, Kp, split3, s);
+    if (st == RTB_OK) st = launch_unpack_weight_grad(dwp, Co, Ci, kh, kw, Cp, accumulate, dw, s);
+    ws_free(xh, s);
+    ws_free(col, s);
+    ws_free(dyt, s);
+    ws_free(dwp, s);
+    if (st) return st;
+  }
+  return RTB_OK;
 }
 
 // ---------------------------------------------------------------- small ops

@@ -145,6 +145,20 @@ int conv2d_fwd_packed_noalloc(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, in
                               const float* w_packed, const float* bias, const float* residual,
                               int act, float* y, int y_layout, int precision, void* stream);
 
+// Backward-pass layout kernels (rtb_backward.cu).
+int launch_dilate_nchw_to_nhwc(const float* dy, int64_t N, int64_t Co, int64_t Ho, int64_t Wo,
+                               int64_t sh, int64_t sw, int64_t Hd, int64_t Wd, int64_t Cop,
+                               float* out, cudaStream_t s);
+int launch_prepack_flip(const float* w, int64_t Co, int64_t Ci, int64_t R, int64_t S, int64_t Cop,
+                        float* wt, cudaStream_t s);
+int launch_im2col_nhwc(const float* x, int64_t N, int64_t H, int64_t W, int64_t Cp, int64_t Ho,
+                       int64_t Wo, int64_t R, int64_t S, int64_t sh, int64_t sw, int64_t ph,
+                       int64_t pw, float* col, cudaStream_t s);
+int launch_nchw_to_cmajor(const float* dy, int64_t N, int64_t Co, int64_t HW, int64_t ldp,
+                          float* dyt, cudaStream_t s);
+int launch_unpack_weight_grad(const float* dwp, int64_t Co, int64_t Ci, int64_t R, int64_t S,
+                              int64_t Cp, int accumulate, float* dw, cudaStream_t s);
+
 // Stream-ordered workspace.
 int ws_alloc(rtb_ctx* ctx, void** p, size_t bytes, cudaStream_t s);
 void ws_free(void* p, cudaStream_t s);

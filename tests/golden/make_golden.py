@@ -51,6 +51,18 @@ def main(root: str) -> None:
                  "a": a, "a_shape": ash, "b": b, "b_shape": bsh,
                  "expected": exp, "abs_tol": tol})
 
+    # MatmulBackward through loss = sum(a . b): grad_a = 1 . b^T, grad_b = a^T . 1
+    body, line = _fn_body(src, "test_matmul_backward_precision_under_1e6")
+    a, ash = _tensor_new(body, "a")
+    b, bsh = _tensor_new(body, "b")
+    exp_a = _floats(re.search(r"expected_a\s*=\s*\[(.*?)\]", body, re.S).group(1))
+    exp_b = _floats(re.search(r"expected_b\s*=\s*\[(.*?)\]", body, re.S).group(1))
+    tol = float(re.search(r"err < ([0-9e\.\-]+)", body).group(1))
+    kats.append({"name": "matmul_backward_2x2", "op": "matmul_backward",
+                 "source": f"{rel}:{line}", "a": a, "a_shape": ash, "b": b, "b_shape": bsh,
+                 "grad_out": "ones (loss = sum of the product)",
+                 "expected_grad_a": exp_a, "expected_grad_b": exp_b, "abs_tol": tol})
+
     body, line = _fn_body(src, "test_conv2d_forward_precision_under_1e6")
     x, xsh = _tensor_new(body, "input")
     w, wsh = _tensor_new(body, "weight")

@@ -147,3 +147,29 @@ def test_prng_distribution(orc):
     # deterministic and keyed by (seed, tensor id)
     np.testing.assert_array_equal(orc.normal((17,), 4, 2), orc.normal((17,), 4, 2))
     assert not np.array_equal(orc.normal((17,), 4, 2), orc.normal((17,), 4, 3))
+
+
+def test_matmul_backward_kat(orc, kats):
+    """MatmulBackward restated (ops.rs:529-570) against the reference's test
+    (loss = sum(a . b), so the incoming gradient is all ones)."""
+    k = kats["matmul_backward_2x2"]
+    a = np.array(k["a"], np.float32).reshape(k["a_shape"])
+    b = np.array(k["b"], np.float32).reshape(k["b_shape"])
+    ga, gb = orc.matmul_backward_f64(a, b, np.ones((a.shape[0], b.shape[1])))
+    assert np.max(np.abs(ga.reshape(-1) - k["expected_grad_a"])) < k["abs_tol"]
+    assert np.max(np.abs(gb.reshape(-1) - k["expected_grad_b"])) < k["abs_tol"]
+
+
+@pytest.mark.parametrize("stride,pad", [((1, 1), (1, 0)), ((2, 2), (1, 1)), ((2, 1), (0, 2))])
+def test_conv_backward_adjoint(orc, stride, pad):
+    """The Conv2dBackward restatements (conv.rs:336-502) are the adjoints of the
+    pinned forward conv: <conv(x, w), g> = <x, grad_input(g, w)> = <w, grad_weight(x, g)>."""
+    x = orc.normal((2, 3, 9, 11), 1, 1)
+    w = orc.normal((4, 3, 3, 2), 1, 2)
+    y = orc.conv2d_f64(x, w, stride, pad)
+    g = orc.normal(y.shape, 1, 3)
+    gx = orc.conv2d_grad_input_f64(g, w, x.shape, stride, pad)
+    gw = orc.conv2d_grad_weight_f64(x, g, w.shape, stride, pad)
+    lhs = float((y * g.astype(np.float64)).sum())
+    assert abs(float((x.astype(np.float64) * gx).sum()) - lhs) <= 1e-10 * max(1.0, abs(lhs))
+    assert abs(float((w.astype(np.float64) * gw).sum()) - lhs) <= 1e-10 * max(1.0, abs(lhs))
