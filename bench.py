@@ -356,26 +356,36 @@ class GemmWorkload:
         self.bs = [torch.from_numpy(b).to(dev) for _ in range(self.nsets)]
         self.cs = [torch.empty((m, n), device=dev) for _ in range(self.nsets)]
         self.i = 0
+        # N-split: fused GEMM + exchange (epilogue P2P stores into every rank's C
+        # over NVLink) unless RTB_NSPLIT_NCCL=1 asks for GEMM then NCCL all-gather
+        self.fused = self.nsplit and os.environ.get("RTB_NSPLIT_NCCL", "0") != "1"
         if self.nsplit:
-            from rustorch_b200.dist import NsplitGemm
-            self.gemm = NsplitGemm(rb.get_context(dev.index or 0), world, rank)
+            from rustorch_b200.dist import NsplitGemm, NsplitGemmP2P
+            ctx = rb.get_context(dev.index or 0)
+            self.gemm = (NsplitGemmP2P(ctx, world, rank, m, n) if self.fused
+                         else NsplitGemm(ctx, world, rank))
             self.parts = torch.empty((world, m, self.n_local), device=dev)
             self.c_local = torch.empty((m, self.n_local), device=dev)
-        par = (f"N-split x{world}: A . B[:, cols(rank)] on each GPU + NCCL all-gather of C"
-               if self.nsplit else None)
+        par = None
+        if self.nsplit:
+            par = (f"N-split x{world}: A . B[:, cols(rank)] per GPU, epilogue stores every tile "
+                   f"into all ranks' C over NVLink (fused exchange)" if self.fused else
+                   f"N-split x{world}: A . B[:, cols(rank)] per GPU + NCCL all-gather of C")
         self.config = {"workload": f"f32 matmul {m}x{n}x{k}", "seed": seed,
                        "layout": "row-major A[M,K], B[K,N]",
                        "l2": (f"rotating {self.nsets} operand sets" if self.nsets > 1 else
                               "operands larger than L2")}
         if par:
             self.config["parallelism_detail"] = par
-        # the all-gather and its repack are two more launches (NCCL + unsplit)
-        self.launches_per_step = 2 if self.nsplit else 1
+        # GEMM-then-all-gather adds the repack kernel (NCCL's own launches not counted)
+        self.launches_per_step = 2 if (self.nsplit and not self.fused) else 1
 
     def step(self):
         k = self.i % self.nsets
         self.i += 1
-        if self.nsplit:
+        if self.fused:
+            self.gemm(self.as_[k], self.bs[k], precision=PRECISION[0])
+        elif self.nsplit:
             self.gemm(self.as_[k], self.bs[k], precision=PRECISION[0], out=self.cs[k],
                       parts=self.parts)
         else:
@@ -423,7 +433,10 @@ class GemmWorkload:
         for key, dst in (("a", a), ("b", b)):
             p, nb = slot[key]
             rb.call("rtb_memcpy_h2d", ctx.handle, ctypes.c_void_p(dst.data_ptr()), p, nb, stream)
-        if self.nsplit:
+        if self.fused:
+            with self.torch.cuda.stream(st):
+                c = self.gemm(a, b, precision=PRECISION[0])
+        elif self.nsplit:
             with self.torch.cuda.stream(st):
                 self.gemm(a, b, precision=PRECISION[0], out=c, parts=self.parts)
         else:

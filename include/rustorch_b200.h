@@ -247,6 +247,25 @@ int rtb_sgemm_nsplit_allgather(rtb_ctx* ctx, void* comm, int64_t M, int64_t N, i
                                const float* A, const float* B_local, float* c_parts, float* C,
                                int precision, void* stream);
 
+/* N-split GEMM fused with its exchange: C [M,N] = A [M,K] . B [K,N] with B's
+ * columns split over the communicator's ranks (B_local = B[:, cols(rank)],
+ * [K, N/P] row-major).  The GEMM epilogue stores each finished tile of the
+ * rank's block into every rank's C over NVLink (P2P stores into CUDA IPC
+ * mappings), overlapping the exchange with the remaining tiles; a one-int
+ * all-reduce before and after the GEMM orders it against the previous
+ * reader and the peers' stores.  C lives in a peer buffer made once per
+ * communicator (collective calls, every rank with the same size):
+ * rtb_peer_buffer_local gives this rank's copy (valid until the next call on
+ * any rank).  Needs K and N/P multiples of 4 and 16-byte aligned A, B_local
+ * (RTB_E_UNSUPPORTED otherwise; rtb_sgemm_nsplit_allgather has no such
+ * limits).  No counterpart in the reference (multi-GPU extension). */
+int rtb_peer_buffer_create(rtb_ctx* ctx, void* comm, size_t bytes, void** peer_buffer);
+int rtb_peer_buffer_local(void* peer_buffer, float** local);
+int rtb_peer_buffer_destroy(void* peer_buffer, void* comm);
+int rtb_sgemm_nsplit_p2p(rtb_ctx* ctx, void* comm, void* peer_buffer, int64_t M, int64_t N,
+                         int64_t K, const float* A, const float* B_local, int precision,
+                         void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -62,6 +62,10 @@ SIGNATURES = {
     "rtb_conv2d_fwd": (_i, [_p] + [_i64] * 11 + [_p, _i, _p, _p, _p, _i, _p, _i, _i, _p]),
     "rtb_conv2d_fwd_noalloc": (_i, [_p] + [_i64] * 11 + [_p, _i, _p, _p, _p, _i, _p, _i, _i, _p]),
     "rtb_matmul_backward": (_i, [_p, _i64, _i64, _i64, _p, _p, _p, _p, _p, _i, _i, _p]),
+    "rtb_peer_buffer_create": (_i, [_p, _p, _sz, _p]),
+    "rtb_peer_buffer_local": (_i, [_p, _p]),
+    "rtb_peer_buffer_destroy": (_i, [_p, _p]),
+    "rtb_sgemm_nsplit_p2p": (_i, [_p, _p, _p, _i64, _i64, _i64, _p, _p, _i, _p]),
     "rtb_conv2d_backward": (_i, [_p] + [_i64] * 11 + [_p, _p, _p, _p, _p, _i, _i, _p]),
     "rtb_conv2d_packed_weight_size": (_i64, [_i64] * 4),
     "rtb_conv2d_prepack_weight": (_i, [_p, _i64, _i64, _i64, _i64, _p, _p, _p]),

@@ -139,6 +139,11 @@ int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
   p.relu = d.relu;
   p.out_mode = d.out_mode;
   p.hw = d.hw;
+  p.peer_c = d.peer_c;
+  p.npeers = d.npeers;
+  p.col_off = d.col_off;
+  if (d.out_mode == 2 && (!d.peer_c || d.npeers <= 0 || d.residual))
+    return set_error(RTB_E_INVALID, "gemm_run: peer output needs peer pointers and no residual");
   auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
   p.vec_ok = (d.out_mode == 0) && al16(d.C) && (d.ldc % 4 == 0) && (!d.bias || al16(d.bias)) &&
              (!d.residual || (al16(d.residual) && d.ldr % 4 == 0));

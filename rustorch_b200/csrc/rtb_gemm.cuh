@@ -65,7 +65,8 @@ struct GemmParams {
   const float* residual; // same indexing as C, or null
   int64_t ldr;
   int relu;
-  int out_mode;          // 0: C[m*ldc+n]; 1: NCHW scatter, m=(img,pix), C[(img*N+n)*hw+pix]
+  int out_mode;          // 0: C[m*ldc+n]; 1: NCHW scatter, m=(img,pix), C[(img*N+n)*hw+pix];
+                         // 2: every rank's C, peer_c[r][m*ldc + col_off + n] (N-split)
   int hw;                // Ho*Wo for out_mode 1
   int vec_ok;            // 16-byte aligned C/residual/bias with ldc, ldr % 4 == 0
   int c_tma;             // out_mode 0 with a TMA-storable C (tmC valid)
@@ -73,6 +74,11 @@ struct GemmParams {
   // implicit-GEMM conv (A gathered from NHWC input with Cp channels, Cp % 4 == 0)
   const float* x;
   int H, W, Cp, Ho, Wo, R, S, sh, sw, ph, pw;
+  // out_mode 2: base pointers of the npeers ranks' C (this rank's own included),
+  // written over NVLink by the epilogue; col_off = this rank's first column
+  float* const* peer_c;
+  int npeers;
+  int64_t col_off;
   // failure reporting
   int* err;
   unsigned long long timeout_ns;
@@ -257,6 +263,41 @@ __device__ __forceinline__ void epilogue_store32(const GemmParams& p, int m, int
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       if (n0 + j < p.N) crow[n0 + j] = p.relu ? fmaxf(v[j], 0.0f) : v[j];
+    }
+  }
+}
+
+// N-split epilogue: this thread's row m, columns n0..n0+31 of the rank's
+// block, stored into every rank's row-major C at column col_off + n0 (P2P
+// stores over NVLink for the peers; 16-byte aligned by the host's checks).
+__device__ __forceinline__ void epilogue_store_peers(const GemmParams& p, int m, int n0,
+                                                     const uint32_t (&r)[32], uint32_t sb) {
+  if (m >= p.M) return;
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+  if (p.bias) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      const float4 b = lds128(sb + 4 * j);
+      v[j] += b.x; v[j + 1] += b.y; v[j + 2] += b.z; v[j + 3] += b.w;
+    }
+  }
+  if (p.relu) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.0f);
+  }
+  const bool full = n0 + 32 <= p.N;
+  for (int q = 0; q < p.npeers; ++q) {
+    float* crow = p.peer_c[q] + (int64_t)m * p.ldc + p.col_off;
+    if (full) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4)
+        *reinterpret_cast<float4*>(crow + n0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (n0 + j < p.N) crow[n0 + j] = v[j];
     }
   }
 }
@@ -648,6 +689,8 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
         const uint32_t buf = smem_u32(sOut + (chunk % Cfg::kOutBufs) * kOutChunkBytes);
         epilogue_nchw_chunk(p, buf, row, et, tm * kBM, n0, r, sb);
         ++chunk;
+      } else if (p.out_mode == 2) {
+        epilogue_store_peers(p, m, n0, r, sb);
       } else {
         epilogue_store32(p, m, n0, r, sb);
       }
@@ -787,6 +830,9 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
         trace_stamp(p, 7 + 6 * tj);
     }
     if (p.c_tma && et == 0) bulk_wait_group<0>();  // all output stores complete
+    // peer stores are ordered before anything that follows the kernel on the
+    // stream (the cross-rank barrier after an N-split GEMM)
+    if (p.out_mode == 2) __threadfence_system();
   } else if (SPLIT && warp >= Roles::kWarpConv && warp < Roles::kWarpConv + 4) {
     // ------------------------------------------------------------ converters
     // Per k-block: thread = tile row (TMEM lane 32*(warp%4)+lane).  The A row

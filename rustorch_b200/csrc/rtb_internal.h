@@ -89,8 +89,11 @@ struct GemmDesc {
   const float* residual = nullptr;
   int64_t ldr = 0;
   int relu = 0;
-  int out_mode = 0;  // 0 row-major, 1 NCHW scatter
+  int out_mode = 0;  // 0 row-major, 1 NCHW scatter, 2 every rank's C (N-split)
   int hw = 0;
+  float* const* peer_c = nullptr;  // out_mode 2: device array of npeers C bases
+  int npeers = 0;
+  int64_t col_off = 0;
   // conv A producer: 0 = none (A is a matrix), 1 = cp.async gather, 2 = TMA im2col
   // (one tap x 32 channels per k-block), 3 = multi-tap TMA im2col (32 / Cp taps
   // of Cp channels per k-block, Cp in {4, 8, 16}; 3xTF32 only; selected for 8, 16)

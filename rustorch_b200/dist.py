@@ -87,4 +87,54 @@ class NsplitGemm:
         return c
 
 
-__all__ = ["shard_columns", "broadcast_id", "NsplitGemm", "lib"]
+class _DeviceArray:
+    """A device pointer with __cuda_array_interface__ (zero-copy torch view)."""
+
+    def __init__(self, ptr: int, shape):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": "<f4",
+                                         "data": (ptr, False), "version": 3, "strides": None}
+
+
+class NsplitGemmP2P:
+    """C = A . B with B's columns split across ranks, fused with the exchange:
+    the GEMM epilogue writes every tile into all ranks' C over NVLink
+    (rtb_sgemm_nsplit_p2p).  C is a library-owned peer buffer of [M, N]; `c`
+    is this rank's copy as a torch tensor (valid until the next call)."""
+
+    def __init__(self, ctx, world: int, rank: int, M: int, N: int, group=None):
+        import torch
+        self.ctx = ctx
+        self.world, self.rank = world, rank
+        self.M, self.N = M, N
+        uid = broadcast_id(group)
+        comm = ctypes.c_void_p()
+        call("rtb_nccl_comm_init", ctx.handle, ctypes.c_char_p(uid), world, rank,
+             ctypes.byref(comm))
+        self.comm = comm
+        pb = ctypes.c_void_p()
+        call("rtb_peer_buffer_create", ctx.handle, comm, M * N * 4, ctypes.byref(pb))
+        self.pbuf = pb
+        local = ctypes.c_void_p()
+        call("rtb_peer_buffer_local", pb, ctypes.byref(local))
+        self.c = torch.as_tensor(_DeviceArray(local.value, (M, N)),
+                                 device=torch.device("cuda", torch.cuda.current_device()))
+
+    def close(self) -> None:
+        if self.pbuf:
+            call("rtb_peer_buffer_destroy", self.pbuf, self.comm)
+            self.pbuf = None
+        if self.comm:
+            call("rtb_nccl_comm_destroy", self.comm)
+            self.comm = None
+
+    def __call__(self, a, b_local, precision: int = _lib.PREC_DEFAULT):
+        """a: [M,K] (replicated), b_local: [K, N/world]; returns C [M, N]."""
+        import torch
+        K = a.shape[1]
+        stream = ctypes.c_void_p(torch.cuda.current_stream(a.device).cuda_stream)
+        call("rtb_sgemm_nsplit_p2p", self.ctx.handle, self.comm, self.pbuf, self.M, self.N, K,
+             ctypes.c_void_p(a.data_ptr()), ctypes.c_void_p(b_local.data_ptr()), precision, stream)
+        return self.c
+
+
+__all__ = ["shard_columns", "broadcast_id", "NsplitGemm", "NsplitGemmP2P", "lib"]

@@ -1,5 +1,6 @@
-"""N-split GEMM with the NCCL all-gather of C on 2 GPUs (one process per GPU).
-Skipped on a single-GPU box."""
+"""N-split GEMM on 2 GPUs (one process per GPU): GEMM then NCCL all-gather of
+C, and the fused form whose epilogue writes every tile into both ranks' C over
+NVLink.  Skipped on a single-GPU box."""
 import multiprocessing as mp
 import os
 import socket
@@ -36,12 +37,23 @@ def _worker(rank, world, port, q):
         b = torch.randn(K, N, generator=g)
         lo, hi = rdist.shard_columns(N, world, rank)
         ns = rdist.NsplitGemm(ctx, world, rank)
-        c = ns(a.cuda(), b[:, lo:hi].contiguous().cuda())
+        da, db = a.cuda(), b[:, lo:hi].contiguous().cuda()
+        c = ns(da, db)
         torch.cuda.synchronize()
         ref = a.double() @ b.double()
         err = float((c.cpu().double() - ref).norm() / ref.norm())
         ns.close()
-        q.put((rank, err, ctx.device_error()))
+        # fused GEMM + exchange over NVLink: the same local GEMM, so the same
+        # bits as GEMM-then-all-gather; twice, the second with other inputs
+        fused = rdist.NsplitGemmP2P(ctx, world, rank, M, N)
+        c2 = fused(da, db).clone()
+        same = bool(torch.equal(c2, c))
+        a3 = torch.randn(M, K, generator=g)
+        c3 = fused(a3.cuda(), db).cpu().double()
+        ref3 = a3.double() @ b.double()
+        err3 = float((c3 - ref3).norm() / ref3.norm())
+        fused.close()
+        q.put((rank, err, ctx.device_error(), same, err3))
     finally:
         dist.destroy_process_group()
 
@@ -60,5 +72,6 @@ def test_nsplit_allgather_two_gpus(gpu):
         p.join(timeout=300)
         assert p.exitcode == 0
     res = sorted(q.get(timeout=10) for _ in range(2))
-    for rank, err, code in res:
+    for rank, err, code, same, err3 in res:
         assert err <= 1e-5 and code == 0, res
+        assert same and err3 <= 1e-5, res
