@@ -726,13 +726,26 @@ for _name, (_m, _n, _k, _seed) in GEMM_SHAPES.items():
 # ------------------------------------------------------------------ timing
 def _time_steps(torch, fn, steps, warmup, dev, dist=None, min_warm_s=0.3, pipe=None):
     # At least `warmup` steps, and at least min_warm_s of work so the SM
-    # clocks have left their idle state before the timed region starts.
+    # clocks have left their idle state before the timed region starts.  With
+    # several ranks every rank runs the same number of steps (a step may hold
+    # collectives, which must match across ranks): the extra count is agreed
+    # with a max all-reduce.
     t0 = time.perf_counter()
-    n = 0
-    while n < warmup or time.perf_counter() - t0 < min_warm_s:
+    for _ in range(warmup):
         fn()
-        n += 1
-        if n % 16 == 0:
+    torch.cuda.synchronize(dev)
+    elapsed = time.perf_counter() - t0
+    extra = 0
+    if elapsed < min_warm_s:
+        per_step = max(elapsed / max(1, warmup), 1e-6)
+        extra = int(math.ceil((min_warm_s - elapsed) / per_step))
+    if dist is not None:
+        t = torch.tensor([extra], device=dev, dtype=torch.int64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        extra = int(t.item())
+    for i in range(extra):
+        fn()
+        if (i + 1) % 16 == 0:
             torch.cuda.synchronize(dev)
     torch.cuda.synchronize(dev)
     if dist is not None:

@@ -267,37 +267,29 @@ __device__ __forceinline__ void epilogue_store32(const GemmParams& p, int m, int
   }
 }
 
-// N-split epilogue: this thread's row m, columns n0..n0+31 of the rank's
-// block, stored into every rank's row-major C at column col_off + n0 (P2P
-// stores over NVLink for the peers; 16-byte aligned by the host's checks).
-__device__ __forceinline__ void epilogue_store_peers(const GemmParams& p, int m, int n0,
-                                                     const uint32_t (&r)[32], uint32_t sb) {
-  if (m >= p.M) return;
-  float v[32];
-#pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-  if (p.bias) {
-#pragma unroll
-    for (int j = 0; j < 32; j += 4) {
-      const float4 b = lds128(sb + 4 * j);
-      v[j] += b.x; v[j + 1] += b.y; v[j + 2] += b.z; v[j + 3] += b.w;
-    }
-  }
-  if (p.relu) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.0f);
-  }
-  const bool full = n0 + 32 <= p.N;
-  for (int q = 0; q < p.npeers; ++q) {
-    float* crow = p.peer_c[q] + (int64_t)m * p.ldc + p.col_off;
-    if (full) {
-#pragma unroll
-      for (int j = 0; j < 32; j += 4)
-        *reinterpret_cast<float4*>(crow + n0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (n0 + j < p.N) crow[n0 + j] = v[j];
+// N-split epilogue, after epilogue_stage_rowmajor has put the 128 x 32 chunk
+// (bias/ReLU applied) into the 128B-swizzled staging buffer: thread et moves
+// float4 f = et + 128*i (row f/8, column group f%8), so each warp store covers
+// four whole 128-byte rows of C, into every rank's C at column col_off + n0
+// (P2P stores over NVLink for the peers; whole-line writes, 16-byte aligned by
+// the host's checks).
+__device__ __forceinline__ void epilogue_store_peers(const GemmParams& p, uint32_t buf, int et,
+                                                     int m0, int n0) {
+#pragma unroll 2
+  for (int i = 0; i < 8; ++i) {
+    const int f = et + 128 * i;
+    const int row = f >> 3, c4 = f & 7;
+    const int m = m0 + row, n = n0 + 4 * c4;
+    if (m >= p.M || n >= p.N) continue;
+    const float4 v = lds128(buf + row * 128 + ((c4 ^ (row & 7)) << 4));
+    for (int q = 0; q < p.npeers; ++q) {
+      float* dst = p.peer_c[q] + (int64_t)m * p.ldc + p.col_off + n;
+      if (n + 4 <= p.N) {
+        *reinterpret_cast<float4*>(dst) = v;
+      } else {
+        const float e[4] = {v.x, v.y, v.z, v.w};
+        for (int j = 0; j < 4 && n + j < p.N; ++j) dst[j] = e[j];
+      }
     }
   }
 }
@@ -690,7 +682,12 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
         epilogue_nchw_chunk(p, buf, row, et, tm * kBM, n0, r, sb);
         ++chunk;
       } else if (p.out_mode == 2) {
-        epilogue_store_peers(p, m, n0, r, sb);
+        const uint32_t buf = smem_u32(sOut + (chunk % Cfg::kOutBufs) * kOutChunkBytes);
+        epilogue_stage_rowmajor(p, buf, row, n0, m, r, sb);
+        named_bar_sync(1, 128);
+        epilogue_store_peers(p, buf, et, tm * kBM, n0);
+        named_bar_sync(1, 128);
+        ++chunk;
       } else {
         epilogue_store32(p, m, n0, r, sb);
       }
