@@ -9,19 +9,22 @@ Workloads (default: conv):
   gemm1024  f32 matmul 1024^3, A, B ~ N(0,1), seed 0.  Replicas at N>1.
   gemm2048, gemm4096, gemm8192, gemm16384
             square f32 matmul sweep, seed 4.  2048/4096 replicas at N>1;
-            8192/16384 N-split across the GPUs + NCCL all-gather of C (strong
-            scaling: one problem per job).
+            8192/16384 N-split across the GPUs, the GEMM epilogue storing every
+            tile into all ranks' C over NVLink (RTB_NSPLIT_NCCL=1: GEMM then NCCL
+            all-gather instead); strong scaling: one problem per job.
   gemm_m16, gemm_m64, gemm_m256
             skinny f32 matmul M x 8192 x 8192, seed 4 (HBM-bound for M < 128:
             roofline in GB/s).  Replicas at N>1.
   mlp       3-layer MLP forward, batch 4096, 1024->4096->4096->1024, seed 2.  Replicas.
+  conv_bwd  Conv2dBackward (grad_input + grad_weight) of the conv layer above, dy ~ N(0,1).
 
 Timing: W warm-up steps, then K steps between barrier + synchronize, CUDA
 events on the launching stream, max over ranks.  Inputs/outputs rotate over
 enough copies to exceed the 126 MB L2 so no step reads the previous step's
 data from L2.  `value` is the whole-job throughput (sum over ranks of the
 algorithmic FLOPs / max time).  `e2e` times the same call through the C ABI
-with host buffers (pinned H2D of the step's inputs, D2H of its output).
+with host buffers (pinned H2D of the step's inputs, D2H of its output), steps
+pipelined over 2-3 streams so one step's copies overlap another's call.
 """
 from __future__ import annotations
 
@@ -308,6 +311,118 @@ class ConvWorkload:
         flops = self.flops * nimg / self.N
         return flops / dt / 1e12, (f"{nimg} of 32 images per call (im2col + row-parallel core, "
                                    f"bias, ReLU), {reps} calls")
+
+
+class ConvBwdWorkload:
+    """Conv2dBackward of the ResNet-50 stage-2 3x3 layer: grad_input and
+    grad_weight for x [32,128,28,28], w [128,128,3,3], dy ~ N(0,1), NCHW."""
+    name = "conv2d_backward_resnet50_3x3"
+
+    def __init__(self, rb, torch, dev):
+        self.rb, self.torch, self.dev = rb, torch, dev
+        self.N, self.C, self.H, self.W, self.Co = 32, 128, 28, 28, 128
+        self.flops = 2 * 2.0 * self.N * self.H * self.W * self.Co * self.C * 9  # dx and dw
+        x = rb.fill_normal((self.N, self.C, self.H, self.W), 1, 0)
+        w = rb.fill_normal((self.Co, self.C, 3, 3), 1, 1, 0.0, math.sqrt(2.0 / (self.C * 9)))
+        dy = rb.fill_normal((self.N, self.Co, self.H, self.W), 1, 3)
+        self.host = {"x": x, "w": w, "dy": dy}
+        per_set = (x.nbytes + dy.nbytes + x.nbytes)
+        self.nsets = max(2, int(math.ceil(2 * L2_BYTES / per_set)))
+        self.xs = [torch.from_numpy(x).to(dev) for _ in range(self.nsets)]
+        self.dys = [torch.from_numpy(dy).to(dev) for _ in range(self.nsets)]
+        self.dxs = [torch.empty_like(self.xs[0]) for _ in range(self.nsets)]
+        self.w = torch.from_numpy(w).to(dev)
+        self.dw = torch.empty_like(self.w)
+        self.i = 0
+        self.config = {"workload": "conv2d backward (grad_input + grad_weight), ResNet-50 "
+                                   "stage-2 3x3", "input": [32, 128, 28, 28],
+                       "weight": [128, 128, 3, 3], "stride": 1, "pad": 1, "seed": 1,
+                       "layout": "NCHW", "roofline_note": "achieved = the whole backward call",
+                       "l2": f"rotating {self.nsets} x/dy/dx sets"}
+        # dx: dilate, flip-pack, conv; dw: layout, im2col, transpose, GEMM, unpack
+        self.launches_per_step = 8
+
+    def _call(self, x, dy, dx, dw, stream, w=None):
+        rb = self.rb
+        ctx = rb.get_context(self.dev.index or 0)
+        w = self.w if w is None else w
+        rb.call("rtb_conv2d_backward", ctx.handle, self.N, self.C, self.H, self.W, self.Co, 3, 3,
+                1, 1, 1, 1, ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(w.data_ptr()),
+                ctypes.c_void_p(dy.data_ptr()), ctypes.c_void_p(dx.data_ptr()),
+                ctypes.c_void_p(dw.data_ptr()), 0, PRECISION[0], stream)
+
+    def step(self):
+        k = self.i % self.nsets
+        self.i += 1
+        stream = ctypes.c_void_p(self.torch.cuda.current_stream(self.dev).cuda_stream)
+        self._call(self.xs[k], self.dys[k], self.dxs[k], self.dw, stream)
+
+    def kernel_setup(self):
+        pass
+
+    def kernel_step(self):
+        self.step()
+
+    def e2e_setup(self):
+        rb, torch = self.rb, self.torch
+        ctx = rb.get_context(self.dev.index or 0)
+        self.pipe = E2EPipeline(torch, self.dev, 2)
+        self.slots = []
+        for _ in range(self.pipe.depth):
+            slot = {key: _pinned_copy(rb, ctx, arr) for key, arr in self.host.items()}
+            slot["pdx"] = _pinned_empty(rb, ctx, self.host["x"].nbytes)
+            slot["pdw"] = _pinned_empty(rb, ctx, self.host["w"].nbytes)
+            slot["dx_"] = torch.empty_like(self.xs[0])
+            slot["dy_"] = torch.empty_like(self.dys[0])
+            slot["x_"] = torch.empty_like(self.xs[0])
+            slot["ddx"] = torch.empty_like(self.xs[0])
+            slot["ddw"] = torch.empty_like(self.w)
+            slot["w_"] = torch.empty_like(self.w)
+            self.slots.append(slot)
+        self.h2d_bytes = sum(a.nbytes for a in self.host.values())
+        self.d2h_bytes = self.host["x"].nbytes + self.host["w"].nbytes
+
+    def e2e_step(self):
+        rb = self.rb
+        ctx = rb.get_context(self.dev.index or 0)
+        k, _, stream = self.pipe.next()
+        sl = self.slots[k]
+        for key, dst in (("x", sl["x_"]), ("dy", sl["dy_"])):
+            rb.call("rtb_memcpy_h2d", ctx.handle, ctypes.c_void_p(dst.data_ptr()), sl[key],
+                    self.host[key].nbytes, stream)
+        rb.call("rtb_memcpy_h2d", ctx.handle, ctypes.c_void_p(sl["w_"].data_ptr()), sl["w"],
+                self.host["w"].nbytes, stream)
+        self._call(sl["x_"], sl["dy_"], sl["ddx"], sl["ddw"], stream, sl["w_"])
+        rb.call("rtb_memcpy_d2h", ctx.handle, sl["pdx"], ctypes.c_void_p(sl["ddx"].data_ptr()),
+                self.host["x"].nbytes, stream)
+        rb.call("rtb_memcpy_d2h", ctx.handle, sl["pdw"], ctypes.c_void_p(sl["ddw"].data_ptr()),
+                self.host["w"].nbytes, stream)
+
+    def e2e_teardown(self):
+        ctx = self.rb.get_context(self.dev.index or 0)
+        for sl in self.slots:
+            for key in ("x", "w", "dy", "pdx", "pdw"):
+                self.rb.call("rtb_host_free", ctx.handle, sl[key])
+        self.slots = []
+
+    def cpu_sample(self, threads):
+        """The reference's Conv2dBackward direct cores (f64 accumulation,
+        conv.rs:336-502) restated, on one image of the batch."""
+        from oracle import oracle as orc
+        x = orc.normal((1, self.C, self.H, self.W), 1, 0)
+        w = orc.normal((self.Co, self.C, 3, 3), 1, 1, 0.0, math.sqrt(2.0 / (self.C * 9)))
+        dy = orc.normal((1, self.Co, self.H, self.W), 1, 3)
+        t0 = time.perf_counter()
+        reps = 0
+        while True:
+            orc.conv2d_grad_input_f64(dy, w, x.shape, (1, 1), (1, 1), threads=threads)
+            orc.conv2d_grad_weight_f64(x, dy, w.shape, (1, 1), (1, 1), threads=threads)
+            reps += 1
+            if time.perf_counter() - t0 > 10.0 or reps >= 20:
+                break
+        dt = (time.perf_counter() - t0) / reps
+        return self.flops / self.N / dt / 1e12, (f"1 of 32 images per call (direct f64 grad_input "
+                                                 f"and grad_weight cores), {reps} calls")
 
 
 # f32 matmul shapes (M, N, K, seed): the 1024^3 workload and the large-GEMM
@@ -707,6 +822,7 @@ class MlpWorkload:
 
 WORKLOADS = {
     "conv": lambda rb, torch, dev: ConvWorkload(rb, torch, dev),
+    "conv_bwd": lambda rb, torch, dev: ConvBwdWorkload(rb, torch, dev),
     "resnet18": lambda rb, torch, dev: ResNet18Workload(rb, torch, dev),
     "mlp": lambda rb, torch, dev: MlpWorkload(rb, torch, dev),
 }
@@ -892,6 +1008,14 @@ def run_reference(args):
         wl.flops = 2.0 * wl.N * wl.H * wl.W * wl.Co * wl.C * 9
         cfg = {"workload": "conv2d+bias+relu ResNet-50 stage-2 3x3", "input": [32, 128, 28, 28],
                "weight": [128, 128, 3, 3], "stride": 1, "pad": 1, "seed": 1}
+        unit = "TFLOP/s"
+    elif args.workload == "conv_bwd":
+        wl = ConvBwdWorkload.__new__(ConvBwdWorkload)
+        wl.N, wl.C, wl.H, wl.W, wl.Co = 32, 128, 28, 28, 128
+        wl.flops = 2 * 2.0 * wl.N * wl.H * wl.W * wl.Co * wl.C * 9
+        cfg = {"workload": "conv2d backward (grad_input + grad_weight), ResNet-50 stage-2 3x3",
+               "input": [32, 128, 28, 28], "weight": [128, 128, 3, 3], "stride": 1, "pad": 1,
+               "seed": 1}
         unit = "TFLOP/s"
     elif args.workload == "resnet18":
         wl = ResNet18Workload.__new__(ResNet18Workload)
