@@ -130,6 +130,14 @@ Tensor add(const Tensor& lhs, const Tensor& rhs);
 Tensor mul(const Tensor& lhs, const Tensor& rhs);
 Tensor max_pool2d(const Tensor& input, Pair kernel_size, Pair stride, Pair padding);
 Tensor global_avg_pool(const Tensor& input);  // [N,C,H,W] -> [N,C]
+// MatmulBackward::backward (rustorch-core/src/ops.rs:529-570) for
+// out = lhs.matmul(rhs): {grad.matmul(rhs.t()), lhs.t().matmul(grad)}.
+std::pair<Tensor, Tensor> matmul_backward(const Tensor& lhs, const Tensor& rhs,
+                                          const Tensor& grad);
+// Conv2dBackward::backward (rustorch-core/src/ops/conv.rs:648-736):
+// {grad_input, grad_weight} of conv2d(input, weight, stride, padding).
+std::pair<Tensor, Tensor> conv2d_backward(const Tensor& input, const Tensor& weight,
+                                          const Tensor& grad, Pair stride, Pair padding);
 }  // namespace ops
 
 namespace nn {

@@ -453,6 +453,43 @@ Tensor max_pool2d(const Tensor& input, Pair k, Pair s, Pair pd) {
   return finish(y, p);
 }
 
+std::pair<Tensor, Tensor> matmul_backward(const Tensor& lhs, const Tensor& rhs,
+                                          const Tensor& grad) {
+  if (lhs.dim() != 2 || rhs.dim() != 2 || grad.dim() != 2) throw Panic("Matmul only supports 2D");
+  const size_t m = lhs.shape()[0], k = lhs.shape()[1], n = rhs.shape()[1];
+  if (rhs.shape()[0] != k || grad.shape()[0] != m || grad.shape()[1] != n)
+    throw Panic("Matmul dimension mismatch");
+  Placement p = place({&lhs, &rhs, &grad});
+  Tensor a = on(lhs, p).contiguous(), b = on(rhs, p).contiguous(), g = on(grad, p).contiguous();
+  Tensor da = make_contig(Device::cuda(p.device), {m, k});
+  Tensor db = make_contig(Device::cuda(p.device), {k, n});
+  chk(rtb_matmul_backward(context(p.device), (int64_t)m, (int64_t)n, (int64_t)k, a.device_ptr(),
+                          b.device_ptr(), g.device_ptr(), da.device_ptr(), db.device_ptr(), 0,
+                          g_precision, nullptr),
+      "matmul_backward");
+  return {finish(da, p), finish(db, p)};
+}
+
+std::pair<Tensor, Tensor> conv2d_backward(const Tensor& input, const Tensor& weight,
+                                          const Tensor& grad, Pair stride, Pair padding) {
+  if (input.dim() != 4 || weight.dim() != 4 || grad.dim() != 4)
+    throw Panic("Conv2d requires 4D tensors");
+  const auto& is = input.shape();
+  const auto& ws = weight.shape();
+  Placement p = place({&input, &weight, &grad});
+  Tensor x = on(input, p).contiguous(), w = on(weight, p).contiguous();
+  Tensor g = on(grad, p).contiguous();
+  Tensor dx = make_contig(Device::cuda(p.device), is);
+  Tensor dw = make_contig(Device::cuda(p.device), ws);
+  chk(rtb_conv2d_backward(context(p.device), (int64_t)is[0], (int64_t)is[1], (int64_t)is[2],
+                          (int64_t)is[3], (int64_t)ws[0], (int64_t)ws[2], (int64_t)ws[3],
+                          (int64_t)stride.first, (int64_t)stride.second, (int64_t)padding.first,
+                          (int64_t)padding.second, x.device_ptr(), w.device_ptr(), g.device_ptr(),
+                          dx.device_ptr(), dw.device_ptr(), 0, g_precision, nullptr),
+      "conv2d_backward");
+  return {finish(dx, p), finish(dw, p)};
+}
+
 Tensor global_avg_pool(const Tensor& input) {
   if (input.dim() != 4) throw Panic("global_avg_pool requires 4D tensor (N, C, H, W)");
   Placement p = place({&input});

@@ -120,6 +120,30 @@ static void device_tests() {
     for (int i = 0; i < 4; ++i)
       expect(std::fabs(got[i] - expected[i]) < 1e-6f, "matmul value " + std::to_string(i));
   });
+  run("test_matmul_backward_precision_under_1e6", [] {
+    // loss = sum(a.matmul(b)): the incoming gradient is all ones
+    Tensor a = Tensor::new_({1.0, 2.0, 3.0, 4.0}, {2, 2});
+    Tensor b = Tensor::new_({5.0, 6.0, 7.0, 8.0}, {2, 2});
+    auto grads = ops::matmul_backward(a, b, Tensor::ones({2, 2}));
+    std::vector<float> ga = grads.first.data(), gb = grads.second.data();
+    kat("matmul_backward_2x2_a", ga);
+    kat("matmul_backward_2x2_b", gb);
+    const float ea[4] = {11.0f, 15.0f, 11.0f, 15.0f}, eb[4] = {4.0f, 4.0f, 6.0f, 6.0f};
+    for (int i = 0; i < 4; ++i) {
+      expect(std::fabs(ga[i] - ea[i]) < 1e-6f, "grad_a value " + std::to_string(i));
+      expect(std::fabs(gb[i] - eb[i]) < 1e-6f, "grad_b value " + std::to_string(i));
+    }
+  });
+  run("conv2d_backward_shapes", [] {
+    Tensor x = Tensor::ones({1, 1, 3, 3});
+    Tensor w = Tensor::ones({1, 1, 2, 2});
+    auto grads = ops::conv2d_backward(x, w, Tensor::ones({1, 1, 2, 2}), {1, 1}, {0, 0});
+    // each input element is covered by 1, 2 or 4 windows; each weight by 4 positions
+    std::vector<float> gx = grads.first.data(), gw = grads.second.data();
+    const float ex[9] = {1, 2, 1, 2, 4, 2, 1, 2, 1};
+    for (int i = 0; i < 9; ++i) expect(std::fabs(gx[i] - ex[i]) < 1e-6f, "grad_input value");
+    for (int i = 0; i < 4; ++i) expect(std::fabs(gw[i] - 4.0f) < 1e-6f, "grad_weight value");
+  });
   run("test_conv2d_forward_precision_under_1e6", [] {
     Tensor input = Tensor::new_({1, 2, 3, 4, 5, 6, 7, 8, 9}, {1, 1, 3, 3});
     Tensor weight = Tensor::new_({1.0, 0.0, 0.0, -1.0}, {1, 1, 2, 2});

@@ -51,5 +51,10 @@ def test_reference_tests_on_device(binary, kats, gpu):
                                atol=kats["matmul_2x2"]["abs_tol"], rtol=0)
     np.testing.assert_allclose(got["conv2d_3x3_k2"], kats["conv2d_3x3_k2"]["expected"],
                                atol=kats["conv2d_3x3_k2"]["abs_tol"], rtol=0)
+    kb = kats["matmul_backward_2x2"]
+    np.testing.assert_allclose(got["matmul_backward_2x2_a"], kb["expected_grad_a"],
+                               atol=kb["abs_tol"], rtol=0)
+    np.testing.assert_allclose(got["matmul_backward_2x2_b"], kb["expected_grad_b"],
+                               atol=kb["abs_tol"], rtol=0)
     k = kats["jit_conv2d_relu_ones"]
     assert abs(got["jit_conv2d_relu_ones"][0] - k["expected_first"]) < k["abs_tol"]
