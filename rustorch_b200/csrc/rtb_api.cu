@@ -779,11 +779,15 @@ int rtb_conv2d_backward(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t 
     float* wt = nullptr;
     const size_t dyd_bytes = (size_t)(N * Hd * Wd * Cop) * 4;
     st = ws_alloc(ctx, (void**)&dyd, dyd_bytes, s);
-    if (st == RTB_OK) {
+    if (st == RTB_OK && Hd == Ho && Wd == Wo) {
+      // nothing to dilate (stride 1): the plain channel-padded NHWC copy
+      st = launch_nchw_to_nhwc_padded(dy, N, Co, Ho, Wo, Cop, dyd, s);
+    } else if (st == RTB_OK) {
       cudaError_t e = cudaMemsetAsync(dyd, 0, dyd_bytes, s);
       st = e == cudaSuccess ? RTB_OK : cuda_status(e, "conv_backward memset");
+      if (st == RTB_OK)
+        st = launch_dilate_nchw_to_nhwc(dy, N, Co, Ho, Wo, sh, sw, Hd, Wd, Cop, dyd, s);
     }
-    if (st == RTB_OK) st = launch_dilate_nchw_to_nhwc(dy, N, Co, Ho, Wo, sh, sw, Hd, Wd, Cop, dyd, s);
     if (st == RTB_OK) st = ws_alloc(ctx, (void**)&wt, (size_t)(Ci * kh * kw * Cop) * 4, s);
     if (st == RTB_OK) st = launch_prepack_flip(w, Co, Ci, kh, kw, Cop, wt, s);
     if (st == RTB_OK)

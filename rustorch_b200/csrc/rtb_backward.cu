@@ -73,41 +73,43 @@ __global__ void prepack_flip_kernel(const float* __restrict__ w, int Co, int Ci,
 
 // x NHWC [N, H, W, Cp] -> col [P, R*S*Cp], col[p][(r*S + s)*Cp + c] =
 // x[n][oh*sh - ph + r][ow*sw - pw + s][c] (zero outside the image), the same
-// (tap, channel) order as the forward conv's packed weight.  16-byte copies.
+// (tap, channel) order as the forward conv's packed weight.  One block row per
+// output pixel p (grid.x strides over P), threads over the row's 16-byte
+// groups: both the read (a tap's Cp channels) and the write are contiguous.
 __global__ void im2col_nhwc_kernel(const float4* __restrict__ x, int H, int W, int Cp4, int Ho,
                                    int Wo, int R, int S, int sh, int sw, int ph, int pw,
                                    int64_t P, float4* __restrict__ col) {
-  const int64_t Kp4 = (int64_t)R * S * Cp4;
-  const int64_t total = P * Kp4;
-  const int64_t HoWo = (int64_t)Ho * Wo;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t p = i / Kp4;
-    const int k4 = (int)(i - p * Kp4);
-    const int tap = k4 / Cp4, c4 = k4 - tap * Cp4;
-    const int r = tap / S, s = tap - r * S;
+  const int Kp4 = R * S * Cp4;
+  const int HoWo = Ho * Wo;
+  for (int64_t p = blockIdx.x; p < P; p += gridDim.x) {
     const int64_t n = p / HoWo;
     const int pix = (int)(p - n * HoWo);
     const int oh = pix / Wo, ow = pix - oh * Wo;
-    const int ih = oh * sh - ph + r, iw = ow * sw - pw + s;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (ih >= 0 && ih < H && iw >= 0 && iw < W) v = x[((n * H + ih) * W + iw) * Cp4 + c4];
-    col[i] = v;
+    const float4* xn = x + n * H * W * Cp4;
+    float4* dst = col + p * Kp4;
+    for (int k4 = threadIdx.x; k4 < Kp4; k4 += blockDim.x) {
+      const int tap = k4 / Cp4, c4 = k4 - tap * Cp4;
+      const int r = tap / S, s = tap - r * S;
+      const int ih = oh * sh - ph + r, iw = ow * sw - pw + s;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (ih >= 0 && ih < H && iw >= 0 && iw < W) v = xn[((int64_t)ih * W + iw) * Cp4 + c4];
+      dst[k4] = v;
+    }
   }
 }
 
 // dy NCHW [N, Co, HW] -> dyt [Co, ldp], dyt[co][n*HW + pix] = dy[n][co][pix]
-// (the K-major left operand of grad_weight).
-__global__ void nchw_to_cmajor_kernel(const float* __restrict__ dy, int64_t N, int Co, int64_t HW,
+// (the K-major left operand of grad_weight): one block row per (n, co) plane,
+// a contiguous copy.
+__global__ void nchw_to_cmajor_kernel(const float* __restrict__ dy, int64_t N, int Co, int HW,
                                       int64_t ldp, float* __restrict__ dyt) {
-  const int64_t total = N * Co * HW;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t pix = i % HW;
-    const int64_t t = i / HW;
-    const int64_t co = t % Co;
-    const int64_t n = t / Co;
-    dyt[co * ldp + n * HW + pix] = dy[i];
+  const int64_t planes = N * Co;
+  for (int64_t pl = blockIdx.x; pl < planes; pl += gridDim.x) {
+    const int64_t n = pl / Co;
+    const int co = (int)(pl - n * Co);
+    const float* src = dy + pl * HW;
+    float* dst = dyt + (int64_t)co * ldp + n * HW;
+    for (int i = threadIdx.x; i < HW; i += blockDim.x) dst[i] = src[i];
   }
 }
 
@@ -153,8 +155,11 @@ int launch_im2col_nhwc(const float* x, int64_t N, int64_t H, int64_t W, int64_t 
                        int64_t Wo, int64_t R, int64_t S, int64_t sh, int64_t sw, int64_t ph,
                        int64_t pw, float* col, cudaStream_t s) {
   const int64_t P = N * Ho * Wo;
+  if (R * S * (Cp / 4) > INT32_MAX || H * W > INT32_MAX || Ho * Wo > INT32_MAX)
+    return set_error(RTB_E_UNSUPPORTED, "im2col: too large");
+  const int64_t blocks = P < 148 * 64 ? P : 148 * 64;
   clear_stale_cuda_error();
-  im2col_nhwc_kernel<<<grid_for(P * R * S * (Cp / 4)), kT, 0, s>>>(
+  im2col_nhwc_kernel<<<(unsigned)blocks, 128, 0, s>>>(
       reinterpret_cast<const float4*>(x), (int)H, (int)W, (int)(Cp / 4), (int)Ho, (int)Wo, (int)R,
       (int)S, (int)sh, (int)sw, (int)ph, (int)pw, P, reinterpret_cast<float4*>(col));
   return launch_check("im2col_nhwc");
@@ -162,8 +167,11 @@ int launch_im2col_nhwc(const float* x, int64_t N, int64_t H, int64_t W, int64_t 
 
 int launch_nchw_to_cmajor(const float* dy, int64_t N, int64_t Co, int64_t HW, int64_t ldp,
                           float* dyt, cudaStream_t s) {
+  if (HW > INT32_MAX || Co > INT32_MAX) return set_error(RTB_E_UNSUPPORTED, "nchw_to_cmajor: too large");
+  const int64_t planes = N * Co;
+  const int64_t blocks = planes < 148 * 64 ? planes : 148 * 64;
   clear_stale_cuda_error();
-  nchw_to_cmajor_kernel<<<grid_for(N * Co * HW), kT, 0, s>>>(dy, N, (int)Co, HW, ldp, dyt);
+  nchw_to_cmajor_kernel<<<(unsigned)blocks, 256, 0, s>>>(dy, N, (int)Co, (int)HW, ldp, dyt);
   return launch_check("nchw_to_cmajor");
 }
 

@@ -69,10 +69,16 @@ int pick_bn(rtb_ctx* ctx, const GemmDesc& d) {
   const int cands_fast[3] = {256, 128, 64};
   const int* c = d.split3 ? cands_split : cands_fast;
   const int nc = d.split3 ? 2 : 3;
+  const int64_t num_kb = (d.K + kBK - 1) / kBK;
   for (int i = 0; i < nc; ++i) {
     if (c[i] > 64 && d.N <= c[i] / 2) continue;  // half the tile (or more) would be padding
     const int64_t tiles = tm * ((d.N + c[i] - 1) / c[i]);
     if (tiles >= ctx->sm_count) return c[i];
+    // few tiles but a long K: the K split of the work units fills the SMs,
+    // and a wider tile halves the per-k-block overhead per flop
+    if (c[i] == 128 && d.allow_workspace && tiles * 2 <= ctx->sm_count &&
+        num_kb >= 4 * ((ctx->sm_count + tiles - 1) / tiles))
+      return 128;
   }
   return 64;
 }
@@ -190,8 +196,12 @@ int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
     const int64_t G = ctx->sm_count;
     const int64_t rem = tiles % G;
     if (rem > 0 && rem * 2 <= G) {
+      // up to 16 pieces (a few tiles with a very long K, e.g. a conv's weight
+      // gradient: 9 tiles x 784 k-blocks), each piece >= 4 k-blocks once the
+      // split passes 8 (the last piece's fix-up reads every piece)
       int sk = (int)(G / rem);
-      if (sk > 8) sk = 8;
+      if (sk > 16) sk = 16;
+      if (sk > 8 && sk > p.num_kb / 4) sk = p.num_kb / 4 > 8 ? p.num_kb / 4 : 8;
       if (sk > p.num_kb / 2) sk = p.num_kb / 2;  // every piece keeps >= 2 k-blocks
       if (sk >= 2) {
         const size_t part_bytes = (size_t)rem * sk * bn * kBM * sizeof(float);
