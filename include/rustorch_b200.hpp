@@ -60,6 +60,10 @@ int precision();
 // Waits for the device and turns a device-side timeout into a Panic.
 void synchronize(int device);
 
+// Host <-> device tensor copies made so far by this process (Tensor::to and
+// the ops' staging of CPU operands); diagnostics for keeping data resident.
+uint64_t transfer_count();
+
 using Pair = std::pair<size_t, size_t>;
 
 class Tensor {

@@ -4,6 +4,7 @@
 #include <rustorch_b200.hpp>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstring>
 #include <map>
@@ -187,9 +188,16 @@ std::vector<float> Tensor::data() const {
   return out;
 }
 
+namespace {
+std::atomic<uint64_t> g_transfers{0};
+}  // namespace
+
+uint64_t transfer_count() { return g_transfers.load(); }
+
 Tensor Tensor::to(Device d) const {
   if (!storage_) return *this;
   if (d == device()) return *this;
+  if (d.is_cuda() != device().is_cuda()) g_transfers.fetch_add(1);
   Tensor src = contiguous();
   Tensor dst = make_contig(d, shape_);
   const size_t bytes = numel() * sizeof(float);
@@ -644,11 +652,27 @@ void fuse(Graph& g) {
 
 void Optimizer::optimize(Graph& graph) { fuse(graph); }
 
+// Device-resident execution: CPU inputs and weights move to the device once,
+// every node runs on device tensors (no per-node host round trip), and the
+// outputs come back to the CPU at the end (jit.rs:216 runs nodes in index
+// order on whatever the inputs are; results are returned where they were).
 std::vector<Tensor> Executor::run(const Graph& graph, const std::vector<Tensor>& inputs) {
   std::map<size_t, Tensor> values;
+  bool host = false;
+  int dev = -1;
+  for (size_t i = 0; i < graph.inputs.size() && i < inputs.size(); ++i) {
+    if (!inputs[i].defined()) continue;
+    if (inputs[i].device().is_cuda()) {
+      if (dev < 0) dev = inputs[i].device().index;
+    } else {
+      host = true;
+    }
+  }
+  if (dev < 0) dev = 0;
+  const Device on_dev = Device::cuda(dev);
   for (size_t i = 0; i < graph.inputs.size(); ++i) {
     if (i >= inputs.size()) throw Panic("Executor::run: missing input");
-    values[graph.inputs[i]] = inputs[i];
+    values[graph.inputs[i]] = inputs[i].defined() ? inputs[i].to(on_dev) : inputs[i];
   }
   auto get = [&](size_t id) -> const Tensor& {
     auto it = values.find(id);
@@ -661,7 +685,7 @@ std::vector<Tensor> Executor::run(const Graph& graph, const std::vector<Tensor>&
     Tensor v;
     switch (op.op) {
       case Op::Input: throw Panic("Input should be loaded");
-      case Op::Weight: v = op.weight; break;
+      case Op::Weight: v = op.weight.defined() ? op.weight.to(on_dev) : op.weight; break;
       case Op::Add: v = get(op.a).add(get(op.b)); break;
       case Op::Mul: v = get(op.a).mul(get(op.b)); break;
       case Op::MatMul: v = get(op.a).matmul(get(op.b)); break;
@@ -685,7 +709,7 @@ std::vector<Tensor> Executor::run(const Graph& graph, const std::vector<Tensor>&
     values[node.id] = v;
   }
   std::vector<Tensor> out;
-  for (size_t id : graph.outputs) out.push_back(get(id));
+  for (size_t id : graph.outputs) out.push_back(host ? get(id).to_cpu() : get(id));
   return out;
 }
 

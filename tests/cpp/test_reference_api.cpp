@@ -144,6 +144,27 @@ static void device_tests() {
     for (int i = 0; i < 9; ++i) expect(std::fabs(gx[i] - ex[i]) < 1e-6f, "grad_input value");
     for (int i = 0; i < 4; ++i) expect(std::fabs(gw[i] - 4.0f) < 1e-6f, "grad_weight value");
   });
+  run("jit_executor_keeps_values_on_device", [] {
+    // conv -> relu -> relu with CPU inputs: the inputs go to the device once
+    // and the output comes back once; no per-node host round trip
+    jit::Graph g;
+    size_t in = g.add_input({1, 2, 6, 6});
+    size_t w = g.add_input({3, 2, 3, 3});
+    size_t c = g.add_node(jit::NodeType::Conv2d(in, w, {1, 1}, {1, 1}), {1, 3, 6, 6});
+    size_t r = g.add_node(jit::NodeType::Relu(c), {1, 3, 6, 6});
+    size_t r2 = g.add_node(jit::NodeType::Relu(r), {1, 3, 6, 6});
+    g.outputs.push_back(r2);
+    Tensor x = Tensor::randn({1, 2, 6, 6}, 1, 1), wt = Tensor::randn({3, 2, 3, 3}, 1, 2);
+    const uint64_t t0 = transfer_count();
+    auto res = jit::Executor::run(g, {x, wt});
+    expect(transfer_count() - t0 == 3, "expected 2 uploads + 1 download, got " +
+                                           std::to_string(transfer_count() - t0));
+    expect(res[0].device().kind == Device::Cpu, "CPU inputs must give a CPU result");
+    std::vector<float> got = res[0].data();
+    std::vector<float> ref = ops::relu(ops::conv2d(x, wt, {1, 1}, {1, 1})).data();
+    for (size_t i = 0; i < got.size(); ++i)
+      expect(std::fabs(got[i] - ref[i]) <= 1e-5f * (1.0f + std::fabs(ref[i])), "jit value");
+  });
   run("test_conv2d_forward_precision_under_1e6", [] {
     Tensor input = Tensor::new_({1, 2, 3, 4, 5, 6, 7, 8, 9}, {1, 1, 3, 3});
     Tensor weight = Tensor::new_({1.0, 0.0, 0.0, -1.0}, {1, 1, 2, 2});
