@@ -820,11 +820,111 @@ class MlpWorkload:
         return self.flops * rows / self.M / dt / 1e12, f"{rows} of 4096 rows, {reps} passes"
 
 
+class LinearNormWorkload:
+    """nn::Linear::forward_fused_norm_activation (rustorch-nn/src/linear.rs:53-71
+    -> ops::matmul_bias_norm_activation, rustorch-core/src/ops.rs:1815-1886):
+    X [8192, 1024] . W^T (W [4096, 1024]) + bias, LayerNorm over the 4096
+    features (weight, bias, eps 1e-5), ReLU.  Two launches: the tcgen05 GEMM
+    with the bias in its epilogue, then the row-wise LayerNorm + ReLU."""
+    name = "linear_norm_relu"
+
+    def __init__(self, rb, torch, dev):
+        self.rb, self.torch, self.dev = rb, torch, dev
+        self.M, self.K, self.N = 8192, 1024, 4096
+        self.flops = 2.0 * self.M * self.K * self.N   # GEMM FLOPs (LayerNorm's ~9 per element omitted)
+        bound = 1.0 / math.sqrt(self.K)
+        self.host = {"x": rb.fill_normal((self.M, self.K), 4, 0),
+                     "w": rb.fill_uniform((self.N, self.K), 4, 1, -bound, bound),
+                     "b": rb.fill_uniform((self.N,), 4, 2, -bound, bound),
+                     "g": rb.fill_normal((self.N,), 4, 3, 1.0, 0.1),
+                     "beta": rb.fill_normal((self.N,), 4, 4, 0.0, 0.1)}
+        t = {k: torch.from_numpy(v).to(dev) for k, v in self.host.items()}
+        self.x, self.w, self.b, self.g, self.beta = t["x"], t["w"], t["b"], t["g"], t["beta"]
+        self.y = torch.empty((self.M, self.N), device=dev)
+        self.config = {"workload": "Linear 1024->4096 + bias, LayerNorm(4096) + ReLU over 8192 rows",
+                       "seed": 4, "l2": "operands + output larger than L2 (~180 MB)"}
+        self.launches_per_step = 2
+        self.unit = "TFLOP/s"
+        self.ln_bytes = 2.0 * 4 * self.M * self.N     # LayerNorm pass: read C, write Y
+
+    def _fwd(self, x, y):
+        self.rb.matmul_bias_norm_activation(x, self.w.t(), self.b, self.g, self.beta, 1e-5,
+                                            self.rb.ACT_RELU, PRECISION[0], out=y)
+
+    def step(self):
+        self._fwd(self.x, self.y)
+
+    def kernel_setup(self):
+        pass
+
+    def kernel_step(self):  # the dominant kernel: the GEMM with its bias epilogue
+        self.rb.sgemm(self.x, self.w.t(), bias=self.b, precision=PRECISION[0], out=self.y)
+
+    def secondary_step(self):  # the LayerNorm + ReLU pass alone, in place on C
+        self.rb.layer_norm(self.y, self.g, self.beta, 1e-5, self.rb.ACT_RELU, out=self.y)
+
+    def e2e_setup(self):
+        rb, torch = self.rb, self.torch
+        ctx = rb.get_context(self.dev.index or 0)
+        self.pipe = E2EPipeline(torch, self.dev, 2)
+        self.slots = []
+        for k in range(self.pipe.depth):
+            self.slots.append({"px": _pinned_copy(rb, ctx, self.host["x"]),
+                               "py": _pinned_empty(rb, ctx, self.M * self.N * 4),
+                               "dx": self.x if k == 0 else torch.empty_like(self.x),
+                               "dy": self.y if k == 0 else torch.empty_like(self.y)})
+        self.h2d_bytes = self.M * self.K * 4
+        self.d2h_bytes = self.M * self.N * 4
+
+    def e2e_step(self):
+        rb = self.rb
+        ctx = rb.get_context(self.dev.index or 0)
+        k, st, stream = self.pipe.next()
+        slot = self.slots[k]
+        rb.call("rtb_memcpy_h2d", ctx.handle, ctypes.c_void_p(slot["dx"].data_ptr()), slot["px"],
+                self.h2d_bytes, stream)
+        with self.torch.cuda.stream(st):
+            self._fwd(slot["dx"], slot["dy"])
+        rb.call("rtb_memcpy_d2h", ctx.handle, slot["py"], ctypes.c_void_p(slot["dy"].data_ptr()),
+                self.d2h_bytes, stream)
+
+    def e2e_teardown(self):
+        ctx = self.rb.get_context(self.dev.index or 0)
+        for slot in self.slots:
+            self.rb.call("rtb_host_free", ctx.handle, slot["px"])
+            self.rb.call("rtb_host_free", ctx.handle, slot["py"])
+        self.slots = []
+
+    def cpu_sample(self, threads):
+        """The reference's CPU pipeline (matmul + bias, one-pass f32 layer_norm,
+        ReLU) on a 64-row sample."""
+        return linear_norm_cpu_sample(self.M, self.K, self.N, threads)
+
+
+def linear_norm_cpu_sample(M, K, N, threads, rows=64):
+    from oracle import oracle as orc
+    bound = 1.0 / math.sqrt(K)
+    x = orc.normal((M, K), 4, 0)[:rows]
+    w = orc.uniform((N, K), 4, 1, -bound, bound)
+    b = orc.uniform((N,), 4, 2, -bound, bound)
+    g = orc.normal((N,), 4, 3, 1.0, 0.1)
+    beta = orc.normal((N,), 4, 4, 0.0, 0.1)
+    wt = np.ascontiguousarray(w.T)
+    t0 = time.perf_counter()
+    reps = 0
+    while reps < 1 or (time.perf_counter() - t0 < 10.0 and reps < 10):
+        orc.matmul_bias_norm_activation(x, wt, b, g, beta, 1e-5, 1, threads)
+        reps += 1
+    dt = (time.perf_counter() - t0) / reps
+    return 2.0 * rows * K * N / dt / 1e12, f"{rows} of {M} rows, {reps} passes"
+
+
 WORKLOADS = {
     "conv": lambda rb, torch, dev: ConvWorkload(rb, torch, dev),
     "conv_bwd": lambda rb, torch, dev: ConvBwdWorkload(rb, torch, dev),
     "resnet18": lambda rb, torch, dev: ResNet18Workload(rb, torch, dev),
     "mlp": lambda rb, torch, dev: MlpWorkload(rb, torch, dev),
+    "linear_norm": lambda rb, torch, dev: LinearNormWorkload(rb, torch, dev),
 }
 
 
@@ -951,6 +1051,16 @@ def run_ours(args):
                     "tensor_pipe_frac": round(MMAS_PER_MAC[0] * k_tflops / tf32_peak, 4),
                     "kernel_ms": round(kms / args.steps, 5)}
 
+    if hasattr(wl, "secondary_step"):
+        # the second launch of a two-kernel step (HBM-bound), timed alone
+        sms = _time_steps(torch, wl.secondary_step, args.steps, max(3, args.warmup), dev, None)
+        s_gbs = wl.ln_bytes * args.steps / (sms / 1e3) / 1e9
+        roofline["secondary"] = {"kernel": "layernorm_act", "bound": "hbm",
+                                 "achieved": round(s_gbs, 1), "peak": peaks["hbm_gbs"],
+                                 "unit": "GB/s", "frac": round(s_gbs / peaks["hbm_gbs"], 4),
+                                 "algorithmic_bytes": wl.ln_bytes,
+                                 "kernel_ms": round(sms / args.steps, 5)}
+
     # end to end through the C ABI with host buffers
     wl.e2e_setup()
     ems = _time_steps(torch, wl.e2e_step, args.steps, max(3, args.warmup), dev, dist,
@@ -1027,6 +1137,14 @@ def run_reference(args):
         wl.dims, wl.M = [1024, 4096, 4096, 1024], 4096
         wl.flops = float(sum(2 * wl.M * wl.dims[i] * wl.dims[i + 1] for i in range(3)))
         cfg = {"workload": "3-layer MLP forward 4096x(1024->4096->4096->1024)", "seed": 2}
+        unit = "TFLOP/s"
+    elif args.workload == "linear_norm":
+        wl = LinearNormWorkload.__new__(LinearNormWorkload)
+        wl.M, wl.K, wl.N = 8192, 1024, 4096
+        wl.flops = 2.0 * wl.M * wl.K * wl.N
+        wl.cpu_sample = lambda threads: linear_norm_cpu_sample(wl.M, wl.K, wl.N, threads)
+        cfg = {"workload": "Linear 1024->4096 + bias, LayerNorm(4096) + ReLU over 8192 rows",
+               "seed": 4}
         unit = "TFLOP/s"
     else:
         m, n, k, seed = GEMM_SHAPES[args.workload]

@@ -47,8 +47,9 @@ enum {
   RTB_E_NCCL = 6         /* NCCL error */
 };
 
-/* backend::Activation (rustorch-core/src/backend/mod.rs:1-7).  Only NONE and
- * RELU are fused; SIGMOID/TANH return RTB_E_UNSUPPORTED. */
+/* backend::Activation (rustorch-core/src/backend/mod.rs:1-7).  The GEMM and
+ * conv epilogues fuse NONE and RELU (SIGMOID/TANH return RTB_E_UNSUPPORTED
+ * there); rtb_matmul_bias_norm_act takes all four. */
 enum { RTB_ACT_NONE = 0, RTB_ACT_RELU = 1, RTB_ACT_SIGMOID = 2, RTB_ACT_TANH = 3 };
 
 /* Contraction precision.  3xTF32 (default) splits every fp32 operand into a
@@ -131,6 +132,30 @@ int rtb_sgemm_batched(rtb_ctx* ctx, int64_t batch, int64_t M, int64_t N, int64_t
                       const float* A, int64_t lda, int64_t strideA, int transA, const float* B,
                       int64_t ldb, int64_t strideB, int transB, const float* bias, int act,
                       float* C, int64_t ldc, int64_t strideC, int precision, void* stream);
+
+/* C[M,N] = act(layer_norm_N(op(A) . op(B) + bias) * norm_weight + norm_bias):
+ * ops::matmul_bias_norm_activation (rustorch-core/src/ops.rs:1815-1886, with
+ * layer_norm over the last dimension, ops/norm.rs:613-700, and
+ * apply_activation, ops.rs:1773-1780).  Arguments as rtb_sgemm; norm_weight,
+ * norm_bias: [N] or NULL (1 and 0); eps as the reference's (LayerNorm's
+ * default is 1e-5); act: any RTB_ACT_* (sigmoid = 1/(1+exp(-x)), tanh).  The
+ * mean and variance are taken in two passes (the reference uses
+ * E[x^2] - E[x]^2 in f32); results agree with the exact values to the
+ * contraction's precision. */
+int rtb_matmul_bias_norm_act(rtb_ctx* ctx, int64_t M, int64_t N, int64_t K, const float* A,
+                             int64_t lda, int transA, const float* B, int64_t ldb, int transB,
+                             const float* bias, const float* norm_weight, const float* norm_bias,
+                             float eps, int act, float* C, int64_t ldc, int precision,
+                             void* stream);
+
+/* y[r, :] = act(layer_norm(x[r, :]) * norm_weight + norm_bias) for r < rows:
+ * ops::layer_norm over the last dimension (rustorch-core/src/ops/norm.rs:
+ * 613-700, normalized_shape = [d]) with an optional activation.  x and y are
+ * row-major with leading dimensions ldx, ldy >= d; x == y (in place) is
+ * allowed.  Mean and variance in two passes, as rtb_matmul_bias_norm_act. */
+int rtb_layer_norm(rtb_ctx* ctx, int64_t rows, int64_t d, const float* x, int64_t ldx,
+                   const float* norm_weight, const float* norm_bias, float eps, int act, float* y,
+                   int64_t ldy, void* stream);
 
 /* ---------------------------------------------------------------- conv */
 /* y = act(conv2d(x, w, stride, padding) + bias + residual).

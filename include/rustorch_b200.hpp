@@ -125,6 +125,11 @@ class Tensor {
 namespace ops {
 Tensor matmul(const Tensor& lhs, const Tensor& rhs);
 Tensor matmul_fused(const Tensor& lhs, const Tensor& rhs, const Tensor* bias, Activation act);
+// ops::matmul_bias_norm_activation (rustorch-core/src/ops.rs:1815-1886):
+// act(layer_norm(lhs.matmul(rhs) + bias, [n], norm_weight, norm_bias, eps)).
+Tensor matmul_bias_norm_activation(const Tensor& lhs, const Tensor& rhs, const Tensor* bias,
+                                   const Tensor* norm_weight, const Tensor* norm_bias, float eps,
+                                   Activation act);
 Tensor conv2d(const Tensor& input, const Tensor& weight, Pair stride, Pair padding);
 // One fused kernel: act(conv2d(input, weight) + bias[c] + residual).
 Tensor conv2d_fused(const Tensor& input, const Tensor& weight, const Tensor* bias, Pair stride,

@@ -622,6 +622,78 @@ ORC_API void orc_global_avg_pool(int64_t n, int64_t c, int64_t hw, const float* 
 }
 
 /* ------------------------------------------------------------------------ */
+/* LayerNorm + activation (matmul_bias_norm_activation's second half)        */
+/* ------------------------------------------------------------------------ */
+
+/* layer_norm over the last dimension, in place, f32, the reference's own
+ * formula (rustorch-core/src/ops/norm.rs:613-700 with the scalar row kernel
+ * norm.rs:536-544): s += v; q += v*v sequentially in f32, m = s/D,
+ * var = q/D - m*m, inv_s = 1/sqrt(var + eps), out = (v - m)*inv_s*g + b
+ * (g = 1, b = 0 when absent). */
+ORC_API void orc_layer_norm_ref(float* x, int64_t rows, int64_t d, const float* g, const float* b,
+                                float eps) {
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < rows; ++i) {
+    float* row = x + i * d;
+    float s = 0.0f, q = 0.0f;
+    for (int64_t j = 0; j < d; ++j) {
+      s += row[j];
+      q += row[j] * row[j];
+    }
+    const float m = s / (float)d;
+    const float v = q / (float)d - m * m;
+    const float inv_s = 1.0f / sqrtf(v + eps);
+    for (int64_t j = 0; j < d; ++j) {
+      const float xh = (row[j] - m) * inv_s;
+      row[j] = xh * (g ? g[j] : 1.0f) + (b ? b[j] : 0.0f);
+    }
+  }
+}
+
+/* The same normalisation in f64 with a two-pass variance (mean first, then the
+ * mean of squared deviations): the exact value the reference's f32 formula
+ * approximates.  x is f64 [rows, d], in place. */
+ORC_API void orc_layer_norm_f64(double* x, int64_t rows, int64_t d, const float* g, const float* b,
+                                double eps) {
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < rows; ++i) {
+    double* row = x + i * d;
+    double s = 0.0;
+    for (int64_t j = 0; j < d; ++j) s += row[j];
+    const double m = s / (double)d;
+    double q = 0.0;
+    for (int64_t j = 0; j < d; ++j) q += (row[j] - m) * (row[j] - m);
+    const double inv_s = 1.0 / sqrt(q / (double)d + eps);
+    for (int64_t j = 0; j < d; ++j)
+      row[j] = (row[j] - m) * inv_s * (g ? (double)g[j] : 1.0) + (b ? (double)b[j] : 0.0);
+  }
+}
+
+/* apply_activation (rustorch-core/src/ops.rs:1773-1780): 1 ReLU, 2 sigmoid
+ * 1/(1+exp(-x)) (ops/activations.rs:47-50), 3 tanh (activations.rs:213),
+ * 0 none.  In place, f32. */
+ORC_API void orc_activation(float* x, int64_t n, int act) {
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < n; ++i) {
+    const float v = x[i];
+    if (act == 1) x[i] = v > 0.0f ? v : 0.0f;
+    else if (act == 2) x[i] = 1.0f / (1.0f + expf(-v));
+    else if (act == 3) x[i] = tanhf(v);
+  }
+}
+
+/* The same activations in f64. */
+ORC_API void orc_activation_f64(double* x, int64_t n, int act) {
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < n; ++i) {
+    const double v = x[i];
+    if (act == 1) x[i] = v > 0.0 ? v : 0.0;
+    else if (act == 2) x[i] = 1.0 / (1.0 + exp(-v));
+    else if (act == 3) x[i] = tanh(v);
+  }
+}
+
+/* ------------------------------------------------------------------------ */
 /* Error metrics                                                             */
 /* ------------------------------------------------------------------------ */
 

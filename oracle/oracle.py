@@ -67,6 +67,10 @@ def lib():
         L.orc_conv2d_grad_weight_f64.argtypes = conv_args
         L.orc_max_pool2d.argtypes = [_i64] * 10 + [_p, _p]
         L.orc_global_avg_pool.argtypes = [_i64] * 3 + [_p, _p]
+        L.orc_layer_norm_ref.argtypes = [_p, _i64, _i64, _p, _p, ctypes.c_float]
+        L.orc_layer_norm_f64.argtypes = [_p, _i64, _i64, _p, _p, ctypes.c_double]
+        L.orc_activation.argtypes = [_p, _i64, ctypes.c_int]
+        L.orc_activation_f64.argtypes = [_p, _i64, ctypes.c_int]
         L.orc_rel_frob.restype = ctypes.c_double
         L.orc_rel_frob.argtypes = [_p, _p, _i64]
         _lib = L
@@ -289,6 +293,53 @@ def conv2d_grad_weight_f64(x, gy, w_shape, stride=(1, 1), padding=(0, 0), thread
     lib().orc_conv2d_grad_weight_f64(n, ci, h, wd, co, kh, kw, stride[0], stride[1], padding[0],
                                      padding[1], _ptr(x), _ptr(gy), _ptr(gw), threads)
     return gw
+
+
+def layer_norm(x, g=None, b=None, eps: float = 1e-5) -> np.ndarray:
+    """ops::layer_norm over the last dimension, f32, the reference's one-pass
+    formula (rustorch-core/src/ops/norm.rs:613-700)."""
+    y = _f32(x).copy()
+    gk = _f32(g) if g is not None else None
+    bk = _f32(b) if b is not None else None
+    d = y.shape[-1]
+    lib().orc_layer_norm_ref(_ptr(y), y.size // d if d else 0, d,
+                             _ptr(gk) if gk is not None else None,
+                             _ptr(bk) if bk is not None else None, eps)
+    return y
+
+
+def activation(x, act: int) -> np.ndarray:
+    """apply_activation (rustorch-core/src/ops.rs:1773-1780), f32."""
+    y = _f32(x).copy()
+    lib().orc_activation(_ptr(y), y.size, act)
+    return y
+
+
+def matmul_bias_norm_activation(a, b, bias=None, g=None, beta=None, eps: float = 1e-5,
+                                act: int = 0, threads: int = 0) -> np.ndarray:
+    """ops::matmul_bias_norm_activation (rustorch-core/src/ops.rs:1815-1886),
+    f32: matmul_fused(a, b, bias) (the pipeline_fused order, ops.rs:1801-1813),
+    layer_norm over N, then the activation."""
+    c = matmul(a, b, bias, threads)[0]
+    return activation(layer_norm(c, g, beta, eps), act)
+
+
+def matmul_bias_norm_activation_f64(a, b, bias=None, g=None, beta=None, eps: float = 1e-5,
+                                    act: int = 0, threads: int = 0) -> np.ndarray:
+    """The same pipeline in float64 with a two-pass variance: the exact value
+    the CUDA path is checked against."""
+    c = matmul_f64(a, b, threads)
+    if bias is not None:
+        c += np.asarray(bias, np.float64)[None, :]
+    c = np.ascontiguousarray(c)
+    gk = _f32(g) if g is not None else None
+    bk = _f32(beta) if beta is not None else None
+    d = c.shape[-1]
+    lib().orc_layer_norm_f64(_ptr(c), c.size // d if d else 0, d,
+                             _ptr(gk) if gk is not None else None,
+                             _ptr(bk) if bk is not None else None, eps)
+    lib().orc_activation_f64(_ptr(c), c.size, act)
+    return c
 
 
 def matmul_backward_f64(a, b, gc):

@@ -22,7 +22,9 @@ from . import _lib
 from ._lib import (ACT_NONE, ACT_RELU, ACT_SIGMOID, ACT_TANH, LAYOUT_NCHW, LAYOUT_NHWC,
                    PREC_3XTF32, PREC_DEFAULT, PREC_TF32, RtbError, call, lib)
 
-__all__ = ["Context", "get_context", "sgemm", "sgemm_batched", "conv2d_fwd", "matmul_backward",
+__all__ = ["Context", "get_context", "sgemm", "sgemm_batched", "matmul_bias_norm_activation",
+           "layer_norm",
+           "conv2d_fwd", "matmul_backward",
            "conv2d_backward", "max_pool2d",
            "global_avg_pool", "add", "relu", "fill_normal", "fill_uniform", "RtbError",
            "ACT_NONE", "ACT_RELU", "ACT_SIGMOID", "ACT_TANH", "PREC_3XTF32", "PREC_TF32",
@@ -135,6 +137,63 @@ def sgemm(a, b, bias=None, act: int = ACT_NONE, precision: int = PREC_DEFAULT, o
     ctx = get_context(_dev(a))
     call("rtb_sgemm", ctx.handle, M, N, K, _ptr(a_), lda, ta, _ptr(b_), ldb, tb, _ptr(bias), act,
          _ptr(out), out.stride(0), precision, _stream_of(a))
+    return out
+
+
+def matmul_bias_norm_activation(a, b, bias=None, norm_weight=None, norm_bias=None,
+                                eps: float = 1e-5, act: int = ACT_NONE,
+                                precision: int = PREC_DEFAULT, out=None):
+    """ops::matmul_bias_norm_activation: act(layer_norm(a @ b + bias) * norm_weight
+    + norm_bias), the LayerNorm over the last dimension (N), for 2-D float32
+    CUDA tensors a [M,K], b [K,N]; act is any ACT_*."""
+    torch = _torch()
+    _check_f32_cuda(a, b, bias, norm_weight, norm_bias, out)
+    if a.dim() != 2 or b.dim() != 2:
+        raise ValueError("Matmul only supports 2D")
+    M, K = a.shape
+    K2, N = b.shape
+    if K != K2:
+        raise ValueError("Matmul dimension mismatch")
+    for t in (bias, norm_weight, norm_bias):
+        if t is not None and t.numel() != N:
+            raise ValueError("bias / norm parameters must have N elements")
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float32, device=a.device)
+    a_, lda, ta = _operand_2d(a)
+    b_, ldb, tb = _operand_2d(b)
+    bias, norm_weight, norm_bias = (t.contiguous() if t is not None else None
+                                    for t in (bias, norm_weight, norm_bias))
+    ctx = get_context(_dev(a))
+    call("rtb_matmul_bias_norm_act", ctx.handle, M, N, K, _ptr(a_), lda, ta, _ptr(b_), ldb, tb,
+         _ptr(bias), _ptr(norm_weight), _ptr(norm_bias), float(eps), act, _ptr(out),
+         out.stride(0), precision, _stream_of(a))
+    return out
+
+
+def layer_norm(x, norm_weight=None, norm_bias=None, eps: float = 1e-5, act: int = ACT_NONE,
+               out=None):
+    """ops::layer_norm over the last dimension (+ an optional activation) for a
+    float32 CUDA tensor whose rows are contiguous; out may be x (in place)."""
+    torch = _torch()
+    _check_f32_cuda(x, norm_weight, norm_bias, out)
+    if x.dim() == 0:
+        raise ValueError("LayerNorm: Input shape smaller than normalized shape")
+    d = x.shape[-1]
+    x2 = x.reshape(-1, d) if d else x.reshape(-1, 0)
+    if x2.numel() and x2.stride(1) != 1:
+        x2 = x2.contiguous()
+    for t in (norm_weight, norm_bias):
+        if t is not None and t.numel() != d:
+            raise ValueError("LayerNorm: Input shape does not match normalized shape")
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.float32, device=x.device)
+    y2 = out.view(-1, d) if d else out.reshape(-1, 0)
+    norm_weight, norm_bias = (t.contiguous() if t is not None else None
+                              for t in (norm_weight, norm_bias))
+    ctx = get_context(_dev(x))
+    call("rtb_layer_norm", ctx.handle, x2.shape[0], d, _ptr(x2), max(x2.stride(0), d),
+         _ptr(norm_weight), _ptr(norm_bias), float(eps), act, _ptr(y2), max(y2.stride(0), d),
+         _stream_of(x))
     return out
 
 

@@ -61,6 +61,9 @@ SIGNATURES = {
                                _p, _i, _p, _i64, _i64, _i, _p]),
     "rtb_conv2d_fwd": (_i, [_p] + [_i64] * 11 + [_p, _i, _p, _p, _p, _i, _p, _i, _i, _p]),
     "rtb_conv2d_fwd_noalloc": (_i, [_p] + [_i64] * 11 + [_p, _i, _p, _p, _p, _i, _p, _i, _i, _p]),
+    "rtb_matmul_bias_norm_act": (_i, [_p, _i64, _i64, _i64, _p, _i64, _i, _p, _i64, _i, _p, _p, _p,
+                                      ctypes.c_float, _i, _p, _i64, _i, _p]),
+    "rtb_layer_norm": (_i, [_p, _i64, _i64, _p, _i64, _p, _p, ctypes.c_float, _i, _p, _i64, _p]),
     "rtb_matmul_backward": (_i, [_p, _i64, _i64, _i64, _p, _p, _p, _p, _p, _i, _i, _p]),
     "rtb_peer_buffer_create": (_i, [_p, _p, _sz, _p]),
     "rtb_peer_buffer_local": (_i, [_p, _p]),

@@ -534,6 +534,44 @@ int rtb_sgemm_batched(rtb_ctx* ctx, int64_t batch, int64_t M, int64_t N, int64_t
   return RTB_OK;
 }
 
+// ops::matmul_bias_norm_activation (rustorch-core/src/ops.rs:1815-1886): the
+// engine's GEMM with the bias in its epilogue, then one row-wise LayerNorm +
+// activation pass over C (the reference's pipeline_fused order).
+int rtb_matmul_bias_norm_act(rtb_ctx* ctx, int64_t M, int64_t N, int64_t K, const float* A,
+                             int64_t lda, int transA, const float* B, int64_t ldb, int transB,
+                             const float* bias, const float* norm_weight, const float* norm_bias,
+                             float eps, int act, float* C, int64_t ldc, int precision,
+                             void* stream) {
+  RTB_CHECK_CTX(ctx);
+  int st = check_gemm_args(M, N, K, A, lda, transA, B, ldb, transB, C, ldc);
+  if (st) return st;
+  if (act < RTB_ACT_NONE || act > RTB_ACT_TANH) return set_error(RTB_E_INVALID, "unknown activation");
+  int split3 = 1;
+  if ((st = resolve_precision(ctx, precision, &split3))) return st;
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = pick_stream(ctx, stream);
+  if ((st = sgemm_one(ctx, M, N, K, A, lda, transA, B, ldb, transB, bias, 0, C, ldc, split3, s)))
+    return st;
+  if (M == 0 || N == 0) return RTB_OK;
+  return launch_layernorm_act(C, ldc, C, ldc, M, N, norm_weight, norm_bias, eps, act, s);
+}
+
+// ops::layer_norm over the last dimension (rustorch-core/src/ops/norm.rs:613-700)
+// followed by an activation, rows of X into rows of Y.
+int rtb_layer_norm(rtb_ctx* ctx, int64_t rows, int64_t d, const float* x, int64_t ldx,
+                   const float* norm_weight, const float* norm_bias, float eps, int act, float* y,
+                   int64_t ldy, void* stream) {
+  RTB_CHECK_CTX(ctx);
+  if (rows < 0 || d < 0) return set_error(RTB_E_INVALID, "negative size");
+  if (rows == 0 || d == 0) return RTB_OK;
+  if (!x || !y) return set_error(RTB_E_INVALID, "null tensor");
+  if (ldx < d || ldy < d) return set_error(RTB_E_INVALID, "leading dimension below d");
+  if (act < RTB_ACT_NONE || act > RTB_ACT_TANH) return set_error(RTB_E_INVALID, "unknown activation");
+  DeviceGuard g(ctx->device);
+  return launch_layernorm_act(x, ldx, y, ldy, rows, d, norm_weight, norm_bias, eps, act,
+                              pick_stream(ctx, stream));
+}
+
 // ---------------------------------------------------------------- conv
 int64_t rtb_conv2d_packed_weight_size(int64_t Co, int64_t Ci, int64_t kh, int64_t kw) {
   return Co * kh * kw * round_up(Ci, 4);

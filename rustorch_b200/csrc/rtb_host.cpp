@@ -391,6 +391,38 @@ Tensor matmul_fused(const Tensor& lhs, const Tensor& rhs, const Tensor* bias, Ac
   return finish(y, p);
 }
 
+Tensor matmul_bias_norm_activation(const Tensor& lhs, const Tensor& rhs, const Tensor* bias,
+                                   const Tensor* norm_weight, const Tensor* norm_bias, float eps,
+                                   Activation act) {
+  if (lhs.dim() != 2 || rhs.dim() != 2) throw Panic("Matmul only supports 2D");
+  const size_t m = lhs.shape()[0], k = lhs.shape()[1], k2 = rhs.shape()[0], n = rhs.shape()[1];
+  if (k != k2) throw Panic("Matmul dimension mismatch");
+  for (const Tensor* t : {bias, norm_weight, norm_bias})
+    if (t && t->numel() != n)
+      throw Panic("LayerNorm: Input shape does not match normalized shape");
+  Placement p = place({&lhs, &rhs, bias, norm_weight, norm_bias});
+  Tensor a = on(lhs, p), b = on(rhs, p);
+  Tensor bz = bias ? on(*bias, p).contiguous() : Tensor();
+  Tensor gz = norm_weight ? on(*norm_weight, p).contiguous() : Tensor();
+  Tensor nz = norm_bias ? on(*norm_bias, p).contiguous() : Tensor();
+  Tensor y = make_contig(Device::cuda(p.device), {m, n});
+  if (m && n) {
+    int64_t lda = 1, ldb = (int64_t)n;
+    int ta = 0, tb = 0;
+    Tensor a2 = k ? gemm_operand(a, lda, ta) : a, b2 = k ? gemm_operand(b, ldb, tb) : b;
+    chk(rtb_matmul_bias_norm_act(context(p.device), (int64_t)m, (int64_t)n, (int64_t)k,
+                                 k ? a2.device_ptr() : nullptr, lda, ta,
+                                 k ? b2.device_ptr() : nullptr, ldb, tb,
+                                 bias ? bz.device_ptr() : nullptr,
+                                 norm_weight ? gz.device_ptr() : nullptr,
+                                 norm_bias ? nz.device_ptr() : nullptr, eps,
+                                 static_cast<int>(act), y.device_ptr(), (int64_t)n, g_precision,
+                                 nullptr),
+        "matmul_bias_norm_activation");
+  }
+  return finish(y, p);
+}
+
 Tensor matmul(const Tensor& lhs, const Tensor& rhs) {
   return matmul_fused(lhs, rhs, nullptr, Activation::None);
 }

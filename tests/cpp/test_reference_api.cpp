@@ -120,6 +120,24 @@ static void device_tests() {
     for (int i = 0; i < 4; ++i)
       expect(std::fabs(got[i] - expected[i]) < 1e-6f, "matmul value " + std::to_string(i));
   });
+  run("matmul_bias_norm_activation_2x2", [] {
+    // [[1,2],[3,4]] . I + 0: every row normalises to [-1, 1] (mean m, variance
+    // 1/4, eps 0), so ReLU gives [0, 1] and tanh [-tanh 1, tanh 1].
+    Tensor a = Tensor::new_({1.0, 2.0, 3.0, 4.0}, {2, 2});
+    Tensor eye = Tensor::new_({1.0, 0.0, 0.0, 1.0}, {2, 2});
+    Tensor y = ops::matmul_bias_norm_activation(a, eye, nullptr, nullptr, nullptr, 0.0f,
+                                                Activation::ReLU);
+    std::vector<float> got = y.data();
+    kat("matmul_bias_norm_relu_2x2", got);
+    const float er[4] = {0.0f, 1.0f, 0.0f, 1.0f};
+    for (int i = 0; i < 4; ++i) expect(std::fabs(got[i] - er[i]) < 1e-6f, "relu value");
+    Tensor g = Tensor::new_({2.0, 3.0}, {2});
+    Tensor b = Tensor::new_({0.5, -0.5}, {2});
+    Tensor t = ops::matmul_bias_norm_activation(a, eye, nullptr, &g, &b, 0.0f, Activation::Tanh);
+    std::vector<float> gt = t.data();
+    const float et[4] = {std::tanh(-1.5f), std::tanh(2.5f), std::tanh(-1.5f), std::tanh(2.5f)};
+    for (int i = 0; i < 4; ++i) expect(std::fabs(gt[i] - et[i]) < 1e-6f, "tanh value");
+  });
   run("test_matmul_backward_precision_under_1e6", [] {
     // loss = sum(a.matmul(b)): the incoming gradient is all ones
     Tensor a = Tensor::new_({1.0, 2.0, 3.0, 4.0}, {2, 2});

@@ -173,3 +173,70 @@ def test_conv_backward_adjoint(orc, stride, pad):
     lhs = float((y * g.astype(np.float64)).sum())
     assert abs(float((x.astype(np.float64) * gx).sum()) - lhs) <= 1e-10 * max(1.0, abs(lhs))
     assert abs(float((w.astype(np.float64) * gw).sum()) - lhs) <= 1e-10 * max(1.0, abs(lhs))
+
+
+def test_layer_norm_kat_2x2(orc):
+    """matmul_bias_norm_activation on [[1,2],[3,4]] . I: each row has mean m and
+    variance 1/4 under the reference's formula (rustorch-core/src/ops/norm.rs:
+    660-667), so with eps 0 it normalises to [-1, 1] exactly."""
+    a = np.array([[1, 2], [3, 4]], np.float32)
+    eye = np.eye(2, dtype=np.float32)
+    y = orc.matmul_bias_norm_activation(a, eye, eps=0.0, act=0)
+    np.testing.assert_array_equal(y, [[-1, 1], [-1, 1]])
+    np.testing.assert_array_equal(orc.matmul_bias_norm_activation(a, eye, eps=0.0, act=1),
+                                  [[0, 1], [0, 1]])
+    g = np.array([2, 3], np.float32)
+    b = np.array([0.5, -0.5], np.float32)
+    t = orc.matmul_bias_norm_activation(a, eye, None, g, b, eps=0.0, act=3)
+    np.testing.assert_allclose(t, np.tanh([[-1.5, 2.5], [-1.5, 2.5]]), rtol=0, atol=1e-7)
+    s = orc.matmul_bias_norm_activation(a, eye, eps=0.0, act=2)
+    np.testing.assert_allclose(s, 1 / (1 + np.exp([[1.0, -1.0], [1.0, -1.0]])), rtol=0, atol=1e-7)
+    f = orc.matmul_bias_norm_activation_f64(a, eye, None, g, b, eps=0.0, act=3)
+    np.testing.assert_allclose(f, np.tanh([[-1.5, 2.5], [-1.5, 2.5]]), rtol=0, atol=1e-15)
+
+
+@pytest.mark.parametrize("rows,d", [(1, 1), (5, 7), (64, 1000), (33, 4096)])
+def test_layer_norm_ref_vs_torch_and_f64(orc, rows, d):
+    """The reference formula (f32, one pass) against torch's layer_norm and the
+    f64 two-pass restatement on zero-centred rows, where E[x^2] - E[x]^2 does
+    not cancel."""
+    x = orc.normal((rows, d), 21, 1)
+    g = orc.normal((d,), 21, 2)
+    b = orc.normal((d,), 21, 3)
+    y = orc.layer_norm(x, g, b, 1e-5)
+    t = torch.nn.functional.layer_norm(torch.from_numpy(x), (d,), torch.from_numpy(g),
+                                       torch.from_numpy(b), 1e-5).numpy()
+    x64 = x.astype(np.float64)
+    mu = x64.mean(1, keepdims=True)
+    ref = (x64 - mu) / np.sqrt(((x64 - mu) ** 2).mean(1, keepdims=True) + 1e-5) * g + b
+    assert np.abs(y - t).max() < 1e-4
+    assert orc.rel_frob(y, ref) < 1e-5
+    f = orc.matmul_bias_norm_activation_f64(x, np.eye(d, dtype=np.float32), None, g, b, 1e-5, 0)
+    assert np.abs(f - ref).max() < 1e-9
+
+
+def test_layer_norm_reference_cancellation(orc):
+    """Rows with |mean| >> std: the reference's E[x^2] - E[x]^2 in f32 loses the
+    variance (ops/norm.rs:665) -- here it comes out negative and the rows turn
+    to NaN -- while the f64 two-pass value stays exact.  The CUDA path is held
+    to the exact value."""
+    x = (orc.normal((16, 1024), 22, 1) + 1000.0).astype(np.float32)
+    x64 = x.astype(np.float64)
+    mu = x64.mean(1, keepdims=True)
+    ref = (x64 - mu) / np.sqrt(((x64 - mu) ** 2).mean(1, keepdims=True) + 1e-5)
+    y = orc.layer_norm(x, None, None, 1e-5)
+    f = orc.matmul_bias_norm_activation_f64(x, np.eye(1024, dtype=np.float32), None, None, None,
+                                            1e-5, 0)
+    assert np.abs(f - ref).max() < 1e-9
+    assert not np.isfinite(y).all() or orc.rel_frob(y, ref) > 1e-3
+
+
+def test_activation_restatement(orc):
+    x = orc.normal((4096,), 23, 1) * 4
+    x[:3] = [np.nan, 0.0, -0.0]
+    np.testing.assert_array_equal(orc.activation(x, 1)[3:], np.maximum(x[3:], 0))
+    assert orc.activation(x, 1)[0] == 0.0  # f32::max(NaN, 0) = 0
+    np.testing.assert_allclose(orc.activation(x, 2)[1:], 1 / (1 + np.exp(-x[1:].astype(np.float64))),
+                               rtol=1e-6, atol=1e-7)
+    np.testing.assert_allclose(orc.activation(x, 3)[1:], np.tanh(x[1:].astype(np.float64)),
+                               rtol=1e-6, atol=1e-7)
