@@ -592,6 +592,25 @@ class GemmWorkload:
         return 2.0 * rows * n * k / dt / 1e12, (f"{rows} of {m} rows of A per call, "
                                                 f"single-threaded blocked sgemm, {reps} calls")
 
+    def cpu_sample_all_cores(self, threads):
+        """The same blocked sgemm on every host core (64-row panels in parallel):
+        what the CPU does when it is not held to the reference's one thread."""
+        from oracle import oracle as orc
+        m, n, k = self.m, self.n, self.k
+        rows = max(1, min(m, max(64 * threads, int(2e9 * threads / (2 * n * k)))))
+        a = orc.normal((rows, k), self.seed, 0)
+        b = orc.normal((k, n), self.seed, 1)
+        t0 = time.perf_counter()
+        reps = 0
+        while True:
+            orc.sgemm_mm(a, b, threads=threads)
+            reps += 1
+            if time.perf_counter() - t0 > 10.0 or reps >= 10:
+                break
+        dt = (time.perf_counter() - t0) / reps
+        return 2.0 * rows * n * k / dt / 1e12, (f"{rows} of {m} rows of A per call, blocked "
+                                                f"sgemm on {threads} threads, {reps} calls")
+
 
 class ResNet18Workload:
     """ResNet-18 forward, B=256 images per GPU (batch-sharded, no communication)."""
@@ -1074,6 +1093,12 @@ def run_ours(args):
 
     if rank == 0:
         cpu_val, sample = wl.cpu_sample(os.cpu_count())
+        cpu_line = {"value": round(cpu_val, 6), "unit": unit, "cores": os.cpu_count(),
+                    "kind": "port", "sample": sample}
+        if hasattr(wl, "cpu_sample_all_cores") and scaling != "strong":
+            v_all, s_all = wl.cpu_sample_all_cores(os.cpu_count())
+            cpu_line["all_cores"] = {"value": round(v_all, 6), "cores": os.cpu_count(),
+                                     "sample": s_all}
         if scaling == "strong":
             par = f"N-split x{world} + NCCL all-gather"
         elif unit == "img/s":
@@ -1089,8 +1114,7 @@ def run_ours(args):
             "data": "synthetic (SplitMix64/Box-Muller, seeded)",
             "config": dict(wl.config, parallelism=par),
             "roofline": roofline,
-            "cpu_baseline": {"value": round(cpu_val, 6), "unit": unit,
-                             "cores": os.cpu_count(), "kind": "port", "sample": sample},
+            "cpu_baseline": cpu_line,
             "e2e": {"value": round(e2e, 3), "unit": unit,
                     "h2d_bytes_per_step": wl.h2d_bytes, "d2h_bytes_per_step": wl.d2h_bytes},
             "gpu_launches": wl.launches_per_step * args.steps,

@@ -553,7 +553,7 @@ int rtb_matmul_bias_norm_act(rtb_ctx* ctx, int64_t M, int64_t N, int64_t K, cons
   if ((st = sgemm_one(ctx, M, N, K, A, lda, transA, B, ldb, transB, bias, 0, C, ldc, split3, s)))
     return st;
   if (M == 0 || N == 0) return RTB_OK;
-  return launch_layernorm_act(C, ldc, C, ldc, M, N, norm_weight, norm_bias, eps, act, s);
+  return launch_layernorm_act(ctx, C, ldc, C, ldc, M, N, norm_weight, norm_bias, eps, act, s);
 }
 
 // ops::layer_norm over the last dimension (rustorch-core/src/ops/norm.rs:613-700)
@@ -568,7 +568,7 @@ int rtb_layer_norm(rtb_ctx* ctx, int64_t rows, int64_t d, const float* x, int64_
   if (ldx < d || ldy < d) return set_error(RTB_E_INVALID, "leading dimension below d");
   if (act < RTB_ACT_NONE || act > RTB_ACT_TANH) return set_error(RTB_E_INVALID, "unknown activation");
   DeviceGuard g(ctx->device);
-  return launch_layernorm_act(x, ldx, y, ldy, rows, d, norm_weight, norm_bias, eps, act,
+  return launch_layernorm_act(ctx, x, ldx, y, ldy, rows, d, norm_weight, norm_bias, eps, act,
                               pick_stream(ctx, stream));
 }
 

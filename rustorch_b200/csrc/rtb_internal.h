@@ -165,8 +165,9 @@ int launch_unpack_weight_grad(const float* dwp, int64_t Co, int64_t Ci, int64_t 
 // Row-wise LayerNorm (last dimension, two-pass variance) + activation:
 // Y = act((X - mean) / sqrt(var + eps) * g + b) over row-major [M, N]
 // matrices (X == Y allowed); g / b optional.
-int launch_layernorm_act(const float* X, int64_t ldx, float* Y, int64_t ldy, int64_t M, int64_t N,
-                         const float* g, const float* b, float eps, int act, cudaStream_t s);
+int launch_layernorm_act(rtb_ctx* ctx, const float* X, int64_t ldx, float* Y, int64_t ldy,
+                         int64_t M, int64_t N, const float* g, const float* b, float eps, int act,
+                         cudaStream_t s);
 
 // Stream-ordered workspace.
 int ws_alloc(rtb_ctx* ctx, void** p, size_t bytes, cudaStream_t s);

@@ -67,7 +67,8 @@ def test_kat_2x2(gpu):
 # threshold for its fused order (m >= 128, k >= 128, n >= 32), rows kept on
 # chip and rows re-read (n > 16384), the small-M contraction path (m <= 32)
 SHAPES = [(1, 1, 1), (7, 33, 19), (128, 256, 128), (300, 1000, 257), (16, 512, 4096),
-          (50, 16385, 32), (64, 20000, 64), (2048, 1024, 1024)]
+          (64, 2048, 64), (33, 4096, 32), (17, 8192, 16), (40, 12000, 48), (50, 16385, 32),
+          (64, 20000, 64), (2048, 1024, 1024)]
 
 
 @pytest.mark.parametrize("m,n,k", SHAPES)
@@ -151,8 +152,12 @@ def test_rejects_bad_parameters(gpu):
         gpu.matmul_bias_norm_activation(a, b, act=7)
 
 
-@pytest.mark.parametrize("rows,d", [(1, 1), (3, 5), (1000, 768), (37, 4097), (8, 16384),
-                                    (4, 16388), (2, 40000)])
+# d picks the kernel: one warp per row (<= 1024, scalar <= 512), 64/128/256
+# threads per row in registers (<= 2048/4096/8192), the bulk-copy ring
+# (<= 16384), plain staged rows (unaligned), rows re-read beyond 16384
+@pytest.mark.parametrize("rows,d", [(1, 1), (3, 5), (9, 500), (1000, 768), (5, 1500), (7, 3000),
+                                    (300, 4096), (3, 6000), (37, 4097), (8, 16384), (4, 16388),
+                                    (2, 40000)])
 @pytest.mark.parametrize("act", [0, 2])
 def test_layer_norm(gpu, orc, rows, d, act):
     """ops::layer_norm alone against the f64 restatement: only fp32 rounding is
