@@ -53,6 +53,11 @@ TRAFFIC = {
     "conv": (13.52e6, "profiles/conv2d_bias_relu_r50s2_3x3.md"),
     "gemm8192": (3.485e9, "profiles/sgemm_8192_3xtf32.md"),
     "gemm_m16": (273.3e6, "profiles/sgemm_small_m16_8192.md"),
+    "linear_norm": (154.7e6, "profiles/linear_norm_relu_8192x1024x4096.md"),
+}
+# DRAM bytes per launch of a workload's second kernel (roofline.secondary)
+TRAFFIC_SECONDARY = {
+    "linear_norm": (211.1e6, "profiles/linear_norm_relu_8192x1024x4096.md"),
 }
 PRECISION = [0]  # rtb precision enum used by every workload call (0 = 3xTF32, 1 = TF32)
 MMAS_PER_MAC = [3]
@@ -1078,6 +1083,9 @@ def run_ours(args):
                                  "achieved": round(s_gbs, 1), "peak": peaks["hbm_gbs"],
                                  "unit": "GB/s", "frac": round(s_gbs / peaks["hbm_gbs"], 4),
                                  "algorithmic_bytes": wl.ln_bytes,
+                                 "traffic": TRAFFIC_SECONDARY.get(args.workload, (None,))[0],
+                                 "traffic_source": TRAFFIC_SECONDARY.get(args.workload,
+                                                                         (None, None))[1],
                                  "kernel_ms": round(sms / args.steps, 5)}
 
     # end to end through the C ABI with host buffers
