@@ -142,12 +142,20 @@ struct GemmCfg {
   // running sum the epilogue warps promote the partials into, then a ring of
   // kAStages converted k-blocks: A's 32-column hi and lo parts in TMEM, B's
   // low part in a shared-memory slot (the MMAs read only B from smem).
-  static constexpr int kAccCols = (SPLIT ? 3 : 2) * BN;
+  // Wide mode (3xTF32 with BN = 64): B's low part sits right after the raw B
+  // tile in the ring stage, so hi_A . [B | B_lo] is ONE N=128 MMA (partial
+  // columns [0,64) = hi.hi, [64,128) = hi.lo) and lo_A . B one N=64 MMA: two
+  // tensor-core instructions per k-step instead of three (an N=64 MMA costs
+  // about as long as an N=128 one); the epilogue adds the two halves.
+  static constexpr bool kWide = SPLIT && BN == 64;
+  static constexpr int kAccW = kWide ? 2 * BN : BN;  // TMEM columns of one partial buffer
+  static constexpr int kAccCols = 2 * kAccW + (SPLIT ? BN : 0);
   static constexpr int kAStagesRaw = SPLIT ? (512 - kAccCols) / (2 * kBK) : 0;
   static constexpr int kAStages = kAStagesRaw > 4 ? 4 : kAStagesRaw;
-  static constexpr int kBloBytes = SPLIT ? kAStages * kBBytes : 0;
-  // Load ring stage: the raw A and B tiles (TMA).
-  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBStage = kWide ? 2 * kBBytes : kBBytes;  // B slot of a ring stage
+  static constexpr int kBloBytes = (SPLIT && !kWide) ? kAStages * kBBytes : 0;
+  // Load ring stage: the raw A and B tiles (TMA) (+ B's low part in wide mode).
+  static constexpr int kStageBytes = kABytes + kBStage;
   // Epilogue staging: two 16 KB chunks alternate, unless dropping one gives
   // the load ring another stage.
   static constexpr int kRingBytes = kSmemLimit - kSmemReserve - kBloBytes;
@@ -441,8 +449,8 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
                                              ~uintptr_t(1023));
   constexpr int kAS = SPLIT ? Cfg::kAStages : 1;
   uint8_t* sA = base;                                  // S x 16 KB
-  uint8_t* sB = sA + S * kABytes;                      // S x BN*128
-  uint8_t* sBlo = sB + S * kBBytes;                    // SPLIT: kAS x BN*128
+  uint8_t* sB = sA + S * kABytes;                      // S x kBStage (BN*128, wide: x2)
+  uint8_t* sBlo = sB + S * Cfg::kBStage;               // SPLIT, not wide: kAS x BN*128
   uint8_t* sOut = sBlo + Cfg::kBloBytes;               // kOutBufs x 16 KB epilogue staging
   uint8_t* tail = sOut + Cfg::kOutBytes;
   float* sBias = reinterpret_cast<float*>(tail);         // epilogue: the tile's BN bias values
@@ -562,11 +570,11 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
                                (uint16_t)ss, (uint16_t)rr);
           }
           if (B_MN == 0) {
-            tma_load_2d(sB + s * kBBytes, &tmB, &full_bar[s], kb * kBK, tn * BN);
+            tma_load_2d(sB + s * Cfg::kBStage, &tmB, &full_bar[s], kb * kBK, tn * BN);
           } else {
 #pragma unroll
             for (int j = 0; j < BN / 32; ++j)
-              tma_load_2d(sB + s * kBBytes + j * 4096, &tmB, &full_bar[s], tn * BN + j * 32,
+              tma_load_2d(sB + s * Cfg::kBStage + j * 4096, &tmB, &full_bar[s], tn * BN + j * 32,
                           kb * kBK);
           }
           if (++s == S) { s = 0; ph ^= 1; }
@@ -577,6 +585,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
     // ------------------------------------------------------------ UMMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_tf32(kBM, BN, 0, B_MN);
+      constexpr uint32_t idesc_w = umma_idesc_tf32(kBM, Cfg::kWide ? 2 * BN : BN, 0, B_MN);
       int s = 0;
       uint32_t ph = 0;
       int g = 0;  // accumulation-unit counter (selects the TMEM partial buffer)
@@ -595,7 +604,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t d_tmem = tmem_base + (uint32_t)(b * BN);
+          const uint32_t d_tmem = tmem_base + (uint32_t)(b * Cfg::kAccW);
           const int kend = (kb0 + p.kb_per_acc) < u.kb1 ? (kb0 + p.kb_per_acc) : u.kb1;
           for (int kb = kb0; kb < kend; ++kb) {
             uint64_t* ready = SPLIT ? &conv_bar[ja] : &full_bar[s];
@@ -610,8 +619,9 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
             // generic-proxy writes visible to the tensor core's async proxy.
             if (GATHER && !SPLIT) fence_proxy_async_smem();
             const uint32_t a_addr = smem_u32(sA + s * kABytes);
-            const uint32_t b_addr = smem_u32(sB + s * kBBytes);
-            const uint32_t blo_addr = smem_u32(sBlo + ja * kBBytes);
+            const uint32_t b_addr = smem_u32(sB + s * Cfg::kBStage);
+            const uint32_t blo_addr =
+                Cfg::kWide ? b_addr + (uint32_t)kBBytes : smem_u32(sBlo + ja * kBBytes);
             // 3xTF32: A's hi / lo k-block in TMEM columns (lane 0 = tile row 0)
             const uint32_t a_hi = tmem_base + (uint32_t)(Cfg::kAccCols + ja * 2 * kBK);
             const uint32_t a_lo = a_hi + (uint32_t)kBK;
@@ -624,7 +634,12 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
                   B_MN == 0 ? umma_desc(b_addr + k * 32, 16, 1024, kLayoutSW128)
                             : umma_desc(b_addr + k * 1024, 4096, 512, kLayoutSW128Base32B);
               const uint32_t acc = (kb > kb0 || k > 0) ? 1u : 0u;
-              if (SPLIT) {
+              if (Cfg::kWide) {
+                // one N=128 MMA over [B | B_lo] (hi.hi and hi.lo side by side),
+                // then lo.hi into the hi.hi columns
+                umma_tf32_ts(d_tmem, a_hi + k * 8, db, idesc_w, acc);
+                umma_tf32_ts(d_tmem, a_lo + k * 8, db, idesc, 1u);
+              } else if (SPLIT) {
                 const uint64_t dbl =
                     B_MN == 0 ? umma_desc(blo_addr + k * 32, 16, 1024, kLayoutSW128)
                               : umma_desc(blo_addr + k * 1024, 4096, 512, kLayoutSW128Base32B);
@@ -655,7 +670,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
     const int lane_base = 32 * (warp & 3);
     const int row = lane_base + lane;
     const uint32_t t_lane = tmem_base + ((uint32_t)lane_base << 16);
-    const uint32_t t_run = t_lane + (uint32_t)(2 * BN);  // fp32 running sum (3xTF32)
+    const uint32_t t_run = t_lane + (uint32_t)(2 * Cfg::kAccW);  // fp32 running sum (3xTF32)
     const int et = threadIdx.x - Roles::kWarpEpi * 32;  // 0..127 within the epilogue group
     int chunk = 0;  // staging-buffer sequence number
     int g = 0;
@@ -735,7 +750,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
           if (a == 0) trace_stamp(p, 5 + 6 * tj);
           if (last) trace_stamp(p, 6 + 6 * tj);
         }
-        const uint32_t t_part = t_lane + (uint32_t)(b * BN);
+        const uint32_t t_part = t_lane + (uint32_t)(b * Cfg::kAccW);
         // One finished chunk: a split piece's partial to the workspace, else to C.
         auto out = [&](int c, const uint32_t (&r)[32]) {
           if (piece) {
@@ -754,6 +769,14 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
           uint32_t r[32];
           tmem_ld_32x32b_x32(t_part + (uint32_t)c, r);
           tmem_ld_wait();
+          if (Cfg::kWide) {  // + the hi.lo half
+            uint32_t q[32];
+            tmem_ld_32x32b_x32(t_part + (uint32_t)(BN + c), q);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(q[j]));
+          }
           if (SPLIT && a > 0) {
             uint32_t q[32];
             tmem_ld_32x32b_x32(t_run + (uint32_t)c, q);
@@ -864,8 +887,8 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
         // then the splits, so the converter's latency is one load round trip.
         constexpr int kBPer = kBBytes / 16 / 128;  // float4 of B per thread
         const uint32_t arow = smem_u32(sA + s * kABytes + row * 128);
-        const uint32_t bb = smem_u32(sB + s * kBBytes);
-        const uint32_t blo = smem_u32(sBlo + ja * kBBytes);
+        const uint32_t bb = smem_u32(sB + s * Cfg::kBStage);
+        const uint32_t blo = Cfg::kWide ? bb + (uint32_t)kBBytes : smem_u32(sBlo + ja * kBBytes);
         float4 av[8], bv[kBPer];
         if (MULTITAP) {
           // float4 q of the row = channels 4*qq.. of tap block j (dense rows of
