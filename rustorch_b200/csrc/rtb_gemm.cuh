@@ -817,7 +817,61 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
           *fix_flag = (old == p.split_k - 1);
         }
         named_bar_sync(1, 128);
-        if (*fix_flag) {
+        // The ring is idle here: a piece is always its CTA's last work unit
+        // (pieces only fill the last wave), and the MMAs that read the ring
+        // have completed.  With room for two chunks of every piece, each
+        // thread stages its own row of all pieces by cp.async (one L2 round
+        // trip per chunk, the next chunk in flight while this one is summed).
+        constexpr int kFixRoom = S * Cfg::kStageBytes;
+        if (*fix_flag && 2 * p.split_k * kOutChunkBytes <= kFixRoom) {
+          __threadfence();
+          const float4* src0 = reinterpret_cast<const float4*>(p.ws) +
+                               (size_t)u.slot * p.split_k * (size_t)(BN * kBM / 4);
+          const int SK = p.split_k;
+          const uint32_t fb = smem_u32(sA);
+          auto stage_chunk = [&](int ci) {  // chunk ci of every piece -> buffer ci & 1
+            const float4* s0 = src0 + (size_t)ci * 8 * kBM + row;
+            const uint32_t d0 = fb + (uint32_t)((ci & 1) * SK * kOutChunkBytes) + row * 16;
+#pragma unroll 1
+            for (int pc = 0; pc < SK; ++pc) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                cp_async_16_cg(d0 + (uint32_t)((pc * 8 + j) * kBM * 16),
+                               s0 + (size_t)pc * (BN * kBM / 4) + j * kBM);
+            }
+            cp_async_commit();
+          };
+          stage_chunk(0);
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 32) {
+            const int ci = c / 32;
+            if (c + 32 < BN) {
+              stage_chunk(ci + 1);
+              cp_async_wait<1>();
+            } else {
+              cp_async_wait<0>();
+            }
+            const uint32_t d0 = fb + (uint32_t)((ci & 1) * SK * kOutChunkBytes) + row * 16;
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float4 q = lds128(d0 + (uint32_t)(j * kBM * 16));
+              v[4 * j] = q.x; v[4 * j + 1] = q.y; v[4 * j + 2] = q.z; v[4 * j + 3] = q.w;
+            }
+#pragma unroll 1
+            for (int pc = 1; pc < SK; ++pc) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float4 q = lds128(d0 + (uint32_t)((pc * 8 + j) * kBM * 16));
+                v[4 * j] += q.x; v[4 * j + 1] += q.y; v[4 * j + 2] += q.z; v[4 * j + 3] += q.w;
+              }
+            }
+            uint32_t r[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(v[j]);
+            emit(tm, tn, c, m, r);
+          }
+        } else if (*fix_flag) {
           __threadfence();
           const float4* src0 = reinterpret_cast<const float4*>(p.ws) +
                                (size_t)u.slot * p.split_k * (size_t)(BN * kBM / 4);

@@ -197,6 +197,10 @@ __device__ __forceinline__ void cp_async_16(void* smem_dst, const void* gsrc, ui
                "l"(gsrc), "r"(src_bytes)
                : "memory");
 }
+// 16-byte cp.async (L2 only) to a shared-window address.
+__device__ __forceinline__ void cp_async_16_cg(uint32_t smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_dst), "l"(gsrc) : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() {
   asm volatile("cp.async.commit_group;" ::: "memory");
 }
