@@ -214,7 +214,7 @@ class ConvWorkload:
                        "pad": 1, "seed": 1, "layout": "NCHW in/out",
                        "l2": f"rotating {self.nsets} input/output sets "
                              f"({self.nsets * bytes_per_set / 2**20:.0f} MiB > 126 MiB L2)"}
-        self.launches_per_step = 3  # NCHW->NHWC, weight prepack, implicit-GEMM conv
+        self.launches_per_step = 2  # NCHW->NHWC + weight prepack (one launch), implicit-GEMM conv
 
     def step(self):
         rb = self.rb

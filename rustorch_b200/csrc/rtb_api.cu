@@ -725,20 +725,23 @@ int rtb_conv2d_fwd(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, in
   float* xs = nullptr;
   float* ws = nullptr;
   const float* xin = x;
+  st = ws_alloc(ctx, (void**)&ws, (size_t)rtb_conv2d_packed_weight_size(Co, Ci, kh, kw) * 4, s);
+  if (st) return st;
   if (x_layout == RTB_LAYOUT_NCHW || Cp != Ci || !aligned16(x)) {
     st = ws_alloc(ctx, (void**)&xs, (size_t)(N * H * W * Cp) * 4, s);
-    if (st) return st;
-    if (x_layout == RTB_LAYOUT_NCHW) {
-      st = launch_nchw_to_nhwc_padded(x, N, Ci, H, W, Cp, xs, s);
-    } else {
-      // NHWC with Ci % 4 != 0 or unaligned: repack rows of Ci into rows of Cp.
-      st = launch_pack_kmajor(x, N * H * W, Ci, Ci, 1, xs, Cp, s);
+    if (st == RTB_OK) {
+      if (x_layout == RTB_LAYOUT_NCHW) {
+        // layout change and weight repack in one launch
+        st = launch_conv_prologue(x, N, Ci, H, W, Cp, xs, w, Co, kh, kw, ws, s);
+      } else {
+        // NHWC with Ci % 4 != 0 or unaligned: repack rows of Ci into rows of Cp.
+        st = launch_pack_kmajor(x, N * H * W, Ci, Ci, 1, xs, Cp, s);
+        if (st == RTB_OK) st = launch_prepack_weight(w, Co, Ci, kh, kw, Cp, ws, s);
+      }
     }
     xin = xs;
-  }
-  if (st == RTB_OK) {
-    st = ws_alloc(ctx, (void**)&ws, (size_t)rtb_conv2d_packed_weight_size(Co, Ci, kh, kw) * 4, s);
-    if (st == RTB_OK) st = launch_prepack_weight(w, Co, Ci, kh, kw, Cp, ws, s);
+  } else {
+    st = launch_prepack_weight(w, Co, Ci, kh, kw, Cp, ws, s);
   }
   if (st == RTB_OK)
     st = conv_core(ctx, N, Ci, H, W, Co, kh, kw, sh, sw, ph, pw, Ho, Wo, xin, ws, bias, residual,

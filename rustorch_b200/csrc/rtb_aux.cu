@@ -69,13 +69,15 @@ __global__ void fill_rows_kernel(float* C, int64_t M, int64_t N, int64_t ldc,
 // warp writes 4 pixels x 32 channels as 16-byte stores.  32-bit index math
 // within an image.
 constexpr int kT2Pix = 128;
-__global__ void __launch_bounds__(256) nchw_to_nhwc_kernel(const float* __restrict__ x, int C,
-                                                            int HW, int Cp, int vec,
-                                                            int vec_out, float* __restrict__ y) {
-  __shared__ float tile[32][kT2Pix + 1];
-  const int p0 = blockIdx.x * kT2Pix, c0 = blockIdx.y * 32;
-  const float* xi = x + (int64_t)blockIdx.z * C * HW;
-  float* yi = y + (int64_t)blockIdx.z * HW * Cp;
+// One 32-channel x 128-pixel tile (tile index p_t, channel block c_t, image n);
+// `tile` is 32 x (kT2Pix + 1) floats of shared memory.
+__device__ __forceinline__ void nchw_to_nhwc_tile(const float* __restrict__ x, int C, int HW,
+                                                  int Cp, int vec, int vec_out,
+                                                  float* __restrict__ y, int p_t, int c_t,
+                                                  int64_t n, float (*tile)[kT2Pix + 1]) {
+  const int p0 = p_t * kT2Pix, c0 = c_t * 32;
+  const float* xi = x + n * C * HW;
+  float* yi = y + n * HW * Cp;
   const int t = threadIdx.x;
   // load: 32 channels x 32 four-pixel groups, 4 per thread
 #pragma unroll
@@ -118,6 +120,13 @@ __global__ void __launch_bounds__(256) nchw_to_nhwc_kernel(const float* __restri
   }
 }
 
+__global__ void __launch_bounds__(256) nchw_to_nhwc_kernel(const float* __restrict__ x, int C,
+                                                            int HW, int Cp, int vec,
+                                                            int vec_out, float* __restrict__ y) {
+  __shared__ float tile[32][kT2Pix + 1];
+  nchw_to_nhwc_tile(x, C, HW, Cp, vec, vec_out, y, blockIdx.x, blockIdx.y, blockIdx.z, tile);
+}
+
 // Small-channel variant (C <= 4, Cp == 4): one thread per pixel reads its C
 // channel values (coalesced across threads within each plane) and writes one
 // 16-byte NHWC pixel.
@@ -158,11 +167,10 @@ __global__ void nhwc_to_nchw_kernel(const float* __restrict__ x, int64_t C, int6
 // One block per output channel: its Ci*kh*kw weights are read contiguously
 // into shared memory (when they fit), then written in (tap, ci) order.
 constexpr int kPrepackSmemFloats = 12288;  // 48 KB
-__global__ void __launch_bounds__(256) prepack_weight_kernel(const float* __restrict__ w, int Ci,
-                                                              int taps, int Cp,
-                                                              float* __restrict__ wp) {
-  __shared__ float sw[kPrepackSmemFloats];
-  const int co = blockIdx.x;
+// Output channel co's weights; `sw` is kPrepackSmemFloats floats of shared memory.
+__device__ __forceinline__ void prepack_weight_block(const float* __restrict__ w, int Ci, int taps,
+                                                     int Cp, float* __restrict__ wp, int co,
+                                                     float* sw) {
   const int n_in = Ci * taps;
   const float* src = w + (int64_t)co * n_in;
   float* dst = wp + (int64_t)co * taps * Cp;
@@ -179,6 +187,35 @@ __global__ void __launch_bounds__(256) prepack_weight_kernel(const float* __rest
       const int tap = k / Cp, ci = k - tap * Cp;
       dst[k] = ci < Ci ? __ldg(src + ci * taps + tap) : 0.0f;
     }
+  }
+}
+
+__global__ void __launch_bounds__(256) prepack_weight_kernel(const float* __restrict__ w, int Ci,
+                                                              int taps, int Cp,
+                                                              float* __restrict__ wp) {
+  __shared__ float sw[kPrepackSmemFloats];
+  prepack_weight_block(w, Ci, taps, Cp, wp, blockIdx.x, sw);
+}
+
+// A conv call's two input repacks in one launch: blocks [0, n_tiles) move
+// NCHW -> NHWC tiles (tiles_p x tiles_c per image), the next Co blocks repack
+// the weight (one output channel each).  Shared memory is one 48 KB buffer
+// used by either role.
+__global__ void __launch_bounds__(256) conv_prologue_kernel(
+    const float* __restrict__ x, int C, int HW, int Cp, int vec, int vec_out,
+    float* __restrict__ y, int tiles_p, int tiles_c, int64_t n_tiles,
+    const float* __restrict__ w, int taps, float* __restrict__ wp) {
+  __shared__ __align__(16) float buf[kPrepackSmemFloats];
+  const int64_t b = blockIdx.x;
+  if (b < n_tiles) {
+    const int64_t per_img = (int64_t)tiles_p * tiles_c;
+    const int64_t n = b / per_img;
+    const int r = (int)(b - n * per_img);
+    const int c_t = r / tiles_p, p_t = r - c_t * tiles_p;
+    nchw_to_nhwc_tile(x, C, HW, Cp, vec, vec_out, y, p_t, c_t, n,
+                      reinterpret_cast<float (*)[kT2Pix + 1]>(buf));
+  } else {
+    prepack_weight_block(w, C, taps, Cp, wp, (int)(b - n_tiles), buf);
   }
 }
 
@@ -395,6 +432,30 @@ int launch_nchw_to_nhwc_padded(const float* x, int64_t N, int64_t C, int64_t H, 
   clear_stale_cuda_error();
   nchw_to_nhwc_kernel<<<grid, 256, 0, s>>>(x, (int)C, (int)HW, (int)Cp, vec, vec_out, y);
   return launch_check("nchw_to_nhwc");
+}
+
+int launch_conv_prologue(const float* x, int64_t N, int64_t C, int64_t H, int64_t W, int64_t Cp,
+                         float* y, const float* w, int64_t Co, int64_t kh, int64_t kw, float* wp,
+                         cudaStream_t s) {
+  const int64_t HW = H * W, taps = kh * kw;
+  if (Cp == 4 || HW > INT32_MAX || C > INT32_MAX || Cp > INT32_MAX || Co > INT32_MAX ||
+      C * taps > INT32_MAX || taps * Cp > INT32_MAX) {
+    // small-channel inputs keep their own transform kernel
+    int st = launch_nchw_to_nhwc_padded(x, N, C, H, W, Cp, y, s);
+    return st ? st : launch_prepack_weight(w, Co, C, kh, kw, Cp, wp, s);
+  }
+  const int tiles_p = (int)((HW + kT2Pix - 1) / kT2Pix);
+  const int tiles_c = (int)((Cp + 31) / 32);
+  const int64_t n_tiles = N * tiles_p * tiles_c;
+  const int64_t blocks = n_tiles + Co;
+  if (blocks > INT32_MAX) return set_error(RTB_E_UNSUPPORTED, "conv prologue: too large");
+  const int vec = (HW % 4 == 0) && (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
+  const int vec_out = (Cp % 4 == 0) && (reinterpret_cast<uintptr_t>(y) & 15u) == 0;
+  clear_stale_cuda_error();
+  conv_prologue_kernel<<<(unsigned)blocks, 256, 0, s>>>(x, (int)C, (int)HW, (int)Cp, vec, vec_out,
+                                                        y, tiles_p, tiles_c, n_tiles, w, (int)taps,
+                                                        wp);
+  return launch_check("conv prologue");
 }
 
 int launch_nhwc_to_nchw(const float* x, float* y, int64_t N, int64_t C, int64_t HW,

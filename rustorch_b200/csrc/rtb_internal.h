@@ -125,6 +125,11 @@ int launch_nchw_to_nhwc_padded(const float* x, int64_t N, int64_t C, int64_t H, 
                                int64_t Cp, float* y, cudaStream_t s);
 int launch_prepack_weight(const float* w, int64_t Co, int64_t Ci, int64_t kh, int64_t kw,
                           int64_t Cp, float* wp, cudaStream_t s);
+// NCHW -> NHWC (channels padded to Cp) of x and the weight prepack of
+// launch_prepack_weight in one launch (two launches when Cp == 4).
+int launch_conv_prologue(const float* x, int64_t N, int64_t C, int64_t H, int64_t W, int64_t Cp,
+                         float* y, const float* w, int64_t Co, int64_t kh, int64_t kw, float* wp,
+                         cudaStream_t s);
 int launch_max_pool2d(const float* x, float* y, int64_t N, int64_t C, int64_t H, int64_t W,
                       int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw,
                       int layout, cudaStream_t s);
