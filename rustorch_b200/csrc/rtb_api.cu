@@ -725,6 +725,29 @@ int rtb_conv2d_fwd(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, in
   float* xs = nullptr;
   float* ws = nullptr;
   const float* xin = x;
+  // Stride-2 convs over <= 4 channels (the ResNet stem: 7x7 s2 over RGB): as
+  // a stride-1 conv of the 16-channel space-to-depth input, whose k-blocks
+  // are two 16-channel filter taps fetched by TMA im2col, instead of the
+  // 4-channel cp.async gather.  3xTF32 only (the multi-tap producer feeds the
+  // split converters).
+  static const bool s2d_env = std::getenv("RTB_CONV_S2D") == nullptr ||
+                              std::string(std::getenv("RTB_CONV_S2D")) != "0";
+  if (x_layout == RTB_LAYOUT_NCHW && split3 && Ci <= 4 && sh == 2 && sw == 2 && kh >= 2 &&
+      kw >= 2 && s2d_env && std::getenv("RTB_CONV_GATHER") == nullptr) {
+    const int64_t kh2 = (kh + 1) / 2, kw2 = (kw + 1) / 2;
+    const int64_t Hs = Ho + kh2 - 1, Ws = Wo + kw2 - 1;
+    st = ws_alloc(ctx, (void**)&ws, (size_t)(Co * kh2 * kw2 * 16) * 4, s);
+    if (st) return st;
+    st = ws_alloc(ctx, (void**)&xs, (size_t)(N * Hs * Ws * 16) * 4, s);
+    if (st == RTB_OK)
+      st = launch_conv_prologue_s2d(x, N, Ci, H, W, ph, pw, Hs, Ws, xs, w, Co, kh, kw, ws, s);
+    if (st == RTB_OK)
+      st = conv_core(ctx, N, 16, Hs, Ws, Co, kh2, kw2, 1, 1, 0, 0, Ho, Wo, xs, ws, bias, residual,
+                     relu, y, y_layout, split3, s);
+    ws_free(xs, s);
+    ws_free(ws, s);
+    return st;
+  }
   st = ws_alloc(ctx, (void**)&ws, (size_t)rtb_conv2d_packed_weight_size(Co, Ci, kh, kw) * 4, s);
   if (st) return st;
   if (x_layout == RTB_LAYOUT_NCHW || Cp != Ci || !aligned16(x)) {

@@ -458,6 +458,68 @@ int launch_conv_prologue(const float* x, int64_t N, int64_t C, int64_t H, int64_
   return launch_check("conv prologue");
 }
 
+// Space-to-depth form of a stride-2 conv over an input of at most 4 channels:
+//   y[n][hs][ws][(pr*2 + pc)*4 + c] = x[n][c][2*hs + pr - ph][2*ws + pc - pw]
+// (zero outside the image, c >= C zero), an NHWC tensor of 16 channels whose
+// stride-1, unpadded conv with the kernel
+//   w2[co][(R*kw2 + S)][(pr*2 + pc)*4 + c] = w[co][c][2R + pr][2S + pc]
+// (zero where 2R + pr >= kh or 2S + pc >= kw), kh2 = ceil(kh/2), equals the
+// original conv.  Blocks [0, pix_blocks) write one s2d pixel (64 bytes) per
+// thread; the next Co blocks write one output channel's repacked weights.
+__global__ void __launch_bounds__(256) conv_prologue_s2d_kernel(
+    const float* __restrict__ x, int C, int H, int W, int ph, int pw, int Hs, int Ws,
+    int64_t npix, int64_t pix_blocks, float4* __restrict__ y, const float* __restrict__ w,
+    int kh, int kw, int kh2, int kw2, float* __restrict__ w2) {
+  const int64_t b = blockIdx.x;
+  if (b < pix_blocks) {
+    const int64_t i = b * 256 + threadIdx.x;
+    if (i >= npix) return;
+    const int64_t n = i / ((int64_t)Hs * Ws);
+    const int rem = (int)(i - n * Hs * Ws);
+    const int hs = rem / Ws, ws = rem - hs * Ws;
+    const float* xn = x + n * C * H * W;
+    float v[16];
+#pragma unroll
+    for (int ph2 = 0; ph2 < 4; ++ph2) {
+      const int ih = 2 * hs + (ph2 >> 1) - ph, iw = 2 * ws + (ph2 & 1) - pw;
+      const bool in = ih >= 0 && ih < H && iw >= 0 && iw < W;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        v[ph2 * 4 + c] = (in && c < C) ? __ldg(xn + ((int64_t)c * H + ih) * W + iw) : 0.0f;
+    }
+    float4* dst = y + i * 4;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  } else {
+    const int co = (int)(b - pix_blocks);
+    const int n_out = kh2 * kw2 * 16;
+    for (int k = threadIdx.x; k < n_out; k += 256) {
+      const int tap = k >> 4, j = k & 15;
+      const int R = tap / kw2, S = tap - R * kw2;
+      const int r = 2 * R + (j >> 3), sc = 2 * S + ((j >> 2) & 1), c = j & 3;
+      w2[(int64_t)co * n_out + k] =
+          (r < kh && sc < kw && c < C) ? __ldg(w + (((int64_t)co * C + c) * kh + r) * kw + sc) : 0.0f;
+    }
+  }
+}
+
+int launch_conv_prologue_s2d(const float* x, int64_t N, int64_t C, int64_t H, int64_t W,
+                             int64_t ph, int64_t pw, int64_t Hs, int64_t Ws, float* y,
+                             const float* w, int64_t Co, int64_t kh, int64_t kw, float* w2,
+                             cudaStream_t s) {
+  const int64_t npix = N * Hs * Ws;
+  const int64_t pix_blocks = (npix + 255) / 256;
+  if (C > 4 || H * W > INT32_MAX || Hs * Ws > INT32_MAX || pix_blocks + Co > INT32_MAX ||
+      (reinterpret_cast<uintptr_t>(y) & 15u) != 0)
+    return set_error(RTB_E_UNSUPPORTED, "conv s2d prologue: unsupported shape");
+  clear_stale_cuda_error();
+  conv_prologue_s2d_kernel<<<(unsigned)(pix_blocks + Co), 256, 0, s>>>(
+      x, (int)C, (int)H, (int)W, (int)ph, (int)pw, (int)Hs, (int)Ws, npix, pix_blocks,
+      reinterpret_cast<float4*>(y), w, (int)kh, (int)kw, (int)((kh + 1) / 2), (int)((kw + 1) / 2),
+      w2);
+  return launch_check("conv s2d prologue");
+}
+
 int launch_nhwc_to_nchw(const float* x, float* y, int64_t N, int64_t C, int64_t HW,
                         cudaStream_t s) {
   dim3 grid((unsigned)((HW + 31) / 32), (unsigned)((C + 31) / 32), (unsigned)N);

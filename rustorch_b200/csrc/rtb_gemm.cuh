@@ -695,6 +695,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
       } else if (p.out_mode == 1) {
         const uint32_t buf = smem_u32(sOut + (chunk % Cfg::kOutBufs) * kOutChunkBytes);
         epilogue_nchw_chunk(p, buf, row, et, tm * kBM, n0, r, sb);
+        if (Cfg::kOutBufs == 1) named_bar_sync(1, 128);  // single buffer: readers done first
         ++chunk;
       } else if (p.out_mode == 2) {
         const uint32_t buf = smem_u32(sOut + (chunk % Cfg::kOutBufs) * kOutChunkBytes);

@@ -764,7 +764,7 @@ struct ResNet18::Impl {
   std::vector<Tensor> wp;      // prepacked weights [Co, k*k*Cp] (device)
   Tensor fc_w, fc_b;           // [1000,512], [1000] (device)
   int64_t cap_batch = 0;
-  Tensor x0, bufA, bufB, bufC, bufD, pooled;  // NHWC activation buffers
+  Tensor bufA, bufB, bufC, bufD, pooled;  // NHWC activation buffers
 };
 
 ResNet18::ResNet18(uint64_t seed, int device, int prec) : impl_(new Impl) {
@@ -849,7 +849,6 @@ void ResNet18::forward_device(int64_t B, const float* x_nchw, float* logits, voi
   const Device d = Device::cuda(I.device);
   if (B > I.cap_batch) {
     const size_t b = (size_t)B;
-    I.x0 = Tensor::empty({b * 224 * 224 * 4}, d);
     const size_t big = b * 112 * 112 * 64;  // largest activation (stem output)
     I.bufA = Tensor::empty({big}, d);
     I.bufB = Tensor::empty({big}, d);
@@ -869,9 +868,17 @@ void ResNet18::forward_device(int64_t B, const float* x_nchw, float* logits, voi
         "resnet conv");
     return (H + 2 * (int64_t)c.p - (int64_t)c.k) / (int64_t)c.s + 1;
   };
-  chk(rtb_nchw_to_nhwc_padded(ctx, B, 3, 224, 224, x_nchw, I.x0.device_ptr(), stream),
-      "resnet input layout");
-  int64_t h = conv(0, I.x0.device_ptr(), 224, 224, I.bufA.device_ptr(), nullptr, true);  // 112
+  // stem straight from the NCHW input (the conv's prologue writes the stride-2
+  // space-to-depth layout in 3xTF32 mode, NHWC otherwise)
+  {
+    const auto& c = I.specs[0];
+    chk(rtb_conv2d_fwd(ctx, B, (int64_t)c.ci, 224, 224, (int64_t)c.co, (int64_t)c.k, (int64_t)c.k,
+                       (int64_t)c.s, (int64_t)c.s, (int64_t)c.p, (int64_t)c.p, x_nchw,
+                       RTB_LAYOUT_NCHW, I.w[0].device_ptr(), I.b[0].device_ptr(), nullptr,
+                       RTB_ACT_RELU, I.bufA.device_ptr(), RTB_LAYOUT_NHWC, I.prec, stream),
+        "resnet stem");
+  }
+  int64_t h = (224 + 2 * 3 - 7) / 2 + 1;  // 112
   chk(rtb_max_pool2d(ctx, B, 64, h, h, 3, 3, 2, 2, 1, 1, I.bufA.device_ptr(), I.bufB.device_ptr(),
                      RTB_LAYOUT_NHWC, stream),
       "resnet maxpool");

@@ -130,6 +130,13 @@ int launch_prepack_weight(const float* w, int64_t Co, int64_t Ci, int64_t kh, in
 int launch_conv_prologue(const float* x, int64_t N, int64_t C, int64_t H, int64_t W, int64_t Cp,
                          float* y, const float* w, int64_t Co, int64_t kh, int64_t kw, float* wp,
                          cudaStream_t s);
+// Stride-2 conv over <= 4 input channels as a stride-1 conv of its space-to-
+// depth form: NCHW x -> NHWC [N, Hs, Ws, 16] (padding applied) and w [Co, C,
+// kh, kw] -> [Co, ceil(kh/2)*ceil(kw/2), 16], in one launch.
+int launch_conv_prologue_s2d(const float* x, int64_t N, int64_t C, int64_t H, int64_t W,
+                             int64_t ph, int64_t pw, int64_t Hs, int64_t Ws, float* y,
+                             const float* w, int64_t Co, int64_t kh, int64_t kw, float* w2,
+                             cudaStream_t s);
 int launch_max_pool2d(const float* x, float* y, int64_t N, int64_t C, int64_t H, int64_t W,
                       int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw,
                       int layout, cudaStream_t s);

@@ -85,6 +85,12 @@ def test_conv_bias_relu_resnet50_layer(gpu, orc, prec):
     ((1, 36, 5, 5), (10, 36, 5, 5), (1, 1), (0, 0)),        # K-blocks straddle taps
     ((8, 7, 40, 40), (16, 7, 3, 3), (1, 1), (1, 1)),        # Cp=8: 4 taps per k-block
     ((4, 13, 48, 48), (32, 13, 5, 5), (2, 2), (2, 2)),      # Cp=16: 2 taps per k-block
+    # stride 2 over <= 4 channels: 3xTF32 runs these as stride-1 convs of the
+    # 16-channel space-to-depth input (odd sizes, even and odd kernels)
+    ((2, 1, 33, 30), (8, 1, 4, 5), (2, 2), (1, 2)),
+    ((3, 4, 17, 19), (16, 4, 3, 3), (2, 2), (1, 1)),
+    ((2, 2, 64, 64), (24, 2, 2, 2), (2, 2), (0, 0)),
+    ((4, 3, 100, 90), (32, 3, 5, 5), (2, 2), (2, 2)),       # large enough for TMA im2col
 ])
 @pytest.mark.parametrize("prec", [0, 1])
 @pytest.mark.parametrize("producer", ["auto", "gather"])
