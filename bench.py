@@ -148,28 +148,57 @@ def _dist_env():
 
 
 class E2EPipeline:
-    """Round-robin slots for the end-to-end measurement, each with its own CUDA
-    stream and its own device and pinned host buffers: step i runs its H2D
-    copies, its call and its D2H copy in order on slot i % depth, so one step's
-    upload overlaps the previous step's call and the one before's download
-    (PCIe is full duplex).  Every step still moves its own inputs and result."""
+    """End-to-end steps on three streams: uploads (H2D) on one, the calls on
+    one, downloads (D2H) on one, so each copy engine moves step after step
+    back to back while the calls run between them (PCIe is full duplex).
+    `depth` slots of device and pinned host buffers rotate; events keep a
+    slot's upload behind the previous call that read it and its call behind
+    the previous download of its result.  Every step still moves its own
+    inputs and result.  Per step:
+        k = pipe.next()            # then the H2D copies on pipe.h_in
+        pipe.compute(k)            # then the call(s) on pipe.h_c / pipe.s_c
+        pipe.download(k)           # then the D2H copies on pipe.h_out
+        pipe.finish(k)
+    """
 
     def __init__(self, torch, dev, depth):
         self.torch, self.dev, self.depth = torch, dev, depth
-        self.streams = [torch.cuda.Stream(dev) for _ in range(depth)]
+        self.s_in, self.s_c, self.s_out = (torch.cuda.Stream(dev) for _ in range(3))
+        self.h_in, self.h_c, self.h_out = (ctypes.c_void_p(st.cuda_stream)
+                                           for st in (self.s_in, self.s_c, self.s_out))
+        self.ev_in = [torch.cuda.Event() for _ in range(depth)]
+        self.ev_comp = [torch.cuda.Event() for _ in range(depth)]
+        self.ev_out = [torch.cuda.Event() for _ in range(depth)]
+        self.used = [False] * depth
         self.i = 0
 
     def next(self):
         k = self.i % self.depth
         self.i += 1
-        return k, self.streams[k], ctypes.c_void_p(self.streams[k].cuda_stream)
+        if self.used[k]:  # the slot's inputs were read by its previous call
+            self.s_in.wait_event(self.ev_comp[k])
+        return k
+
+    def compute(self, k):
+        self.ev_in[k].record(self.s_in)
+        self.s_c.wait_event(self.ev_in[k])
+        if self.used[k]:  # the slot's result buffer was read by its previous download
+            self.s_c.wait_event(self.ev_out[k])
+
+    def download(self, k):
+        self.ev_comp[k].record(self.s_c)
+        self.s_out.wait_event(self.ev_comp[k])
+
+    def finish(self, k):
+        self.ev_out[k].record(self.s_out)
+        self.used[k] = True
 
     def begin(self, ev):
-        for st in self.streams:
+        for st in (self.s_in, self.s_c, self.s_out):
             st.wait_event(ev)
 
     def join(self, cur):
-        for st in self.streams:
+        for st in (self.s_in, self.s_c, self.s_out):
             e = self.torch.cuda.Event()
             e.record(st)
             cur.wait_event(e)
@@ -275,19 +304,23 @@ class ConvWorkload:
     def e2e_step(self):
         rb = self.rb
         ctx = rb.get_context(self.dev.index or 0)
-        k, _, stream = self.pipe.next()
+        pipe = self.pipe
+        k = pipe.next()
         slot = self.slots[k]
         for key, dst in (("x", slot["dx"]), ("w", slot["dw"]), ("b", slot["db"])):
             p, nb = slot[key]
-            rb.call("rtb_memcpy_h2d", ctx.handle, ctypes.c_void_p(dst.data_ptr()), p, nb, stream)
+            rb.call("rtb_memcpy_h2d", ctx.handle, ctypes.c_void_p(dst.data_ptr()), p, nb, pipe.h_in)
+        pipe.compute(k)
         y = slot["dy"]
         rb.call("rtb_conv2d_fwd", ctx.handle, self.N, self.C, self.H, self.W, self.Co, 3, 3, 1, 1, 1,
                 1, ctypes.c_void_p(slot["dx"].data_ptr()), rb.LAYOUT_NCHW,
                 ctypes.c_void_p(slot["dw"].data_ptr()), ctypes.c_void_p(slot["db"].data_ptr()),
                 None, rb.ACT_RELU, ctypes.c_void_p(y.data_ptr()), rb.LAYOUT_NCHW, PRECISION[0],
-                stream)
+                pipe.h_c)
+        pipe.download(k)
         p, nb = slot["y"]
-        rb.call("rtb_memcpy_d2h", ctx.handle, p, ctypes.c_void_p(y.data_ptr()), nb, stream)
+        rb.call("rtb_memcpy_d2h", ctx.handle, p, ctypes.c_void_p(y.data_ptr()), nb, pipe.h_out)
+        pipe.finish(k)
 
     def e2e_teardown(self):
         ctx = self.rb.get_context(self.dev.index or 0)
@@ -390,18 +423,22 @@ class ConvBwdWorkload:
     def e2e_step(self):
         rb = self.rb
         ctx = rb.get_context(self.dev.index or 0)
-        k, _, stream = self.pipe.next()
+        pipe = self.pipe
+        k = pipe.next()
         sl = self.slots[k]
         for key, dst in (("x", sl["x_"]), ("dy", sl["dy_"])):
             rb.call("rtb_memcpy_h2d", ctx.handle, ctypes.c_void_p(dst.data_ptr()), sl[key],
-                    self.host[key].nbytes, stream)
+                    self.host[key].nbytes, pipe.h_in)
         rb.call("rtb_memcpy_h2d", ctx.handle, ctypes.c_void_p(sl["w_"].data_ptr()), sl["w"],
-                self.host["w"].nbytes, stream)
-        self._call(sl["x_"], sl["dy_"], sl["ddx"], sl["ddw"], stream, sl["w_"])
+                self.host["w"].nbytes, pipe.h_in)
+        pipe.compute(k)
+        self._call(sl["x_"], sl["dy_"], sl["ddx"], sl["ddw"], pipe.h_c, sl["w_"])
+        pipe.download(k)
         rb.call("rtb_memcpy_d2h", ctx.handle, sl["pdx"], ctypes.c_void_p(sl["ddx"].data_ptr()),
-                self.host["x"].nbytes, stream)
+                self.host["x"].nbytes, pipe.h_out)
         rb.call("rtb_memcpy_d2h", ctx.handle, sl["pdw"], ctypes.c_void_p(sl["ddw"].data_ptr()),
-                self.host["w"].nbytes, stream)
+                self.host["w"].nbytes, pipe.h_out)
+        pipe.finish(k)
 
     def e2e_teardown(self):
         ctx = self.rb.get_context(self.dev.index or 0)
@@ -547,25 +584,29 @@ class GemmWorkload:
     def e2e_step(self):
         rb = self.rb
         ctx = rb.get_context(self.dev.index or 0)
-        k, st, stream = self.pipe.next()
+        pipe = self.pipe
+        k = pipe.next()
         slot = self.slots[k]
         a, b, c = slot["da"], slot["db"], slot["dc"]
         for key, dst in (("a", a), ("b", b)):
             p, nb = slot[key]
-            rb.call("rtb_memcpy_h2d", ctx.handle, ctypes.c_void_p(dst.data_ptr()), p, nb, stream)
+            rb.call("rtb_memcpy_h2d", ctx.handle, ctypes.c_void_p(dst.data_ptr()), p, nb, pipe.h_in)
+        pipe.compute(k)
         if self.fused:
-            with self.torch.cuda.stream(st):
+            with self.torch.cuda.stream(pipe.s_c):
                 c = self.gemm(a, b, precision=PRECISION[0])
         elif self.nsplit:
-            with self.torch.cuda.stream(st):
+            with self.torch.cuda.stream(pipe.s_c):
                 self.gemm(a, b, precision=PRECISION[0], out=c, parts=self.parts)
         else:
             rb.call("rtb_sgemm", ctx.handle, self.m, self.n, self.k,
                     ctypes.c_void_p(a.data_ptr()), self.k, 0, ctypes.c_void_p(b.data_ptr()),
                     self.n_local, 0, None, rb.ACT_NONE, ctypes.c_void_p(c.data_ptr()), self.n,
-                    PRECISION[0], stream)
+                    PRECISION[0], pipe.h_c)
+        pipe.download(k)
         p, nb = slot["c"]
-        rb.call("rtb_memcpy_d2h", ctx.handle, p, ctypes.c_void_p(c.data_ptr()), nb, stream)
+        rb.call("rtb_memcpy_d2h", ctx.handle, p, ctypes.c_void_p(c.data_ptr()), nb, pipe.h_out)
+        pipe.finish(k)
 
     def e2e_teardown(self):
         ctx = self.rb.get_context(self.dev.index or 0)
@@ -677,14 +718,18 @@ class ResNet18Workload:
     def e2e_step(self):
         rb = self.rb
         ctx = rb.get_context(self.dev.index or 0)
-        k, _, stream = self.pipe.next()
+        pipe = self.pipe
+        k = pipe.next()
         slot = self.slots[k]
         rb.call("rtb_memcpy_h2d", ctx.handle, ctypes.c_void_p(slot["dx"].data_ptr()), slot["px"],
-                self.h2d_bytes, stream)
+                self.h2d_bytes, pipe.h_in)
+        pipe.compute(k)
         rb.call("rtb_resnet18_forward", slot["h"], self.B, ctypes.c_void_p(slot["dx"].data_ptr()),
-                ctypes.c_void_p(slot["dy"].data_ptr()), stream)
+                ctypes.c_void_p(slot["dy"].data_ptr()), pipe.h_c)
+        pipe.download(k)
         rb.call("rtb_memcpy_d2h", ctx.handle, slot["py"], ctypes.c_void_p(slot["dy"].data_ptr()),
-                self.d2h_bytes, stream)
+                self.d2h_bytes, pipe.h_out)
+        pipe.finish(k)
 
     def e2e_teardown(self):
         ctx = self.rb.get_context(self.dev.index or 0)
@@ -807,14 +852,18 @@ class MlpWorkload:
     def e2e_step(self):
         rb = self.rb
         ctx = rb.get_context(self.dev.index or 0)
-        k, st, stream = self.pipe.next()
+        pipe = self.pipe
+        k = pipe.next()
         slot = self.slots[k]
         rb.call("rtb_memcpy_h2d", ctx.handle, ctypes.c_void_p(slot["dx"].data_ptr()), slot["px"],
-                self.h2d_bytes, stream)
-        with self.torch.cuda.stream(st):  # rb.sgemm launches on torch's current stream
+                self.h2d_bytes, pipe.h_in)
+        pipe.compute(k)
+        with self.torch.cuda.stream(pipe.s_c):  # rb.sgemm launches on torch's current stream
             self._fwd(slot["dx"], slot["h"])
+        pipe.download(k)
         rb.call("rtb_memcpy_d2h", ctx.handle, slot["py"], ctypes.c_void_p(slot["h"][2].data_ptr()),
-                self.d2h_bytes, stream)
+                self.d2h_bytes, pipe.h_out)
+        pipe.finish(k)
 
     def e2e_teardown(self):
         ctx = self.rb.get_context(self.dev.index or 0)
@@ -903,14 +952,18 @@ class LinearNormWorkload:
     def e2e_step(self):
         rb = self.rb
         ctx = rb.get_context(self.dev.index or 0)
-        k, st, stream = self.pipe.next()
+        pipe = self.pipe
+        k = pipe.next()
         slot = self.slots[k]
         rb.call("rtb_memcpy_h2d", ctx.handle, ctypes.c_void_p(slot["dx"].data_ptr()), slot["px"],
-                self.h2d_bytes, stream)
-        with self.torch.cuda.stream(st):
+                self.h2d_bytes, pipe.h_in)
+        pipe.compute(k)
+        with self.torch.cuda.stream(pipe.s_c):
             self._fwd(slot["dx"], slot["dy"])
+        pipe.download(k)
         rb.call("rtb_memcpy_d2h", ctx.handle, slot["py"], ctypes.c_void_p(slot["dy"].data_ptr()),
-                self.d2h_bytes, stream)
+                self.d2h_bytes, pipe.h_out)
+        pipe.finish(k)
 
     def e2e_teardown(self):
         ctx = self.rb.get_context(self.dev.index or 0)
