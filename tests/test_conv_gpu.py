@@ -123,6 +123,24 @@ def test_conv_nhwc_residual(gpu, orc):
     assert orc.rel_frob(y, np.maximum(pre, 0)) <= 1e-5
 
 
+@pytest.mark.parametrize("shape", [(2, 64, 32, 32), (3, 48, 28, 28), (2, 40, 9, 9)])
+def test_conv_nchw_residual(gpu, orc, shape):
+    """NCHW in/out with a residual and ReLU: 1024-pixel images (every tile
+    inside one image: 3-D TMA stores), 784-pixel images (tiles across image
+    boundaries take the direct stores) and 81-pixel images (hw % 4 != 0)."""
+    n, c, h, w_ = shape
+    x = orc.normal(shape, 9, 1)
+    w = orc.normal((c + 8, c, 3, 3), 9, 2, 0.0, float(np.sqrt(2.0 / (9 * c))))
+    b = orc.uniform((c + 8,), 9, 3, -0.1, 0.1)
+    r = orc.normal((n, c + 8, h, w_), 9, 4)
+    pre = (orc.conv2d_f64(x, w, (1, 1), (1, 1)) + b.astype(np.float64)[None, :, None, None]
+           + r.astype(np.float64))
+    for prec, tol in ((0, 1e-5), (1, 5e-3)):
+        y = _host(gpu.conv2d_fwd(_dev(x), _dev(w), _dev(b), (1, 1), (1, 1), residual=_dev(r),
+                                 act=gpu.ACT_RELU, precision=prec))
+        assert orc.rel_frob(y, np.maximum(pre, 0)) <= tol
+
+
 def test_conv_errors(gpu):
     x = torch.ones((1, 3, 8, 8), device="cuda")
     with pytest.raises(ValueError, match="must match input channels"):
