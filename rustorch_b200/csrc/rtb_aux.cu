@@ -170,12 +170,12 @@ constexpr int kPrepackSmemFloats = 12288;  // 48 KB
 // Output channel co's weights; `sw` is kPrepackSmemFloats floats of shared memory.
 __device__ __forceinline__ void prepack_weight_block(const float* __restrict__ w, int Ci, int taps,
                                                      int Cp, float* __restrict__ wp, int co,
-                                                     float* sw) {
+                                                     float* sw, int sw_floats) {
   const int n_in = Ci * taps;
   const float* src = w + (int64_t)co * n_in;
   float* dst = wp + (int64_t)co * taps * Cp;
   const int Kw = taps * Cp;
-  if (n_in <= kPrepackSmemFloats) {
+  if (n_in <= sw_floats) {
     for (int i = threadIdx.x; i < n_in; i += blockDim.x) sw[i] = __ldg(src + i);
     __syncthreads();
     for (int k = threadIdx.x; k < Kw; k += blockDim.x) {
@@ -194,18 +194,21 @@ __global__ void __launch_bounds__(256) prepack_weight_kernel(const float* __rest
                                                               int taps, int Cp,
                                                               float* __restrict__ wp) {
   __shared__ float sw[kPrepackSmemFloats];
-  prepack_weight_block(w, Ci, taps, Cp, wp, blockIdx.x, sw);
+  prepack_weight_block(w, Ci, taps, Cp, wp, blockIdx.x, sw, kPrepackSmemFloats);
 }
 
 // A conv call's two input repacks in one launch: blocks [0, n_tiles) move
 // NCHW -> NHWC tiles (tiles_p x tiles_c per image), the next Co blocks repack
-// the weight (one output channel each).  Shared memory is one 48 KB buffer
-// used by either role.
+// the weight (one output channel each).  Shared memory is the transpose
+// tile (16.5 KB), which the weight role reuses when one output channel's
+// weights fit (Ci*kh*kw <= 4128, else it reads them from global), so 8 CTAs
+// fit on an SM.
+constexpr int kPrologueSmemFloats = 32 * (kT2Pix + 1);
 __global__ void __launch_bounds__(256) conv_prologue_kernel(
     const float* __restrict__ x, int C, int HW, int Cp, int vec, int vec_out,
     float* __restrict__ y, int tiles_p, int tiles_c, int64_t n_tiles,
     const float* __restrict__ w, int taps, float* __restrict__ wp) {
-  __shared__ __align__(16) float buf[kPrepackSmemFloats];
+  __shared__ __align__(16) float buf[kPrologueSmemFloats];
   const int64_t b = blockIdx.x;
   if (b < n_tiles) {
     const int64_t per_img = (int64_t)tiles_p * tiles_c;
@@ -215,7 +218,7 @@ __global__ void __launch_bounds__(256) conv_prologue_kernel(
     nchw_to_nhwc_tile(x, C, HW, Cp, vec, vec_out, y, p_t, c_t, n,
                       reinterpret_cast<float (*)[kT2Pix + 1]>(buf));
   } else {
-    prepack_weight_block(w, C, taps, Cp, wp, (int)(b - n_tiles), buf);
+    prepack_weight_block(w, C, taps, Cp, wp, (int)(b - n_tiles), buf, kPrologueSmemFloats);
   }
 }
 
