@@ -206,19 +206,25 @@ int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
       if (sk >= 2) {
         const size_t part_bytes = (size_t)rem * sk * bn * kBM * sizeof(float);
         const size_t cnt_off = (part_bytes + 255) & ~size_t(255);
-        st = ws_alloc(ctx, &split_ws, cnt_off + (size_t)rem * sizeof(int), stream);
+        // counters zeroed by an earlier kernel of the same call, or a memset
+        const bool pre = d.zeroed_cnt && rem <= d.zeroed_cnt_n;
+        st = ws_alloc(ctx, &split_ws, pre ? part_bytes : cnt_off + (size_t)rem * sizeof(int),
+                      stream);
         if (st != RTB_OK) return st;
-        cudaError_t e = cudaMemsetAsync(static_cast<char*>(split_ws) + cnt_off, 0,
-                                        (size_t)rem * sizeof(int), stream);
-        if (e != cudaSuccess) {
-          ws_free(split_ws, stream);
-          return cuda_status(e, "split counters memset");
+        if (!pre) {
+          cudaError_t e = cudaMemsetAsync(static_cast<char*>(split_ws) + cnt_off, 0,
+                                          (size_t)rem * sizeof(int), stream);
+          if (e != cudaSuccess) {
+            ws_free(split_ws, stream);
+            return cuda_status(e, "split counters memset");
+          }
         }
         p.full_units = (int)(tiles - rem);
         p.split_k = sk;
         p.num_units = (int)(tiles - rem + rem * sk);
         p.ws = static_cast<float*>(split_ws);
-        p.ws_cnt = reinterpret_cast<int*>(static_cast<char*>(split_ws) + cnt_off);
+        p.ws_cnt = pre ? d.zeroed_cnt
+                       : reinterpret_cast<int*>(static_cast<char*>(split_ws) + cnt_off);
       }
     }
   }

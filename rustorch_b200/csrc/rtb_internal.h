@@ -104,6 +104,11 @@ struct GemmDesc {
   int split3 = 1;     // 3xTF32 (1) or TF32 (0)
   int bn = 0;         // 0 = heuristic
   int allow_workspace = 1;  // 0: never allocate (tail balancing off)
+  // Optional split-tile arrival counters already zeroed on the stream (by an
+  // earlier kernel of the same call); used instead of a memset when they
+  // cover the tail's tiles.
+  int* zeroed_cnt = nullptr;
+  int zeroed_cnt_n = 0;
 };
 
 // Validated launch of the tcgen05 engine (A/B already TMA-compatible).
@@ -126,17 +131,22 @@ int launch_nchw_to_nhwc_padded(const float* x, int64_t N, int64_t C, int64_t H, 
 int launch_prepack_weight(const float* w, int64_t Co, int64_t Ci, int64_t kh, int64_t kw,
                           int64_t Cp, float* wp, cudaStream_t s);
 // NCHW -> NHWC (channels padded to Cp) of x and the weight prepack of
-// launch_prepack_weight in one launch (two launches when Cp == 4).
+// launch_prepack_weight in one launch (two launches when Cp == 4); the one
+// launch also zeroes `ncnt` (<= 256) split-tile counters (*cnt_zeroed says
+// whether it did).
 int launch_conv_prologue(const float* x, int64_t N, int64_t C, int64_t H, int64_t W, int64_t Cp,
                          float* y, const float* w, int64_t Co, int64_t kh, int64_t kw, float* wp,
-                         cudaStream_t s);
+                         int* cnt, int ncnt, bool* cnt_zeroed, cudaStream_t s);
 // Stride-2 conv over <= 4 input channels as a stride-1 conv of its space-to-
 // depth form: NCHW x -> NHWC [N, Hs, Ws, 16] (padding applied) and w [Co, C,
 // kh, kw] -> [Co, ceil(kh/2)*ceil(kw/2), 16], in one launch.
 int launch_conv_prologue_s2d(const float* x, int64_t N, int64_t C, int64_t H, int64_t W,
                              int64_t ph, int64_t pw, int64_t Hs, int64_t Ws, float* y,
                              const float* w, int64_t Co, int64_t kh, int64_t kw, float* w2,
-                             cudaStream_t s);
+                             int* cnt, int ncnt, cudaStream_t s);
+// Capacity of the counter block a conv prologue zeroes (>= the largest tail
+// of a 148-SM wave split).
+constexpr int kPrologueCounters = 256;
 int launch_max_pool2d(const float* x, float* y, int64_t N, int64_t C, int64_t H, int64_t W,
                       int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw,
                       int layout, cudaStream_t s);
