@@ -142,6 +142,26 @@ void ws_free(void* p, cudaStream_t s) {
   if (p) cudaFreeAsync(p, s);
 }
 
+int split_counters(rtb_ctx* ctx, cudaStream_t s, unsigned long long** d, unsigned long long* gen) {
+  std::lock_guard<std::mutex> lk(ctx->cnt_mu);
+  auto& c = ctx->split_cnt[s];
+  if (!c.d) {
+    // zeroed once (generation 0 is never issued); later launches on this
+    // stream tag their arrivals with increasing generations
+    cudaError_t e = cudaMalloc(&c.d, kSplitCounters * sizeof(unsigned long long));
+    if (e == cudaSuccess)
+      e = cudaMemsetAsync(c.d, 0, kSplitCounters * sizeof(unsigned long long), s);
+    if (e != cudaSuccess) {
+      if (c.d) cudaFree(c.d);
+      c.d = nullptr;
+      return cuda_status(e, "split counters");
+    }
+  }
+  *d = c.d;
+  *gen = ++c.gen;
+  return RTB_OK;
+}
+
 }  // namespace rtb
 
 using namespace rtb;
@@ -216,6 +236,9 @@ int rtb_destroy(rtb_ctx* ctx) {
   RTB_CHECK_CTX(ctx);
   DeviceGuard g(ctx->device);
   cudaStreamSynchronize(ctx->stream);
+  cudaDeviceSynchronize();  // launches on other streams may still use the counter blocks
+  for (auto& kv : ctx->split_cnt)
+    if (kv.second.d) cudaFree(kv.second.d);
   cudaFree(ctx->d_err);
   cudaStreamDestroy(ctx->stream);
   delete ctx;
@@ -615,8 +638,7 @@ static int conv_core(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, 
                      int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw,
                      int64_t Ho, int64_t Wo, const float* x_nhwc, const float* wp,
                      const float* bias, const float* residual, int relu, float* y, int y_layout,
-                     int split3, cudaStream_t s, bool allow_workspace = true,
-                     int* zeroed_cnt = nullptr, int zeroed_cnt_n = 0) {
+                     int split3, cudaStream_t s, bool allow_workspace = true) {
   const int64_t Cp = round_up(Ci, 4);
   const int64_t M = N * Ho * Wo;
   if (M == 0) return RTB_OK;
@@ -650,8 +672,6 @@ static int conv_core(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, 
   d.R = (int)kh; d.S = (int)kw; d.sh = (int)sh; d.sw = (int)sw; d.ph = (int)ph; d.pw = (int)pw;
   d.split3 = split3;
   d.allow_workspace = allow_workspace ? 1 : 0;
-  d.zeroed_cnt = zeroed_cnt;
-  d.zeroed_cnt_n = zeroed_cnt_n;
   return gemm_run(ctx, d, s);
 }
 
@@ -739,35 +759,26 @@ int rtb_conv2d_fwd(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, in
       kw >= 2 && s2d_env && std::getenv("RTB_CONV_GATHER") == nullptr) {
     const int64_t kh2 = (kh + 1) / 2, kw2 = (kw + 1) / 2;
     const int64_t Hs = Ho + kh2 - 1, Ws = Wo + kw2 - 1;
-    int* cnt = nullptr;
     st = ws_alloc(ctx, (void**)&ws, (size_t)(Co * kh2 * kw2 * 16) * 4, s);
     if (st) return st;
     st = ws_alloc(ctx, (void**)&xs, (size_t)(N * Hs * Ws * 16) * 4, s);
-    if (st == RTB_OK) st = ws_alloc(ctx, (void**)&cnt, kPrologueCounters * sizeof(int), s);
     if (st == RTB_OK)
-      st = launch_conv_prologue_s2d(x, N, Ci, H, W, ph, pw, Hs, Ws, xs, w, Co, kh, kw, ws, cnt,
-                                    kPrologueCounters, s);
+      st = launch_conv_prologue_s2d(x, N, Ci, H, W, ph, pw, Hs, Ws, xs, w, Co, kh, kw, ws, s);
     if (st == RTB_OK)
       st = conv_core(ctx, N, 16, Hs, Ws, Co, kh2, kw2, 1, 1, 0, 0, Ho, Wo, xs, ws, bias, residual,
-                     relu, y, y_layout, split3, s, true, cnt, kPrologueCounters);
-    ws_free(cnt, s);
+                     relu, y, y_layout, split3, s);
     ws_free(xs, s);
     ws_free(ws, s);
     return st;
   }
-  int* cnt = nullptr;
-  bool cnt_zeroed = false;
   st = ws_alloc(ctx, (void**)&ws, (size_t)rtb_conv2d_packed_weight_size(Co, Ci, kh, kw) * 4, s);
   if (st) return st;
   if (x_layout == RTB_LAYOUT_NCHW || Cp != Ci || !aligned16(x)) {
     st = ws_alloc(ctx, (void**)&xs, (size_t)(N * H * W * Cp) * 4, s);
     if (st == RTB_OK) {
       if (x_layout == RTB_LAYOUT_NCHW) {
-        // layout change, weight repack and the split counters in one launch
-        st = ws_alloc(ctx, (void**)&cnt, kPrologueCounters * sizeof(int), s);
-        if (st == RTB_OK)
-          st = launch_conv_prologue(x, N, Ci, H, W, Cp, xs, w, Co, kh, kw, ws, cnt,
-                                    kPrologueCounters, &cnt_zeroed, s);
+        // layout change and weight repack in one launch
+        st = launch_conv_prologue(x, N, Ci, H, W, Cp, xs, w, Co, kh, kw, ws, s);
       } else {
         // NHWC with Ci % 4 != 0 or unaligned: repack rows of Ci into rows of Cp.
         st = launch_pack_kmajor(x, N * H * W, Ci, Ci, 1, xs, Cp, s);
@@ -780,9 +791,7 @@ int rtb_conv2d_fwd(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, in
   }
   if (st == RTB_OK)
     st = conv_core(ctx, N, Ci, H, W, Co, kh, kw, sh, sw, ph, pw, Ho, Wo, xin, ws, bias, residual,
-                   relu, y, y_layout, split3, s, true, cnt_zeroed ? cnt : nullptr,
-                   cnt_zeroed ? kPrologueCounters : 0);
-  ws_free(cnt, s);
+                   relu, y, y_layout, split3, s);
   ws_free(xs, s);
   ws_free(ws, s);
   return st;

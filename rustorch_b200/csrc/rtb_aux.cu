@@ -207,11 +207,9 @@ constexpr int kPrologueSmemFloats = 32 * (kT2Pix + 1);
 __global__ void __launch_bounds__(256) conv_prologue_kernel(
     const float* __restrict__ x, int C, int HW, int Cp, int vec, int vec_out,
     float* __restrict__ y, int tiles_p, int tiles_c, int64_t n_tiles,
-    const float* __restrict__ w, int taps, float* __restrict__ wp, int* __restrict__ cnt,
-    int ncnt) {
+    const float* __restrict__ w, int taps, float* __restrict__ wp) {
   __shared__ __align__(16) float buf[kPrologueSmemFloats];
   const int64_t b = blockIdx.x;
-  if (b == 0 && threadIdx.x < ncnt) cnt[threadIdx.x] = 0;
   if (b < n_tiles) {
     const int64_t per_img = (int64_t)tiles_p * tiles_c;
     const int64_t n = b / per_img;
@@ -441,10 +439,8 @@ int launch_nchw_to_nhwc_padded(const float* x, int64_t N, int64_t C, int64_t H, 
 
 int launch_conv_prologue(const float* x, int64_t N, int64_t C, int64_t H, int64_t W, int64_t Cp,
                          float* y, const float* w, int64_t Co, int64_t kh, int64_t kw, float* wp,
-                         int* cnt, int ncnt, bool* cnt_zeroed, cudaStream_t s) {
+                         cudaStream_t s) {
   const int64_t HW = H * W, taps = kh * kw;
-  *cnt_zeroed = false;
-  if (!cnt || ncnt > 256) ncnt = 0;
   if (Cp == 4 || HW > INT32_MAX || C > INT32_MAX || Cp > INT32_MAX || Co > INT32_MAX ||
       C * taps > INT32_MAX || taps * Cp > INT32_MAX) {
     // small-channel inputs keep their own transform kernel
@@ -461,10 +457,8 @@ int launch_conv_prologue(const float* x, int64_t N, int64_t C, int64_t H, int64_
   clear_stale_cuda_error();
   conv_prologue_kernel<<<(unsigned)blocks, 256, 0, s>>>(x, (int)C, (int)HW, (int)Cp, vec, vec_out,
                                                         y, tiles_p, tiles_c, n_tiles, w, (int)taps,
-                                                        wp, cnt, ncnt);
-  const int st = launch_check("conv prologue");
-  *cnt_zeroed = (st == RTB_OK && ncnt > 0);
-  return st;
+                                                        wp);
+  return launch_check("conv prologue");
 }
 
 // Space-to-depth form of a stride-2 conv over an input of at most 4 channels:
@@ -478,9 +472,8 @@ int launch_conv_prologue(const float* x, int64_t N, int64_t C, int64_t H, int64_
 __global__ void __launch_bounds__(256) conv_prologue_s2d_kernel(
     const float* __restrict__ x, int C, int H, int W, int ph, int pw, int Hs, int Ws,
     int64_t npix, int64_t pix_blocks, float4* __restrict__ y, const float* __restrict__ w,
-    int kh, int kw, int kh2, int kw2, float* __restrict__ w2, int* __restrict__ cnt, int ncnt) {
+    int kh, int kw, int kh2, int kw2, float* __restrict__ w2) {
   const int64_t b = blockIdx.x;
-  if (b == 0 && threadIdx.x < ncnt) cnt[threadIdx.x] = 0;
   if (b < pix_blocks) {
     const int64_t i = b * 256 + threadIdx.x;
     if (i >= npix) return;
@@ -516,9 +509,8 @@ __global__ void __launch_bounds__(256) conv_prologue_s2d_kernel(
 int launch_conv_prologue_s2d(const float* x, int64_t N, int64_t C, int64_t H, int64_t W,
                              int64_t ph, int64_t pw, int64_t Hs, int64_t Ws, float* y,
                              const float* w, int64_t Co, int64_t kh, int64_t kw, float* w2,
-                             int* cnt, int ncnt, cudaStream_t s) {
+                             cudaStream_t s) {
   const int64_t npix = N * Hs * Ws;
-  if (!cnt || ncnt > 256) ncnt = 0;
   const int64_t pix_blocks = (npix + 255) / 256;
   if (C > 4 || H * W > INT32_MAX || Hs * Ws > INT32_MAX || pix_blocks + Co > INT32_MAX ||
       (reinterpret_cast<uintptr_t>(y) & 15u) != 0)
@@ -527,7 +519,7 @@ int launch_conv_prologue_s2d(const float* x, int64_t N, int64_t C, int64_t H, in
   conv_prologue_s2d_kernel<<<(unsigned)(pix_blocks + Co), 256, 0, s>>>(
       x, (int)C, (int)H, (int)W, (int)ph, (int)pw, (int)Hs, (int)Ws, npix, pix_blocks,
       reinterpret_cast<float4*>(y), w, (int)kh, (int)kw, (int)((kh + 1) / 2), (int)((kw + 1) / 2),
-      w2, cnt, ncnt);
+      w2);
   return launch_check("conv s2d prologue");
 }
 

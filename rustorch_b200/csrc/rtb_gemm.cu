@@ -190,6 +190,7 @@ int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
   p.num_units = (int)tiles;
   p.ws = nullptr;
   p.ws_cnt = nullptr;
+  p.cnt_gen = 0;
   void* split_ws = nullptr;
   static const int tail_env = env_int("RTB_TAIL_SPLIT", 1);
   if (tail_env && d.allow_workspace) {
@@ -203,28 +204,16 @@ int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
       if (sk > 16) sk = 16;
       if (sk > 8 && sk > p.num_kb / 4) sk = p.num_kb / 4 > 8 ? p.num_kb / 4 : 8;
       if (sk > p.num_kb / 2) sk = p.num_kb / 2;  // every piece keeps >= 2 k-blocks
-      if (sk >= 2) {
+      if (sk >= 2 && rem <= kSplitCounters) {
         const size_t part_bytes = (size_t)rem * sk * bn * kBM * sizeof(float);
-        const size_t cnt_off = (part_bytes + 255) & ~size_t(255);
-        // counters zeroed by an earlier kernel of the same call, or a memset
-        const bool pre = d.zeroed_cnt && rem <= d.zeroed_cnt_n;
-        st = ws_alloc(ctx, &split_ws, pre ? part_bytes : cnt_off + (size_t)rem * sizeof(int),
-                      stream);
+        st = split_counters(ctx, stream, &p.ws_cnt, &p.cnt_gen);
         if (st != RTB_OK) return st;
-        if (!pre) {
-          cudaError_t e = cudaMemsetAsync(static_cast<char*>(split_ws) + cnt_off, 0,
-                                          (size_t)rem * sizeof(int), stream);
-          if (e != cudaSuccess) {
-            ws_free(split_ws, stream);
-            return cuda_status(e, "split counters memset");
-          }
-        }
+        st = ws_alloc(ctx, &split_ws, part_bytes, stream);
+        if (st != RTB_OK) return st;
         p.full_units = (int)(tiles - rem);
         p.split_k = sk;
         p.num_units = (int)(tiles - rem + rem * sk);
         p.ws = static_cast<float*>(split_ws);
-        p.ws_cnt = pre ? d.zeroed_cnt
-                       : reinterpret_cast<int*>(static_cast<char*>(split_ws) + cnt_off);
       }
     }
   }

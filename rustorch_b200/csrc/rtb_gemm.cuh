@@ -94,7 +94,8 @@ struct GemmParams {
   int split_k;           // 1 = no split
   int num_units;
   float* ws;             // [tail tile][piece][BN/32][8][128] float4
-  int* ws_cnt;           // [tail tile] arrival counters, zero at launch
+  unsigned long long* ws_cnt;  // [tail tile] arrival words (generation << 8 | count)
+  unsigned long long cnt_gen;  // this launch's generation (older tags count as zero)
 };
 
 struct WorkUnit {
@@ -814,8 +815,12 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
         __threadfence();
         named_bar_sync(1, 128);
         if (et == 0) {
-          const int old = atomicAdd(p.ws_cnt + u.slot, 1);
-          *fix_flag = (old == p.split_k - 1);
+          const int arrived = tagged_arrive(p.ws_cnt + u.slot, p.cnt_gen);
+          if (arrived < 0) {
+            atomicCAS(p.err, 0, (int)DEV_BAD_CONFIG);
+            *abort_flag = 1;
+          }
+          *fix_flag = (arrived == p.split_k - 1);
         }
         named_bar_sync(1, 128);
         // The ring is idle here: a piece is always its CTA's last work unit

@@ -6,6 +6,7 @@
 #include <cstdint>
 #include <mutex>
 #include <string>
+#include <unordered_map>
 
 #include "../../include/rustorch_b200.h"
 
@@ -20,6 +21,16 @@ struct rtb_ctx {
   int default_precision = RTB_PREC_3XTF32;
   unsigned long long* trace = nullptr;  // kernel timeline trace buffer (diagnostics)
   int64_t trace_capacity = 0;           // in 64-bit stamps
+  // Split-tile arrival counters, one block per stream this context launches
+  // on (launches on one stream run in order, so they can share it).  A word
+  // holds (launch generation << 8 | arrivals): a launch counts only arrivals
+  // tagged with its own generation, so the block never needs re-zeroing.
+  struct SplitCounters {
+    unsigned long long* d = nullptr;
+    unsigned long long gen = 0;
+  };
+  std::mutex cnt_mu;
+  std::unordered_map<cudaStream_t, SplitCounters> split_cnt;
 };
 
 namespace rtb {
@@ -104,11 +115,6 @@ struct GemmDesc {
   int split3 = 1;     // 3xTF32 (1) or TF32 (0)
   int bn = 0;         // 0 = heuristic
   int allow_workspace = 1;  // 0: never allocate (tail balancing off)
-  // Optional split-tile arrival counters already zeroed on the stream (by an
-  // earlier kernel of the same call); used instead of a memset when they
-  // cover the tail's tiles.
-  int* zeroed_cnt = nullptr;
-  int zeroed_cnt_n = 0;
 };
 
 // Validated launch of the tcgen05 engine (A/B already TMA-compatible).
@@ -131,22 +137,17 @@ int launch_nchw_to_nhwc_padded(const float* x, int64_t N, int64_t C, int64_t H, 
 int launch_prepack_weight(const float* w, int64_t Co, int64_t Ci, int64_t kh, int64_t kw,
                           int64_t Cp, float* wp, cudaStream_t s);
 // NCHW -> NHWC (channels padded to Cp) of x and the weight prepack of
-// launch_prepack_weight in one launch (two launches when Cp == 4); the one
-// launch also zeroes `ncnt` (<= 256) split-tile counters (*cnt_zeroed says
-// whether it did).
+// launch_prepack_weight in one launch (two launches when Cp == 4).
 int launch_conv_prologue(const float* x, int64_t N, int64_t C, int64_t H, int64_t W, int64_t Cp,
                          float* y, const float* w, int64_t Co, int64_t kh, int64_t kw, float* wp,
-                         int* cnt, int ncnt, bool* cnt_zeroed, cudaStream_t s);
+                         cudaStream_t s);
 // Stride-2 conv over <= 4 input channels as a stride-1 conv of its space-to-
 // depth form: NCHW x -> NHWC [N, Hs, Ws, 16] (padding applied) and w [Co, C,
 // kh, kw] -> [Co, ceil(kh/2)*ceil(kw/2), 16], in one launch.
 int launch_conv_prologue_s2d(const float* x, int64_t N, int64_t C, int64_t H, int64_t W,
                              int64_t ph, int64_t pw, int64_t Hs, int64_t Ws, float* y,
                              const float* w, int64_t Co, int64_t kh, int64_t kw, float* w2,
-                             int* cnt, int ncnt, cudaStream_t s);
-// Capacity of the counter block a conv prologue zeroes (>= the largest tail
-// of a 148-SM wave split).
-constexpr int kPrologueCounters = 256;
+                             cudaStream_t s);
 int launch_max_pool2d(const float* x, float* y, int64_t N, int64_t C, int64_t H, int64_t W,
                       int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw,
                       int layout, cudaStream_t s);
@@ -194,5 +195,10 @@ int launch_layernorm_act(rtb_ctx* ctx, const float* X, int64_t ldx, float* Y, in
 // Stream-ordered workspace.
 int ws_alloc(rtb_ctx* ctx, void** p, size_t bytes, cudaStream_t s);
 void ws_free(void* p, cudaStream_t s);
+// Capacity (words) of a stream's split-counter block: >= the tail tiles of
+// one wave split (at most half the SMs).
+constexpr int kSplitCounters = 256;
+// The split-counter block for `s` and the next launch generation on it.
+int split_counters(rtb_ctx* ctx, cudaStream_t s, unsigned long long** d, unsigned long long* gen);
 
 }  // namespace rtb

@@ -89,6 +89,21 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
+// Arrival on a split-counter word holding (generation << 8 | count): tags of
+// another generation are stale and count as zero.  Returns the arrivals
+// before this one, or -1 if the word kept changing (at most as many
+// contenders as pieces race on a word, so 64 tries are ample).
+__device__ __forceinline__ int tagged_arrive(unsigned long long* w, unsigned long long gen) {
+  unsigned long long cur = atomicAdd(w, 0ull);
+  for (int tries = 0; tries < 64; ++tries) {
+    const unsigned long long base = (cur >> 8) == gen ? cur : (gen << 8);
+    const unsigned long long prev = atomicCAS(w, cur, base + 1);
+    if (prev == cur) return (int)(base & 0xFFull);
+    cur = prev;
+  }
+  return -1;
+}
+
 // Shared-memory loads/stores by 32-bit shared-window address (a pointer that
 // went through an integer alignment round trip would otherwise be a generic
 // address, and generic accesses to shared memory take the slower path).

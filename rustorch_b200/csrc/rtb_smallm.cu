@@ -44,7 +44,8 @@ struct SmallMParams {
   int relu;
   float* ws;     // [S][M][ws_ld] partial sums (S > 1)
   int64_t ws_ld;
-  int* cnt;      // [nblk] arrival counters, zero at launch (S > 1)
+  unsigned long long* cnt;  // [nblk] arrival words (generation << 8 | count), S > 1
+  unsigned long long cnt_gen;
   int* err;
   unsigned long long timeout_ns;
 };
@@ -230,7 +231,11 @@ __global__ void __launch_bounds__(256, 1)
   }
   __threadfence();
   __syncthreads();
-  if (tid == 0) *last_flag = (atomicAdd(p.cnt + blk, 1) == p.S - 1);
+  if (tid == 0) {
+    const int arrived = tagged_arrive(p.cnt + blk, p.cnt_gen);
+    if (arrived < 0) atomicCAS(p.err, 0, (int)DEV_BAD_CONFIG);
+    *last_flag = (arrived == p.S - 1);
+  }
   __syncthreads();
   if (!*last_flag || !owner) return;
   __threadfence();
@@ -308,20 +313,15 @@ int smallm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
   if (S < 1 || !d.allow_workspace) S = 1;
   p.S = S;
   void* ws = nullptr;
+  if (S > 1 && p.nblk > kSplitCounters) S = p.S = 1;  // no counter word for every column block
   if (S > 1) {
     p.ws_ld = (d.N + 3) / 4 * 4;
     const size_t part_bytes = (size_t)S * d.M * p.ws_ld * sizeof(float);
-    const size_t cnt_off = (part_bytes + 255) & ~size_t(255);
-    st = ws_alloc(ctx, &ws, cnt_off + (size_t)p.nblk * sizeof(int), stream);
+    st = split_counters(ctx, stream, &p.cnt, &p.cnt_gen);
     if (st != RTB_OK) return st;
-    cudaError_t e = cudaMemsetAsync(static_cast<char*>(ws) + cnt_off, 0,
-                                    (size_t)p.nblk * sizeof(int), stream);
-    if (e != cudaSuccess) {
-      ws_free(ws, stream);
-      return cuda_status(e, "smallm counters memset");
-    }
+    st = ws_alloc(ctx, &ws, part_bytes, stream);
+    if (st != RTB_OK) return st;
     p.ws = static_cast<float*>(ws);
-    p.cnt = reinterpret_cast<int*>(static_cast<char*>(ws) + cnt_off);
   }
   if (RG == 1)
     st = d.b_mn_major ? launch_smallm<1, 1>(ctx, tmA, tmB, p, stream)
