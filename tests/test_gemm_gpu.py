@@ -244,3 +244,29 @@ def test_small_m_skinny_8192(gpu, orc, m):
     cols = np.random.default_rng(2).integers(0, 8192, 256)
     ref = a.astype(np.float64) @ b[:, cols].astype(np.float64)
     assert orc.rel_frob(c[:, cols], ref) <= TOL[0]
+
+
+def test_split_counters_across_launches_and_streams(gpu, orc):
+    """Tail-split GEMMs (1024^3: 64 tiles cut into K pieces) and small-M split-K
+    GEMMs count piece arrivals in per-stream, generation-tagged words that are
+    never cleared: launches repeated on one stream and interleaved on two
+    streams give bit-identical results."""
+    a = orc.normal((1024, 1024), 40, 1)
+    b = orc.normal((1024, 1024), 40, 2)
+    s_m = orc.normal((8, 4096), 40, 3)
+    s_b = orc.normal((4096, 2048), 40, 4)
+    da, db, dsm, dsb = (torch.from_numpy(t).cuda() for t in (a, b, s_m, s_b))
+    ref = gpu.sgemm(da, db).cpu().numpy()
+    ref_s = gpu.sgemm(dsm, dsb).cpu().numpy()
+    assert orc.rel_frob(ref, orc.matmul_f64(a, b)) <= 1e-5
+    assert orc.rel_frob(ref_s, orc.matmul_f64(s_m, s_b)) <= 1e-5
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    outs = []
+    for i in range(6):
+        with torch.cuda.stream(streams[i % 2]):
+            outs.append((gpu.sgemm(da, db), gpu.sgemm(dsm, dsb)))
+    torch.cuda.synchronize()
+    for c, cs in outs:
+        np.testing.assert_array_equal(c.cpu().numpy(), ref)
+        np.testing.assert_array_equal(cs.cpu().numpy(), ref_s)
+    assert gpu.get_context(0).device_error() == 0
