@@ -677,7 +677,7 @@ class ResNet18Workload:
                        "batch_per_gpu": self.B, "input": [self.B, 3, 224, 224], "seed": 3,
                        "flops_per_image": self.flops_img,
                        "l2": "inputs larger than L2 (154 MB per batch)"}
-        self.launches_per_step = 24  # layout, 20 convs, max pool, avg pool, fc
+        self.launches_per_step = 24  # stem prologue, 20 convs, max pool, avg pool, fc
         self.unit = "img/s"
 
     def _fwd(self, x):

@@ -240,3 +240,37 @@ def test_activation_restatement(orc):
                                rtol=1e-6, atol=1e-7)
     np.testing.assert_allclose(orc.activation(x, 3)[1:], np.tanh(x[1:].astype(np.float64)),
                                rtol=1e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("N,C,H,W,Co,kh,kw,ph,pw", [
+    (2, 3, 23, 20, 5, 7, 7, 3, 3),   # the ResNet stem's form, odd sizes
+    (1, 1, 9, 9, 4, 4, 5, 1, 2),     # even and odd kernel extents
+    (2, 4, 10, 11, 3, 3, 3, 1, 1),
+    (1, 2, 8, 8, 2, 2, 2, 0, 0),
+])
+def test_space_to_depth_identity(orc, N, C, H, W, Co, kh, kw, ph, pw):
+    """The identity behind the CUDA path for stride-2 convs over <= 4 channels:
+    conv(x, w, stride 2, pad p) equals the stride-1, unpadded conv of the
+    16-channel space-to-depth input x2[n][(pr*2+pc)*4+c][hs][ws] =
+    x[n][c][2hs+pr-ph][2ws+pc-pw] with the kernel w2[co][(pr*2+pc)*4+c][R][S] =
+    w[co][c][2R+pr][2S+pc] (zero outside), Hs = Ho + ceil(kh/2) - 1."""
+    x = orc.normal((N, C, H, W), 41, 1)
+    w = orc.normal((Co, C, kh, kw), 41, 2)
+    ref = orc.conv2d_f64(x, w, (2, 2), (ph, pw))
+    Ho, Wo = ref.shape[2:]
+    kh2, kw2 = (kh + 1) // 2, (kw + 1) // 2
+    Hs, Ws = Ho + kh2 - 1, Wo + kw2 - 1
+    xp = np.zeros((N, C, 2 * Hs + 2, 2 * Ws + 2), np.float32)
+    hh, ww = min(H, 2 * Hs + 2 - ph), min(W, 2 * Ws + 2 - pw)
+    xp[:, :, ph:ph + hh, pw:pw + ww] = x[:, :, :hh, :ww]
+    x2 = np.zeros((N, 16, Hs, Ws), np.float32)
+    w2 = np.zeros((Co, 16, kh2, kw2), np.float32)
+    for pr in range(2):
+        for pc in range(2):
+            ch = (pr * 2 + pc) * 4
+            x2[:, ch:ch + C] = xp[:, :, pr:pr + 2 * Hs:2, pc:pc + 2 * Ws:2]
+            sub = w[:, :, pr::2, pc::2]
+            w2[:, ch:ch + C, :sub.shape[2], :sub.shape[3]] = sub
+    got = orc.conv2d_f64(x2, w2, (1, 1), (0, 0))
+    assert got.shape == ref.shape
+    np.testing.assert_allclose(got, ref, rtol=0, atol=1e-9)
