@@ -304,11 +304,11 @@ int launch_layernorm_act(rtb_ctx* ctx, const float* X, int64_t ldx, float* Y, in
     if (per <= 8) return launch_ln_rows<32, 8, false>(ctx, X, ldx, Y, ldy, M, n, g, b, eps, act, s);
     return launch_ln_rows<32, 16, false>(ctx, X, ldx, Y, ldy, M, n, g, b, eps, act, s);
   }
-  const bool on_chip = N <= kLnMaxOnChip;
-  if (vec) return on_chip ? launch_ln<true, true>(X, ldx, Y, ldy, M, (int)N, g, b, eps, act, s)
-                          : launch_ln<true, false>(X, ldx, Y, ldy, M, (int)N, g, b, eps, act, s);
-  return on_chip ? launch_ln<false, true>(X, ldx, Y, ldy, M, (int)N, g, b, eps, act, s)
-                 : launch_ln<false, false>(X, ldx, Y, ldy, M, (int)N, g, b, eps, act, s);
+  // a CTA per row: float4-aligned rows beyond 16384 columns (re-read through
+  // L2), other rows staged in shared memory up to 16384 columns
+  if (vec) return launch_ln<true, false>(X, ldx, Y, ldy, M, n, g, b, eps, act, s);
+  return N <= kLnMaxOnChip ? launch_ln<false, true>(X, ldx, Y, ldy, M, n, g, b, eps, act, s)
+                           : launch_ln<false, false>(X, ldx, Y, ldy, M, n, g, b, eps, act, s);
 }
 
 }  // namespace rtb
