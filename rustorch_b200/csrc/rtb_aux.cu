@@ -209,6 +209,8 @@ __global__ void __launch_bounds__(256) conv_prologue_kernel(
     float* __restrict__ y, int tiles_p, int tiles_c, int64_t n_tiles,
     const float* __restrict__ w, int taps, float* __restrict__ wp) {
   __shared__ __align__(16) float buf[kPrologueSmemFloats];
+  griddep_wait();  // launched with programmatic stream serialization
+  griddep_launch_dependents();
   const int64_t b = blockIdx.x;
   if (b < n_tiles) {
     const int64_t per_img = (int64_t)tiles_p * tiles_c;
@@ -454,10 +456,19 @@ int launch_conv_prologue(const float* x, int64_t N, int64_t C, int64_t H, int64_
   if (blocks > INT32_MAX) return set_error(RTB_E_UNSUPPORTED, "conv prologue: too large");
   const int vec = (HW % 4 == 0) && (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
   const int vec_out = (Cp % 4 == 0) && (reinterpret_cast<uintptr_t>(y) & 15u) == 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)blocks);
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   clear_stale_cuda_error();
-  conv_prologue_kernel<<<(unsigned)blocks, 256, 0, s>>>(x, (int)C, (int)HW, (int)Cp, vec, vec_out,
-                                                        y, tiles_p, tiles_c, n_tiles, w, (int)taps,
-                                                        wp);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, conv_prologue_kernel, x, (int)C, (int)HW, (int)Cp, vec,
+                                     vec_out, y, tiles_p, tiles_c, n_tiles, w, (int)taps, wp);
+  if (e != cudaSuccess) return cuda_status(e, "conv prologue launch");
   return launch_check("conv prologue");
 }
 

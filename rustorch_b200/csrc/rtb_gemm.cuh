@@ -498,6 +498,11 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Everything above touched only shared memory, TMEM and the kernel
+  // parameters; global memory is read and written after the previous kernel
+  // on the stream has completed (programmatic dependent launch).
+  griddep_wait();
+  griddep_launch_dependents();
   if (threadIdx.x == 0) trace_stamp(p, 0);
 
   if (warp == Roles::kWarpTma) {

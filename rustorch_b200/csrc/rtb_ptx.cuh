@@ -104,6 +104,18 @@ __device__ __forceinline__ int tagged_arrive(unsigned long long* w, unsigned lon
   return -1;
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialization may start while the previous kernel on the stream finishes;
+// griddep_wait() blocks until that kernel has completed and its memory is
+// visible (a no-op without a prerequisite grid), griddep_launch_dependents()
+// lets the next such kernel be scheduled.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Shared-memory loads/stores by 32-bit shared-window address (a pointer that
 // went through an integer alignment round trip would otherwise be a generic
 // address, and generic accesses to shared memory take the slower path).
