@@ -253,6 +253,8 @@ __global__ void max_pool_nchw_kernel(const float* __restrict__ x, float* __restr
 __global__ void max_pool_nhwc4_kernel(const float4* __restrict__ x, float4* __restrict__ y,
                                       int N, int C4, int H, int W, int Ho, int Wo, int kh, int kw,
                                       int sh, int sw, int ph, int pw) {
+  griddep_wait();  // launched with programmatic stream serialization
+  griddep_launch_dependents();
   const int total = N * Ho * Wo * C4;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
     const int c = i % C4;
@@ -317,6 +319,8 @@ __global__ void avg_pool_nchw_kernel(const float* __restrict__ x, float* __restr
 
 __global__ void avg_pool_nhwc_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t N,
                                      int64_t C, int64_t HW) {
+  griddep_wait();  // launched with programmatic stream serialization
+  griddep_launch_dependents();
   const int64_t total = N * C;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -456,18 +460,10 @@ int launch_conv_prologue(const float* x, int64_t N, int64_t C, int64_t H, int64_
   if (blocks > INT32_MAX) return set_error(RTB_E_UNSUPPORTED, "conv prologue: too large");
   const int vec = (HW % 4 == 0) && (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
   const int vec_out = (Cp % 4 == 0) && (reinterpret_cast<uintptr_t>(y) & 15u) == 0;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)blocks);
-  cfg.blockDim = dim3(256);
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
   clear_stale_cuda_error();
-  cudaError_t e = cudaLaunchKernelEx(&cfg, conv_prologue_kernel, x, (int)C, (int)HW, (int)Cp, vec,
-                                     vec_out, y, tiles_p, tiles_c, n_tiles, w, (int)taps, wp);
+  cudaError_t e = launch_pdl(conv_prologue_kernel, dim3((unsigned)blocks), dim3(256), 0, s, x,
+                             (int)C, (int)HW, (int)Cp, vec, vec_out, y, tiles_p, tiles_c, n_tiles,
+                             w, (int)taps, wp);
   if (e != cudaSuccess) return cuda_status(e, "conv prologue launch");
   return launch_check("conv prologue");
 }
@@ -484,6 +480,8 @@ __global__ void __launch_bounds__(256) conv_prologue_s2d_kernel(
     const float* __restrict__ x, int C, int H, int W, int ph, int pw, int Hs, int Ws,
     int64_t npix, int64_t pix_blocks, float4* __restrict__ y, const float* __restrict__ w,
     int kh, int kw, int kh2, int kw2, float* __restrict__ w2) {
+  griddep_wait();  // launched with programmatic stream serialization
+  griddep_launch_dependents();
   const int64_t b = blockIdx.x;
   if (b < pix_blocks) {
     const int64_t i = b * 256 + threadIdx.x;
@@ -527,10 +525,11 @@ int launch_conv_prologue_s2d(const float* x, int64_t N, int64_t C, int64_t H, in
       (reinterpret_cast<uintptr_t>(y) & 15u) != 0)
     return set_error(RTB_E_UNSUPPORTED, "conv s2d prologue: unsupported shape");
   clear_stale_cuda_error();
-  conv_prologue_s2d_kernel<<<(unsigned)(pix_blocks + Co), 256, 0, s>>>(
-      x, (int)C, (int)H, (int)W, (int)ph, (int)pw, (int)Hs, (int)Ws, npix, pix_blocks,
-      reinterpret_cast<float4*>(y), w, (int)kh, (int)kw, (int)((kh + 1) / 2), (int)((kw + 1) / 2),
-      w2);
+  cudaError_t e = launch_pdl(conv_prologue_s2d_kernel, dim3((unsigned)(pix_blocks + Co)), dim3(256),
+                             0, s, x, (int)C, (int)H, (int)W, (int)ph, (int)pw, (int)Hs, (int)Ws,
+                             npix, pix_blocks, reinterpret_cast<float4*>(y), w, (int)kh, (int)kw,
+                             (int)((kh + 1) / 2), (int)((kw + 1) / 2), w2);
+  if (e != cudaSuccess) return cuda_status(e, "conv s2d prologue launch");
   return launch_check("conv s2d prologue");
 }
 
@@ -565,9 +564,13 @@ int launch_max_pool2d(const float* x, float* y, int64_t N, int64_t C, int64_t H,
                                                              (int)pw);
   else if (C % 4 == 0 && total / 4 < INT32_MAX && N * H * W * C < INT32_MAX * 4LL &&
            (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0)
-    max_pool_nhwc4_kernel<<<grid_for(total / 4), kThreads, 0, s>>>(
-        reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(y), (int)N, (int)(C / 4),
-        (int)H, (int)W, (int)Ho, (int)Wo, (int)kh, (int)kw, (int)sh, (int)sw, (int)ph, (int)pw);
+  {
+    cudaError_t e = launch_pdl(max_pool_nhwc4_kernel, dim3(grid_for(total / 4)), dim3(kThreads), 0,
+                               s, reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(y),
+                               (int)N, (int)(C / 4), (int)H, (int)W, (int)Ho, (int)Wo, (int)kh,
+                               (int)kw, (int)sh, (int)sw, (int)ph, (int)pw);
+    if (e != cudaSuccess) return cuda_status(e, "max_pool2d launch");
+  }
   else
     max_pool_nhwc_kernel<<<grid_for(total), kThreads, 0, s>>>(x, y, N, C, H, W, Ho, Wo, (int)kh,
                                                              (int)kw, (int)sh, (int)sw, (int)ph,
@@ -584,7 +587,9 @@ int launch_global_avg_pool(const float* x, float* y, int64_t N, int64_t C, int64
         x, y, N * C, HW);
   } else {
     clear_stale_cuda_error();
-    avg_pool_nhwc_kernel<<<grid_for(N * C), kThreads, 0, s>>>(x, y, N, C, HW);
+    cudaError_t e = launch_pdl(avg_pool_nhwc_kernel, dim3(grid_for(N * C)), dim3(kThreads), 0, s,
+                               x, y, N, C, HW);
+    if (e != cudaSuccess) return cuda_status(e, "global_avg_pool launch");
   }
   return launch_check("global_avg_pool");
 }

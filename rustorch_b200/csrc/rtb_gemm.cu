@@ -22,21 +22,12 @@ int launch_variant(rtb_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB,
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
   if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemm smem)");
   const int grid = p.num_units < ctx->sm_count ? p.num_units : ctx->sm_count;
-  // programmatic stream serialization: the kernel's setup (barriers, TMEM)
+  // programmatic dependent launch: the kernel's setup (barriers, TMEM)
   // overlaps the end of the previous kernel; it waits for that kernel before
   // its first global-memory access (griddep_wait in the kernel)
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)grid);
-  cfg.blockDim = dim3(Roles::kThreads);
-  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
   clear_stale_cuda_error();
-  e = cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmC, p);
+  e = launch_pdl(kern, dim3((unsigned)grid), dim3(Roles::kThreads), Cfg::kSmemBytes, stream, tmA,
+                 tmB, tmC, p);
   if (e != cudaSuccess) return cuda_status(e, "gemm kernel launch");
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_status(e, "gemm kernel launch");

@@ -195,6 +195,25 @@ int launch_layernorm_act(rtb_ctx* ctx, const float* X, int64_t ldx, float* Y, in
 // Stream-ordered workspace.
 int ws_alloc(rtb_ctx* ctx, void** p, size_t bytes, cudaStream_t s);
 void ws_free(void* p, cudaStream_t s);
+// Launch with programmatic stream serialization (programmatic dependent
+// launch): the kernel may be scheduled while the previous kernel on the
+// stream finishes, so it must call griddep_wait() before its first access
+// to global memory.  Used for the kernels of the contraction chains.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
 // Capacity (words) of a stream's split-counter block: >= the tail tiles of
 // one wave split (at most half the SMs).
 constexpr int kSplitCounters = 256;

@@ -17,6 +17,7 @@
 #include <cmath>
 
 #include "rtb_internal.h"
+#include "rtb_ptx.cuh"
 
 namespace rtb {
 
@@ -73,6 +74,8 @@ __global__ void __launch_bounds__(256) layernorm_act_rows_kernel(const float* X,
   constexpr int R = 256 / T;          // rows per CTA
   constexpr int W = T / 32;           // warps per row
   __shared__ double red_s[R][W], red_q[R][W];
+  griddep_wait();  // launched with programmatic stream serialization
+  griddep_launch_dependents();
   const int t = threadIdx.x % T, grp = threadIdx.x / T, w = t >> 5;
   const int64_t groups = (int64_t)gridDim.x * R;
   const int units = VEC ? (N >> 2) : N;
@@ -159,6 +162,8 @@ __global__ void __launch_bounds__(kLnThreads) layernorm_act_kernel(const float* 
   extern __shared__ float4 srow4[];
   float* srow = reinterpret_cast<float*>(srow4);
   __shared__ double red[kLnThreads / 32];
+  griddep_wait();  // launched with programmatic stream serialization
+  griddep_launch_dependents();
   const int n4 = N >> 2;
   for (int64_t m = blockIdx.x; m < M; m += gridDim.x) {
     const float* row = X + m * ldx;
@@ -255,8 +260,9 @@ int launch_ln(const float* X, int64_t ldx, float* Y, int64_t ldy, int64_t M, int
   const int64_t cap = (int64_t)sms * per_sm;
   const int64_t blocks = M < cap ? M : cap;
   clear_stale_cuda_error();
-  k<<<(unsigned)blocks, kLnThreads, smem, s>>>(X, ldx, Y, ldy, M, N, g, b, eps, act);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(k, dim3((unsigned)blocks), dim3(kLnThreads), smem, s, X, ldx, Y, ldy,
+                             M, N, g, b, eps, act);
+  if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? RTB_OK : cuda_status(e, "layernorm kernel launch");
 }
 
@@ -271,8 +277,9 @@ int launch_ln_rows(rtb_ctx* ctx, const float* X, int64_t ldx, float* Y, int64_t 
   const int64_t cap = (int64_t)ctx->sm_count * per_sm;
   const int64_t blocks = need < cap ? need : cap;
   clear_stale_cuda_error();
-  k<<<(unsigned)blocks, 256, 0, s>>>(X, ldx, Y, ldy, M, N, g, b, eps, act);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(k, dim3((unsigned)blocks), dim3(256), 0, s, X, ldx, Y, ldy, M, N, g, b,
+                             eps, act);
+  if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? RTB_OK : cuda_status(e, "layernorm (rows) kernel launch");
 }
 

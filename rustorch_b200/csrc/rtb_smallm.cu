@@ -97,6 +97,10 @@ __global__ void __launch_bounds__(256, 1)
     fence_mbar_init();
   }
   __syncthreads();
+  // global memory only after the previous kernel on the stream has completed
+  // (launched with programmatic stream serialization)
+  griddep_wait();
+  griddep_launch_dependents();
   auto issue = [&](int s, int chunk) {
     uint8_t* sa = base + s * Cfg::kStage;
     mbar_arrive_expect_tx(&full[s], Cfg::kStage);
@@ -266,8 +270,9 @@ int launch_smallm(rtb_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB,
                            cudaSharedmemCarveoutMaxShared);
   if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(smallm carveout)");
   clear_stale_cuda_error();
-  kern<<<p.nblk * p.S, Cfg::kThreads, Cfg::kSmem, s>>>(tmA, tmB, p);
-  e = cudaGetLastError();
+  e = launch_pdl(kern, dim3((unsigned)(p.nblk * p.S)), dim3(Cfg::kThreads), Cfg::kSmem, s, tmA, tmB,
+                 p);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_status(e, "smallm kernel launch");
   (void)ctx;
   return RTB_OK;
