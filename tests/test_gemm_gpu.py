@@ -270,3 +270,26 @@ def test_split_counters_across_launches_and_streams(gpu, orc):
         np.testing.assert_array_equal(c.cpu().numpy(), ref)
         np.testing.assert_array_equal(cs.cpu().numpy(), ref_s)
     assert gpu.get_context(0).device_error() == 0
+
+
+def test_inputs_written_by_the_previous_kernel(gpu, orc):
+    """The contraction, LayerNorm and small-M kernels are launched with
+    programmatic stream serialization and wait (griddepcontrol.wait) for the
+    previous kernel before reading: inputs that a torch kernel writes right
+    before each call must be seen complete, every time."""
+    torch.manual_seed(7)
+    x = torch.randn(1024, 1024, device="cuda")
+    y = torch.randn(1024, 1024, device="cuda")
+    s = torch.randn(16, 4096, device="cuda")
+    t = torch.randn(4096, 4096, device="cuda")
+    for i in range(4):
+        a = x * (i + 1.0)            # written by a torch kernel just before the call
+        c = gpu.sgemm(a, y)
+        ln = gpu.layer_norm(c * 0.5 + i)
+        cs = gpu.sgemm(s * (i + 2.0), t)   # small-M path
+        ref = (a.double() @ y.double())
+        assert float((c.double() - ref).norm() / ref.norm()) <= 1e-5
+        lref = torch.nn.functional.layer_norm((ref * 0.5 + i).float(), (1024,))
+        assert float((ln - lref).norm() / lref.norm()) <= 1e-5
+        sref = (s.double() * (i + 2.0)) @ t.double()
+        assert float((cs.double() - sref).norm() / sref.norm()) <= 1e-5
