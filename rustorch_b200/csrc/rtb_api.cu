@@ -143,6 +143,13 @@ void ws_free(void* p, cudaStream_t s) {
 }
 
 int split_counters(rtb_ctx* ctx, cudaStream_t s, unsigned long long** d, unsigned long long* gen) {
+  // A captured launch replays with the generation baked into its parameters,
+  // so under stream capture the caller zeroes per-launch counters instead.
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) {
+    clear_stale_cuda_error();
+    return RTB_E_UNSUPPORTED;
+  }
   std::lock_guard<std::mutex> lk(ctx->cnt_mu);
   auto& c = ctx->split_cnt[s];
   if (!c.d) {

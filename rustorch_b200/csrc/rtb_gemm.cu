@@ -211,10 +211,21 @@ int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
       if (sk > p.num_kb / 2) sk = p.num_kb / 2;  // every piece keeps >= 2 k-blocks
       if (sk >= 2 && rem <= kSplitCounters) {
         const size_t part_bytes = (size_t)rem * sk * bn * kBM * sizeof(float);
+        const size_t cnt_off = (part_bytes + 255) & ~size_t(255);
         st = split_counters(ctx, stream, &p.ws_cnt, &p.cnt_gen);
+        const bool own = (st == RTB_E_UNSUPPORTED);  // capturing: counters of this launch
+        if (st != RTB_OK && !own) return st;
+        st = ws_alloc(ctx, &split_ws, own ? cnt_off + (size_t)rem * 8 : part_bytes, stream);
         if (st != RTB_OK) return st;
-        st = ws_alloc(ctx, &split_ws, part_bytes, stream);
-        if (st != RTB_OK) return st;
+        if (own) {
+          p.ws_cnt = reinterpret_cast<unsigned long long*>(static_cast<char*>(split_ws) + cnt_off);
+          p.cnt_gen = 1;
+          cudaError_t e = cudaMemsetAsync(p.ws_cnt, 0, (size_t)rem * 8, stream);
+          if (e != cudaSuccess) {
+            ws_free(split_ws, stream);
+            return cuda_status(e, "split counters memset");
+          }
+        }
         p.full_units = (int)(tiles - rem);
         p.split_k = sk;
         p.num_units = (int)(tiles - rem + rem * sk);

@@ -217,7 +217,9 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
 // Capacity (words) of a stream's split-counter block: >= the tail tiles of
 // one wave split (at most half the SMs).
 constexpr int kSplitCounters = 256;
-// The split-counter block for `s` and the next launch generation on it.
+// The split-counter block for `s` and the next launch generation on it;
+// RTB_E_UNSUPPORTED (no error recorded) while `s` is capturing a graph, when
+// the caller allocates and zeroes counters for the launch itself (gen 1).
 int split_counters(rtb_ctx* ctx, cudaStream_t s, unsigned long long** d, unsigned long long* gen);
 
 }  // namespace rtb

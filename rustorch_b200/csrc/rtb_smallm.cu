@@ -322,10 +322,21 @@ int smallm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
   if (S > 1) {
     p.ws_ld = (d.N + 3) / 4 * 4;
     const size_t part_bytes = (size_t)S * d.M * p.ws_ld * sizeof(float);
+    const size_t cnt_off = (part_bytes + 255) & ~size_t(255);
     st = split_counters(ctx, stream, &p.cnt, &p.cnt_gen);
+    const bool own = (st == RTB_E_UNSUPPORTED);  // capturing: counters of this launch
+    if (st != RTB_OK && !own) return st;
+    st = ws_alloc(ctx, &ws, own ? cnt_off + (size_t)p.nblk * 8 : part_bytes, stream);
     if (st != RTB_OK) return st;
-    st = ws_alloc(ctx, &ws, part_bytes, stream);
-    if (st != RTB_OK) return st;
+    if (own) {
+      p.cnt = reinterpret_cast<unsigned long long*>(static_cast<char*>(ws) + cnt_off);
+      p.cnt_gen = 1;
+      cudaError_t e = cudaMemsetAsync(p.cnt, 0, (size_t)p.nblk * 8, stream);
+      if (e != cudaSuccess) {
+        ws_free(ws, stream);
+        return cuda_status(e, "smallm counters memset");
+      }
+    }
     p.ws = static_cast<float*>(ws);
   }
   if (RG == 1)

@@ -293,3 +293,46 @@ def test_inputs_written_by_the_previous_kernel(gpu, orc):
         assert float((ln - lref).norm() / lref.norm()) <= 1e-5
         sref = (s.double() * (i + 2.0)) @ t.double()
         assert float((cs.double() - sref).norm() / sref.norm()) <= 1e-5
+
+
+def test_cuda_graph_capture_and_replay(gpu, orc):
+    """A tail-split GEMM (1024^3), a small-M split-K GEMM and a conv captured
+    into one CUDA graph and replayed with new inputs: under capture the split
+    counters are the launch's own, zeroed by a memset node, so every replay
+    elects its fix-up pieces afresh."""
+    torch.manual_seed(11)
+    a = torch.randn(1024, 1024, device="cuda")
+    b = torch.randn(1024, 1024, device="cuda")
+    sm = torch.randn(8, 4096, device="cuda")
+    sb = torch.randn(4096, 2048, device="cuda")
+    x = torch.randn(32, 128, 28, 28, device="cuda")
+    w = torch.randn(128, 128, 3, 3, device="cuda") * 0.03
+    bias = torch.randn(128, device="cuda") * 0.1
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):  # warm-up outside the capture
+        for _ in range(2):
+            gpu.sgemm(a, b)
+            gpu.sgemm(sm, sb)
+            gpu.conv2d_fwd(x, w, bias, (1, 1), (1, 1), act=gpu.ACT_RELU)
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        c = gpu.sgemm(a, b)
+        cs = gpu.sgemm(sm, sb)
+        y = gpu.conv2d_fwd(x, w, bias, (1, 1), (1, 1), act=gpu.ACT_RELU)
+    for i in range(3):
+        a.mul_(-1.0 if i % 2 else 2.0)
+        sm.add_(0.5)
+        x.mul_(1.5)
+        g.replay()
+        torch.cuda.synchronize()
+        ref = a.double() @ b.double()
+        assert float((c.double() - ref).norm() / ref.norm()) <= 1e-5
+        sref = sm.double() @ sb.double()
+        assert float((cs.double() - sref).norm() / sref.norm()) <= 1e-5
+        yref = torch.relu(torch.nn.functional.conv2d(x.double(), w.double(), bias.double(),
+                                                     padding=1))
+        assert float((y.double() - yref).norm() / yref.norm()) <= 1e-5
+    assert gpu.get_context(0).device_error() == 0
