@@ -32,3 +32,12 @@ def test_reference_arm_skinny_names_shape():
     d = _run("--impl", "reference", "--workload", "gemm_m16", "--steps", "1")
     assert d["metric"].startswith("sgemm_16x8192x8192")
     assert d["value"] > 0
+
+
+def test_reference_arm_linear_norm_matches_our_config():
+    """The Linear + LayerNorm + ReLU workload's reference arm names the same
+    metric and workload as our arm (the driver pairs the two lines)."""
+    d = _run("--impl", "reference", "--workload", "linear_norm", "--steps", "1")
+    assert d["metric"].startswith("linear_norm_relu TFLOP/s")
+    assert d["config"]["workload"] == "Linear 1024->4096 + bias, LayerNorm(4096) + ReLU over 8192 rows"
+    assert d["value"] > 0 and d["cpu_baseline"]["sample"].startswith("64 of 8192 rows")
