@@ -7,6 +7,7 @@
 // These kernels only move bytes (HBM-bound); 32-bit index math inside an
 // image, 64-bit across images.
 #include "rtb_internal.h"
+#include "rtb_ptx.cuh"
 
 namespace rtb {
 
@@ -33,6 +34,8 @@ inline int launch_check(const char* what) {
 __global__ void dilate_nchw_to_nhwc_kernel(const float* __restrict__ dy, int Co, int Ho, int Wo,
                                            int sh, int sw, int Hd, int Wd, int Cop,
                                            float* __restrict__ out) {
+  griddep_wait();  // launched with programmatic stream serialization
+  griddep_launch_dependents();
   __shared__ float tile[32][33];
   const int HoWo = Ho * Wo;
   const int p0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
@@ -59,6 +62,8 @@ __global__ void dilate_nchw_to_nhwc_kernel(const float* __restrict__ dy, int Co,
 // channels = Co, output channels = Ci); co >= Co zero.
 __global__ void prepack_flip_kernel(const float* __restrict__ w, int Co, int Ci, int R, int S,
                                     int Cop, float* __restrict__ wt) {
+  griddep_wait();  // launched with programmatic stream serialization
+  griddep_launch_dependents();
   const int64_t total = (int64_t)Ci * R * S * Cop;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -79,6 +84,8 @@ __global__ void prepack_flip_kernel(const float* __restrict__ w, int Co, int Ci,
 __global__ void im2col_nhwc_kernel(const float4* __restrict__ x, int H, int W, int Cp4, int Ho,
                                    int Wo, int R, int S, int sh, int sw, int ph, int pw,
                                    int64_t P, float4* __restrict__ col) {
+  griddep_wait();  // launched with programmatic stream serialization
+  griddep_launch_dependents();
   const int Kp4 = R * S * Cp4;
   const int HoWo = Ho * Wo;
   for (int64_t p = blockIdx.x; p < P; p += gridDim.x) {
@@ -103,6 +110,8 @@ __global__ void im2col_nhwc_kernel(const float4* __restrict__ x, int H, int W, i
 // a contiguous copy.
 __global__ void nchw_to_cmajor_kernel(const float* __restrict__ dy, int64_t N, int Co, int HW,
                                       int64_t ldp, float* __restrict__ dyt) {
+  griddep_wait();  // launched with programmatic stream serialization
+  griddep_launch_dependents();
   const int64_t planes = N * Co;
   for (int64_t pl = blockIdx.x; pl < planes; pl += gridDim.x) {
     const int64_t n = pl / Co;
@@ -116,6 +125,8 @@ __global__ void nchw_to_cmajor_kernel(const float* __restrict__ dy, int64_t N, i
 // dwp [Co, R*S*Cp] -> dw [Co, Ci, R, S] (added to dw when accumulate).
 __global__ void unpack_weight_grad_kernel(const float* __restrict__ dwp, int Co, int Ci, int R,
                                           int S, int Cp, int accumulate, float* __restrict__ dw) {
+  griddep_wait();  // launched with programmatic stream serialization
+  griddep_launch_dependents();
   const int64_t total = (int64_t)Co * Ci * R * S;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -138,16 +149,18 @@ int launch_dilate_nchw_to_nhwc(const float* dy, int64_t N, int64_t Co, int64_t H
   dim3 grid((unsigned)((Ho * Wo + 31) / 32), (unsigned)((Co + 31) / 32), (unsigned)N);
   if (grid.y > 65535) return set_error(RTB_E_UNSUPPORTED, "dilate: too many channels");
   clear_stale_cuda_error();
-  dilate_nchw_to_nhwc_kernel<<<grid, dim3(32, 8), 0, s>>>(dy, (int)Co, (int)Ho, (int)Wo, (int)sh,
-                                                          (int)sw, (int)Hd, (int)Wd, (int)Cop, out);
+  cudaError_t e = launch_pdl(dilate_nchw_to_nhwc_kernel, grid, dim3(32, 8), 0, s, dy, (int)Co,
+                             (int)Ho, (int)Wo, (int)sh, (int)sw, (int)Hd, (int)Wd, (int)Cop, out);
+  if (e != cudaSuccess) return cuda_status(e, "dilate_nchw_to_nhwc launch");
   return launch_check("dilate_nchw_to_nhwc");
 }
 
 int launch_prepack_flip(const float* w, int64_t Co, int64_t Ci, int64_t R, int64_t S, int64_t Cop,
                         float* wt, cudaStream_t s) {
   clear_stale_cuda_error();
-  prepack_flip_kernel<<<grid_for(Ci * R * S * Cop), kT, 0, s>>>(w, (int)Co, (int)Ci, (int)R,
-                                                               (int)S, (int)Cop, wt);
+  cudaError_t e = launch_pdl(prepack_flip_kernel, dim3(grid_for(Ci * R * S * Cop)), dim3(kT), 0, s,
+                             w, (int)Co, (int)Ci, (int)R, (int)S, (int)Cop, wt);
+  if (e != cudaSuccess) return cuda_status(e, "prepack_flip launch");
   return launch_check("prepack_flip");
 }
 
@@ -159,9 +172,11 @@ int launch_im2col_nhwc(const float* x, int64_t N, int64_t H, int64_t W, int64_t 
     return set_error(RTB_E_UNSUPPORTED, "im2col: too large");
   const int64_t blocks = P < 148 * 64 ? P : 148 * 64;
   clear_stale_cuda_error();
-  im2col_nhwc_kernel<<<(unsigned)blocks, 128, 0, s>>>(
-      reinterpret_cast<const float4*>(x), (int)H, (int)W, (int)(Cp / 4), (int)Ho, (int)Wo, (int)R,
-      (int)S, (int)sh, (int)sw, (int)ph, (int)pw, P, reinterpret_cast<float4*>(col));
+  cudaError_t e = launch_pdl(im2col_nhwc_kernel, dim3((unsigned)blocks), dim3(128), 0, s,
+                             reinterpret_cast<const float4*>(x), (int)H, (int)W, (int)(Cp / 4),
+                             (int)Ho, (int)Wo, (int)R, (int)S, (int)sh, (int)sw, (int)ph, (int)pw, P,
+                             reinterpret_cast<float4*>(col));
+  if (e != cudaSuccess) return cuda_status(e, "im2col_nhwc launch");
   return launch_check("im2col_nhwc");
 }
 
@@ -171,15 +186,18 @@ int launch_nchw_to_cmajor(const float* dy, int64_t N, int64_t Co, int64_t HW, in
   const int64_t planes = N * Co;
   const int64_t blocks = planes < 148 * 64 ? planes : 148 * 64;
   clear_stale_cuda_error();
-  nchw_to_cmajor_kernel<<<(unsigned)blocks, 256, 0, s>>>(dy, N, (int)Co, (int)HW, ldp, dyt);
+  cudaError_t e = launch_pdl(nchw_to_cmajor_kernel, dim3((unsigned)blocks), dim3(256), 0, s, dy, N,
+                             (int)Co, (int)HW, ldp, dyt);
+  if (e != cudaSuccess) return cuda_status(e, "nchw_to_cmajor launch");
   return launch_check("nchw_to_cmajor");
 }
 
 int launch_unpack_weight_grad(const float* dwp, int64_t Co, int64_t Ci, int64_t R, int64_t S,
                               int64_t Cp, int accumulate, float* dw, cudaStream_t s) {
   clear_stale_cuda_error();
-  unpack_weight_grad_kernel<<<grid_for(Co * Ci * R * S), kT, 0, s>>>(dwp, (int)Co, (int)Ci, (int)R,
-                                                                    (int)S, (int)Cp, accumulate, dw);
+  cudaError_t e = launch_pdl(unpack_weight_grad_kernel, dim3(grid_for(Co * Ci * R * S)), dim3(kT),
+                             0, s, dwp, (int)Co, (int)Ci, (int)R, (int)S, (int)Cp, accumulate, dw);
+  if (e != cudaSuccess) return cuda_status(e, "unpack_weight_grad launch");
   return launch_check("unpack_weight_grad");
 }
 
