@@ -66,6 +66,11 @@ def test_null_context_rejected(rb):
     assert "rtb_ctx" in rb._lib.last_error()
     assert L.rtb_conv2d_fwd(None, *([1] * 11), None, 0, None, None, None, 0, None, 0, 0,
                             None) == rb._lib.RTB_E_INVALID
+    assert L.rtb_matmul_bias_norm_act(None, 2, 2, 2, None, 2, 0, None, 2, 0, None, None, None,
+                                      1e-5, 0, None, 2, 0, None) == rb._lib.RTB_E_INVALID
+    assert L.rtb_layer_norm(None, 2, 2, None, 2, None, None, 1e-5, 0, None, 2,
+                            None) == rb._lib.RTB_E_INVALID
+    assert "rtb_ctx" in rb._lib.last_error()
 
 
 def test_init_without_gpu_fails_cleanly(rb):
