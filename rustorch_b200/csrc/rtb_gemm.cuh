@@ -796,16 +796,18 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
             tc_fence_before();
             mbar_arrive(&tempty_bar[b]);  // partial buffer b may be overwritten now
           }
-          if (SPLIT) {
+          if (SPLIT && units > 1) {
             // running sum; after the last unit the finished tile, which leaves
             // from there so the accumulator is not held during the stores
             tmem_st_32x32b_x32(t_run + (uint32_t)c, r);
           } else {
+            // a tile (or piece) of one unit leaves straight from the partial
+            // (short-K tiles: no running-sum round trip through TMEM)
             out(c, r);
           }
         }
-        if (SPLIT) tmem_st_wait();
-        if (SPLIT && last) {
+        if (SPLIT && units > 1) tmem_st_wait();
+        if (SPLIT && units > 1 && last) {
 #pragma unroll 1
           for (int c = 0; c < BN; c += 32) {
             uint32_t r[32];
