@@ -2,10 +2,16 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
 
-Workloads (default: conv):
+Workloads (default: resnet18):
+  resnet18  ResNet-18 forward (BatchNorm folded), B=256 images per GPU, x ~ N(0,1), seed 3.
+            Batch-sharded at N>1 (no collective).  The line also carries `gemm`: the
+            device-timed f32 matmul 1024^3 (replicas) and 8192^3 (N-split at N>1).
   conv      Conv2d+bias+ReLU, ResNet-50 stage-2 3x3 layer: x [32,128,28,28] ~ N(0,1),
             w [128,128,3,3] Kaiming-normal, b ~ U(-0.1,0.1), stride 1, pad 1, seed 1.
             One step = one reference-facing conv call (NCHW in/out).  Replicas at N>1.
+  conv_r50s1, conv_r50s3, conv_r50s4
+            the same call on ResNet-50's other 3x3 layers at batch 32: 64 channels at
+            56x56, 256 at 14x14, 512 at 7x7 (seed 1 + stage).
   gemm1024  f32 matmul 1024^3, A, B ~ N(0,1), seed 0.  Replicas at N>1.
   gemm2048, gemm4096, gemm8192, gemm16384
             square f32 matmul sweep, seed 4.  2048/4096 replicas at N>1;
@@ -54,6 +60,13 @@ TRAFFIC = {
     "gemm8192": (3.485e9, "profiles/sgemm_8192_3xtf32.md"),
     "gemm_m16": (273.3e6, "profiles/sgemm_small_m16_8192.md"),
     "linear_norm": (154.7e6, "profiles/linear_norm_relu_8192x1024x4096.md"),
+}
+# Tensor-pipe activity of each workload's dominant kernel(s) as ncu counts it
+# (sm__pipe_tensor_cycles_active, % of elapsed cycles), from the named capture.
+TENSOR_PIPE = {
+    "conv": (0.340, "profiles/conv2d_bias_relu_r50s2_3x3.md"),
+    "gemm8192": (0.575, "profiles/sgemm_8192_3xtf32.md"),
+    "linear_norm": (0.564, "profiles/linear_norm_relu_8192x1024x4096.md"),
 }
 # DRAM bytes per launch of a workload's second kernel (roofline.secondary)
 TRAFFIC_SECONDARY = {
@@ -218,17 +231,36 @@ def _pinned_empty(rb, ctx, nbytes):
 
 
 # ------------------------------------------------------------------ workloads
+# ResNet-50's 3x3 layers at batch 32: stage -> (channels, image side).  Stage 2
+# is the conv workload (seed 1); the other stages draw their inputs with seed
+# 1 + stage, as their GPU parity tests do.
+R50_STAGES = {1: (64, 56), 2: (128, 28), 3: (256, 14), 4: (512, 7)}
+
+
+def _r50_seed(stage):
+    return 1 if stage == 2 else 1 + stage
+
+
 class ConvWorkload:
     name = "conv2d_bias_relu_resnet50_3x3"
 
-    def __init__(self, rb, torch, dev):
-        self.rb, self.torch, self.dev = rb, torch, dev
-        self.N, self.C, self.H, self.W, self.Co = 32, 128, 28, 28, 128
-        n = self.N * self.C * self.H * self.W
+    def _shape(self, stage):
+        c, hw = R50_STAGES[stage]
+        self.stage = stage
+        self.seed = _r50_seed(stage)
+        self.N, self.C, self.H, self.W, self.Co = 32, c, hw, hw, c
         self.flops = 2.0 * self.N * self.H * self.W * self.Co * self.C * 9
-        x = rb.fill_normal((self.N, self.C, self.H, self.W), 1, 0)
-        w = rb.fill_normal((self.Co, self.C, 3, 3), 1, 1, 0.0, math.sqrt(2.0 / (self.C * 9)))
-        b = rb.fill_uniform((self.Co,), 1, 2, -0.1, 0.1)
+        if stage != 2:
+            self.name = f"conv2d_bias_relu_resnet50_s{stage}_3x3"
+
+    def __init__(self, rb, torch, dev, stage=2):
+        self.rb, self.torch, self.dev = rb, torch, dev
+        self._shape(stage)
+        n = self.N * self.C * self.H * self.W
+        x = rb.fill_normal((self.N, self.C, self.H, self.W), self.seed, 0)
+        w = rb.fill_normal((self.Co, self.C, 3, 3), self.seed, 1, 0.0,
+                           math.sqrt(2.0 / (self.C * 9)))
+        b = rb.fill_uniform((self.Co,), self.seed, 2, -0.1, 0.1)
         self.host = {"x": x, "w": w, "b": b}
         bytes_per_set = 2 * n * 4
         self.nsets = max(2, int(math.ceil(2 * L2_BYTES / bytes_per_set)))
@@ -238,9 +270,10 @@ class ConvWorkload:
         self.w = torch.from_numpy(w).to(dev)
         self.b = torch.from_numpy(b).to(dev)
         self.i = 0
-        self.config = {"workload": "conv2d+bias+relu ResNet-50 stage-2 3x3",
-                       "input": [32, 128, 28, 28], "weight": [128, 128, 3, 3], "stride": 1,
-                       "pad": 1, "seed": 1, "layout": "NCHW in/out",
+        self.config = {"workload": f"conv2d+bias+relu ResNet-50 stage-{stage} 3x3",
+                       "input": [32, self.C, self.H, self.W],
+                       "weight": [self.Co, self.C, 3, 3], "stride": 1,
+                       "pad": 1, "seed": self.seed, "layout": "NCHW in/out",
                        "l2": f"rotating {self.nsets} input/output sets "
                              f"({self.nsets * bytes_per_set / 2**20:.0f} MiB > 126 MiB L2)"}
         self.launches_per_step = 2  # NCHW->NHWC + weight prepack (one launch), implicit-GEMM conv
@@ -332,9 +365,9 @@ class ConvWorkload:
     # CPU baseline: the reference's own CPU path (oracle restatement) on a sample
     def cpu_sample(self, threads):
         from oracle import oracle as orc
-        x = orc.normal((self.N, self.C, self.H, self.W), 1, 0)
-        w = orc.normal((self.Co, self.C, 3, 3), 1, 1, 0.0, math.sqrt(2.0 / (self.C * 9)))
-        b = orc.uniform((self.Co,), 1, 2, -0.1, 0.1)
+        x = orc.normal((self.N, self.C, self.H, self.W), self.seed, 0)
+        w = orc.normal((self.Co, self.C, 3, 3), self.seed, 1, 0.0, math.sqrt(2.0 / (self.C * 9)))
+        b = orc.uniform((self.Co,), self.seed, 2, -0.1, 0.1)
         nimg = 2
         xs = x[:nimg].copy()
         orc.conv2d_bias_relu(xs[:1], w, b, (1, 1), (1, 1), threads=threads)  # warm
@@ -679,6 +712,16 @@ class ResNet18Workload:
                        "l2": "inputs larger than L2 (154 MB per batch)"}
         self.launches_per_step = 24  # stem prologue, 20 convs, max pool, avg pool, fc
         self.unit = "img/s"
+        self.gemm_extras = True
+        self.kernel_desc = ("the whole forward timed alone: 20 implicit-GEMM conv launches, "
+                            "the fc GEMM, the stem prologue and the two pools")
+
+    def release(self):
+        """Free the model and its buffers before the GEMM sub-benchmarks run."""
+        if self.h:
+            self.rb.call("rtb_resnet18_destroy", self.h)
+            self.h = None
+        self.x = self.logits = None
 
     def _fwd(self, x):
         stream = ctypes.c_void_p(self.torch.cuda.current_stream(self.dev).cuda_stream)
@@ -998,6 +1041,9 @@ def linear_norm_cpu_sample(M, K, N, threads, rows=64):
 
 WORKLOADS = {
     "conv": lambda rb, torch, dev: ConvWorkload(rb, torch, dev),
+    "conv_r50s1": lambda rb, torch, dev: ConvWorkload(rb, torch, dev, 1),
+    "conv_r50s3": lambda rb, torch, dev: ConvWorkload(rb, torch, dev, 3),
+    "conv_r50s4": lambda rb, torch, dev: ConvWorkload(rb, torch, dev, 4),
     "conv_bwd": lambda rb, torch, dev: ConvBwdWorkload(rb, torch, dev),
     "resnet18": lambda rb, torch, dev: ResNet18Workload(rb, torch, dev),
     "mlp": lambda rb, torch, dev: MlpWorkload(rb, torch, dev),
@@ -1065,6 +1111,30 @@ def _time_steps(torch, fn, steps, warmup, dev, dist=None, min_warm_s=0.3, pipe=N
     return ms
 
 
+def _gemm_extras(rb, torch, dev, args, dist, world, roof_peak):
+    """The GEMM half of the headline metric beside the ResNet-18 line: f32
+    matmul 1024^3 (replicas) and 8192^3 (N-split across the ranks at N>1),
+    A, B ~ N(0,1), device-timed like the main workload (CUDA events between
+    barrier + synchronize, max over ranks, operands rotated past L2)."""
+    out = {}
+    for name in ("gemm1024", "gemm8192"):
+        wl = WORKLOADS[name](rb, torch, dev)
+        ms = _time_steps(torch, wl.step, args.steps, args.warmup, dev, dist)
+        jobs = 1 if wl.scaling == "strong" else world
+        v = jobs * wl.flops * args.steps / (ms / 1e3) / 1e12
+        out[name] = {"value": round(v, 3), "unit": "TFLOP/s", "ms_per_step": round(ms / args.steps, 5),
+                     "scaling": wl.scaling,
+                     "parallelism": wl.config.get("parallelism_detail", f"replicas x{world}"),
+                     "frac_of_roof": round(v / (world * roof_peak), 4),
+                     "l2": wl.config["l2"]}
+        if hasattr(wl, "close"):
+            wl.close()
+        del wl
+        torch.cuda.synchronize(dev)
+        torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args):
     import torch
     import rustorch_b200 as rb
@@ -1125,8 +1195,14 @@ def run_ours(args):
                     "traffic_source": TRAFFIC.get(args.workload, (None, None))[1],
                     "peak_basis": f"{peaks['basis']} bf16 {peaks['bf16_tflops']} TFLOP/s "
                                   f"/ 2 (TF32 rate) / {MMAS_PER_MAC[0]} (MMAs per MAC)",
-                    "tensor_pipe_frac": round(MMAS_PER_MAC[0] * k_tflops / tf32_peak, 4),
+                    "tensor_pipe_frac": TENSOR_PIPE.get(args.workload, (None,))[0],
+                    "tensor_pipe_source": TENSOR_PIPE.get(args.workload, (None, None))[1],
+                    "tensor_pipe_basis": "ncu sm__pipe_tensor_cycles_active, fraction of "
+                                         "elapsed cycles, from the named capture",
+                    "mma_rate_implied": round(MMAS_PER_MAC[0] * k_tflops / tf32_peak, 4),
                     "kernel_ms": round(kms / args.steps, 5)}
+        if hasattr(wl, "kernel_desc"):
+            roofline["kernel"] = wl.kernel_desc
 
     if hasattr(wl, "secondary_step"):
         # the second launch of a two-kernel step (HBM-bound), timed alone
@@ -1151,6 +1227,11 @@ def run_ours(args):
     err = rb.get_context(local).device_error()
     if err:
         raise RuntimeError(f"device error word set: {err}")
+
+    gemm_extra = None
+    if getattr(wl, "gemm_extras", False) and not args.no_gemm_extras:
+        wl.release()
+        gemm_extra = _gemm_extras(rb, torch, dev, args, dist, world, roof_peak)
 
     if rank == 0:
         cpu_val, sample = wl.cpu_sample(os.cpu_count())
@@ -1181,6 +1262,8 @@ def run_ours(args):
             "gpu_launches": wl.launches_per_step * args.steps,
             "clocks": clk.summary(),
         }
+        if gemm_extra is not None:
+            line["gemm"] = gemm_extra
         print(json.dumps(line), flush=True)
     if hasattr(wl, "close"):
         wl.close()
@@ -1197,12 +1280,13 @@ def run_reference(args):
         return
     threads = os.cpu_count()
     # Workload descriptions only (no GPU): cpu_sample needs the sizes.
-    if args.workload == "conv":
+    if args.workload == "conv" or args.workload.startswith("conv_r50s"):
+        stage = 2 if args.workload == "conv" else int(args.workload[-1])
         wl = ConvWorkload.__new__(ConvWorkload)
-        wl.N, wl.C, wl.H, wl.W, wl.Co = 32, 128, 28, 28, 128
-        wl.flops = 2.0 * wl.N * wl.H * wl.W * wl.Co * wl.C * 9
-        cfg = {"workload": "conv2d+bias+relu ResNet-50 stage-2 3x3", "input": [32, 128, 28, 28],
-               "weight": [128, 128, 3, 3], "stride": 1, "pad": 1, "seed": 1}
+        wl._shape(stage)
+        cfg = {"workload": f"conv2d+bias+relu ResNet-50 stage-{stage} 3x3",
+               "input": [32, wl.C, wl.H, wl.W], "weight": [wl.Co, wl.C, 3, 3], "stride": 1,
+               "pad": 1, "seed": wl.seed}
         unit = "TFLOP/s"
     elif args.workload == "conv_bwd":
         wl = ConvBwdWorkload.__new__(ConvBwdWorkload)
@@ -1215,7 +1299,8 @@ def run_reference(args):
     elif args.workload == "resnet18":
         wl = ResNet18Workload.__new__(ResNet18Workload)
         wl.B = 256
-        cfg = {"workload": "ResNet-18 forward (BN folded), fp32", "batch_per_gpu": 256, "seed": 3}
+        cfg = {"workload": "ResNet-18 forward (BN folded), fp32", "batch_per_gpu": 256,
+               "input": [256, 3, 224, 224], "seed": 3, "flops_per_image": 3628146688}
         unit = "img/s"
     elif args.workload == "mlp":
         wl = MlpWorkload.__new__(MlpWorkload)
@@ -1266,7 +1351,9 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="conv", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="resnet18", choices=sorted(WORKLOADS))
+    ap.add_argument("--no-gemm-extras", action="store_true",
+                    help="resnet18: leave out the f32 matmul 1024^3 / 8192^3 sub-object")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--precision", default="3xtf32", choices=["3xtf32", "tf32"])
     args = ap.parse_args()

@@ -47,9 +47,10 @@ enum {
   RTB_E_NCCL = 6         /* NCCL error */
 };
 
-/* backend::Activation (rustorch-core/src/backend/mod.rs:1-7).  The GEMM and
- * conv epilogues fuse NONE and RELU (SIGMOID/TANH return RTB_E_UNSUPPORTED
- * there); rtb_matmul_bias_norm_act takes all four. */
+/* backend::Activation (rustorch-core/src/backend/mod.rs:1-7).  Every entry
+ * point that takes `act` applies all four in its epilogue, after the bias and
+ * residual: RELU = max(x, 0) (NaN -> 0), SIGMOID = 1/(1+exp(-x)), TANH
+ * (matmul_fused's staged activation, rustorch-core/src/ops.rs:1703-1708). */
 enum { RTB_ACT_NONE = 0, RTB_ACT_RELU = 1, RTB_ACT_SIGMOID = 2, RTB_ACT_TANH = 3 };
 
 /* Contraction precision.  3xTF32 (default) splits every fp32 operand into a
@@ -107,6 +108,13 @@ int rtb_memset_zero(rtb_ctx* ctx, void* dst, size_t bytes, void* stream);
 /* ---------------------------------------------------------------- streams */
 /* The context's own non-blocking stream (created by rtb_init). */
 int rtb_context_stream(rtb_ctx* ctx, void** stream);
+/* Streams for the calls below.  The library keeps a small block of
+ * split-tile arrival counters per stream it launches on (the launches of one
+ * stream run in order and share it; cudaStreamPerThread and captured launches
+ * get counters of their own).  rtb_stream_destroy releases the block in the
+ * stream's order.  A stream made elsewhere keeps its block until rtb_destroy:
+ * synchronise such a stream before destroying it if its handle may be reused
+ * for a new stream. */
 int rtb_stream_create(rtb_ctx* ctx, void** stream);
 int rtb_stream_destroy(rtb_ctx* ctx, void* stream);
 /* Synchronise `stream`, then report a device-side timeout if one occurred. */
@@ -117,7 +125,7 @@ int rtb_stream_synchronize(rtb_ctx* ctx, void* stream);
  *   transA = 0: A is [M,K] row-major (lda >= K); 1: A is [K,M] row-major.
  *   transB = 0: B is [K,N] row-major (Tensor::matmul's rhs, ldb >= N);
  *            1: B is [N,K] row-major (nn::Linear's weight, ldb >= K).
- *   bias: [N] or NULL.  act: RTB_ACT_NONE | RTB_ACT_RELU.
+ *   bias: [N] or NULL.  act: any RTB_ACT_*.
  * Replaces ops::matmul (rustorch-core/src/ops.rs:1888-2066) and
  * ops::matmul_fused (ops.rs:1543-1710); M=N=K=0 edge cases follow the
  * reference (K=0 gives bias or zeros). */
@@ -164,7 +172,7 @@ int rtb_layer_norm(rtb_ctx* ctx, int64_t rows, int64_t d, const float* x, int64_
  *   bias: [Co] or NULL; residual: same shape/layout as y, or NULL.
  *   y: [N,Co,Ho,Wo] or [N,Ho,Wo,Co] per y_layout; Ho = (H+2ph-kh)/sh+1.
  * Implicit GEMM (M = N*Ho*Wo, N = Co, K = kh*kw*Ci) on the tensor cores with
- * the bias/residual/ReLU epilogue fused.  Replaces ops::conv2d
+ * the bias/residual/activation epilogue fused.  Replaces ops::conv2d
  * (rustorch-core/src/ops/conv.rs:738-919) + nn::Conv2d's bias add
  * (rustorch-nn/src/conv.rs:52-63) + the JIT's Conv2dRelu lowering
  * (rustorch-core/src/jit.rs:254-262). */

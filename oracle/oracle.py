@@ -185,8 +185,10 @@ def matmul_fused(a, b, bias=None, act: int = 0, threads: int = 0) -> np.ndarray:
         lib().orc_add_bias_rows(_ptr(c), _ptr(bias_keep), c.shape[0], c.shape[1])
     if act == 1:
         lib().orc_relu(_ptr(c), c.size)
+    elif act in (2, 3):  # ops/activations.rs:47-50 (sigmoid), :213 (tanh)
+        lib().orc_activation(_ptr(c), c.size, act)
     else:
-        raise NotImplementedError("only None/ReLU activations are on the contraction path")
+        raise ValueError(f"unknown activation {act}")
     return c
 
 

@@ -150,23 +150,39 @@ int split_counters(rtb_ctx* ctx, cudaStream_t s, unsigned long long** d, unsigne
     clear_stale_cuda_error();
     return RTB_E_UNSUPPORTED;
   }
+  // cudaStreamPerThread is one handle for a different stream in every host
+  // thread: launches under it from two threads may run at the same time, so
+  // they cannot share a block either; they get per-launch counters too.
+  if (s == cudaStreamPerThread) return RTB_E_UNSUPPORTED;
   std::lock_guard<std::mutex> lk(ctx->cnt_mu);
   auto& c = ctx->split_cnt[s];
   if (!c.d) {
     // zeroed once (generation 0 is never issued); later launches on this
-    // stream tag their arrivals with increasing generations
-    cudaError_t e = cudaMalloc(&c.d, kSplitCounters * sizeof(unsigned long long));
+    // stream tag their arrivals with increasing generations.  Stream-ordered,
+    // so rtb_stream_destroy can release it behind the stream's last launch.
+    cudaError_t e = cudaMallocAsync(&c.d, kSplitCounters * sizeof(unsigned long long), s);
     if (e == cudaSuccess)
       e = cudaMemsetAsync(c.d, 0, kSplitCounters * sizeof(unsigned long long), s);
     if (e != cudaSuccess) {
-      if (c.d) cudaFree(c.d);
-      c.d = nullptr;
+      if (c.d) cudaFreeAsync(c.d, s);
+      ctx->split_cnt.erase(s);
       return cuda_status(e, "split counters");
     }
   }
   *d = c.d;
   *gen = ++c.gen;
   return RTB_OK;
+}
+
+// Drops the counter block of a stream that is about to be destroyed: freed in
+// the stream's order (after its last launch), so a later stream that reuses
+// the handle starts with a fresh block.
+static void release_split_counters(rtb_ctx* ctx, cudaStream_t s) {
+  std::lock_guard<std::mutex> lk(ctx->cnt_mu);
+  auto it = ctx->split_cnt.find(s);
+  if (it == ctx->split_cnt.end()) return;
+  if (it->second.d) cudaFreeAsync(it->second.d, s);
+  ctx->split_cnt.erase(it);
 }
 
 }  // namespace rtb
@@ -244,8 +260,10 @@ int rtb_destroy(rtb_ctx* ctx) {
   DeviceGuard g(ctx->device);
   cudaStreamSynchronize(ctx->stream);
   cudaDeviceSynchronize();  // launches on other streams may still use the counter blocks
-  for (auto& kv : ctx->split_cnt)
-    if (kv.second.d) cudaFree(kv.second.d);
+  for (auto& kv : ctx->split_cnt)  // stream-ordered blocks: freed on the context's stream
+    if (kv.second.d) cudaFreeAsync(kv.second.d, ctx->stream);
+  ctx->split_cnt.clear();
+  cudaStreamSynchronize(ctx->stream);
   cudaFree(ctx->d_err);
   cudaStreamDestroy(ctx->stream);
   delete ctx;
@@ -412,6 +430,7 @@ int rtb_stream_destroy(rtb_ctx* ctx, void* stream) {
   RTB_CHECK_CTX(ctx);
   if (!stream) return RTB_OK;
   DeviceGuard g(ctx->device);
+  release_split_counters(ctx, static_cast<cudaStream_t>(stream));
   cudaError_t e = cudaStreamDestroy(static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_status(e, "rtb_stream_destroy");
   return RTB_OK;
@@ -443,12 +462,12 @@ static int resolve_precision(rtb_ctx* ctx, int precision, int* split3) {
   return RTB_OK;
 }
 
-static int check_act(int act, int* relu) {
-  if (act == RTB_ACT_NONE) { *relu = 0; return RTB_OK; }
-  if (act == RTB_ACT_RELU) { *relu = 1; return RTB_OK; }
-  if (act == RTB_ACT_SIGMOID || act == RTB_ACT_TANH)
-    return set_error(RTB_E_UNSUPPORTED, "only None/ReLU activations are fused on this path");
-  return set_error(RTB_E_INVALID, "unknown activation");
+// The reference's Activation enum (rustorch-core/src/backend/mod.rs:1-7):
+// None, ReLU, Sigmoid and Tanh are all applied in the contraction's epilogue.
+static int check_act(int act) {
+  if (act < RTB_ACT_NONE || act > RTB_ACT_TANH)
+    return set_error(RTB_E_INVALID, "unknown activation");
+  return RTB_OK;
 }
 
 // One 2-D GEMM on the current device/stream (helper for single and batched).
@@ -456,18 +475,18 @@ static int check_act(int act, int* relu) {
 // residual == C accumulates into C.
 static int sgemm_one(rtb_ctx* ctx, int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
                      int transA, const float* B, int64_t ldb, int transB, const float* bias,
-                     int relu, float* C, int64_t ldc, int split3, cudaStream_t s,
+                     int act, float* C, int64_t ldc, int split3, cudaStream_t s,
                      const float* residual = nullptr) {
   if (M == 0 || N == 0) return RTB_OK;
   if (K == 0) {
-    if (residual == C && !bias && !relu) return RTB_OK;  // C += 0
+    if (residual == C && !bias && act == RTB_ACT_NONE) return RTB_OK;  // C += 0
     if (residual) return set_error(RTB_E_UNSUPPORTED, "K == 0 with a residual");
-    return launch_fill_rows(C, M, N, ldc, bias, relu, s);
+    return launch_fill_rows(C, M, N, ldc, bias, act, s);
   }
 
   GemmDesc d;
   d.M = M; d.N = N; d.K = K;
-  d.C = C; d.ldc = ldc; d.bias = bias; d.relu = relu; d.split3 = split3;
+  d.C = C; d.ldc = ldc; d.bias = bias; d.act = act; d.split3 = split3;
   d.residual = residual; d.ldr = ldc;
   float* wsA = nullptr;
   float* wsB = nullptr;
@@ -534,11 +553,11 @@ int rtb_sgemm(rtb_ctx* ctx, int64_t M, int64_t N, int64_t K, const float* A, int
   RTB_CHECK_CTX(ctx);
   int st = check_gemm_args(M, N, K, A, lda, transA, B, ldb, transB, C, ldc);
   if (st) return st;
-  int relu = 0, split3 = 1;
-  if ((st = check_act(act, &relu))) return st;
+  int split3 = 1;
+  if ((st = check_act(act))) return st;
   if ((st = resolve_precision(ctx, precision, &split3))) return st;
   DeviceGuard g(ctx->device);
-  return sgemm_one(ctx, M, N, K, A, lda, transA, B, ldb, transB, bias, relu, C, ldc, split3,
+  return sgemm_one(ctx, M, N, K, A, lda, transA, B, ldb, transB, bias, act, C, ldc, split3,
                    pick_stream(ctx, stream));
 }
 
@@ -550,14 +569,14 @@ int rtb_sgemm_batched(rtb_ctx* ctx, int64_t batch, int64_t M, int64_t N, int64_t
   if (batch < 0) return set_error(RTB_E_INVALID, "negative batch");
   int st = check_gemm_args(M, N, K, A, lda, transA, B, ldb, transB, C, ldc);
   if (st) return st;
-  int relu = 0, split3 = 1;
-  if ((st = check_act(act, &relu))) return st;
+  int split3 = 1;
+  if ((st = check_act(act))) return st;
   if ((st = resolve_precision(ctx, precision, &split3))) return st;
   DeviceGuard g(ctx->device);
   cudaStream_t s = pick_stream(ctx, stream);
   for (int64_t b = 0; b < batch; ++b) {
     st = sgemm_one(ctx, M, N, K, A ? A + b * strideA : nullptr, lda, transA,
-                   B ? B + b * strideB : nullptr, ldb, transB, bias, relu, C + b * strideC, ldc,
+                   B ? B + b * strideB : nullptr, ldb, transB, bias, act, C + b * strideC, ldc,
                    split3, s);
     if (st) return st;
   }
@@ -644,7 +663,7 @@ static int conv_check(int64_t N, int64_t Ci, int64_t H, int64_t W, int64_t Co, i
 static int conv_core(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, int64_t Co,
                      int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw,
                      int64_t Ho, int64_t Wo, const float* x_nhwc, const float* wp,
-                     const float* bias, const float* residual, int relu, float* y, int y_layout,
+                     const float* bias, const float* residual, int act, float* y, int y_layout,
                      int split3, cudaStream_t s, bool allow_workspace = true) {
   const int64_t Cp = round_up(Ci, 4);
   const int64_t M = N * Ho * Wo;
@@ -654,7 +673,7 @@ static int conv_core(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, 
   GemmDesc d;
   d.M = M; d.N = Co; d.K = kh * kw * Cp;
   d.B = wp; d.ldb = d.K; d.b_mn_major = 0;
-  d.C = y; d.bias = bias; d.residual = residual; d.relu = relu;
+  d.C = y; d.bias = bias; d.residual = residual; d.act = act;
   if (y_layout == RTB_LAYOUT_NHWC) {
     d.out_mode = 0; d.ldc = Co; d.ldr = Co;
   } else {
@@ -698,12 +717,12 @@ static int conv_packed_impl(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int6
     return set_error(RTB_E_INVALID, "conv: packed input/weight must be 16-byte aligned");
   if (y_layout != RTB_LAYOUT_NCHW && y_layout != RTB_LAYOUT_NHWC)
     return set_error(RTB_E_INVALID, "conv: bad y_layout");
-  int relu = 0, split3 = 1;
-  if ((st = check_act(act, &relu))) return st;
+  int split3 = 1;
+  if ((st = check_act(act))) return st;
   if ((st = resolve_precision(ctx, precision, &split3))) return st;
   DeviceGuard g(ctx->device);
   return conv_core(ctx, N, Ci, H, W, Co, kh, kw, sh, sw, ph, pw, Ho, Wo, x_nhwc_padded, w_packed,
-                   bias, residual, relu, y, y_layout, split3, pick_stream(ctx, stream),
+                   bias, residual, act, y, y_layout, split3, pick_stream(ctx, stream),
                    allow_workspace);
 }
 
@@ -746,8 +765,8 @@ int rtb_conv2d_fwd(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, in
     return set_error(RTB_E_INVALID, "conv: bad x_layout");
   if (y_layout != RTB_LAYOUT_NCHW && y_layout != RTB_LAYOUT_NHWC)
     return set_error(RTB_E_INVALID, "conv: bad y_layout");
-  int relu = 0, split3 = 1;
-  if ((st = check_act(act, &relu))) return st;
+  int split3 = 1;
+  if ((st = check_act(act))) return st;
   if ((st = resolve_precision(ctx, precision, &split3))) return st;
   DeviceGuard g(ctx->device);
   cudaStream_t s = pick_stream(ctx, stream);
@@ -773,7 +792,7 @@ int rtb_conv2d_fwd(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, in
       st = launch_conv_prologue_s2d(x, N, Ci, H, W, ph, pw, Hs, Ws, xs, w, Co, kh, kw, ws, s);
     if (st == RTB_OK)
       st = conv_core(ctx, N, 16, Hs, Ws, Co, kh2, kw2, 1, 1, 0, 0, Ho, Wo, xs, ws, bias, residual,
-                     relu, y, y_layout, split3, s);
+                     act, y, y_layout, split3, s);
     ws_free(xs, s);
     ws_free(ws, s);
     return st;
@@ -798,7 +817,7 @@ int rtb_conv2d_fwd(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, in
   }
   if (st == RTB_OK)
     st = conv_core(ctx, N, Ci, H, W, Co, kh, kw, sh, sw, ph, pw, Ho, Wo, xin, ws, bias, residual,
-                   relu, y, y_layout, split3, s);
+                   act, y, y_layout, split3, s);
   ws_free(xs, s);
   ws_free(ws, s);
   return st;

@@ -4,6 +4,7 @@
 // count by the CUDA occupancy rules (256-thread blocks, grid-stride loops).
 #include <cfloat>
 
+#include "rtb_act.cuh"
 #include "rtb_internal.h"
 #include "rtb_ptx.cuh"
 
@@ -49,14 +50,12 @@ __global__ void pack_kmajor_kernel(const float* __restrict__ src, int64_t rows, 
 }
 
 __global__ void fill_rows_kernel(float* C, int64_t M, int64_t N, int64_t ldc,
-                                 const float* bias, int relu) {
+                                 const float* bias, int act) {
   const int64_t total = M * N;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t m = i / N, n = i - m * N;
-    float v = bias ? bias[n] : 0.0f;
-    if (relu) v = fmaxf(v, 0.0f);
-    C[m * ldc + n] = v;
+    C[m * ldc + n] = activate(bias ? bias[n] : 0.0f, act);
   }
 }
 
@@ -416,10 +415,10 @@ int launch_pack_kmajor(const float* src, int64_t rows, int64_t k, int64_t rs, in
   return launch_check("pack_kmajor");
 }
 
-int launch_fill_rows(float* C, int64_t M, int64_t N, int64_t ldc, const float* bias, int relu,
+int launch_fill_rows(float* C, int64_t M, int64_t N, int64_t ldc, const float* bias, int act,
                      cudaStream_t s) {
   clear_stale_cuda_error();
-  fill_rows_kernel<<<grid_for(M * N), kThreads, 0, s>>>(C, M, N, ldc, bias, relu);
+  fill_rows_kernel<<<grid_for(M * N), kThreads, 0, s>>>(C, M, N, ldc, bias, act);
   return launch_check("fill_rows");
 }
 

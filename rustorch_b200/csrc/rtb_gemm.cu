@@ -1,4 +1,5 @@
-// Instantiation and launch of the tcgen05 GEMM engine (rtb_gemm.cuh).
+// Tile selection, tensor maps, work units and launch of the tcgen05 GEMM
+// engine (rtb_gemm.cuh).
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -8,55 +9,23 @@
 
 namespace rtb {
 
-namespace {
-
-template <int BN, bool SPLIT, int A_MODE, int B_MN>
-int launch_variant(rtb_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB,
-                   const CUtensorMap& tmC, const GemmParams& p, cudaStream_t stream) {
-  using Cfg = GemmCfg<BN, SPLIT>;
-  using Roles = GemmRoles<SPLIT, A_MODE == 1>;
-  auto kern = rtb_gemm_kernel<BN, SPLIT, A_MODE, B_MN>;
-  // The attribute is per function and per device; setting it is idempotent
-  // and cheap, so it is set on every launch (covers multi-device processes).
-  cudaError_t e =
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
-  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemm smem)");
-  const int grid = p.num_units < ctx->sm_count ? p.num_units : ctx->sm_count;
-  // programmatic dependent launch: the kernel's setup (barriers, TMEM)
-  // overlaps the end of the previous kernel; it waits for that kernel before
-  // its first global-memory access (griddep_wait in the kernel)
-  clear_stale_cuda_error();
-  e = launch_pdl(kern, dim3((unsigned)grid), dim3(Roles::kThreads), Cfg::kSmemBytes, stream, tmA,
-                 tmB, tmC, p);
-  if (e != cudaSuccess) return cuda_status(e, "gemm kernel launch");
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_status(e, "gemm kernel launch");
-  return RTB_OK;
-}
-
-template <int BN, bool SPLIT>
-int launch_prec(rtb_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB,
-                const CUtensorMap& tmC, const GemmParams& p, const GemmDesc& d, cudaStream_t s) {
-  if (d.gather == 1) return launch_variant<BN, SPLIT, 1, 0>(ctx, tmA, tmB, tmC, p, s);
-  if (d.gather == 2) return launch_variant<BN, SPLIT, 2, 0>(ctx, tmA, tmB, tmC, p, s);
-  if (d.gather == 3) {
-    if constexpr (SPLIT) return launch_variant<BN, SPLIT, 3, 0>(ctx, tmA, tmB, tmC, p, s);
-    else return set_error(RTB_E_INVALID, "multi-tap im2col needs the 3xTF32 converters");
-  }
-  if (d.b_mn_major) return launch_variant<BN, SPLIT, 0, 1>(ctx, tmA, tmB, tmC, p, s);
-  return launch_variant<BN, SPLIT, 0, 0>(ctx, tmA, tmB, tmC, p, s);
-}
-
+// One instantiation per tile width, each in its own translation unit
+// (rtb_gemm_bn64.cu, rtb_gemm_bn128.cu, rtb_gemm_bn256.cu) so they compile in
+// parallel.
 template <int BN>
 int launch_bn(rtb_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB,
-              const CUtensorMap& tmC, const GemmParams& p, const GemmDesc& d, cudaStream_t s) {
-  if (!d.split3) return launch_prec<BN, false>(ctx, tmA, tmB, tmC, p, d, s);
-  if constexpr (BN <= 128) {
-    return launch_prec<BN, true>(ctx, tmA, tmB, tmC, p, d, s);
-  } else {
-    return set_error(RTB_E_INVALID, "3xTF32 tiles are at most 128 columns wide");
-  }
-}
+              const CUtensorMap& tmC, const GemmParams& p, const GemmDesc& d, cudaStream_t s);
+extern template int launch_bn<64>(rtb_ctx*, const CUtensorMap&, const CUtensorMap&,
+                                  const CUtensorMap&, const GemmParams&, const GemmDesc&,
+                                  cudaStream_t);
+extern template int launch_bn<128>(rtb_ctx*, const CUtensorMap&, const CUtensorMap&,
+                                   const CUtensorMap&, const GemmParams&, const GemmDesc&,
+                                   cudaStream_t);
+extern template int launch_bn<256>(rtb_ctx*, const CUtensorMap&, const CUtensorMap&,
+                                   const CUtensorMap&, const GemmParams&, const GemmDesc&,
+                                   cudaStream_t);
+
+namespace {
 
 int env_int(const char* name, int dflt) {
   const char* v = std::getenv(name);
@@ -88,13 +57,110 @@ int pick_bn(rtb_ctx* ctx, const GemmDesc& d) {
   return 64;
 }
 
+// Work-unit schedule of one launch: the first `full` tiles run whole, the
+// other tiles - full are cut along K into `sk` pieces (consecutive k-block
+// ranges) whose partial tiles are summed in piece order by the last to arrive.
+struct SplitPlan {
+  int64_t full = 0;
+  int sk = 1;
+  double cost = 0.0;  // estimated span in k-block times
+};
+
+// Cost model in k-block times: units are dealt round-robin to the G resident
+// CTAs (CTA c runs units c, c + G, ...), a whole tile costs its k-blocks plus
+// one for the pipeline fill and the epilogue tail, a piece its k-blocks plus
+// 8 (the partial tile's round trip through the workspace and the arrival
+// count: fitted to B200 timings of 1024^3, 2048^3 and ResNet convs with 2 to
+// 5 pieces per tile, where a piece cost 7.6 to 13 k-block times more than its
+// share of the mainloop) plus the share of its tile's fix-up (every partial
+// read back: 0.4 per piece when the partials are staged through the idle load
+// ring, which holds two chunks of up to 5 pieces; 1.5 per piece read straight
+// from L2 beyond that).
+double plan_cost(int64_t tiles, int64_t split, int sk, int num_kb, int64_t G) {
+  const int64_t full = tiles - split;
+  const int64_t units = full + split * sk;
+  const int64_t grid = units < G ? units : G;
+  const double c_tile = num_kb + 1.0;
+  const double c_piece = (double)((num_kb + sk - 1) / sk) + 8.0 + (sk <= 5 ? 0.4 : 1.5) * sk;
+  double worst = 0.0;
+  for (int64_t c = 0; c < grid; ++c) {
+    const int64_t n_full = full > c ? (full - c + grid - 1) / grid : 0;
+    // first unit index >= full that CTA c runs
+    int64_t first = c + n_full * grid;
+    const int64_t n_piece = first < units ? (units - 1 - first) / grid + 1 : 0;
+    const double t = n_full * c_tile + n_piece * c_piece;
+    worst = t > worst ? t : worst;
+  }
+  return worst;
+}
+
+// The cheapest schedule for `tiles` tiles of num_kb k-blocks on G CTAs: no
+// split, or the last `split` tiles (the partial last wave, plus whole waves
+// before it) cut into 2..16 pieces of >= 2 k-blocks (>= 4 beyond 8 pieces),
+// within the split-counter block and a 256 MiB partial-tile workspace.
+SplitPlan plan_split(int64_t tiles, int num_kb, int64_t G, int bn) {
+  SplitPlan best;
+  best.full = tiles;
+  best.cost = plan_cost(tiles, 0, 1, num_kb, G);
+  const double base = best.cost;
+  const int64_t rem = tiles % G;
+  if (rem == 0) return best;
+  // RTB_SPLIT_K: the last wave's tiles cut into exactly that many pieces
+  // (measurements)
+  static const int forced_sk = env_int("RTB_SPLIT_K", 0);
+  if (forced_sk >= 2 && forced_sk <= 16 && num_kb / forced_sk >= 2 && rem <= kSplitCounters) {
+    best.full = tiles - rem;
+    best.sk = forced_sk;
+    best.cost = plan_cost(tiles, rem, forced_sk, num_kb, G);
+    return best;
+  }
+  for (int64_t split = rem; split <= tiles && split <= kSplitCounters; split += G) {
+    for (int sk = 2; sk <= 16; ++sk) {
+      const int kbp = num_kb / sk;
+      if (kbp < 2 || (sk > 8 && kbp < 4)) break;
+      if ((double)split * sk * bn * kBM * 4.0 > 256.0 * (1 << 20)) break;
+      const double c = plan_cost(tiles, split, sk, num_kb, G);
+      if (c < best.cost && c < base - 0.5) {  // a split must beat no split by half a k-block
+        best.full = tiles - split;
+        best.sk = sk;
+        best.cost = c;
+      }
+    }
+  }
+  return best;
+}
+
 }  // namespace
 
 int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
   if (d.M <= 0 || d.N <= 0 || d.K <= 0) return set_error(RTB_E_INVALID, "gemm_run: empty problem");
   if (d.M > INT32_MAX || d.N > INT32_MAX || d.K > INT32_MAX)
     return set_error(RTB_E_UNSUPPORTED, "gemm_run: dimension exceeds 2^31-1");
-  const int bn = d.bn ? d.bn : pick_bn(ctx, d);
+  static const int tail_env = env_int("RTB_TAIL_SPLIT", 1);
+  const bool can_split = tail_env && d.allow_workspace;
+  const int64_t num_kb64 = (d.K + kBK - 1) / kBK;
+  const int64_t tiles_m64 = (d.M + kBM - 1) / kBM;
+  int bn = d.bn ? d.bn : pick_bn(ctx, d);
+  SplitPlan plan;
+  plan.full = tiles_m64 * ((d.N + bn - 1) / bn);
+  if (can_split && num_kb64 <= INT32_MAX) {
+    plan = plan_split(plan.full, (int)num_kb64, ctx->sm_count, bn);
+    // 3xTF32 with the tile width left open: 128 and 64 columns compared under
+    // their schedules, at the measured k-block times of the two modes (B200:
+    // 0.77 us per 128-column k-block, 0.67 us per 64-column one in the wide
+    // mode, which does half the work)
+    if (d.split3 && !d.bn && std::getenv("RTB_GEMM_BN") == nullptr && d.N > 64) {
+      const int alt = bn == 128 ? 64 : 128;
+      const int64_t tiles_alt = tiles_m64 * ((d.N + alt - 1) / alt);
+      const SplitPlan pa = plan_split(tiles_alt, (int)num_kb64, ctx->sm_count, alt);
+      const double t_cur = plan.cost * (bn == 128 ? 0.77 : 0.67);
+      const double t_alt = pa.cost * (alt == 128 ? 0.77 : 0.67);
+      if (t_alt < t_cur * 0.97) {
+        bn = alt;
+        plan = pa;
+      }
+    }
+  }
 
   CUtensorMap tmA, tmB;
   int st;
@@ -141,13 +207,20 @@ int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
   p.split_trunc = trunc_env != 0;
   p.tiles_m = (int)((d.M + kBM - 1) / kBM);
   p.tiles_n = (int)((d.N + bn - 1) / bn);
-  p.group_m = p.tiles_m < 16 ? p.tiles_m : 16;
+  // Raster: consecutive tiles walk down group_m M-tiles, then across N
+  // (RTB_GROUP_M overrides the band height for measurements).
+  // Measured on B200 (3xTF32, RTB_GROUP_M sweep): 8192^3 203.5 / 200.2 /
+  // 198.8 / 201.8 / 195.2 TFLOP/s and 16384^3 185.2 / 183.5 / 180.2 / 175.4 /
+  // 169.4 for bands of 4 / 8 / 16 / 32 / 64 M-tiles.
+  static const int gm_env = env_int("RTB_GROUP_M", 4);
+  const int gm = gm_env > 0 ? gm_env : 4;
+  p.group_m = p.tiles_m < gm ? p.tiles_m : gm;
   p.C = d.C;
   p.ldc = d.ldc;
   p.bias = d.bias;
   p.residual = d.residual;
   p.ldr = d.ldr;
-  p.relu = d.relu;
+  p.act = d.act;
   p.out_mode = d.out_mode;
   p.hw = d.hw;
   p.peer_c = d.peer_c;
@@ -183,11 +256,12 @@ int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
   p.err = ctx->d_err;
   p.timeout_ns = ctx->timeout_ns;
 
-  // Tail balancing: when the last wave of tiles would leave at least half of
-  // the SMs idle, its tiles are cut along K into split_k pieces that run on
-  // the otherwise idle SMs (e.g. 196 tiles on 148 SMs: 148 whole tiles, then
-  // 48 tiles x 3 pieces).  The pieces' partial tiles go through a stream-
-  // ordered workspace; RTB_TAIL_SPLIT=0 turns this off.
+  // K-split schedule (plan_split above): the last `rem` tiles (the partial
+  // last wave, or whole waves more when that balances better) are cut along K
+  // into split_k pieces, e.g. R50 stage-4 3x3 (52 tiles of 144 k-blocks on
+  // 148 SMs): 52 x 5 pieces instead of 52 whole tiles on 52 SMs.  The pieces'
+  // partial tiles go through a stream-ordered workspace; RTB_TAIL_SPLIT=0
+  // turns splitting off.
   const int64_t tiles = (int64_t)p.tiles_m * p.tiles_n;
   if (tiles > INT32_MAX / 8) return set_error(RTB_E_UNSUPPORTED, "gemm_run: too many tiles");
   p.full_units = (int)tiles;
@@ -197,41 +271,29 @@ int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
   p.ws_cnt = nullptr;
   p.cnt_gen = 0;
   void* split_ws = nullptr;
-  static const int tail_env = env_int("RTB_TAIL_SPLIT", 1);
-  if (tail_env && d.allow_workspace) {
-    const int64_t G = ctx->sm_count;
-    const int64_t rem = tiles % G;
-    if (rem > 0 && rem * 2 <= G) {
-      // up to 16 pieces (a few tiles with a very long K, e.g. a conv's weight
-      // gradient: 9 tiles x 784 k-blocks), each piece >= 4 k-blocks once the
-      // split passes 8 (the last piece's fix-up reads every piece)
-      int sk = (int)(G / rem);
-      if (sk > 16) sk = 16;
-      if (sk > 8 && sk > p.num_kb / 4) sk = p.num_kb / 4 > 8 ? p.num_kb / 4 : 8;
-      if (sk > p.num_kb / 2) sk = p.num_kb / 2;  // every piece keeps >= 2 k-blocks
-      if (sk >= 2 && rem <= kSplitCounters) {
-        const size_t part_bytes = (size_t)rem * sk * bn * kBM * sizeof(float);
-        const size_t cnt_off = (part_bytes + 255) & ~size_t(255);
-        st = split_counters(ctx, stream, &p.ws_cnt, &p.cnt_gen);
-        const bool own = (st == RTB_E_UNSUPPORTED);  // capturing: counters of this launch
-        if (st != RTB_OK && !own) return st;
-        st = ws_alloc(ctx, &split_ws, own ? cnt_off + (size_t)rem * 8 : part_bytes, stream);
-        if (st != RTB_OK) return st;
-        if (own) {
-          p.ws_cnt = reinterpret_cast<unsigned long long*>(static_cast<char*>(split_ws) + cnt_off);
-          p.cnt_gen = 1;
-          cudaError_t e = cudaMemsetAsync(p.ws_cnt, 0, (size_t)rem * 8, stream);
-          if (e != cudaSuccess) {
-            ws_free(split_ws, stream);
-            return cuda_status(e, "split counters memset");
-          }
-        }
-        p.full_units = (int)(tiles - rem);
-        p.split_k = sk;
-        p.num_units = (int)(tiles - rem + rem * sk);
-        p.ws = static_cast<float*>(split_ws);
+  if (plan.sk > 1 && plan.full < tiles) {
+    const int64_t rem = tiles - plan.full;
+    const int sk = plan.sk;
+    const size_t part_bytes = (size_t)rem * sk * bn * kBM * sizeof(float);
+    const size_t cnt_off = (part_bytes + 255) & ~size_t(255);
+    st = split_counters(ctx, stream, &p.ws_cnt, &p.cnt_gen);
+    const bool own = (st == RTB_E_UNSUPPORTED);  // capture / per-thread stream: own counters
+    if (st != RTB_OK && !own) return st;
+    st = ws_alloc(ctx, &split_ws, own ? cnt_off + (size_t)rem * 8 : part_bytes, stream);
+    if (st != RTB_OK) return st;
+    if (own) {
+      p.ws_cnt = reinterpret_cast<unsigned long long*>(static_cast<char*>(split_ws) + cnt_off);
+      p.cnt_gen = 1;
+      cudaError_t e = cudaMemsetAsync(p.ws_cnt, 0, (size_t)rem * 8, stream);
+      if (e != cudaSuccess) {
+        ws_free(split_ws, stream);
+        return cuda_status(e, "split counters memset");
       }
     }
+    p.full_units = (int)(tiles - rem);
+    p.split_k = sk;
+    p.num_units = (int)(tiles - rem + rem * sk);
+    p.ws = static_cast<float*>(split_ws);
   }
   {
     const int64_t grid = p.num_units < ctx->sm_count ? p.num_units : ctx->sm_count;

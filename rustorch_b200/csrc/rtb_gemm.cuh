@@ -6,7 +6,7 @@
 // 128-byte swizzle atom).  Roles (warp index):
 //   0        TMA producer: A (unless gathered) and B tiles -> smem ring
 //   1        TMEM allocator + single-thread UMMA issuer (kind::tf32, M=128)
-//   2..5     epilogue: TMEM -> registers -> bias/residual/ReLU -> global
+//   2..5     epilogue: TMEM -> registers -> bias/residual/activation -> global
 //   6..9     (3xTF32 only) converters: split each fp32 tile in smem into a
 //            TF32 "hi" part (in place, round-to-nearest) and the exact fp32
 //            remainder "lo" (separate plane); UMMA then accumulates
@@ -37,6 +37,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include "rtb_act.cuh"
 #include "rtb_ptx.cuh"
 
 namespace rtb {
@@ -64,7 +65,7 @@ struct GemmParams {
   const float* bias;     // [N] or null
   const float* residual; // same indexing as C, or null
   int64_t ldr;
-  int relu;
+  int act;               // RTB_ACT_*: none, ReLU, sigmoid, tanh (after bias and residual)
   int out_mode;          // 0: C[m*ldc+n]; 1: NCHW scatter, m=(img,pix), C[(img*N+n)*hw+pix];
                          // 2: every rank's C, peer_c[r][m*ldc + col_off + n] (N-split)
   int hw;                // Ho*Wo for out_mode 1
@@ -256,10 +257,7 @@ __device__ __forceinline__ void epilogue_store32(const GemmParams& p, int m, int
         v[4 * j] += q[j].x; v[4 * j + 1] += q[j].y; v[4 * j + 2] += q[j].z; v[4 * j + 3] += q[j].w;
       }
     }
-    if (p.relu) {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.0f);
-    }
+    activate_n<32>(v, p.act);
 #pragma unroll
     for (int j = 0; j < 32; j += 4)
       *reinterpret_cast<float4*>(crow + n0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
@@ -269,15 +267,16 @@ __device__ __forceinline__ void epilogue_store32(const GemmParams& p, int m, int
       for (int j = 0; j < 32; ++j)
         if (n0 + j < p.N) v[j] += __ldg(rrow + n0 + j);
     }
+    activate_n<32>(v, p.act);
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
-      if (n0 + j < p.N) crow[n0 + j] = p.relu ? fmaxf(v[j], 0.0f) : v[j];
+      if (n0 + j < p.N) crow[n0 + j] = v[j];
     }
   }
 }
 
 // N-split epilogue, after epilogue_stage_rowmajor has put the 128 x 32 chunk
-// (bias/ReLU applied) into the 128B-swizzled staging buffer: thread et moves
+// (bias/activation applied) into the 128B-swizzled staging buffer: thread et moves
 // float4 f = et + 128*i (row f/8, column group f%8), so each warp store covers
 // four whole 128-byte rows of C, into every rank's C at column col_off + n0
 // (P2P stores over NVLink for the peers; whole-line writes, 16-byte aligned by
@@ -303,7 +302,7 @@ __device__ __forceinline__ void epilogue_store_peers(const GemmParams& p, uint32
   }
 }
 
-// Row-major epilogue via TMA store: bias, residual and ReLU in registers, then
+// Row-major epilogue via TMA store: bias, residual and activation in registers, then
 // this thread's row (32 fp32) into the 128 x 32 staging chunk, 128-byte
 // swizzled (16-byte unit j of row r at position j ^ (r % 8)) to match the
 // store map and keep the 8-thread phases of the writes conflict-free.
@@ -336,10 +335,7 @@ __device__ __forceinline__ void epilogue_stage_rowmajor(const GemmParams& p, uin
         if (n0 + j < p.N) v[j] += __ldg(rrow + n0 + j);
     }
   }
-  if (p.relu) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.0f);
-  }
+  activate_n<32>(v, p.act);
   const uint32_t rowp = buf + row * 128;
 #pragma unroll
   for (int j = 0; j < 8; ++j)
@@ -350,7 +346,7 @@ __device__ __forceinline__ void epilogue_stage_rowmajor(const GemmParams& p, uin
 // memory ([32 channels][128 pixels]), then each thread writes 4 consecutive
 // pixels of 8 channels with 16-byte stores (a warp covers 512 contiguous bytes
 // of one channel plane per store), adding bias and the NCHW residual and
-// applying ReLU there.  A thread keeps the same 4-pixel group (et % 32) for
+// applying the activation there.  A thread keeps the same 4-pixel group (et % 32) for
 // all of its channels, so the pixel -> (image, offset) division happens once
 // per chunk, and the 8 loads are issued before the 8 stores.
 __device__ __forceinline__ void epilogue_nchw_chunk(const GemmParams& p, uint32_t buf, int row,
@@ -387,13 +383,8 @@ __device__ __forceinline__ void epilogue_nchw_chunk(const GemmParams& p, uint32_
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const int ch = cw + 4 * (4 * h + k);
-          if (n0 + ch < p.N) {
-            float4 v = o[k];
-            if (p.relu) {
-              v.x = fmaxf(v.x, 0.f); v.y = fmaxf(v.y, 0.f); v.z = fmaxf(v.z, 0.f); v.w = fmaxf(v.w, 0.f);
-            }
-            *reinterpret_cast<float4*>(cbase + (int64_t)ch * p.hw) = v;
-          }
+          if (n0 + ch < p.N)
+            *reinterpret_cast<float4*>(cbase + (int64_t)ch * p.hw) = activate4(o[k], p.act);
         }
       }
     } else {
@@ -424,7 +415,7 @@ __device__ __forceinline__ void epilogue_nchw_chunk(const GemmParams& p, uint32_
         }
 #pragma unroll
         for (int e = 0; e < 4; ++e)
-          if (e < cnt) p.C[pb[e] + (int64_t)ch * p.hw] = p.relu ? fmaxf(sv[e], 0.f) : sv[e];
+          if (e < cnt) p.C[pb[e] + (int64_t)ch * p.hw] = activate(sv[e], p.act);
       }
     }
   }
@@ -465,6 +456,10 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* fix_flag = abort_flag + 1;  // epilogue: this CTA sums a split tile
   volatile int* epi_vote = abort_flag + 2;  // epilogue: per-warp wait outcome (4 ints)
+  // epilogue: split tiles this CTA sums after its last unit: [0] = count,
+  // then (tile, slot) pairs
+  volatile int* pend = abort_flag + 6;
+  constexpr int kMaxPending = 8;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -483,6 +478,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
       mbar_init(&aempty_bar[j], 1);
     }
     *abort_flag = 0;
+    pend[0] = 0;
     fence_mbar_init();
   }
   if (warp == Roles::kWarpTma && lane == 0) {
@@ -714,6 +710,123 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
         epilogue_store32(p, m, n0, r, sb);
       }
     };
+    // Split-tile fix-up: the sum of the tile's split_k partials (in piece
+    // order, so the result does not depend on arrival order) goes through the
+    // epilogue like a finished tile.
+    constexpr int kFixRoom = S * Cfg::kStageBytes;
+    const bool fix_room = 2 * p.split_k * kOutChunkBytes <= kFixRoom;
+    // Staged: each thread copies its own row of every piece by cp.async into
+    // the idle load ring (one L2 round trip per chunk, the next chunk in
+    // flight while this one is summed).  `restage_bias`: the tile is not the
+    // one whose bias is in sBias (a queued tile).
+    auto fix_staged = [&](int tile, int slot, bool restage_bias) {
+      int tm, tn;
+      tile_coords(tile, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
+      const int m = tm * kBM + row;
+      if (restage_bias && p.bias) {
+        named_bar_sync(1, 128);
+        for (int i = et; i < BN; i += 128) {
+          const int n = tn * BN + i;
+          sts32(smem_u32(sBias) + 4 * i, n < p.N ? __ldg(p.bias + n) : 0.0f);
+        }
+        named_bar_sync(1, 128);
+      }
+      __threadfence();
+      const float4* src0 =
+          reinterpret_cast<const float4*>(p.ws) + (size_t)slot * p.split_k * (size_t)(BN * kBM / 4);
+      const int SK = p.split_k;
+      const uint32_t fb = smem_u32(sA);
+      auto stage_chunk = [&](int ci) {  // chunk ci of every piece -> buffer ci & 1
+        const float4* s0 = src0 + (size_t)ci * 8 * kBM + row;
+        const uint32_t d0 = fb + (uint32_t)((ci & 1) * SK * kOutChunkBytes) + row * 16;
+#pragma unroll 1
+        for (int pc = 0; pc < SK; ++pc) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            cp_async_16_cg(d0 + (uint32_t)((pc * 8 + j) * kBM * 16),
+                           s0 + (size_t)pc * (BN * kBM / 4) + j * kBM);
+        }
+        cp_async_commit();
+      };
+      stage_chunk(0);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        const int ci = c / 32;
+        if (c + 32 < BN) {
+          stage_chunk(ci + 1);
+          cp_async_wait<1>();
+        } else {
+          cp_async_wait<0>();
+        }
+        const uint32_t d0 = fb + (uint32_t)((ci & 1) * SK * kOutChunkBytes) + row * 16;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 q = lds128(d0 + (uint32_t)(j * kBM * 16));
+          v[4 * j] = q.x; v[4 * j + 1] = q.y; v[4 * j + 2] = q.z; v[4 * j + 3] = q.w;
+        }
+#pragma unroll 1
+        for (int pc = 1; pc < SK; ++pc) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 q = lds128(d0 + (uint32_t)((pc * 8 + j) * kBM * 16));
+            v[4 * j] += q.x; v[4 * j + 1] += q.y; v[4 * j + 2] += q.z; v[4 * j + 3] += q.w;
+          }
+        }
+        uint32_t r[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(v[j]);
+        emit(tm, tn, c, m, r);
+      }
+    };
+    // Straight from L2 (the ring is busy, or too small for every piece): the
+    // next piece's loads are issued before the current one is added.
+    auto fix_direct = [&](int tile, int slot) {
+      int tm, tn;
+      tile_coords(tile, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
+      const int m = tm * kBM + row;
+      __threadfence();
+      const float4* src0 =
+          reinterpret_cast<const float4*>(p.ws) + (size_t)slot * p.split_k * (size_t)(BN * kBM / 4);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        const float4* s0 = src0 + (size_t)(c / 32) * 8 * kBM + row;
+        float v[32];
+        float4 q[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) q[j] = __ldcg(s0 + j * kBM);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          v[4 * j] = q[j].x; v[4 * j + 1] = q[j].y; v[4 * j + 2] = q[j].z; v[4 * j + 3] = q[j].w;
+        }
+        if (p.split_k > 1) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) q[j] = __ldcg(s0 + (size_t)(BN * kBM / 4) + j * kBM);
+        }
+#pragma unroll 1
+        for (int pc = 1; pc < p.split_k; ++pc) {
+          float4 nq[8];
+          if (pc + 1 < p.split_k) {
+            const float4* sp = s0 + (size_t)(pc + 1) * (BN * kBM / 4);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) nq[j] = __ldcg(sp + j * kBM);
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            v[4 * j] += q[j].x; v[4 * j + 1] += q[j].y; v[4 * j + 2] += q[j].z;
+            v[4 * j + 3] += q[j].w;
+          }
+          if (pc + 1 < p.split_k) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) q[j] = nq[j];
+          }
+        }
+        uint32_t r[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(v[j]);
+        emit(tm, tn, c, m, r);
+      }
+    };
     for (int w = blockIdx.x; w < p.num_units && ok; w += gridDim.x) {
       const WorkUnit u = work_unit(p, w);
       const int tj = (w - (int)blockIdx.x) / (int)gridDim.x;
@@ -818,7 +931,11 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
         }
       }
       if (ok && piece) {
-        // Publish this piece, count arrivals; the last piece sums all of them.
+        // Publish this piece, count arrivals; the last piece's CTA sums all of
+        // them: at once when this piece is its last work unit (the ring is
+        // idle: no more loads are issued and the MMAs that read it have
+        // completed) or when there is no room to stage; otherwise the tile is
+        // queued and summed after the CTA's last unit, through the idle ring.
         __threadfence();
         named_bar_sync(1, 128);
         if (et == 0) {
@@ -827,94 +944,33 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
             atomicCAS(p.err, 0, (int)DEV_BAD_CONFIG);
             *abort_flag = 1;
           }
-          *fix_flag = (arrived == p.split_k - 1);
+          int mode = 0;  // 0 nothing, 1 sum now (staged), 2 queued, 3 sum now (from L2)
+          if (arrived == p.split_k - 1) {
+            const bool ring_idle = w + (int)gridDim.x >= p.num_units;
+            if (!fix_room) mode = 3;
+            else if (ring_idle) mode = 1;
+            else if (pend[0] < kMaxPending) mode = 2;
+            else mode = 3;
+            if (mode == 2) {
+              const int q = pend[0];
+              pend[1 + 2 * q] = u.tile;
+              pend[2 + 2 * q] = u.slot;
+              pend[0] = q + 1;
+            }
+          }
+          *fix_flag = mode;
         }
         named_bar_sync(1, 128);
-        // The ring is idle here: a piece is always its CTA's last work unit
-        // (pieces only fill the last wave), and the MMAs that read the ring
-        // have completed.  With room for two chunks of every piece, each
-        // thread stages its own row of all pieces by cp.async (one L2 round
-        // trip per chunk, the next chunk in flight while this one is summed).
-        constexpr int kFixRoom = S * Cfg::kStageBytes;
-        if (*fix_flag && 2 * p.split_k * kOutChunkBytes <= kFixRoom) {
-          __threadfence();
-          const float4* src0 = reinterpret_cast<const float4*>(p.ws) +
-                               (size_t)u.slot * p.split_k * (size_t)(BN * kBM / 4);
-          const int SK = p.split_k;
-          const uint32_t fb = smem_u32(sA);
-          auto stage_chunk = [&](int ci) {  // chunk ci of every piece -> buffer ci & 1
-            const float4* s0 = src0 + (size_t)ci * 8 * kBM + row;
-            const uint32_t d0 = fb + (uint32_t)((ci & 1) * SK * kOutChunkBytes) + row * 16;
-#pragma unroll 1
-            for (int pc = 0; pc < SK; ++pc) {
-#pragma unroll
-              for (int j = 0; j < 8; ++j)
-                cp_async_16_cg(d0 + (uint32_t)((pc * 8 + j) * kBM * 16),
-                               s0 + (size_t)pc * (BN * kBM / 4) + j * kBM);
-            }
-            cp_async_commit();
-          };
-          stage_chunk(0);
-#pragma unroll 1
-          for (int c = 0; c < BN; c += 32) {
-            const int ci = c / 32;
-            if (c + 32 < BN) {
-              stage_chunk(ci + 1);
-              cp_async_wait<1>();
-            } else {
-              cp_async_wait<0>();
-            }
-            const uint32_t d0 = fb + (uint32_t)((ci & 1) * SK * kOutChunkBytes) + row * 16;
-            float v[32];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const float4 q = lds128(d0 + (uint32_t)(j * kBM * 16));
-              v[4 * j] = q.x; v[4 * j + 1] = q.y; v[4 * j + 2] = q.z; v[4 * j + 3] = q.w;
-            }
-#pragma unroll 1
-            for (int pc = 1; pc < SK; ++pc) {
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const float4 q = lds128(d0 + (uint32_t)((pc * 8 + j) * kBM * 16));
-                v[4 * j] += q.x; v[4 * j + 1] += q.y; v[4 * j + 2] += q.z; v[4 * j + 3] += q.w;
-              }
-            }
-            uint32_t r[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(v[j]);
-            emit(tm, tn, c, m, r);
-          }
-        } else if (*fix_flag) {
-          __threadfence();
-          const float4* src0 = reinterpret_cast<const float4*>(p.ws) +
-                               (size_t)u.slot * p.split_k * (size_t)(BN * kBM / 4);
-#pragma unroll 1
-          for (int c = 0; c < BN; c += 32) {
-            float v[32];
-            const float4* s0 = src0 + (size_t)(c / 32) * 8 * kBM + row;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const float4 q = __ldcg(s0 + j * kBM);
-              v[4 * j] = q.x; v[4 * j + 1] = q.y; v[4 * j + 2] = q.z; v[4 * j + 3] = q.w;
-            }
-#pragma unroll 1
-            for (int pc = 1; pc < p.split_k; ++pc) {
-              const float4* sp = s0 + (size_t)pc * (BN * kBM / 4);
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const float4 q = __ldcg(sp + j * kBM);
-                v[4 * j] += q.x; v[4 * j + 1] += q.y; v[4 * j + 2] += q.z; v[4 * j + 3] += q.w;
-              }
-            }
-            uint32_t r[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(v[j]);
-            emit(tm, tn, c, m, r);
-          }
-        }
+        const int mode = *fix_flag;
+        if (mode == 1) fix_staged(u.tile, u.slot, false);
+        else if (mode == 3) fix_direct(u.tile, u.slot);
       }
       if (ok && warp == Roles::kWarpEpi && lane == 0 && tj < kTraceTiles)
         trace_stamp(p, 7 + 6 * tj);
+    }
+    if (ok) {  // queued split tiles, now that the ring is idle
+      const int np = pend[0];
+      for (int i = 0; i < np; ++i) fix_staged(pend[1 + 2 * i], pend[2 + 2 * i], true);
     }
     if (p.c_tma && et == 0) bulk_wait_group<0>();  // all output stores complete
     // peer stores are ordered before anything that follows the kernel on the

@@ -367,8 +367,6 @@ Tensor matmul_fused(const Tensor& lhs, const Tensor& rhs, const Tensor* bias, Ac
   const size_t m = lhs.shape()[0], k = lhs.shape()[1], k2 = rhs.shape()[0], n = rhs.shape()[1];
   if (k != k2) throw Panic("Matmul dimension mismatch");
   if (bias && (bias->numel() != n)) throw Panic("matmul_fused: bias must have N elements");
-  if (act == Activation::Sigmoid || act == Activation::Tanh)
-    throw Panic("matmul_fused: only None/ReLU activations are fused on this backend");
   Placement p = place({&lhs, &rhs, bias});
   Tensor a = on(lhs, p), b = on(rhs, p);
   Tensor bz = bias ? on(*bias, p).contiguous() : Tensor();
@@ -435,8 +433,6 @@ Tensor conv2d_fused(const Tensor& input, const Tensor& weight, const Tensor* bia
   if (ws[1] != is[1])
     throw Panic("Weight input channels " + std::to_string(ws[1]) + " must match input channels " +
                 std::to_string(is[1]));
-  if (act == Activation::Sigmoid || act == Activation::Tanh)
-    throw Panic("conv2d: only None/ReLU activations are fused on this backend");
   const size_t N = is[0], C = is[1], H = is[2], W = is[3], Co = ws[0], kh = ws[2], kw = ws[3];
   if (H + 2 * padding.first < kh || W + 2 * padding.second < kw)
     throw Panic("Conv2d: kernel larger than padded input");

@@ -52,12 +52,16 @@ inline cudaStream_t pick_stream(rtb_ctx* ctx, void* stream) {
   return static_cast<cudaStream_t>(stream);
 }
 
-// RAII guard making ctx->device current for the calling thread.
+// RAII guard making ctx->device current for the calling thread.  The device
+// is set even when it already is the thread's current device: cudaSetDevice
+// also binds the device's primary context to the thread, which the driver-API
+// calls made here (tensor-map encoding) need in a thread that has not used
+// the runtime yet (e.g. a worker thread of the caller's pool).
 struct DeviceGuard {
   int prev = -1;
   explicit DeviceGuard(int dev) {
     cudaGetDevice(&prev);
-    if (prev != dev) cudaSetDevice(dev);
+    cudaSetDevice(dev);
   }
   ~DeviceGuard() {
     int cur = -1;
@@ -99,7 +103,7 @@ struct GemmDesc {
   const float* bias = nullptr;
   const float* residual = nullptr;
   int64_t ldr = 0;
-  int relu = 0;
+  int act = 0;  // RTB_ACT_* applied after bias and residual
   int out_mode = 0;  // 0 row-major, 1 NCHW scatter, 2 every rank's C (N-split)
   int hw = 0;
   float* const* peer_c = nullptr;  // out_mode 2: device array of npeers C bases
@@ -130,7 +134,7 @@ int smallm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream);
 // Aux kernels (rtb_aux.cu).
 int launch_pack_kmajor(const float* src, int64_t rows, int64_t k, int64_t rs, int64_t cs,
                        float* dst, int64_t kp, cudaStream_t s);
-int launch_fill_rows(float* C, int64_t M, int64_t N, int64_t ldc, const float* bias, int relu,
+int launch_fill_rows(float* C, int64_t M, int64_t N, int64_t ldc, const float* bias, int act,
                      cudaStream_t s);
 int launch_nchw_to_nhwc_padded(const float* x, int64_t N, int64_t C, int64_t H, int64_t W,
                                int64_t Cp, float* y, cudaStream_t s);
@@ -218,8 +222,9 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
 // one wave split (at most half the SMs).
 constexpr int kSplitCounters = 256;
 // The split-counter block for `s` and the next launch generation on it;
-// RTB_E_UNSUPPORTED (no error recorded) while `s` is capturing a graph, when
-// the caller allocates and zeroes counters for the launch itself (gen 1).
+// RTB_E_UNSUPPORTED (no error recorded) while `s` is capturing a graph or is
+// cudaStreamPerThread (a different stream in every host thread), when the
+// caller allocates and zeroes counters for the launch itself (gen 1).
 int split_counters(rtb_ctx* ctx, cudaStream_t s, unsigned long long** d, unsigned long long* gen);
 
 }  // namespace rtb

@@ -16,6 +16,7 @@
 // written with streaming stores.
 #include <cmath>
 
+#include "rtb_act.cuh"
 #include "rtb_internal.h"
 #include "rtb_ptx.cuh"
 
@@ -42,13 +43,6 @@ __device__ __forceinline__ double block_sum(double v, double* red) {
   }
   __syncthreads();
   return red[0];
-}
-
-__device__ __forceinline__ float activate(float y, int act) {
-  if (act == RTB_ACT_RELU) return fmaxf(y, 0.0f);  // NaN -> 0, as f32::max
-  if (act == RTB_ACT_SIGMOID) return 1.0f / (1.0f + expf(-y));
-  if (act == RTB_ACT_TANH) return tanhf(y);
-  return y;
 }
 
 __device__ __forceinline__ double warp_sum(double v) {

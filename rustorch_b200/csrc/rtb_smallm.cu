@@ -19,10 +19,11 @@
 // K is split into S slices when N alone gives too few CTAs; every slice
 // writes its fp32 partial block to a workspace and the last slice of a column
 // block to arrive (per-block counter) sums the slices in slice order, adds
-// the bias and applies ReLU, so the result does not depend on arrival order.
+// the bias and applies the activation, so the result does not depend on arrival order.
 #include <cstdint>
 #include <cstring>
 
+#include "rtb_act.cuh"
 #include "rtb_internal.h"
 #include "rtb_ptx.cuh"
 
@@ -41,7 +42,7 @@ struct SmallMParams {
   float* C;
   int64_t ldc;
   const float* bias;
-  int relu;
+  int act;       // RTB_ACT_*
   float* ws;     // [S][M][ws_ld] partial sums (S > 1)
   int64_t ws_ld;
   unsigned long long* cnt;  // [nblk] arrival words (generation << 8 | count), S > 1
@@ -206,7 +207,7 @@ __global__ void __launch_bounds__(256, 1)
   auto col = [&](int j) { return B_MN ? n0 + 4 * cg + j : n0 + cg + 64 * j; };
   auto finish = [&](int m, int n, float v) {
     if (p.bias) v += __ldg(p.bias + n);
-    if (p.relu) v = fmaxf(v, 0.0f);
+    v = activate(v, p.act);
     p.C[(int64_t)m * p.ldc + n] = v;
   };
   if (p.S == 1) {
@@ -309,7 +310,7 @@ int smallm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
   p.C = d.C;
   p.ldc = d.ldc;
   p.bias = d.bias;
-  p.relu = d.relu;
+  p.act = d.act;
   p.err = ctx->d_err;
   p.timeout_ns = ctx->timeout_ns;
   // K slices: one wave of CTAs (one per SM), at least 4 chunks per slice.
@@ -324,7 +325,7 @@ int smallm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
     const size_t part_bytes = (size_t)S * d.M * p.ws_ld * sizeof(float);
     const size_t cnt_off = (part_bytes + 255) & ~size_t(255);
     st = split_counters(ctx, stream, &p.cnt, &p.cnt_gen);
-    const bool own = (st == RTB_E_UNSUPPORTED);  // capturing: counters of this launch
+    const bool own = (st == RTB_E_UNSUPPORTED);  // capture / per-thread stream: own counters
     if (st != RTB_OK && !own) return st;
     st = ws_alloc(ctx, &ws, own ? cnt_off + (size_t)p.nblk * 8 : part_bytes, stream);
     if (st != RTB_OK) return st;

@@ -138,6 +138,21 @@ static void device_tests() {
     const float et[4] = {std::tanh(-1.5f), std::tanh(2.5f), std::tanh(-1.5f), std::tanh(2.5f)};
     for (int i = 0; i < 4; ++i) expect(std::fabs(gt[i] - et[i]) < 1e-6f, "tanh value");
   });
+  run("matmul_fused_sigmoid_tanh_2x2", [] {
+    // a . I + bias = [[0.6, -0.7], [0.8, -0.1]] exactly (identity products and
+    // these sums are exact), then the reference's staged activation
+    // (ops.rs:1703-1708): 1/(1+exp(-x)) and tanh(x).
+    Tensor a = Tensor::new_({0.1, -0.2, 0.3, 0.4}, {2, 2});
+    Tensor eye = Tensor::new_({1.0, 0.0, 0.0, 1.0}, {2, 2});
+    Tensor bias = Tensor::new_({0.5, -0.5}, {2});
+    const float pre[4] = {0.1f + 0.5f, -0.2f - 0.5f, 0.3f + 0.5f, 0.4f - 0.5f};
+    std::vector<float> s = ops::matmul_fused(a, eye, &bias, Activation::Sigmoid).data();
+    std::vector<float> t = ops::matmul_fused(a, eye, &bias, Activation::Tanh).data();
+    for (int i = 0; i < 4; ++i) {
+      expect(std::fabs(s[i] - 1.0f / (1.0f + std::exp(-pre[i]))) < 1e-6f, "sigmoid value");
+      expect(std::fabs(t[i] - std::tanh(pre[i])) < 1e-6f, "tanh value");
+    }
+  });
   run("test_matmul_backward_precision_under_1e6", [] {
     // loss = sum(a.matmul(b)): the incoming gradient is all ones
     Tensor a = Tensor::new_({1.0, 2.0, 3.0, 4.0}, {2, 2});

@@ -1,13 +1,13 @@
 """Generate tests/golden/reference_kat.json from the reference's own tests.
 
-Run in a container where the RusTorch sources are mounted (default
-/root/reference, or pass a path).  The reference is Rust and cannot be built
+Run where the RusTorch sources are checked out, passing their root
+directory.  The reference is Rust and cannot be built
 here, so its known-answer tests are read as text: the literal input and
 expected-output arrays are extracted from the test sources and written out with
 their file:line.  The committed JSON is what the tests use; this script is only
 needed to regenerate it.
 
-    python tests/golden/make_golden.py [/path/to/RusTorch]
+    python tests/golden/make_golden.py /path/to/RusTorch
 """
 from __future__ import annotations
 
@@ -138,4 +138,6 @@ def main(root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py /path/to/RusTorch")
+    main(sys.argv[1])

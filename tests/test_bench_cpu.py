@@ -41,3 +41,19 @@ def test_reference_arm_linear_norm_matches_our_config():
     assert d["metric"].startswith("linear_norm_relu TFLOP/s")
     assert d["config"]["workload"] == "Linear 1024->4096 + bias, LayerNorm(4096) + ReLU over 8192 rows"
     assert d["value"] > 0 and d["cpu_baseline"]["sample"].startswith("64 of 8192 rows")
+
+
+def test_reference_arm_default_is_resnet18():
+    """With no --workload the bench measures ResNet-18 forward img/s (B=256 per
+    GPU); the reference arm names the same metric and configuration."""
+    d = _run("--impl", "reference", "--steps", "1")
+    assert d["metric"].startswith("resnet18_fwd img/s")
+    assert d["unit"] == "img/s" and d["value"] > 0
+    assert d["config"]["workload"] == "ResNet-18 forward (BN folded), fp32"
+    assert d["config"]["batch_per_gpu"] == 256 and d["config"]["seed"] == 3
+
+
+def test_reference_arm_r50_stage_names():
+    d = _run("--impl", "reference", "--workload", "conv_r50s4", "--steps", "1")
+    assert d["metric"].startswith("conv2d_bias_relu_resnet50_s4_3x3 TFLOP/s")
+    assert d["config"]["input"] == [32, 512, 7, 7] and d["config"]["seed"] == 5

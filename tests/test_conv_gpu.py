@@ -74,6 +74,24 @@ def test_conv_bias_relu_resnet50_layer(gpu, orc, prec):
         assert orc.rel_frob(y, y32.astype(np.float64)) <= 2e-5
 
 
+@pytest.mark.parametrize("stage,c,hw", [(1, 64, 56), (3, 256, 14), (4, 512, 7)])
+@pytest.mark.parametrize("prec", [0, 1])
+def test_conv_bias_relu_resnet50_other_stages(gpu, orc, stage, c, hw, prec):
+    """The other ResNet-50 3x3 layers at batch 32 (stage 1: 64 channels at
+    56x56, stage 3: 256 at 14x14, stage 4: 512 at 7x7), Conv2d+bias+ReLU with
+    the inputs generated like the stage-2 workload (seed 1 + stage)."""
+    x = orc.normal((32, c, hw, hw), 1 + stage, 0)
+    w = orc.normal((c, c, 3, 3), 1 + stage, 1, 0.0, float(np.sqrt(2.0 / (c * 9))))
+    b = orc.uniform((c,), 1 + stage, 2, -0.1, 0.1)
+    pre = orc.conv2d_f64(x, w, (1, 1), (1, 1)) + b.astype(np.float64)[None, :, None, None]
+    y = _host(gpu.conv2d_fwd(_dev(x), _dev(w), _dev(b), (1, 1), (1, 1), act=gpu.ACT_RELU,
+                             precision=prec))
+    assert orc.rel_frob(y, np.maximum(pre, 0)) <= TOL[prec]
+    band = 1e-5 if prec == 0 else 1e-2 * float(np.sqrt(np.mean(pre * pre)))
+    mask = np.abs(pre) >= band
+    assert np.array_equal((y > 0)[mask], (pre > 0)[mask])
+
+
 @pytest.mark.parametrize("shape,wshape,stride,pad", [
     ((2, 3, 224, 224), (64, 3, 7, 7), (2, 2), (3, 3)),      # ResNet stem, Ci=3 -> padded to 4
     ((4, 64, 56, 56), (64, 64, 3, 3), (1, 1), (1, 1)),

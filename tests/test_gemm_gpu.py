@@ -137,8 +137,62 @@ def test_errors(gpu):
     with pytest.raises(ValueError, match="Matmul only supports 2D"):
         gpu.sgemm(torch.ones((2, 2, 2), device="cuda"), a)
     with pytest.raises(gpu.RtbError) as e:
-        gpu.sgemm(a, torch.ones((3, 4), device="cuda"), act=gpu.ACT_SIGMOID)
-    assert e.value.status == 5
+        gpu.sgemm(a, torch.ones((3, 4), device="cuda"), act=7)
+    assert e.value.status == 1  # unknown activation: RTB_E_INVALID
+
+
+def _act64(pre, act):
+    if act == 2:
+        return 1.0 / (1.0 + np.exp(-pre))
+    if act == 3:
+        return np.tanh(pre)
+    return np.maximum(pre, 0.0) if act == 1 else pre
+
+
+@pytest.mark.parametrize("act", [2, 3])
+@pytest.mark.parametrize("prec", [0, 1])
+@pytest.mark.parametrize("m,n,k,trans_b", [
+    (4096, 4096, 1024, 1),   # the MLP's first Linear (W^T view, K-major B)
+    (4096, 1024, 4096, 1),   # its last Linear
+    (333, 500, 256, 0),      # ragged tiles, row-major rhs
+    (16, 1000, 777, 0),      # the small-M path
+    (5, 7, 0, 0),            # K = 0: act(bias)
+])
+def test_matmul_fused_sigmoid_tanh(gpu, orc, act, prec, m, n, k, trans_b):
+    """ops::matmul_fused with Activation::Sigmoid / Tanh (rustorch-core/src/
+    ops.rs:1703-1708): act(A.B + bias) in the GEMM epilogue.  Sigmoid and tanh
+    have slopes <= 1/4 and <= 1, so the contraction's error bound carries
+    over: relative Frobenius error <= 1e-5 (3xTF32) / 5e-3 (TF32) against
+    float64, with 1/(1+exp(-x)) and tanh(x) evaluated in float64."""
+    a = orc.normal((m, k), 12, 1, 0.0, 1.0 / np.sqrt(max(k, 1)))
+    w = orc.normal((n, k) if trans_b else (k, n), 12, 2)
+    b = w.T if trans_b else w
+    bias = orc.uniform((n,), 12, 3, -0.5, 0.5)
+    rows = np.arange(m) if m <= 512 else np.r_[0:40, m // 2:m // 2 + 24, m - 40:m]
+    pre = (orc.matmul_f64(a[rows], np.ascontiguousarray(b)) if k else
+           np.zeros((len(rows), n))) + bias.astype(np.float64)
+    bd = _dev(w).t() if trans_b else _dev(w)
+    y = _host(gpu.sgemm(_dev(a), bd, bias=_dev(bias), act=act, precision=prec))
+    tol = TOL[0] if (m <= 32 or k == 0) else TOL[prec]  # small-M / K=0: exact fp32 in both modes
+    assert orc.rel_frob(y[rows], _act64(pre, act)) <= tol
+    if k and m <= 512:
+        # and the reference's own staged f32 path (matmul -> add bias -> act)
+        y32 = orc.matmul_fused(a, np.ascontiguousarray(b), bias, act)
+        assert orc.rel_frob(y, y32.astype(np.float64)) <= 2 * tol
+
+
+@pytest.mark.parametrize("act", [2, 3])
+def test_conv_sigmoid_tanh_epilogue(gpu, orc, act):
+    """The conv epilogue (NCHW and NHWC stores) applies the same activations."""
+    x = orc.normal((4, 64, 20, 20), 13, 1)
+    w = orc.normal((96, 64, 3, 3), 13, 2, 0.0, float(np.sqrt(2.0 / 576)))
+    bias = orc.uniform((96,), 13, 3, -0.2, 0.2)
+    pre = orc.conv2d_f64(x, w, (1, 1), (1, 1)) + bias.astype(np.float64)[None, :, None, None]
+    y = _host(gpu.conv2d_fwd(_dev(x), _dev(w), _dev(bias), (1, 1), (1, 1), act=act))
+    assert orc.rel_frob(y, _act64(pre, act)) <= TOL[0]
+    yh = _host(gpu.conv2d_fwd(_dev(x), _dev(w), _dev(bias), (1, 1), (1, 1), act=act,
+                              y_layout=gpu.LAYOUT_NHWC))
+    assert orc.rel_frob(yh.transpose(0, 3, 1, 2), _act64(pre, act)) <= TOL[0]
 
 
 @pytest.mark.parametrize("prec", [0, 1])
@@ -148,6 +202,38 @@ def test_batched(gpu, orc, prec):
     c = _host(gpu.sgemm_batched(_dev(a), _dev(b), precision=prec))
     for i in range(3):
         assert orc.rel_frob(c[i], orc.matmul_f64(a[i], b[i])) <= TOL[prec]
+
+
+@pytest.mark.parametrize("prec", [0, 1])
+def test_batched_many_and_transposed_b(gpu, orc, prec):
+    """rtb_sgemm_batched with 48 problems of ragged size, B given row-major
+    [K,N] per batch and as Linear-style [N,K] per batch (transB=1, strided),
+    a shared bias and ReLU, against looped 2-D float64 products (the
+    reference's matmul is 2-D; its oracle for a batch is the loop)."""
+    import ctypes
+    bt, m, n, k = 48, 150, 72, 200
+    a = orc.normal((bt, m, k), 14, 1)
+    w = orc.normal((bt, n, k), 14, 2)          # [N,K] per batch (transposed operand)
+    bias = orc.uniform((n,), 14, 3, -0.5, 0.5)
+    pre = np.stack([orc.matmul_f64(a[i], np.ascontiguousarray(w[i].T)) for i in range(bt)])
+    pre += bias.astype(np.float64)
+    ref = np.maximum(pre, 0.0)
+    da, dw, dbias = _dev(a), _dev(w), _dev(bias)
+    ctx = gpu.get_context(0)
+
+    def run(bptr, ldb, stride_b, trans_b):
+        c = torch.empty((bt, m, n), device="cuda")
+        gpu.call("rtb_sgemm_batched", ctx.handle, bt, m, n, k, ctypes.c_void_p(da.data_ptr()), k,
+                 m * k, 0, ctypes.c_void_p(bptr), ldb, stride_b, trans_b,
+                 ctypes.c_void_p(dbias.data_ptr()), gpu.ACT_RELU, ctypes.c_void_p(c.data_ptr()),
+                 n, m * n, prec, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        return _host(c)
+
+    ct = run(dw.data_ptr(), k, n * k, 1)
+    assert orc.rel_frob(ct, ref) <= TOL[prec]
+    bkn = _dev(np.ascontiguousarray(w.transpose(0, 2, 1)))   # [K,N] per batch
+    cn = run(bkn.data_ptr(), n, k * n, 0)
+    assert orc.rel_frob(cn, ref) <= TOL[prec]
 
 
 def test_skinny_8192_sampled(gpu, orc):
@@ -176,6 +262,45 @@ def test_square_4096_sampled_and_linearity(gpu, orc):
     # linearity: A.(2B) == 2(A.B) exactly (scaling by 2 is exact in every split)
     c2 = gpu.sgemm(da, db * 2)
     assert torch.equal(c2, c * 2)
+
+
+@pytest.mark.parametrize("prec", [0, 1])
+def test_square_2048_k_split_schedule(gpu, orc, prec):
+    """2048^3 (256 tiles on 148 SMs): the scheduler cuts the last 108 tiles
+    into K pieces, several per CTA, whose fix-ups run while the CTA's next
+    piece is in flight; sampled entries against float64."""
+    a = orc.normal((2048, 2048), 4, 5)
+    b = orc.normal((2048, 2048), 4, 6)
+    c = _host(gpu.sgemm(_dev(a), _dev(b), precision=prec))
+    rng = np.random.default_rng(7)
+    rows = rng.integers(0, 2048, 8192)
+    cols = rng.integers(0, 2048, 8192)
+    ref = orc.matmul_f64_sampled(a, b, rows, cols)
+    assert orc.rel_frob(c[rows, cols], ref) <= TOL[prec]
+
+
+@pytest.mark.parametrize("n", [8192, 16384])
+def test_square_large_sampled_and_linearity(gpu, orc, n):
+    """The large square f32 matmuls of the sweep (8192^3, 16384^3; A, B ~ N(0,1),
+    seed 4 as the bench uses them) at full size: 4096 sampled entries against
+    float64 dot products, plus the exact identity A.(2B) == 2(A.B) over the
+    whole of C (scaling by 2 is exact in every split and every sum)."""
+    a = orc.normal((n, n), 4, 0)
+    b = orc.normal((n, n), 4, 1)
+    da, db = _dev(a), _dev(b)
+    c = gpu.sgemm(da, db)
+    rng = np.random.default_rng(n)
+    rows = rng.integers(0, n, 4096)
+    cols = rng.integers(0, n, 4096)
+    ref = orc.matmul_f64_sampled(a, b, rows, cols)
+    torch.cuda.synchronize()
+    got = c[torch.from_numpy(rows).cuda(), torch.from_numpy(cols).cuda()].cpu().numpy()
+    assert orc.rel_frob(got, ref) <= 1e-5
+    del a
+    db.mul_(2.0)
+    c2 = gpu.sgemm(da, db)
+    assert torch.equal(c2, c * 2)
+    assert gpu.get_context(0).device_error() == 0
 
 
 @pytest.mark.parametrize("k", [1024, 16384])
@@ -234,10 +359,10 @@ def test_small_m_path(gpu, orc, m, n, k, trans_b):
         assert _relu_pattern_ok(y / scale, pre / scale, tol_prec)
 
 
-@pytest.mark.parametrize("m", [16, 64])
+@pytest.mark.parametrize("m", [16, 64, 256])
 def test_small_m_skinny_8192(gpu, orc, m):
     """The skinny M x 8192 x 8192 workloads (M=16 on the small-M path, M=64
-    on the tensor cores) against float64 on a sample of columns."""
+    and M=256 on the tensor cores) against float64 on a sample of columns."""
     a = orc.normal((m, 8192), 4, 0)
     b = orc.normal((8192, 8192), 4, 1)
     c = _host(gpu.sgemm(_dev(a), _dev(b)))
@@ -270,6 +395,66 @@ def test_split_counters_across_launches_and_streams(gpu, orc):
         np.testing.assert_array_equal(c.cpu().numpy(), ref)
         np.testing.assert_array_equal(cs.cpu().numpy(), ref_s)
     assert gpu.get_context(0).device_error() == 0
+
+
+def test_split_counters_per_thread_streams(gpu, orc):
+    """Tail-split GEMMs (1024^3) and small-M split-K GEMMs launched from two
+    host threads on cudaStreamPerThread (one handle, a different stream per
+    thread, so launches may overlap): each launch counts its pieces in
+    counters of its own, and every result is bit-identical to the same GEMM
+    on an ordinary stream.  Also a stream made by rtb_stream_create and
+    destroyed between uses (its counter block is released with it)."""
+    import ctypes
+    import threading
+    a = orc.normal((1024, 1024), 41, 1)
+    b = orc.normal((1024, 1024), 41, 2)
+    s_m = orc.normal((8, 4096), 41, 3)
+    s_b = orc.normal((4096, 2048), 41, 4)
+    da, db, dsm, dsb = (torch.from_numpy(t).cuda() for t in (a, b, s_m, s_b))
+    ref = gpu.sgemm(da, db).cpu().numpy()
+    ref_s = gpu.sgemm(dsm, dsb).cpu().numpy()
+    ctx = gpu.get_context(0)
+    per_thread = ctypes.c_void_p(2)  # cudaStreamPerThread
+    outs = [[torch.empty((1024, 1024), device="cuda") for _ in range(4)] for _ in range(2)]
+    outs_s = [[torch.empty((8, 2048), device="cuda") for _ in range(4)] for _ in range(2)]
+    torch.cuda.synchronize()
+    errors = []
+
+    def p(t):
+        return ctypes.c_void_p(t.data_ptr())
+
+    def work(t):
+        try:
+            for i in range(4):
+                gpu.call("rtb_sgemm", ctx.handle, 1024, 1024, 1024, p(da), 1024, 0, p(db), 1024, 0,
+                         None, 0, p(outs[t][i]), 1024, 0, per_thread)
+                gpu.call("rtb_sgemm", ctx.handle, 8, 2048, 4096, p(dsm), 4096, 0, p(dsb), 2048, 0,
+                         None, 0, p(outs_s[t][i]), 2048, 0, per_thread)
+            gpu.call("rtb_stream_synchronize", ctx.handle, per_thread)
+        except Exception as e:  # reported by the main thread
+            errors.append(e)
+
+    th = [threading.Thread(target=work, args=(t,)) for t in range(2)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join()
+    torch.cuda.synchronize()
+    assert not errors, errors
+    for t in range(2):
+        for i in range(4):
+            np.testing.assert_array_equal(outs[t][i].cpu().numpy(), ref)
+            np.testing.assert_array_equal(outs_s[t][i].cpu().numpy(), ref_s)
+    for _ in range(3):  # created, used, destroyed: a reused handle gets a fresh block
+        h = ctypes.c_void_p()
+        gpu.call("rtb_stream_create", ctx.handle, ctypes.byref(h))
+        c = torch.empty((1024, 1024), device="cuda")
+        gpu.call("rtb_sgemm", ctx.handle, 1024, 1024, 1024, p(da), 1024, 0, p(db), 1024, 0, None,
+                 0, p(c), 1024, 0, h)
+        gpu.call("rtb_stream_synchronize", ctx.handle, h)
+        gpu.call("rtb_stream_destroy", ctx.handle, h)
+        np.testing.assert_array_equal(c.cpu().numpy(), ref)
+    assert ctx.device_error() == 0
 
 
 def test_inputs_written_by_the_previous_kernel(gpu, orc):

@@ -83,3 +83,32 @@ def test_resnet18_forward_matches_oracle(gpu, orc):
         assert rb.get_context(0).device_error() == 0
     finally:
         rb.call("rtb_resnet18_destroy", h)
+
+
+def test_resnet18_forward_full_batch_256(gpu, orc):
+    """The benchmarked configuration: the whole B=256 batch in one forward
+    (M reaches 3.2M rows on the stem, so other tile, split and grid-stride
+    paths run than at B=2); images 0, 127 and 255 are checked against the
+    oracle composition of the reference's CPU ops, and the rest of the batch
+    must be finite."""
+    rb = gpu
+    h = ctypes.c_void_p()
+    rb.call("rtb_resnet18_create", 0, 3, rb.PREC_3XTF32, ctypes.byref(h))
+    try:
+        convs, fc_w, fc_b = _params(rb, h)
+        x = orc.normal((256, 3, 224, 224), 3, 1000)
+        xd = torch.from_numpy(x).cuda()
+        logits = torch.empty((256, 1000), device="cuda")
+        rb.call("rtb_resnet18_forward", h, 256, ctypes.c_void_p(xd.data_ptr()),
+                ctypes.c_void_p(logits.data_ptr()), None)
+        torch.cuda.synchronize()
+        got = logits.cpu().numpy()
+        assert np.isfinite(got).all()
+        pick = [0, 127, 255]
+        ref, _ = _oracle_forward(orc, np.ascontiguousarray(x[pick]), convs, fc_w, fc_b)
+        err = orc.rel_frob(got[pick], ref.astype(np.float64))
+        assert err <= 1e-4, err
+        assert np.array_equal(got[pick].argmax(1), ref.argmax(1))
+        assert rb.get_context(0).device_error() == 0
+    finally:
+        rb.call("rtb_resnet18_destroy", h)
