@@ -124,11 +124,12 @@ struct GemmDesc {
 // Validated launch of the tcgen05 engine (A/B already TMA-compatible).
 int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream);
 
-// Small-M path (M <= kSmallMMax, no conv producer): fp32 FMA on the CUDA cores
-// with B streamed once from HBM (rtb_smallm.cu).  Measured on B200 for
-// M x 8192 x 8192: 87 / 113 / 169 us at M = 1 / 16 / 32 against 186 us for the
-// 128-row tensor-core tile; at M = 48 and 64 the tensor path is faster.
-constexpr int64_t kSmallMMax = 32;
+// Small-M path (M <= kSmallMMax, no conv producer): packed fp32 FMAs on the
+// CUDA cores with B streamed once from HBM (rtb_smallm.cu).  Measured on B200
+// for M x 8192 x 8192 (B row-major): 52.9 / 54.2 / 68.6 / 123.2 us at M = 1 /
+// 8 / 16 / 32 against 106.9-109.3 us for the 128-row tensor-core tile (M = 48,
+// 64), so rows beyond 16 go to the tensor cores.
+constexpr int64_t kSmallMMax = 16;
 int smallm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream);
 
 // Aux kernels (rtb_aux.cu).

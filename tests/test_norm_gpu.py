@@ -65,7 +65,7 @@ def test_kat_2x2(gpu):
 
 # (m, n, k): ragged and scalar paths (n % 4 != 0), the reference's Auto
 # threshold for its fused order (m >= 128, k >= 128, n >= 32), rows kept on
-# chip and rows re-read (n > 16384), the small-M contraction path (m <= 32)
+# chip and rows re-read (n > 16384), the small-M contraction path (m <= 16)
 SHAPES = [(1, 1, 1), (7, 33, 19), (128, 256, 128), (300, 1000, 257), (16, 512, 4096),
           (64, 2048, 64), (33, 4096, 32), (17, 8192, 16), (40, 12000, 48), (50, 16385, 32),
           (64, 20000, 64), (2048, 1024, 1024)]
