@@ -56,16 +56,26 @@ L2_BYTES = 126 * 1024 * 1024
 # one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum); the capture and
 # its command are summarised in the named profiles/ file.
 TRAFFIC = {
+    "resnet18": (5.061e9, "profiles/resnet18_fwd_launches.md"),
     "conv": (13.52e6, "profiles/conv2d_bias_relu_r50s2_3x3.md"),
-    "gemm8192": (3.485e9, "profiles/sgemm_8192_3xtf32.md"),
-    "gemm_m16": (273.3e6, "profiles/sgemm_small_m16_8192.md"),
+    "conv_r50s4": (12.77e6, "profiles/kernel_counters_gemm_conv.md"),
+    "gemm1024": (8.49e6, "profiles/kernel_counters_gemm_conv.md"),
+    "gemm8192": (3.617e9, "profiles/sgemm_8192_3xtf32.md"),
+    "gemm_m16": (272.7e6, "profiles/sgemm_small_m16_8192.md"),
+    "gemm_m256": (280.6e6, "profiles/kernel_counters_gemm_conv.md"),
+    "mlp": (665.2e6, "profiles/kernel_counters_gemm_conv.md"),
     "linear_norm": (154.7e6, "profiles/linear_norm_relu_8192x1024x4096.md"),
 }
 # Tensor-pipe activity of each workload's dominant kernel(s) as ncu counts it
 # (sm__pipe_tensor_cycles_active, % of elapsed cycles), from the named capture.
 TENSOR_PIPE = {
+    "resnet18": (0.389, "profiles/resnet18_fwd_launches.md"),
     "conv": (0.340, "profiles/conv2d_bias_relu_r50s2_3x3.md"),
-    "gemm8192": (0.575, "profiles/sgemm_8192_3xtf32.md"),
+    "conv_r50s4": (0.248, "profiles/kernel_counters_gemm_conv.md"),
+    "gemm1024": (0.185, "profiles/kernel_counters_gemm_conv.md"),
+    "gemm8192": (0.566, "profiles/sgemm_8192_3xtf32.md"),
+    "gemm_m256": (0.455, "profiles/kernel_counters_gemm_conv.md"),
+    "mlp": (0.526, "profiles/kernel_counters_gemm_conv.md"),
     "linear_norm": (0.564, "profiles/linear_norm_relu_8192x1024x4096.md"),
 }
 # DRAM bytes per launch of a workload's second kernel (roofline.secondary)
@@ -151,6 +161,19 @@ class ClockSampler:
         reasons = sorted({n for _, rs in self.rows for n, bit in self.REASONS.items() if rs & bit})
         return {"sm_mhz": statistics.median(r[0] for r in self.rows), "sm_max_mhz": self.max_mhz,
                 "reasons": reasons, "samples": len(self.rows), "source": "nvml"}
+
+
+def _host_threads():
+    """Host threads this process may really use: its CPU affinity, capped by a
+    cgroup CPU quota when one is set (os.cpu_count() reports the machine)."""
+    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    try:
+        quota, period = open("/sys/fs/cgroup/cpu.max").read().split()[:2]
+        if quota != "max":
+            n = max(1, min(n, int(int(quota) // int(period))))
+    except (OSError, ValueError):
+        pass
+    return n
 
 
 def _dist_env():
@@ -1234,13 +1257,18 @@ def run_ours(args):
         gemm_extra = _gemm_extras(rb, torch, dev, args, dist, world, roof_peak)
 
     if rank == 0:
-        cpu_val, sample = wl.cpu_sample(os.cpu_count())
-        cpu_line = {"value": round(cpu_val, 6), "unit": unit, "cores": os.cpu_count(),
-                    "kind": "port", "sample": sample}
-        if hasattr(wl, "cpu_sample_all_cores") and scaling != "strong":
-            v_all, s_all = wl.cpu_sample_all_cores(os.cpu_count())
-            cpu_line["all_cores"] = {"value": round(v_all, 6), "cores": os.cpu_count(),
-                                     "sample": s_all}
+        threads = _host_threads()
+        if world == 1:
+            cpu_val, sample = wl.cpu_sample(threads)
+            cpu_line = {"value": round(cpu_val, 6), "unit": unit, "cores": threads,
+                        "kind": "port", "sample": sample}
+            if hasattr(wl, "cpu_sample_all_cores") and scaling != "strong":
+                v_all, s_all = wl.cpu_sample_all_cores(threads)
+                cpu_line["all_cores"] = {"value": round(v_all, 6), "cores": threads,
+                                         "sample": s_all}
+        else:  # the CPU baseline is a one-GPU figure (the N=1 line carries it)
+            cpu_line = {"value": None, "unit": unit, "cores": threads, "kind": "port",
+                        "sample": "measured on the N=1 line only"}
         if scaling == "strong":
             par = f"N-split x{world} + NCCL all-gather"
         elif unit == "img/s":
@@ -1278,7 +1306,7 @@ def run_reference(args):
     rank, world, _ = _dist_env()
     if rank != 0:
         return
-    threads = os.cpu_count()
+    threads = _host_threads()
     # Workload descriptions only (no GPU): cpu_sample needs the sizes.
     if args.workload == "conv" or args.workload.startswith("conv_r50s"):
         stage = 2 if args.workload == "conv" else int(args.workload[-1])

@@ -209,11 +209,13 @@ int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
   p.tiles_n = (int)((d.N + bn - 1) / bn);
   // Raster: consecutive tiles walk down group_m M-tiles, then across N
   // (RTB_GROUP_M overrides the band height for measurements).
-  // Measured on B200 (3xTF32, RTB_GROUP_M sweep): 8192^3 203.5 / 200.2 /
-  // 198.8 / 201.8 / 195.2 TFLOP/s and 16384^3 185.2 / 183.5 / 180.2 / 175.4 /
-  // 169.4 for bands of 4 / 8 / 16 / 32 / 64 M-tiles.
-  static const int gm_env = env_int("RTB_GROUP_M", 4);
-  const int gm = gm_env > 0 ? gm_env : 4;
+  // Bands of 12 M-tiles make a wave of 148 tiles about square (12 x 12.3),
+  // the fewest A and B panels per wave: 8192^3 reads 3.34 GB from DRAM per
+  // launch (8: 3.40, 16: 3.59, 4: 5.08), at the same speed within run-to-run
+  // noise (196-209 TFLOP/s for every band from 4 to 16, interleaved
+  // processes on one B200; the kernel is bound by its mainloop, not DRAM).
+  static const int gm_env = env_int("RTB_GROUP_M", 12);
+  const int gm = gm_env > 0 ? gm_env : 12;
   p.group_m = p.tiles_m < gm ? p.tiles_m : gm;
   p.C = d.C;
   p.ldc = d.ldc;
