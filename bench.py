@@ -74,6 +74,7 @@ TENSOR_PIPE = {
     "conv_r50s4": (0.248, "profiles/kernel_counters_gemm_conv.md"),
     "gemm1024": (0.185, "profiles/kernel_counters_gemm_conv.md"),
     "gemm8192": (0.566, "profiles/sgemm_8192_3xtf32.md"),
+    "gemm8192:tf32": (0.535, "profiles/sgemm_8192_3xtf32.md"),
     "gemm_m256": (0.455, "profiles/kernel_counters_gemm_conv.md"),
     "mlp": (0.526, "profiles/kernel_counters_gemm_conv.md"),
     "linear_norm": (0.564, "profiles/linear_norm_relu_8192x1024x4096.md"),
@@ -1199,6 +1200,8 @@ def run_ours(args):
     kflops = getattr(wl, "kernel_flops", wl.flops)
     k_tflops = kflops * args.steps / (kms / 1e3) / 1e12
     tf32_peak = peaks["bf16_tflops"] / 2.0
+    # captures are per precision (3xTF32 unless the key names TF32)
+    tp_key = f"{args.workload}:tf32" if args.precision == "tf32" else args.workload
     roof_peak = tf32_peak / MMAS_PER_MAC[0]  # 3xTF32: three tensor-core MMAs per algorithmic MAC
     if getattr(wl, "bound", "tensor") == "hbm":
         # below the ridge: bytes that must cross HBM per launch / launch time
@@ -1218,8 +1221,8 @@ def run_ours(args):
                     "traffic_source": TRAFFIC.get(args.workload, (None, None))[1],
                     "peak_basis": f"{peaks['basis']} bf16 {peaks['bf16_tflops']} TFLOP/s "
                                   f"/ 2 (TF32 rate) / {MMAS_PER_MAC[0]} (MMAs per MAC)",
-                    "tensor_pipe_frac": TENSOR_PIPE.get(args.workload, (None,))[0],
-                    "tensor_pipe_source": TENSOR_PIPE.get(args.workload, (None, None))[1],
+                    "tensor_pipe_frac": TENSOR_PIPE.get(tp_key, (None,))[0],
+                    "tensor_pipe_source": TENSOR_PIPE.get(tp_key, (None, None))[1],
                     "tensor_pipe_basis": "ncu sm__pipe_tensor_cycles_active, fraction of "
                                          "elapsed cycles, from the named capture",
                     "mma_rate_implied": round(MMAS_PER_MAC[0] * k_tflops / tf32_peak, 4),

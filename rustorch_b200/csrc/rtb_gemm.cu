@@ -73,15 +73,16 @@ struct SplitPlan {
 // count: fitted to B200 timings of 1024^3, 2048^3 and ResNet convs with 2 to
 // 5 pieces per tile, where a piece cost 7.6 to 13 k-block times more than its
 // share of the mainloop) plus the share of its tile's fix-up (every partial
-// read back: 0.4 per piece when the partials are staged through the idle load
-// ring, which holds two chunks of up to 5 pieces; 1.5 per piece read straight
-// from L2 beyond that).
+// read back: 1 per piece when the partials are staged through the idle load
+// ring, which holds two chunks of up to 5 pieces; 2 per piece read straight
+// from L2 beyond that; a trace of R50 stage 4 with 5 pieces per tile showed
+// the queued fix-ups running 6.5-12.5 us past the CTAs' last units).
 double plan_cost(int64_t tiles, int64_t split, int sk, int num_kb, int64_t G) {
   const int64_t full = tiles - split;
   const int64_t units = full + split * sk;
   const int64_t grid = units < G ? units : G;
   const double c_tile = num_kb + 1.0;
-  const double c_piece = (double)((num_kb + sk - 1) / sk) + 8.0 + (sk <= 5 ? 0.4 : 1.5) * sk;
+  const double c_piece = (double)((num_kb + sk - 1) / sk) + 8.0 + (sk <= 5 ? 1.0 : 2.0) * sk;
   double worst = 0.0;
   for (int64_t c = 0; c < grid; ++c) {
     const int64_t n_full = full > c ? (full - c + grid - 1) / grid : 0;
@@ -260,8 +261,8 @@ int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
 
   // K-split schedule (plan_split above): the last `rem` tiles (the partial
   // last wave, or whole waves more when that balances better) are cut along K
-  // into split_k pieces, e.g. R50 stage-4 3x3 (52 tiles of 144 k-blocks on
-  // 148 SMs): 52 x 5 pieces instead of 52 whole tiles on 52 SMs.  The pieces'
+  // into split_k pieces, e.g. R50 stage-3 3x3 (98 tiles of 72 k-blocks on
+  // 148 SMs): 98 x 3 pieces instead of 98 whole tiles on 98 SMs.  The pieces'
   // partial tiles go through a stream-ordered workspace; RTB_TAIL_SPLIT=0
   // turns splitting off.
   const int64_t tiles = (int64_t)p.tiles_m * p.tiles_n;

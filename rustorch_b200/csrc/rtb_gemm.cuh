@@ -358,8 +358,12 @@ __device__ __forceinline__ void epilogue_nchw_chunk(const GemmParams& p, uint32_
   const int q = et & 31;   // 4-pixel group
   const int cw = et >> 5;  // channels cw, cw+4, ..., cw+28 of the chunk
   const int m = m0 + 4 * q;
-  if (m < p.M) {
-    if ((p.hw % 4 == 0) && p.vec4_nchw && m + 3 < p.M) {
+  // 16-byte stores need every 4-pixel group inside one image and aligned:
+  // images of a multiple of 4 pixels and a whole 128-pixel chunk (uniform
+  // over the chunk)
+  const bool vec = (p.hw % 4 == 0) && p.vec4_nchw && m0 + kBM <= p.M;
+  {
+    if (vec) {
       // the 4 pixels lie in one image
       const int img = m / p.hw;
       const int pix = m - img * p.hw;
@@ -388,34 +392,35 @@ __device__ __forceinline__ void epilogue_nchw_chunk(const GemmParams& p, uint32_
         }
       }
     } else {
-      // general case: each of the 4 pixels resolved on its own
+      // general case (images of any size, the last chunk): warp cw writes
+      // channels cw, cw+4, ..., lane l pixels l, l+32, l+64, l+96, so each
+      // store instruction covers 32 consecutive pixels of one channel plane
+      const int l = et & 31;
       int64_t pb[4];
-      int cnt = 0;
+      bool pv[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int me = m + e;
-        pb[e] = 0;
-        if (me < p.M) {
-          const int im = me / p.hw;
-          pb[e] = ((int64_t)im * p.N + n0) * p.hw + (me - im * p.hw);
-          cnt = e + 1;
-        }
+      for (int j = 0; j < 4; ++j) {
+        const int me = m0 + l + 32 * j;
+        pv[j] = me < p.M;
+        const int im = pv[j] ? me / p.hw : 0;
+        pb[j] = pv[j] ? ((int64_t)im * p.N + n0) * p.hw + (me - im * p.hw) : 0;
       }
 #pragma unroll 1
       for (int k = 0; k < 8; ++k) {
         const int ch = cw + 4 * k;
         if (n0 + ch >= p.N) continue;
-        const float4 o = lds128(buf + (ch * kBM + 4 * q) * 4);
         const float bv = p.bias ? lds32(sb + ch * 4) : 0.0f;
-        float sv[4] = {o.x + bv, o.y + bv, o.z + bv, o.w + bv};
+        float sv[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) sv[j] = lds32(buf + (ch * kBM + l + 32 * j) * 4) + bv;
         if (p.residual) {
 #pragma unroll
-          for (int e = 0; e < 4; ++e)
-            if (e < cnt) sv[e] += __ldg(p.residual + pb[e] + (int64_t)ch * p.hw);
+          for (int j = 0; j < 4; ++j)
+            if (pv[j]) sv[j] += __ldg(p.residual + pb[j] + (int64_t)ch * p.hw);
         }
 #pragma unroll
-        for (int e = 0; e < 4; ++e)
-          if (e < cnt) p.C[pb[e] + (int64_t)ch * p.hw] = activate(sv[e], p.act);
+        for (int j = 0; j < 4; ++j)
+          if (pv[j]) p.C[pb[j] + (int64_t)ch * p.hw] = activate(sv[j], p.act);
       }
     }
   }
