@@ -876,6 +876,9 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
           if (last) trace_stamp(p, 6 + 6 * tj);
         }
         const uint32_t t_part = t_lane + (uint32_t)(b * Cfg::kAccW);
+        // the last unit leaves without the running-sum round trip through
+        // TMEM when holding the accumulator during the stores costs nothing
+        const bool emit_now = last && (piece || w + (int)gridDim.x >= p.num_units);
         // One finished chunk: a split piece's partial to the workspace, else to C.
         auto out = [&](int c, const uint32_t (&r)[32]) {
           if (piece) {
@@ -914,18 +917,19 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
             tc_fence_before();
             mbar_arrive(&tempty_bar[b]);  // partial buffer b may be overwritten now
           }
-          if (SPLIT && units > 1) {
+          if (SPLIT && units > 1 && !emit_now) {
             // running sum; after the last unit the finished tile, which leaves
             // from there so the accumulator is not held during the stores
             tmem_st_32x32b_x32(t_run + (uint32_t)c, r);
           } else {
-            // a tile (or piece) of one unit leaves straight from the partial
-            // (short-K tiles: no running-sum round trip through TMEM)
+            // straight from the partial (+ running sum): a tile (or piece) of
+            // one unit, a piece (its partial goes to L2 fast), and the CTA's
+            // last tile (no later tile waits for the accumulator)
             out(c, r);
           }
         }
-        if (SPLIT && units > 1) tmem_st_wait();
-        if (SPLIT && units > 1 && last) {
+        if (SPLIT && units > 1 && !emit_now) tmem_st_wait();
+        if (SPLIT && units > 1 && last && !emit_now) {
 #pragma unroll 1
           for (int c = 0; c < BN; c += 32) {
             uint32_t r[32];
