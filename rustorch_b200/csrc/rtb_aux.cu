@@ -223,6 +223,35 @@ __global__ void __launch_bounds__(256) conv_prologue_kernel(
   }
 }
 
+// B's 3xTF32 low part, out[r][c] = x - trunc_tf32(x) (x = B[r][c]; the
+// tensor core reads the raw fp32 B as its truncated TF32 hi part), with the
+// padding columns [cols, ldo) zeroed.  One float4 of the output per thread.
+__global__ void __launch_bounds__(256) tf32_lo_kernel(const float* __restrict__ b, int64_t rows,
+                                                      int64_t cols, int64_t ldb, int vec,
+                                                      float* __restrict__ out, int64_t ldo) {
+  griddep_wait();  // launched with programmatic stream serialization
+  griddep_launch_dependents();
+  const int64_t q4 = ldo / 4;
+  const int64_t n = rows * q4;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / q4;
+    const int64_t c = (i - r * q4) * 4;
+    const float* src = b + r * ldb + c;
+    float v[4];
+    if (vec && c + 4 <= cols) {
+      const float4 x = __ldg(reinterpret_cast<const float4*>(src));
+      v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = c + j < cols ? __ldg(src + j) : 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] -= __uint_as_float(__float_as_uint(v[j]) & 0xFFFFE000u);
+    reinterpret_cast<float4*>(out + r * ldo)[c / 4] = make_float4(v[0], v[1], v[2], v[3]);
+  }
+}
+
 // ops::max_pool2d semantics (-inf init, padding skipped, strict >).
 __global__ void max_pool_nchw_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t N,
                                      int64_t C, int64_t H, int64_t W, int64_t Ho, int64_t Wo,
@@ -440,6 +469,22 @@ int launch_nchw_to_nhwc_padded(const float* x, int64_t N, int64_t C, int64_t H, 
   clear_stale_cuda_error();
   nchw_to_nhwc_kernel<<<grid, 256, 0, s>>>(x, (int)C, (int)HW, (int)Cp, vec, vec_out, y);
   return launch_check("nchw_to_nhwc");
+}
+
+int launch_tf32_lo(const float* b, int64_t rows, int64_t cols, int64_t ldb, float* out,
+                   int64_t ldo, cudaStream_t s) {
+  if (rows <= 0 || cols <= 0 || ldo < cols || ldo % 4 != 0 ||
+      (reinterpret_cast<uintptr_t>(out) & 15u) != 0)
+    return set_error(RTB_E_INVALID, "tf32_lo: bad arguments");
+  const int vec = (ldb % 4 == 0) && (reinterpret_cast<uintptr_t>(b) & 15u) == 0;
+  const int64_t n = rows * (ldo / 4);
+  const int64_t blocks64 = (n + 255) / 256;
+  const unsigned blocks = (unsigned)(blocks64 < 148 * 16 ? blocks64 : 148 * 16);
+  clear_stale_cuda_error();
+  cudaError_t e = launch_pdl(tf32_lo_kernel, dim3(blocks), dim3(256), 0, s, b, rows, cols, ldb,
+                             vec, out, ldo);
+  if (e != cudaSuccess) return cuda_status(e, "tf32_lo launch");
+  return launch_check("tf32_lo");
 }
 
 int launch_conv_prologue(const float* x, int64_t N, int64_t C, int64_t H, int64_t W, int64_t Cp,

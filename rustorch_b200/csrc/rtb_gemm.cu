@@ -14,16 +14,17 @@ namespace rtb {
 // parallel.
 template <int BN>
 int launch_bn(rtb_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB,
-              const CUtensorMap& tmC, const GemmParams& p, const GemmDesc& d, cudaStream_t s);
+              const CUtensorMap& tmBlo, const CUtensorMap& tmC, const GemmParams& p,
+              const GemmDesc& d, cudaStream_t s);
 extern template int launch_bn<64>(rtb_ctx*, const CUtensorMap&, const CUtensorMap&,
-                                  const CUtensorMap&, const GemmParams&, const GemmDesc&,
-                                  cudaStream_t);
+                                  const CUtensorMap&, const CUtensorMap&, const GemmParams&,
+                                  const GemmDesc&, cudaStream_t);
 extern template int launch_bn<128>(rtb_ctx*, const CUtensorMap&, const CUtensorMap&,
-                                   const CUtensorMap&, const GemmParams&, const GemmDesc&,
-                                   cudaStream_t);
+                                   const CUtensorMap&, const CUtensorMap&, const GemmParams&,
+                                   const GemmDesc&, cudaStream_t);
 extern template int launch_bn<256>(rtb_ctx*, const CUtensorMap&, const CUtensorMap&,
-                                   const CUtensorMap&, const GemmParams&, const GemmDesc&,
-                                   cudaStream_t);
+                                   const CUtensorMap&, const CUtensorMap&, const GemmParams&,
+                                   const GemmDesc&, cudaStream_t);
 
 namespace {
 
@@ -133,6 +134,14 @@ SplitPlan plan_split(int64_t tiles, int num_kb, int64_t G, int bn) {
 
 }  // namespace
 
+// The tensor core truncates fp32 operands to TF32 (pinned by a GPU test), so
+// the raw tile already is the 3xTF32 "hi" part; RTB_SPLIT_TRUNC=0 selects the
+// round-to-nearest hi written back in place instead.
+static bool trunc_split_enabled() {
+  static const int trunc_env = env_int("RTB_SPLIT_TRUNC", 1);
+  return trunc_env != 0;
+}
+
 int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
   if (d.M <= 0 || d.N <= 0 || d.K <= 0) return set_error(RTB_E_INVALID, "gemm_run: empty problem");
   if (d.M > INT32_MAX || d.N > INT32_MAX || d.K > INT32_MAX)
@@ -201,11 +210,7 @@ int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
   // off unless RTB_PREFETCH_KB asks for it.
   static const int pf_env = env_int("RTB_PREFETCH_KB", 0);
   p.prefetch_kb = pf_env > 0 ? pf_env : 0;
-  // The tensor core truncates fp32 operands to TF32 (pinned by a GPU test), so
-  // the raw tile already is the "hi" part; RTB_SPLIT_TRUNC=0 selects the
-  // round-to-nearest hi written back in place instead.
-  static const int trunc_env = env_int("RTB_SPLIT_TRUNC", 1);
-  p.split_trunc = trunc_env != 0;
+  p.split_trunc = trunc_split_enabled();
   p.tiles_m = (int)((d.M + kBM - 1) / kBM);
   p.tiles_n = (int)((d.N + bn - 1) / bn);
   // Raster: consecutive tiles walk down group_m M-tiles, then across N
@@ -303,13 +308,54 @@ int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
     p.trace = (ctx->trace && ctx->trace_capacity >= grid * kTraceSlots) ? ctx->trace : nullptr;
   }
 
+  // 3xTF32 tiles with a B_lo slot in the ring stage: B's low part
+  // (B - trunc_tf32(B), a property of B alone) computed once per call by a
+  // prepass and brought in by TMA beside B, instead of by the converter warps
+  // of every CTA that reads the B tile (once per M-tile).  Measured on B200
+  // (4096^3): converters 714 -> 341 clocks per k-block, mainloop 1219 -> 970.
+  // The prepass is one more launch the GEMM waits for, so it is left to the
+  // converters below 16 M-tiles (1024^3: 85 -> 70 TFLOP/s with it), and when
+  // no workspace may be allocated.
+  static const int blo_env = env_int("RTB_BLO_PREPASS", -1);
+  const bool blo_slot = d.split3 && (bn == 64 || (bn == 128 && d.gather != 3));
+  const bool want_blo = blo_env >= 0 ? blo_env != 0 : tiles_m64 >= 16;
+  CUtensorMap tmBlo = tmB;
+  void* blo_ws = nullptr;
+  if (blo_slot && want_blo && d.allow_workspace && trunc_split_enabled()) {
+    const int64_t rows = d.b_mn_major ? d.K : d.N;
+    const int64_t cols = d.b_mn_major ? d.N : d.K;
+    const int64_t ldo = (cols + 3) & ~int64_t(3);
+    st = ws_alloc(ctx, &blo_ws, (size_t)(rows * ldo) * sizeof(float), stream);
+    if (st != RTB_OK) {
+      ws_free(split_ws, stream);
+      return st;
+    }
+    float* blo = static_cast<float*>(blo_ws);
+    st = launch_tf32_lo(d.B, rows, cols, d.ldb, blo, ldo, stream);
+    if (st == RTB_OK) {
+      if (d.b_mn_major)
+        st = make_tmap_2d(&tmBlo, blo, (uint64_t)d.N, (uint64_t)d.K, (uint64_t)ldo, 32, kBK, true);
+      else
+        st = make_tmap_2d(&tmBlo, blo, (uint64_t)d.K, (uint64_t)d.N, (uint64_t)ldo, kBK,
+                          (uint32_t)bn, false);
+    }
+    if (st != RTB_OK) {
+      ws_free(blo_ws, stream);
+      ws_free(split_ws, stream);
+      return st;
+    }
+  }
+  p.blo_tma = blo_ws != nullptr;
+
+
   switch (bn) {
-    case 64: st = launch_bn<64>(ctx, tmA, tmB, tmC, p, d, stream); break;
-    case 128: st = launch_bn<128>(ctx, tmA, tmB, tmC, p, d, stream); break;
-    case 256: st = launch_bn<256>(ctx, tmA, tmB, tmC, p, d, stream); break;
+    case 64: st = launch_bn<64>(ctx, tmA, tmB, tmBlo, tmC, p, d, stream); break;
+    case 128: st = launch_bn<128>(ctx, tmA, tmB, tmBlo, tmC, p, d, stream); break;
+    case 256: st = launch_bn<256>(ctx, tmA, tmB, tmBlo, tmC, p, d, stream); break;
     default: st = set_error(RTB_E_INVALID, "gemm_run: bad tile width");
   }
   ws_free(split_ws, stream);
+  ws_free(blo_ws, stream);
   return st;
 }
 

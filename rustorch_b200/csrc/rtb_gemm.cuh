@@ -97,6 +97,9 @@ struct GemmParams {
   float* ws;             // [tail tile][piece][BN/32][8][128] float4
   unsigned long long* ws_cnt;  // [tail tile] arrival words (generation << 8 | count)
   unsigned long long cnt_gen;  // this launch's generation (older tags count as zero)
+  // 3xTF32 wide tiles: B's low part arrives by TMA (tmBlo, B's layout) in the
+  // ring stage's B_lo slot, and the converters leave B alone
+  int blo_tma;
 };
 
 struct WorkUnit {
@@ -137,26 +140,45 @@ __device__ __forceinline__ void trace_stamp(const GemmParams& p, int slot) {
   if (p.trace) p.trace[(size_t)blockIdx.x * kTraceSlots + slot] = globaltimer_ns();
 }
 
-template <int BN, bool SPLIT>
+// Shared-memory read bandwidth (about 128 B per clock per SM on B200) is
+// shared by the tensor core's operand reads and the warps' ld.shared, so the
+// 3xTF32 mainloop keeps A's hi and lo parts in TMEM (the MMAs read only B
+// and B_lo from shared memory) and the converters read each raw A tile once.
+// Per 128-column k-block: 48 KB of operand reads + 16 KB of converter reads
+// (+ 16 KB more when the converters also make B's low part), about 500-625
+// clocks against the 768 clocks of MMAs.
+//
+// BLO (3xTF32 with the A tile in the 128B-swizzled K-major layout, i.e. every
+// producer but the multi-tap im2col): B's low part has a slot in every ring
+// stage, right after the raw B tile, so it can arrive by TMA from a copy
+// computed once per call (B - trunc_tf32(B) is a property of B alone) instead
+// of being recomputed by the converters of every CTA that reads the B tile.
+// (A 128-column tile could then also issue hi . [B | B_lo] as one N=256 MMA,
+// but its 256-column partial leaves TMEM room for one partial buffer only,
+// and the MMAs idling while the epilogue drains it cost more than the third
+// instruction per k-step: three N=128 MMAs, double-buffered partials.)
+template <int BN, bool SPLIT, bool BLO = false>
 struct GemmCfg {
   static constexpr int kBBytes = BN * kBK * 4;
-  // TMEM: two partial-sum buffers (double buffering); with 3xTF32 one fp32
-  // running sum the epilogue warps promote the partials into, then a ring of
-  // kAStages converted k-blocks: A's 32-column hi and lo parts in TMEM, B's
-  // low part in a shared-memory slot (the MMAs read only B from smem).
-  // Wide mode (3xTF32 with BN = 64): B's low part sits right after the raw B
-  // tile in the ring stage, so hi_A . [B | B_lo] is ONE N=128 MMA (partial
-  // columns [0,64) = hi.hi, [64,128) = hi.lo) and lo_A . B one N=64 MMA: two
-  // tensor-core instructions per k-step instead of three (an N=64 MMA costs
-  // about as long as an N=128 one); the epilogue adds the two halves.
+  // TMEM: the partial-sum buffer(s); with 3xTF32 one fp32 running sum the
+  // epilogue warps promote the partials into, then a ring of kAStages
+  // converted k-blocks: A's 32-column hi and lo parts.
+  // Wide mode: B's low part sits right after the raw B tile in the ring
+  // stage, so hi_A . [B | B_lo] is ONE MMA of twice the tile width (partial
+  // columns [0,BN) = hi.hi, [BN,2BN) = hi.lo) and lo_A . B one MMA of the
+  // tile width: two tensor-core instructions per k-step instead of three; the
+  // epilogue adds the two halves.  Otherwise B's low part has its own
+  // shared-memory plane of kAStages slots.
+  static_assert(!BLO || SPLIT, "BLO is a 3xTF32 layout");
   static constexpr bool kWide = SPLIT && BN == 64;
   static constexpr int kAccW = kWide ? 2 * BN : BN;  // TMEM columns of one partial buffer
   static constexpr int kAccCols = 2 * kAccW + (SPLIT ? BN : 0);
   static constexpr int kAStagesRaw = SPLIT ? (512 - kAccCols) / (2 * kBK) : 0;
   static constexpr int kAStages = kAStagesRaw > 4 ? 4 : kAStagesRaw;
-  static constexpr int kBStage = kWide ? 2 * kBBytes : kBBytes;  // B slot of a ring stage
-  static constexpr int kBloBytes = (SPLIT && !kWide) ? kAStages * kBBytes : 0;
-  // Load ring stage: the raw A and B tiles (TMA) (+ B's low part in wide mode).
+  static constexpr bool kBloInStage = kWide || BLO;
+  static constexpr int kBStage = kBloInStage ? 2 * kBBytes : kBBytes;  // B slot of a ring stage
+  static constexpr int kBloBytes = (SPLIT && !kBloInStage) ? kAStages * kBBytes : 0;
+  // Load ring stage: the raw A and B tiles (TMA) (+ B's low part).
   static constexpr int kStageBytes = kABytes + kBStage;
   // Epilogue staging: two 16 KB chunks alternate, unless dropping one gives
   // the load ring another stage.
@@ -177,6 +199,12 @@ struct GemmCfg {
   static_assert(BN == 64 || BN == 128 || BN == 256, "BN must be 64, 128 or 256");
 };
 
+// The configuration a kernel variant uses: B_lo in the ring stage for every
+// 3xTF32 producer whose A tile is in the swizzled K-major layout (all but the
+// multi-tap im2col, whose tiles the converters read in their own layout).
+template <int BN, bool SPLIT, int A_MODE>
+using GemmCfgFor = GemmCfg<BN, SPLIT, SPLIT && A_MODE != 3>;
+
 template <bool SPLIT, bool GATHER>
 struct GemmRoles {  // GATHER: the cp.async im2col producer warps are present
   static constexpr int kWarpTma = 0;
@@ -184,7 +212,9 @@ struct GemmRoles {  // GATHER: the cp.async im2col producer warps are present
   static constexpr int kWarpEpi = 2;                        // 4 warps
   static constexpr int kWarpConv = 6;                       // 4 warps if SPLIT
   static constexpr int kWarpGather = 6 + (SPLIT ? 4 : 0);   // 4 warps if GATHER
-  static constexpr int kWarps = 6 + (SPLIT ? 4 : 0) + (GATHER ? 4 : 0);
+  // second TMA producer (alternate k-blocks with warp 0)
+  static constexpr int kWarpTma2 = 6 + (SPLIT ? 4 : 0) + (GATHER ? 4 : 0);
+  static constexpr int kWarps = kWarpTma2 + 1;
   static constexpr int kThreads = kWarps * 32;
 };
 
@@ -431,12 +461,13 @@ __device__ __forceinline__ void epilogue_nchw_chunk(const GemmParams& p, uint32_
 template <int BN, bool SPLIT, int A_MODE, int B_MN>
 __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
     rtb_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmBlo,
                     const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
   constexpr bool GATHER = (A_MODE == 1);
   constexpr bool IM2COL = (A_MODE == 2 || A_MODE == 3);
   constexpr bool MULTITAP = (A_MODE == 3);
   static_assert(!MULTITAP || SPLIT, "multi-tap im2col tiles are read by the 3xTF32 converters");
-  using Cfg = GemmCfg<BN, SPLIT>;
+  using Cfg = GemmCfgFor<BN, SPLIT, A_MODE>;
   using Roles = GemmRoles<SPLIT, GATHER>;
   constexpr int S = Cfg::kStages;
   constexpr int kBBytes = Cfg::kBBytes;
@@ -446,8 +477,8 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
                                              ~uintptr_t(1023));
   constexpr int kAS = SPLIT ? Cfg::kAStages : 1;
   uint8_t* sA = base;                                  // S x 16 KB
-  uint8_t* sB = sA + S * kABytes;                      // S x kBStage (BN*128, wide: x2)
-  uint8_t* sBlo = sB + S * Cfg::kBStage;               // SPLIT, not wide: kAS x BN*128
+  uint8_t* sB = sA + S * kABytes;                      // S x kBStage (BN*128, + B's low part)
+  uint8_t* sBlo = sB + S * Cfg::kBStage;               // SPLIT, B_lo not in the stage: kAS x BN*128
   uint8_t* sOut = sBlo + Cfg::kBloBytes;               // kOutBufs x 16 KB epilogue staging
   uint8_t* tail = sOut + Cfg::kOutBytes;
   float* sBias = reinterpret_cast<float*>(tail);         // epilogue: the tile's BN bias values
@@ -456,8 +487,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
   uint64_t* empty_bar = conv_bar + kAS;
   uint64_t* tfull_bar = empty_bar + S;
   uint64_t* tempty_bar = tfull_bar + 2;
-  uint64_t* aempty_bar = tempty_bar + 2;  // SPLIT: TMEM A stage consumed by the MMAs
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aempty_bar + kAS);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* fix_flag = abort_flag + 1;  // epilogue: this CTA sums a split tile
   volatile int* epi_vote = abort_flag + 2;  // epilogue: per-warp wait outcome (4 ints)
@@ -478,10 +508,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
       mbar_init(&tfull_bar[b], 1);
       mbar_init(&tempty_bar[b], 128);
     }
-    for (int j = 0; j < kAS; ++j) {
-      mbar_init(&conv_bar[j], 128);
-      mbar_init(&aempty_bar[j], 1);
-    }
+    for (int j = 0; j < kAS; ++j) mbar_init(&conv_bar[j], 128);
     *abort_flag = 0;
     pend[0] = 0;
     fence_mbar_init();
@@ -489,6 +516,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
   if (warp == Roles::kWarpTma && lane == 0) {
     if (!GATHER) tma_prefetch_desc(&tmA);  // tiled or im2col map
     tma_prefetch_desc(&tmB);
+    if (p.blo_tma) tma_prefetch_desc(&tmBlo);
     if (p.c_tma) tma_prefetch_desc(&tmC);
   }
   if (warp == Roles::kWarpMma) {
@@ -506,12 +534,17 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
   griddep_launch_dependents();
   if (threadIdx.x == 0) trace_stamp(p, 0);
 
-  if (warp == Roles::kWarpTma) {
-    // ------------------------------------------------------------ TMA producer
+  if (warp == Roles::kWarpTma || warp == Roles::kWarpTma2) {
+    // ------------------------------------------------------------ TMA producers
+    // Lane 0 of two warps takes alternate k-blocks of the CTA's sequence: one
+    // thread's wait + issue round trip (about 0.2 us on B200, whatever the box
+    // size) would cap the ring's fill rate near 10 TB/s over 148 SMs.
     if (lane == 0) {
+      const int pidx = warp == Roles::kWarpTma ? 0 : 1;
+      int q = 0;  // k-block sequence number of this CTA
       int s = 0;
       uint32_t ph = 0;
-      const uint32_t tx = (GATHER ? 0 : kABytes) + kBBytes;
+      const uint32_t tx = (GATHER ? 0 : kABytes) + kBBytes * (p.blo_tma ? 2 : 1);
       const int HoWo = p.Ho * p.Wo;
       for (int w = blockIdx.x; w < p.num_units && !*abort_flag; w += gridDim.x) {
         const WorkUnit u = work_unit(p, w);
@@ -528,7 +561,11 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
           a_w = (rem - oh * p.Wo) * p.sw - p.pw;
         }
         const int tj = (w - (int)blockIdx.x) / (int)gridDim.x;
-        for (int kb = u.kb0; kb < u.kb1; ++kb) {
+        for (int kb = u.kb0; kb < u.kb1; ++kb, ++q) {
+          if ((q & 1) != pidx) {  // the other producer's k-block
+            if (++s == S) { s = 0; ph ^= 1; }
+            continue;
+          }
           if (!mbar_wait_bounded(&empty_bar[s], ph ^ 1, abort_flag, p.err, DEV_TIMEOUT_EMPTY,
                                  p.timeout_ns))
             break;
@@ -542,7 +579,9 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
             ntaps = ntaps < tpk ? ntaps : tpk;
           }
           mbar_arrive_expect_tx(&full_bar[s],
-                                MULTITAP ? (uint32_t)(ntaps * kBM * p.Cp * 4 + kBBytes) : tx);
+                                MULTITAP ? (uint32_t)(ntaps * kBM * p.Cp * 4 + kBBytes *
+                                                      (p.blo_tma ? 2 : 1))
+                                         : tx);
           // Warm L2 for a k-block `prefetch_kb` ahead (hides DRAM latency beyond
           // what the shared-memory ring can cover).
           const int kp = kb + p.prefetch_kb;
@@ -576,13 +615,17 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
             tma_load_im2col_4d(sA + s * kABytes, &tmA, &full_bar[s], c0, a_w, a_h, a_n,
                                (uint16_t)ss, (uint16_t)rr);
           }
-          if (B_MN == 0) {
-            tma_load_2d(sB + s * Cfg::kBStage, &tmB, &full_bar[s], kb * kBK, tn * BN);
-          } else {
+          // B, then (blo_tma) its low part into the stage's B_lo slot
+          for (int part = 0; part < (Cfg::kBloInStage && p.blo_tma ? 2 : 1); ++part) {
+            const CUtensorMap* mb = part ? &tmBlo : &tmB;
+            uint8_t* dst = sB + s * Cfg::kBStage + part * kBBytes;
+            if (B_MN == 0) {
+              tma_load_2d(dst, mb, &full_bar[s], kb * kBK, tn * BN);
+            } else {
 #pragma unroll
-            for (int j = 0; j < BN / 32; ++j)
-              tma_load_2d(sB + s * Cfg::kBStage + j * 4096, &tmB, &full_bar[s], tn * BN + j * 32,
-                          kb * kBK);
+              for (int j = 0; j < BN / 32; ++j)
+                tma_load_2d(dst + j * 4096, mb, &full_bar[s], tn * BN + j * 32, kb * kBK);
+            }
           }
           if (++s == S) { s = 0; ph ^= 1; }
         }
@@ -590,7 +633,14 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
     }
   } else if (warp == Roles::kWarpMma) {
     // ------------------------------------------------------------ UMMA issuer
-    if (lane == 0) {
+    // The whole warp walks the schedule (operands stay warp-uniform); lane 0
+    // does the barrier waits, one elected lane issues each tcgen05 instruction.
+    {
+      auto warp_wait = [&](uint64_t* bar, uint32_t parity, int code) -> bool {
+        int got = 0;
+        if (lane == 0) got = mbar_wait_bounded(bar, parity, abort_flag, p.err, code, p.timeout_ns);
+        return __shfl_sync(0xffffffffu, got, 0) != 0;
+      };
       constexpr uint32_t idesc = umma_idesc_tf32(kBM, BN, 0, B_MN);
       constexpr uint32_t idesc_w = umma_idesc_tf32(kBM, Cfg::kWide ? 2 * BN : BN, 0, B_MN);
       int s = 0;
@@ -605,8 +655,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
         for (int kb0 = u.kb0; kb0 < u.kb1 && ok; kb0 += p.kb_per_acc, ++g) {
           const int b = g & 1;
           const uint32_t use = (uint32_t)(g >> 1);
-          if (!mbar_wait_bounded(&tempty_bar[b], (use & 1) ^ 1, abort_flag, p.err,
-                                 DEV_TIMEOUT_TMEM_EMPTY, p.timeout_ns)) {
+          if (!warp_wait(&tempty_bar[b], (use & 1) ^ 1, DEV_TIMEOUT_TMEM_EMPTY)) {
             ok = false;
             break;
           }
@@ -615,12 +664,12 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
           const int kend = (kb0 + p.kb_per_acc) < u.kb1 ? (kb0 + p.kb_per_acc) : u.kb1;
           for (int kb = kb0; kb < kend; ++kb) {
             uint64_t* ready = SPLIT ? &conv_bar[ja] : &full_bar[s];
-            if (!mbar_wait_bounded(ready, SPLIT ? pa : ph, abort_flag, p.err,
-                                   SPLIT ? DEV_TIMEOUT_CONV : DEV_TIMEOUT_FULL, p.timeout_ns)) {
+            if (!warp_wait(ready, SPLIT ? pa : ph,
+                           SPLIT ? DEV_TIMEOUT_CONV : DEV_TIMEOUT_FULL)) {
               ok = false;
               break;
             }
-            if (kb == u.kb0 && tj < kTraceTiles) trace_stamp(p, 3 + 6 * tj);
+            if (lane == 0 && kb == u.kb0 && tj < kTraceTiles) trace_stamp(p, 3 + 6 * tj);
             tc_fence_after();
             // cp.async-gathered A (TF32 mode has no converter pass): make the
             // generic-proxy writes visible to the tensor core's async proxy.
@@ -628,7 +677,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
             const uint32_t a_addr = smem_u32(sA + s * kABytes);
             const uint32_t b_addr = smem_u32(sB + s * Cfg::kBStage);
             const uint32_t blo_addr =
-                Cfg::kWide ? b_addr + (uint32_t)kBBytes : smem_u32(sBlo + ja * kBBytes);
+                Cfg::kBloInStage ? b_addr + (uint32_t)kBBytes : smem_u32(sBlo + ja * kBBytes);
             // 3xTF32: A's hi / lo k-block in TMEM columns (lane 0 = tile row 0)
             const uint32_t a_hi = tmem_base + (uint32_t)(Cfg::kAccCols + ja * 2 * kBK);
             const uint32_t a_lo = a_hi + (uint32_t)kBK;
@@ -642,33 +691,33 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
                             : umma_desc(b_addr + k * 1024, 4096, 512, kLayoutSW128Base32B);
               const uint32_t acc = (kb > kb0 || k > 0) ? 1u : 0u;
               if (Cfg::kWide) {
-                // one N=128 MMA over [B | B_lo] (hi.hi and hi.lo side by side),
-                // then lo.hi into the hi.hi columns
-                umma_tf32_ts(d_tmem, a_hi + k * 8, db, idesc_w, acc);
-                umma_tf32_ts(d_tmem, a_lo + k * 8, db, idesc, 1u);
+                // one MMA of twice the tile width over [B | B_lo] (hi.hi and
+                // hi.lo side by side), then lo.hi into the hi.hi columns
+                umma_tf32_ts_e(d_tmem, a_hi + k * 8, db, idesc_w, acc);
+                umma_tf32_ts_e(d_tmem, a_lo + k * 8, db, idesc, 1u);
               } else if (SPLIT) {
                 const uint64_t dbl =
                     B_MN == 0 ? umma_desc(blo_addr + k * 32, 16, 1024, kLayoutSW128)
                               : umma_desc(blo_addr + k * 1024, 4096, 512, kLayoutSW128Base32B);
                 // small cross terms first, then hi*hi; A from TMEM (8 columns per k step)
-                umma_tf32_ts(d_tmem, a_hi + k * 8, dbl, idesc, acc);
-                umma_tf32_ts(d_tmem, a_lo + k * 8, db, idesc, 1u);
-                umma_tf32_ts(d_tmem, a_hi + k * 8, db, idesc, 1u);
+                umma_tf32_ts_e(d_tmem, a_hi + k * 8, dbl, idesc, acc);
+                umma_tf32_ts_e(d_tmem, a_lo + k * 8, db, idesc, 1u);
+                umma_tf32_ts_e(d_tmem, a_hi + k * 8, db, idesc, 1u);
               } else {
                 const uint64_t da = umma_desc(a_addr + k * 32, 16, 1024, kLayoutSW128);
-                umma_tf32(d_tmem, da, db, idesc, acc);
+                umma_tf32_e(d_tmem, da, db, idesc, acc);
               }
             }
-            umma_commit(&empty_bar[s]);
+            // one commit frees the ring stage and (3xTF32) the TMEM A stage
+            umma_commit_e(&empty_bar[s]);
             if (SPLIT) {
-              umma_commit(&aempty_bar[ja]);
               if (++ja == kAS) { ja = 0; pa ^= 1; }
             }
             if (++s == S) { s = 0; ph ^= 1; }
           }
           if (!ok) break;
-          umma_commit(&tfull_bar[b]);
-          if (kb0 + p.kb_per_acc >= u.kb1 && tj < kTraceTiles) trace_stamp(p, 4 + 6 * tj);
+          umma_commit_e(&tfull_bar[b]);
+          if (lane == 0 && kb0 + p.kb_per_acc >= u.kb1 && tj < kTraceTiles) trace_stamp(p, 4 + 6 * tj);
         }
       }
     }
@@ -879,6 +928,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
         // the last unit leaves without the running-sum round trip through
         // TMEM when holding the accumulator during the stores costs nothing
         const bool emit_now = last && (piece || w + (int)gridDim.x >= p.num_units);
+        const bool via_run = SPLIT && units > 1 && !emit_now;
         // One finished chunk: a split piece's partial to the workspace, else to C.
         auto out = [&](int c, const uint32_t (&r)[32]) {
           if (piece) {
@@ -894,30 +944,28 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
         };
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
-          uint32_t r[32];
+          // the chunk's TMEM reads (partial, its hi.lo half, the running sum)
+          // are issued together and waited for once
+          uint32_t r[32], q[32], q2[32];
           tmem_ld_32x32b_x32(t_part + (uint32_t)c, r);
+          if (Cfg::kWide) tmem_ld_32x32b_x32(t_part + (uint32_t)(BN + c), q);
+          if (SPLIT && a > 0) tmem_ld_32x32b_x32(t_run + (uint32_t)c, q2);
           tmem_ld_wait();
+          if (c + 32 == BN) {
+            tc_fence_before();
+            mbar_arrive(&tempty_bar[b]);  // partial buffer b may be overwritten now
+          }
           if (Cfg::kWide) {  // + the hi.lo half
-            uint32_t q[32];
-            tmem_ld_32x32b_x32(t_part + (uint32_t)(BN + c), q);
-            tmem_ld_wait();
 #pragma unroll
             for (int j = 0; j < 32; ++j)
               r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(q[j]));
           }
           if (SPLIT && a > 0) {
-            uint32_t q[32];
-            tmem_ld_32x32b_x32(t_run + (uint32_t)c, q);
-            tmem_ld_wait();
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-              r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(q[j]));
+              r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(q2[j]));
           }
-          if (c + 32 == BN) {
-            tc_fence_before();
-            mbar_arrive(&tempty_bar[b]);  // partial buffer b may be overwritten now
-          }
-          if (SPLIT && units > 1 && !emit_now) {
+          if (via_run) {
             // running sum; after the last unit the finished tile, which leaves
             // from there so the accumulator is not held during the stores
             tmem_st_32x32b_x32(t_run + (uint32_t)c, r);
@@ -928,8 +976,8 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
             out(c, r);
           }
         }
-        if (SPLIT && units > 1 && !emit_now) tmem_st_wait();
-        if (SPLIT && units > 1 && last && !emit_now) {
+        if (via_run) tmem_st_wait();
+        if (via_run && last) {
 #pragma unroll 1
           for (int c = 0; c < BN; c += 32) {
             uint32_t r[32];
@@ -999,17 +1047,21 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
     int s = 0;
     uint32_t ph = 0;
     int ja = 0;
-    uint32_t pa = 0;
+    int q = 0;           // k-block sequence number
+    int s_rel = 0;       // ring stage and phase parity of k-block q - kAS, whose
+    uint32_t ph_rel = 0; // MMAs (one commit) also free TMEM A stage ja
+    const bool b_conv = !(Cfg::kBloInStage && p.blo_tma);  // this warp group makes B_lo
     bool ok = true;
     for (int w = blockIdx.x; w < p.num_units && ok && !*abort_flag; w += gridDim.x) {
       const WorkUnit u = work_unit(p, w);
-      for (int kb = u.kb0; kb < u.kb1; ++kb) {
+      for (int kb = u.kb0; kb < u.kb1; ++kb, ++q) {
         // every lane waits (acquire for its own smem reads); tcgen05.st is
         // .sync.aligned, so the warp proceeds only if all lanes got through
         bool got = mbar_wait_bounded(&full_bar[s], ph, abort_flag, p.err, DEV_TIMEOUT_LOADED,
                                      p.timeout_ns);
-        got = got && mbar_wait_bounded(&aempty_bar[ja], pa ^ 1, abort_flag, p.err,
-                                       DEV_TIMEOUT_TMEM_A, p.timeout_ns);
+        if (q >= kAS)
+          got = got && mbar_wait_bounded(&empty_bar[s_rel], ph_rel, abort_flag, p.err,
+                                         DEV_TIMEOUT_TMEM_A, p.timeout_ns);
         if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           break;
@@ -1020,7 +1072,8 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
         constexpr int kBPer = kBBytes / 16 / 128;  // float4 of B per thread
         const uint32_t arow = smem_u32(sA + s * kABytes + row * 128);
         const uint32_t bb = smem_u32(sB + s * Cfg::kBStage);
-        const uint32_t blo = Cfg::kWide ? bb + (uint32_t)kBBytes : smem_u32(sBlo + ja * kBBytes);
+        const uint32_t blo =
+            Cfg::kBloInStage ? bb + (uint32_t)kBBytes : smem_u32(sBlo + ja * kBBytes);
         float4 av[8], bv[kBPer];
         if (MULTITAP) {
           // float4 q of the row = channels 4*qq.. of tap block j (dense rows of
@@ -1038,8 +1091,10 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
 #pragma unroll
           for (int j = 0; j < 8; ++j) av[j] = lds128(arow + ((j ^ (row & 7)) << 4));
         }
+        if (b_conv) {
 #pragma unroll
-        for (int i = 0; i < kBPer; ++i) bv[i] = lds128(bb + (ct + 128 * i) * 16);
+          for (int i = 0; i < kBPer; ++i) bv[i] = lds128(bb + (ct + 128 * i) * 16);
+        }
         uint32_t hi[32], lo[32];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -1059,7 +1114,8 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
         const uint32_t t_a = t_lane + (uint32_t)(Cfg::kAccCols + ja * 2 * kBK);
         tmem_st_32x32b_x32(t_a, hi);
         tmem_st_32x32b_x32(t_a + (uint32_t)kBK, lo);
-        if (p.split_trunc) {
+        if (!b_conv) {
+        } else if (p.split_trunc) {
 #pragma unroll
           for (int i = 0; i < kBPer; ++i) sts128(blo + (ct + 128 * i) * 16, tf32_trunc_rem4(bv[i]));
         } else {
@@ -1076,7 +1132,8 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
         tc_fence_before();
         mbar_arrive(&conv_bar[ja]);
         if (++s == S) { s = 0; ph ^= 1; }
-        if (++ja == kAS) { ja = 0; pa ^= 1; }
+        if (++ja == kAS) ja = 0;
+        if (q >= kAS && ++s_rel == S) { s_rel = 0; ph_rel ^= 1; }
       }
     }
   } else if (GATHER && warp >= Roles::kWarpGather && warp < Roles::kWarpGather + 4) {

@@ -5,6 +5,6 @@
 namespace rtb {
 
 template int launch_bn<256>(rtb_ctx*, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
-                            const GemmParams&, const GemmDesc&, cudaStream_t);
+                           const CUtensorMap&, const GemmParams&, const GemmDesc&, cudaStream_t);
 
 }  // namespace rtb

@@ -8,8 +8,9 @@ namespace rtb {
 
 template <int BN, bool SPLIT, int A_MODE, int B_MN>
 int launch_variant(rtb_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB,
-                   const CUtensorMap& tmC, const GemmParams& p, cudaStream_t stream) {
-  using Cfg = GemmCfg<BN, SPLIT>;
+                   const CUtensorMap& tmBlo, const CUtensorMap& tmC, const GemmParams& p,
+                   cudaStream_t stream) {
+  using Cfg = GemmCfgFor<BN, SPLIT, A_MODE>;
   using Roles = GemmRoles<SPLIT, A_MODE == 1>;
   auto kern = rtb_gemm_kernel<BN, SPLIT, A_MODE, B_MN>;
   // The attribute is per function and per device; setting it is idempotent
@@ -23,7 +24,7 @@ int launch_variant(rtb_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB,
   // its first global-memory access (griddep_wait in the kernel)
   clear_stale_cuda_error();
   e = launch_pdl(kern, dim3((unsigned)grid), dim3(Roles::kThreads), Cfg::kSmemBytes, stream, tmA,
-                 tmB, tmC, p);
+                 tmB, tmBlo, tmC, p);
   if (e != cudaSuccess) return cuda_status(e, "gemm kernel launch");
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_status(e, "gemm kernel launch");
@@ -32,23 +33,25 @@ int launch_variant(rtb_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB,
 
 template <int BN, bool SPLIT>
 int launch_prec(rtb_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB,
-                const CUtensorMap& tmC, const GemmParams& p, const GemmDesc& d, cudaStream_t s) {
-  if (d.gather == 1) return launch_variant<BN, SPLIT, 1, 0>(ctx, tmA, tmB, tmC, p, s);
-  if (d.gather == 2) return launch_variant<BN, SPLIT, 2, 0>(ctx, tmA, tmB, tmC, p, s);
+                const CUtensorMap& tmBlo, const CUtensorMap& tmC, const GemmParams& p,
+                const GemmDesc& d, cudaStream_t s) {
+  if (d.gather == 1) return launch_variant<BN, SPLIT, 1, 0>(ctx, tmA, tmB, tmBlo, tmC, p, s);
+  if (d.gather == 2) return launch_variant<BN, SPLIT, 2, 0>(ctx, tmA, tmB, tmBlo, tmC, p, s);
   if (d.gather == 3) {
-    if constexpr (SPLIT) return launch_variant<BN, SPLIT, 3, 0>(ctx, tmA, tmB, tmC, p, s);
+    if constexpr (SPLIT) return launch_variant<BN, SPLIT, 3, 0>(ctx, tmA, tmB, tmBlo, tmC, p, s);
     else return set_error(RTB_E_INVALID, "multi-tap im2col needs the 3xTF32 converters");
   }
-  if (d.b_mn_major) return launch_variant<BN, SPLIT, 0, 1>(ctx, tmA, tmB, tmC, p, s);
-  return launch_variant<BN, SPLIT, 0, 0>(ctx, tmA, tmB, tmC, p, s);
+  if (d.b_mn_major) return launch_variant<BN, SPLIT, 0, 1>(ctx, tmA, tmB, tmBlo, tmC, p, s);
+  return launch_variant<BN, SPLIT, 0, 0>(ctx, tmA, tmB, tmBlo, tmC, p, s);
 }
 
 template <int BN>
 int launch_bn(rtb_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB,
-              const CUtensorMap& tmC, const GemmParams& p, const GemmDesc& d, cudaStream_t s) {
-  if (!d.split3) return launch_prec<BN, false>(ctx, tmA, tmB, tmC, p, d, s);
+              const CUtensorMap& tmBlo, const CUtensorMap& tmC, const GemmParams& p,
+              const GemmDesc& d, cudaStream_t s) {
+  if (!d.split3) return launch_prec<BN, false>(ctx, tmA, tmB, tmBlo, tmC, p, d, s);
   if constexpr (BN <= 128) {
-    return launch_prec<BN, true>(ctx, tmA, tmB, tmC, p, d, s);
+    return launch_prec<BN, true>(ctx, tmA, tmB, tmBlo, tmC, p, d, s);
   } else {
     return set_error(RTB_E_INVALID, "3xTF32 tiles are at most 128 columns wide");
   }

@@ -143,6 +143,10 @@ int launch_prepack_weight(const float* w, int64_t Co, int64_t Ci, int64_t kh, in
                           int64_t Cp, float* wp, cudaStream_t s);
 // NCHW -> NHWC (channels padded to Cp) of x and the weight prepack of
 // launch_prepack_weight in one launch (two launches when Cp == 4).
+// out[r][c] = B[r][c] - trunc_tf32(B[r][c]) over rows x cols (row stride ldb),
+// padding columns [cols, ldo) zeroed; ldo % 4 == 0, out 16-byte aligned.
+int launch_tf32_lo(const float* b, int64_t rows, int64_t cols, int64_t ldb, float* out,
+                   int64_t ldo, cudaStream_t s);
 int launch_conv_prologue(const float* x, int64_t N, int64_t C, int64_t H, int64_t W, int64_t Cp,
                          float* y, const float* w, int64_t Co, int64_t kh, int64_t kw, float* wp,
                          cudaStream_t s);
