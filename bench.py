@@ -60,7 +60,7 @@ TRAFFIC = {
     "conv": (13.52e6, "profiles/conv2d_bias_relu_r50s2_3x3.md"),
     "conv_r50s4": (12.77e6, "profiles/kernel_counters_gemm_conv.md"),
     "gemm1024": (8.49e6, "profiles/kernel_counters_gemm_conv.md"),
-    "gemm8192": (3.617e9, "profiles/sgemm_8192_3xtf32.md"),
+    "gemm8192": (5.228e9, "profiles/sgemm_8192_3xtf32.md"),
     "gemm_m16": (272.7e6, "profiles/sgemm_small_m16_8192.md"),
     "gemm_m256": (280.6e6, "profiles/kernel_counters_gemm_conv.md"),
     "mlp": (665.2e6, "profiles/kernel_counters_gemm_conv.md"),
@@ -69,12 +69,11 @@ TRAFFIC = {
 # Tensor-pipe activity of each workload's dominant kernel(s) as ncu counts it
 # (sm__pipe_tensor_cycles_active, % of elapsed cycles), from the named capture.
 TENSOR_PIPE = {
-    "resnet18": (0.389, "profiles/resnet18_fwd_launches.md"),
+    "resnet18": (0.456, "profiles/resnet18_fwd_launches.md"),
     "conv": (0.340, "profiles/conv2d_bias_relu_r50s2_3x3.md"),
     "conv_r50s4": (0.248, "profiles/kernel_counters_gemm_conv.md"),
     "gemm1024": (0.185, "profiles/kernel_counters_gemm_conv.md"),
-    "gemm8192": (0.566, "profiles/sgemm_8192_3xtf32.md"),
-    "gemm8192:tf32": (0.535, "profiles/sgemm_8192_3xtf32.md"),
+    "gemm8192": (0.747, "profiles/sgemm_8192_3xtf32.md"),
     "gemm_m256": (0.455, "profiles/kernel_counters_gemm_conv.md"),
     "mlp": (0.526, "profiles/kernel_counters_gemm_conv.md"),
     "linear_norm": (0.564, "profiles/linear_norm_relu_8192x1024x4096.md"),

@@ -156,15 +156,17 @@ int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
   if (can_split && num_kb64 <= INT32_MAX) {
     plan = plan_split(plan.full, (int)num_kb64, ctx->sm_count, bn);
     // 3xTF32 with the tile width left open: 128 and 64 columns compared under
-    // their schedules, at the measured k-block times of the two modes (B200:
-    // 0.77 us per 128-column k-block, 0.67 us per 64-column one in the wide
-    // mode, which does half the work)
+    // their schedules, at the measured k-block times of the two modes (B200,
+    // 4096^3 forced to each width: 0.70 us per 128-column k-block, 0.47 us per
+    // 64-column one in the wide mode, which does half the work; 1024^3 then
+    // runs as one wave of 64-column tiles, 92 TFLOP/s, instead of 128-column
+    // tiles cut in two K pieces, 77)
     if (d.split3 && !d.bn && std::getenv("RTB_GEMM_BN") == nullptr && d.N > 64) {
       const int alt = bn == 128 ? 64 : 128;
       const int64_t tiles_alt = tiles_m64 * ((d.N + alt - 1) / alt);
       const SplitPlan pa = plan_split(tiles_alt, (int)num_kb64, ctx->sm_count, alt);
-      const double t_cur = plan.cost * (bn == 128 ? 0.77 : 0.67);
-      const double t_alt = pa.cost * (alt == 128 ? 0.77 : 0.67);
+      const double t_cur = plan.cost * (bn == 128 ? 0.70 : 0.47);
+      const double t_alt = pa.cost * (alt == 128 ? 0.70 : 0.47);
       if (t_alt < t_cur * 0.97) {
         bn = alt;
         plan = pa;
