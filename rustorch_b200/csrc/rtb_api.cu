@@ -104,7 +104,7 @@ static EncodeIm2colFn get_encode_im2col() {
 
 int make_tmap_im2col(CUtensorMap* map, const void* x, int N, int H, int W, int Cp, int R, int S,
                      int sh, int sw, int ph, int pw, uint32_t channels_per_pixel,
-                     uint32_t pixels_per_column, bool swizzle128) {
+                     uint32_t pixels_per_column, int swizzle_bytes) {
   EncodeIm2colFn enc = get_encode_im2col();
   if (!enc) return set_error(RTB_E_CUDA, "cuTensorMapEncodeIm2col unavailable");
   if ((reinterpret_cast<uintptr_t>(x) & 15u) != 0 || (Cp * 4) % 16 != 0)
@@ -120,7 +120,10 @@ int make_tmap_im2col(CUtensorMap* map, const void* x, int N, int H, int W, int C
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void*>(x), dims, strides,
                    lower, upper, channels_per_pixel, pixels_per_column, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                   swizzle_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                   : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                   : swizzle_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                         : CU_TENSOR_MAP_SWIZZLE_NONE,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     char buf[160];

@@ -181,10 +181,15 @@ int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
     st = make_tmap_2d(&tmA, d.B, (uint64_t)d.K, (uint64_t)d.N, (uint64_t)d.ldb, kBK, 64, false);
   } else if (d.gather == 2) {
     st = make_tmap_im2col(&tmA, d.x, d.Nimg, d.H, d.W, d.Cp, d.R, d.S, d.sh, d.sw, d.ph, d.pw,
-                          kBK, kBM, true);
-  } else if (d.gather == 3) {  // one dense [128 pixels][Cp] box per filter tap
+                          kBK, kBM, 128);
+  } else if (d.gather == 3) {
+    // one [128 pixels][Cp] box per filter tap, its Cp*4-byte rows swizzled
+    // over their own width (the converters' reads of one 16-byte chunk of
+    // 32 consecutive rows then spread over all banks; dense 64-byte rows
+    // collide 16 ways)
+    const int swz = (d.Cp * 4 == 32 || d.Cp * 4 == 64) ? d.Cp * 4 : 0;
     st = make_tmap_im2col(&tmA, d.x, d.Nimg, d.H, d.W, d.Cp, d.R, d.S, d.sh, d.sw, d.ph, d.pw,
-                          (uint32_t)d.Cp, kBM, false);
+                          (uint32_t)d.Cp, kBM, swz);
   } else {
     st = make_tmap_2d(&tmA, d.A, (uint64_t)d.K, (uint64_t)d.M, (uint64_t)d.lda, kBK, kBM, false);
   }

@@ -1078,14 +1078,19 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
         if (MULTITAP) {
           // float4 q of the row = channels 4*qq.. of tap block j (dense rows of
           // Cp floats); k-block columns past K = R*S*Cp are zero
+          // rows of Cp = 8 / 16 channels arrive with the 32 / 64-byte TMA
+          // swizzle: 16-byte chunk c of row r sits at c ^ ((r * Cp * 4) >> 7)
+          // within the row (address bits 4-5 XOR bits 7-8)
           const int l = p.Cp == 4 ? 0 : (p.Cp == 8 ? 1 : 2);  // log2(Cp / 4)
+          const int mask = (1 << l) - 1;
+          const int swz = ((row * p.Cp * 4) >> 7) & mask;
           const uint32_t a0 = smem_u32(sA + s * kABytes) + row * p.Cp * 4;
           const int kvalid = p.R * p.S * p.Cp - kb * kBK;
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
             av[q] = make_float4(0.f, 0.f, 0.f, 0.f);
             if (4 * q < kvalid)
-              av[q] = lds128(a0 + (q >> l) * (kBM * p.Cp * 4) + (q & ((1 << l) - 1)) * 16);
+              av[q] = lds128(a0 + (q >> l) * (kBM * p.Cp * 4) + (((q & mask) ^ swz) << 4));
           }
         } else {
 #pragma unroll

@@ -82,10 +82,11 @@ int make_tmap_2d_swz(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t
 
 // 4-D im2col map over an NHWC tensor [N, H, W, Cp] for a forward conv with
 // filter R x S, stride (sh, sw), padding (ph, pw): channels_per_pixel x
-// pixels_per_column boxes, 128-byte swizzle or dense rows.
+// pixels_per_column boxes, rows swizzled in 16-byte units over swizzle_bytes
+// (128, 64 or 32; 0 = dense rows).
 int make_tmap_im2col(CUtensorMap* map, const void* x, int N, int H, int W, int Cp, int R, int S,
                      int sh, int sw, int ph, int pw, uint32_t channels_per_pixel,
-                     uint32_t pixels_per_column, bool swizzle128);
+                     uint32_t pixels_per_column, int swizzle_bytes);
 
 // What the GEMM engine computes; see rtb_gemm.cuh (GemmParams) for the epilogue.
 struct GemmDesc {
