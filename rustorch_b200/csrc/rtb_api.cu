@@ -635,7 +635,7 @@ int rtb_conv2d_prepack_weight(rtb_ctx* ctx, int64_t Co, int64_t Ci, int64_t kh, 
   if (Co <= 0 || Ci <= 0 || kh <= 0 || kw <= 0 || !w || !w_packed)
     return set_error(RTB_E_INVALID, "prepack: bad arguments");
   DeviceGuard g(ctx->device);
-  return launch_prepack_weight(w, Co, Ci, kh, kw, round_up(Ci, 4), w_packed,
+  return launch_prepack_weight(w, Co, Ci, kh, kw, round_up(Ci, 4), w_packed, nullptr,
                                pick_stream(ctx, stream));
 }
 
@@ -667,7 +667,8 @@ static int conv_core(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, 
                      int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw,
                      int64_t Ho, int64_t Wo, const float* x_nhwc, const float* wp,
                      const float* bias, const float* residual, int act, float* y, int y_layout,
-                     int split3, cudaStream_t s, bool allow_workspace = true) {
+                     int split3, cudaStream_t s, bool allow_workspace = true,
+                     const float* wlo = nullptr) {
   const int64_t Cp = round_up(Ci, 4);
   const int64_t M = N * Ho * Wo;
   if (M == 0) return RTB_OK;
@@ -676,6 +677,7 @@ static int conv_core(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, 
   GemmDesc d;
   d.M = M; d.N = Co; d.K = kh * kw * Cp;
   d.B = wp; d.ldb = d.K; d.b_mn_major = 0;
+  d.B_lo = wlo;
   d.C = y; d.bias = bias; d.residual = residual; d.act = act;
   if (y_layout == RTB_LAYOUT_NHWC) {
     d.out_mode = 0; d.ldc = Co; d.ldr = Co;
@@ -788,39 +790,46 @@ int rtb_conv2d_fwd(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, in
       kw >= 2 && s2d_env && std::getenv("RTB_CONV_GATHER") == nullptr) {
     const int64_t kh2 = (kh + 1) / 2, kw2 = (kw + 1) / 2;
     const int64_t Hs = Ho + kh2 - 1, Ws = Wo + kw2 - 1;
-    st = ws_alloc(ctx, (void**)&ws, (size_t)(Co * kh2 * kw2 * 16) * 4, s);
+    // the packed weight and its 3xTF32 low part, written by the prologue
+    const int64_t wsz = Co * kh2 * kw2 * 16;
+    st = ws_alloc(ctx, (void**)&ws, (size_t)(2 * wsz) * 4, s);
     if (st) return st;
     st = ws_alloc(ctx, (void**)&xs, (size_t)(N * Hs * Ws * 16) * 4, s);
     if (st == RTB_OK)
-      st = launch_conv_prologue_s2d(x, N, Ci, H, W, ph, pw, Hs, Ws, xs, w, Co, kh, kw, ws, s);
+      st = launch_conv_prologue_s2d(x, N, Ci, H, W, ph, pw, Hs, Ws, xs, w, Co, kh, kw, ws,
+                                    ws + wsz, s);
     if (st == RTB_OK)
       st = conv_core(ctx, N, 16, Hs, Ws, Co, kh2, kw2, 1, 1, 0, 0, Ho, Wo, xs, ws, bias, residual,
-                     act, y, y_layout, split3, s);
+                     act, y, y_layout, split3, s, true, ws + wsz);
     ws_free(xs, s);
     ws_free(ws, s);
     return st;
   }
-  st = ws_alloc(ctx, (void**)&ws, (size_t)rtb_conv2d_packed_weight_size(Co, Ci, kh, kw) * 4, s);
+  // the packed weight, and (3xTF32) its low part: the prologue writes both, so
+  // the GEMM needs no separate low-part pass
+  const int64_t wsz = rtb_conv2d_packed_weight_size(Co, Ci, kh, kw);
+  st = ws_alloc(ctx, (void**)&ws, (size_t)((split3 ? 2 : 1) * wsz) * 4, s);
   if (st) return st;
+  float* wlo = split3 ? ws + wsz : nullptr;
   if (x_layout == RTB_LAYOUT_NCHW || Cp != Ci || !aligned16(x)) {
     st = ws_alloc(ctx, (void**)&xs, (size_t)(N * H * W * Cp) * 4, s);
     if (st == RTB_OK) {
       if (x_layout == RTB_LAYOUT_NCHW) {
         // layout change and weight repack in one launch
-        st = launch_conv_prologue(x, N, Ci, H, W, Cp, xs, w, Co, kh, kw, ws, s);
+        st = launch_conv_prologue(x, N, Ci, H, W, Cp, xs, w, Co, kh, kw, ws, wlo, s);
       } else {
         // NHWC with Ci % 4 != 0 or unaligned: repack rows of Ci into rows of Cp.
         st = launch_pack_kmajor(x, N * H * W, Ci, Ci, 1, xs, Cp, s);
-        if (st == RTB_OK) st = launch_prepack_weight(w, Co, Ci, kh, kw, Cp, ws, s);
+        if (st == RTB_OK) st = launch_prepack_weight(w, Co, Ci, kh, kw, Cp, ws, wlo, s);
       }
     }
     xin = xs;
   } else {
-    st = launch_prepack_weight(w, Co, Ci, kh, kw, Cp, ws, s);
+    st = launch_prepack_weight(w, Co, Ci, kh, kw, Cp, ws, wlo, s);
   }
   if (st == RTB_OK)
     st = conv_core(ctx, N, Ci, H, W, Co, kh, kw, sh, sw, ph, pw, Ho, Wo, xin, ws, bias, residual,
-                   act, y, y_layout, split3, s);
+                   act, y, y_layout, split3, s, true, wlo);
   ws_free(xs, s);
   ws_free(ws, s);
   return st;

@@ -167,33 +167,48 @@ __global__ void nhwc_to_nchw_kernel(const float* __restrict__ x, int64_t C, int6
 // into shared memory (when they fit), then written in (tap, ci) order.
 constexpr int kPrepackSmemFloats = 12288;  // 48 KB
 // Output channel co's weights; `sw` is kPrepackSmemFloats floats of shared memory.
+// The 3xTF32 low part of a weight value: x - trunc_tf32(x) (the tensor core
+// reads the raw value as its truncated TF32 hi part).
+__device__ __forceinline__ float tf32_lo(float x) {
+  return x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+}
+
+// Co row `co` of the packed weight; wlo (nullable) receives its 3xTF32 low part
+// in the same layout.
 __device__ __forceinline__ void prepack_weight_block(const float* __restrict__ w, int Ci, int taps,
                                                      int Cp, float* __restrict__ wp, int co,
-                                                     float* sw, int sw_floats) {
+                                                     float* sw, int sw_floats,
+                                                     float* __restrict__ wlo) {
   const int n_in = Ci * taps;
   const float* src = w + (int64_t)co * n_in;
   float* dst = wp + (int64_t)co * taps * Cp;
+  float* dlo = wlo ? wlo + (int64_t)co * taps * Cp : nullptr;
   const int Kw = taps * Cp;
   if (n_in <= sw_floats) {
     for (int i = threadIdx.x; i < n_in; i += blockDim.x) sw[i] = __ldg(src + i);
     __syncthreads();
     for (int k = threadIdx.x; k < Kw; k += blockDim.x) {
       const int tap = k / Cp, ci = k - tap * Cp;
-      dst[k] = ci < Ci ? sw[ci * taps + tap] : 0.0f;
+      const float v = ci < Ci ? sw[ci * taps + tap] : 0.0f;
+      dst[k] = v;
+      if (dlo) dlo[k] = tf32_lo(v);
     }
   } else {
     for (int k = threadIdx.x; k < Kw; k += blockDim.x) {
       const int tap = k / Cp, ci = k - tap * Cp;
-      dst[k] = ci < Ci ? __ldg(src + ci * taps + tap) : 0.0f;
+      const float v = ci < Ci ? __ldg(src + ci * taps + tap) : 0.0f;
+      dst[k] = v;
+      if (dlo) dlo[k] = tf32_lo(v);
     }
   }
 }
 
 __global__ void __launch_bounds__(256) prepack_weight_kernel(const float* __restrict__ w, int Ci,
                                                               int taps, int Cp,
-                                                              float* __restrict__ wp) {
+                                                              float* __restrict__ wp,
+                                                              float* __restrict__ wlo) {
   __shared__ float sw[kPrepackSmemFloats];
-  prepack_weight_block(w, Ci, taps, Cp, wp, blockIdx.x, sw, kPrepackSmemFloats);
+  prepack_weight_block(w, Ci, taps, Cp, wp, blockIdx.x, sw, kPrepackSmemFloats, wlo);
 }
 
 // A conv call's two input repacks in one launch: blocks [0, n_tiles) move
@@ -206,7 +221,7 @@ constexpr int kPrologueSmemFloats = 32 * (kT2Pix + 1);
 __global__ void __launch_bounds__(256) conv_prologue_kernel(
     const float* __restrict__ x, int C, int HW, int Cp, int vec, int vec_out,
     float* __restrict__ y, int tiles_p, int tiles_c, int64_t n_tiles,
-    const float* __restrict__ w, int taps, float* __restrict__ wp) {
+    const float* __restrict__ w, int taps, float* __restrict__ wp, float* __restrict__ wlo) {
   __shared__ __align__(16) float buf[kPrologueSmemFloats];
   griddep_wait();  // launched with programmatic stream serialization
   griddep_launch_dependents();
@@ -219,7 +234,7 @@ __global__ void __launch_bounds__(256) conv_prologue_kernel(
     nchw_to_nhwc_tile(x, C, HW, Cp, vec, vec_out, y, p_t, c_t, n,
                       reinterpret_cast<float (*)[kT2Pix + 1]>(buf));
   } else {
-    prepack_weight_block(w, C, taps, Cp, wp, (int)(b - n_tiles), buf, kPrologueSmemFloats);
+    prepack_weight_block(w, C, taps, Cp, wp, (int)(b - n_tiles), buf, kPrologueSmemFloats, wlo);
   }
 }
 
@@ -489,13 +504,13 @@ int launch_tf32_lo(const float* b, int64_t rows, int64_t cols, int64_t ldb, floa
 
 int launch_conv_prologue(const float* x, int64_t N, int64_t C, int64_t H, int64_t W, int64_t Cp,
                          float* y, const float* w, int64_t Co, int64_t kh, int64_t kw, float* wp,
-                         cudaStream_t s) {
+                         float* wlo, cudaStream_t s) {
   const int64_t HW = H * W, taps = kh * kw;
   if (Cp == 4 || HW > INT32_MAX || C > INT32_MAX || Cp > INT32_MAX || Co > INT32_MAX ||
       C * taps > INT32_MAX || taps * Cp > INT32_MAX) {
     // small-channel inputs keep their own transform kernel
     int st = launch_nchw_to_nhwc_padded(x, N, C, H, W, Cp, y, s);
-    return st ? st : launch_prepack_weight(w, Co, C, kh, kw, Cp, wp, s);
+    return st ? st : launch_prepack_weight(w, Co, C, kh, kw, Cp, wp, wlo, s);
   }
   const int tiles_p = (int)((HW + kT2Pix - 1) / kT2Pix);
   const int tiles_c = (int)((Cp + 31) / 32);
@@ -507,7 +522,7 @@ int launch_conv_prologue(const float* x, int64_t N, int64_t C, int64_t H, int64_
   clear_stale_cuda_error();
   cudaError_t e = launch_pdl(conv_prologue_kernel, dim3((unsigned)blocks), dim3(256), 0, s, x,
                              (int)C, (int)HW, (int)Cp, vec, vec_out, y, tiles_p, tiles_c, n_tiles,
-                             w, (int)taps, wp);
+                             w, (int)taps, wp, wlo);
   if (e != cudaSuccess) return cuda_status(e, "conv prologue launch");
   return launch_check("conv prologue");
 }
@@ -523,7 +538,7 @@ int launch_conv_prologue(const float* x, int64_t N, int64_t C, int64_t H, int64_
 __global__ void __launch_bounds__(256) conv_prologue_s2d_kernel(
     const float* __restrict__ x, int C, int H, int W, int ph, int pw, int Hs, int Ws,
     int64_t npix, int64_t pix_blocks, float4* __restrict__ y, const float* __restrict__ w,
-    int kh, int kw, int kh2, int kw2, float* __restrict__ w2) {
+    int kh, int kw, int kh2, int kw2, float* __restrict__ w2, float* __restrict__ w2lo) {
   griddep_wait();  // launched with programmatic stream serialization
   griddep_launch_dependents();
   const int64_t b = blockIdx.x;
@@ -553,8 +568,10 @@ __global__ void __launch_bounds__(256) conv_prologue_s2d_kernel(
       const int tap = k >> 4, j = k & 15;
       const int R = tap / kw2, S = tap - R * kw2;
       const int r = 2 * R + (j >> 3), sc = 2 * S + ((j >> 2) & 1), c = j & 3;
-      w2[(int64_t)co * n_out + k] =
+      const float v =
           (r < kh && sc < kw && c < C) ? __ldg(w + (((int64_t)co * C + c) * kh + r) * kw + sc) : 0.0f;
+      w2[(int64_t)co * n_out + k] = v;
+      if (w2lo) w2lo[(int64_t)co * n_out + k] = tf32_lo(v);
     }
   }
 }
@@ -562,7 +579,7 @@ __global__ void __launch_bounds__(256) conv_prologue_s2d_kernel(
 int launch_conv_prologue_s2d(const float* x, int64_t N, int64_t C, int64_t H, int64_t W,
                              int64_t ph, int64_t pw, int64_t Hs, int64_t Ws, float* y,
                              const float* w, int64_t Co, int64_t kh, int64_t kw, float* w2,
-                             cudaStream_t s) {
+                             float* w2lo, cudaStream_t s) {
   const int64_t npix = N * Hs * Ws;
   const int64_t pix_blocks = (npix + 255) / 256;
   if (C > 4 || H * W > INT32_MAX || Hs * Ws > INT32_MAX || pix_blocks + Co > INT32_MAX ||
@@ -572,7 +589,7 @@ int launch_conv_prologue_s2d(const float* x, int64_t N, int64_t C, int64_t H, in
   cudaError_t e = launch_pdl(conv_prologue_s2d_kernel, dim3((unsigned)(pix_blocks + Co)), dim3(256),
                              0, s, x, (int)C, (int)H, (int)W, (int)ph, (int)pw, (int)Hs, (int)Ws,
                              npix, pix_blocks, reinterpret_cast<float4*>(y), w, (int)kh, (int)kw,
-                             (int)((kh + 1) / 2), (int)((kw + 1) / 2), w2);
+                             (int)((kh + 1) / 2), (int)((kw + 1) / 2), w2, w2lo);
   if (e != cudaSuccess) return cuda_status(e, "conv s2d prologue launch");
   return launch_check("conv s2d prologue");
 }
@@ -587,12 +604,12 @@ int launch_nhwc_to_nchw(const float* x, float* y, int64_t N, int64_t C, int64_t 
 }
 
 int launch_prepack_weight(const float* w, int64_t Co, int64_t Ci, int64_t kh, int64_t kw,
-                          int64_t Cp, float* wp, cudaStream_t s) {
+                          int64_t Cp, float* wp, float* wlo, cudaStream_t s) {
   const int64_t taps = kh * kw;
   if (Co > INT32_MAX || Ci * taps > INT32_MAX || taps * Cp > INT32_MAX)
     return set_error(RTB_E_UNSUPPORTED, "prepack_weight: too large");
   clear_stale_cuda_error();
-  prepack_weight_kernel<<<(unsigned)Co, 256, 0, s>>>(w, (int)Ci, (int)taps, (int)Cp, wp);
+  prepack_weight_kernel<<<(unsigned)Co, 256, 0, s>>>(w, (int)Ci, (int)taps, (int)Cp, wp, wlo);
   return launch_check("prepack_weight");
 }
 

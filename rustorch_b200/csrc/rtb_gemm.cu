@@ -328,7 +328,20 @@ int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
   const bool want_blo = blo_env >= 0 ? blo_env != 0 : tiles_m64 >= 16;
   CUtensorMap tmBlo = tmB;
   void* blo_ws = nullptr;
-  if (blo_slot && want_blo && d.allow_workspace && trunc_split_enabled()) {
+  bool blo_given = false;
+  if (blo_slot && d.B_lo && trunc_split_enabled() && blo_env != 0) {
+    // computed by the caller (a weight pack): B's layout and row stride
+    if (d.b_mn_major)
+      st = make_tmap_2d(&tmBlo, d.B_lo, (uint64_t)d.N, (uint64_t)d.K, (uint64_t)d.ldb, 32, kBK, true);
+    else
+      st = make_tmap_2d(&tmBlo, d.B_lo, (uint64_t)d.K, (uint64_t)d.N, (uint64_t)d.ldb, kBK,
+                        (uint32_t)bn, false);
+    if (st != RTB_OK) {
+      ws_free(split_ws, stream);
+      return st;
+    }
+    blo_given = true;
+  } else if (blo_slot && want_blo && d.allow_workspace && trunc_split_enabled()) {
     const int64_t rows = d.b_mn_major ? d.K : d.N;
     const int64_t cols = d.b_mn_major ? d.N : d.K;
     const int64_t ldo = (cols + 3) & ~int64_t(3);
@@ -352,7 +365,7 @@ int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
       return st;
     }
   }
-  p.blo_tma = blo_ws != nullptr;
+  p.blo_tma = blo_given || blo_ws != nullptr;
 
 
   switch (bn) {

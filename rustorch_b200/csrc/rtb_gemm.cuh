@@ -744,7 +744,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
           tma_store_2d(&tmC, stg, n0, tm * kBM);
           bulk_commit_group();
           // the buffer used next is free again
-          if (Cfg::kOutBufs == 2) bulk_wait_group_read<1>(); else bulk_wait_group_read<0>();
+          bulk_wait_group_read<Cfg::kOutBufs - 1>();
         }
         named_bar_sync(1, 128);
         ++chunk;
@@ -926,9 +926,13 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
         }
         const uint32_t t_part = t_lane + (uint32_t)(b * Cfg::kAccW);
         // the last unit leaves without the running-sum round trip through
-        // TMEM when holding the accumulator during the stores costs nothing
+        // TMEM when holding the accumulator during the stores costs nothing;
+        // otherwise (single-unit tiles too) the partial moves to the running
+        // sum and is released before any store: the stem's 8-k-block tiles
+        // waited ~2800 clocks per tile for a partial held through a chunk's
+        // stores
         const bool emit_now = last && (piece || w + (int)gridDim.x >= p.num_units);
-        const bool via_run = SPLIT && units > 1 && !emit_now;
+        const bool via_run = SPLIT && !emit_now;
         // One finished chunk: a split piece's partial to the workspace, else to C.
         auto out = [&](int c, const uint32_t (&r)[32]) {
           if (piece) {

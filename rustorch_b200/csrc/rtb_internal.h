@@ -117,6 +117,9 @@ struct GemmDesc {
   const float* x = nullptr;
   int Nimg = 0;
   int H = 0, W = 0, Cp = 0, Ho = 0, Wo = 0, R = 0, S = 0, sh = 1, sw = 1, ph = 0, pw = 0;
+  // optional: B's 3xTF32 low part (B - trunc_tf32(B)) in B's layout and ldb,
+  // computed by the caller (e.g. with a weight pack); null = gemm_run decides
+  const float* B_lo = nullptr;
   int split3 = 1;     // 3xTF32 (1) or TF32 (0)
   int bn = 0;         // 0 = heuristic
   int allow_workspace = 1;  // 0: never allocate (tail balancing off)
@@ -140,8 +143,10 @@ int launch_fill_rows(float* C, int64_t M, int64_t N, int64_t ldc, const float* b
                      cudaStream_t s);
 int launch_nchw_to_nhwc_padded(const float* x, int64_t N, int64_t C, int64_t H, int64_t W,
                                int64_t Cp, float* y, cudaStream_t s);
+// w [Co, Ci, kh, kw] -> wp [Co, kh*kw*Cp] (channels padded to Cp); wlo
+// (nullable) receives wp's 3xTF32 low part in the same layout.
 int launch_prepack_weight(const float* w, int64_t Co, int64_t Ci, int64_t kh, int64_t kw,
-                          int64_t Cp, float* wp, cudaStream_t s);
+                          int64_t Cp, float* wp, float* wlo, cudaStream_t s);
 // NCHW -> NHWC (channels padded to Cp) of x and the weight prepack of
 // launch_prepack_weight in one launch (two launches when Cp == 4).
 // out[r][c] = B[r][c] - trunc_tf32(B[r][c]) over rows x cols (row stride ldb),
@@ -150,14 +155,14 @@ int launch_tf32_lo(const float* b, int64_t rows, int64_t cols, int64_t ldb, floa
                    int64_t ldo, cudaStream_t s);
 int launch_conv_prologue(const float* x, int64_t N, int64_t C, int64_t H, int64_t W, int64_t Cp,
                          float* y, const float* w, int64_t Co, int64_t kh, int64_t kw, float* wp,
-                         cudaStream_t s);
+                         float* wlo, cudaStream_t s);
 // Stride-2 conv over <= 4 input channels as a stride-1 conv of its space-to-
 // depth form: NCHW x -> NHWC [N, Hs, Ws, 16] (padding applied) and w [Co, C,
 // kh, kw] -> [Co, ceil(kh/2)*ceil(kw/2), 16], in one launch.
 int launch_conv_prologue_s2d(const float* x, int64_t N, int64_t C, int64_t H, int64_t W,
                              int64_t ph, int64_t pw, int64_t Hs, int64_t Ws, float* y,
                              const float* w, int64_t Co, int64_t kh, int64_t kw, float* w2,
-                             cudaStream_t s);
+                             float* w2lo, cudaStream_t s);
 int launch_max_pool2d(const float* x, float* y, int64_t N, int64_t C, int64_t H, int64_t W,
                       int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw,
                       int layout, cudaStream_t s);

@@ -144,7 +144,7 @@ int rtb_conv2d_fwd_noalloc(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64
                                      : rtb::launch_pack_kmajor(x, N * H * W, Ci, Ci, 1, xs, Cp, s);
     if (st) return st;
   }
-  st = rtb::launch_prepack_weight(w, Co, Ci, kh, kw, Cp, wp, s);
+  st = rtb::launch_prepack_weight(w, Co, Ci, kh, kw, Cp, wp, nullptr, s);
   if (st) return st;
   return rtb::conv2d_fwd_packed_noalloc(ctx, N, Ci, H, W, Co, kh, kw, sh, sw, ph, pw,
                                         x_direct ? x : xs, wp, bias, residual, act, y, y_layout,
