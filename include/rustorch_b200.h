@@ -195,6 +195,21 @@ int rtb_conv2d_fwd_packed(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_
                           const float* x_nhwc_padded, const float* w_packed, const float* bias,
                           const float* residual, int act, float* y, int y_layout, int precision,
                           void* stream);
+/* Extension (no counterpart in the reference, whose f32 conv has no 3xTF32
+ * split): the packed weight as rtb_conv2d_prepack_weight writes it, plus its
+ * 3xTF32 low part w_lo[i] = w_packed[i] - trunc_tf32(w_packed[i]) (same size
+ * and layout, 16-byte aligned).  A weight reused across calls keeps both, and
+ * rtb_conv2d_fwd_packed_lo then reads w_lo instead of computing it per call. */
+int rtb_conv2d_prepack_weight_lo(rtb_ctx* ctx, int64_t Co, int64_t Ci, int64_t kh, int64_t kw,
+                                 const float* w, float* w_packed, float* w_lo, void* stream);
+/* rtb_conv2d_fwd_packed with the weight's low part from
+ * rtb_conv2d_prepack_weight_lo (null: as rtb_conv2d_fwd_packed); the same
+ * results, one pass over the weight fewer per 3xTF32 call. */
+int rtb_conv2d_fwd_packed_lo(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, int64_t Co,
+                             int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw,
+                             const float* x_nhwc_padded, const float* w_packed, const float* w_lo,
+                             const float* bias, const float* residual, int act, float* y,
+                             int y_layout, int precision, void* stream);
 /* rtb_conv2d_fwd for callers that cannot allocate device memory (no
  * counterpart in the reference: RusTorch's CPU conv allocates freely).  Same
  * arguments and results as rtb_conv2d_fwd, but the scratch it needs (the

@@ -73,6 +73,8 @@ SIGNATURES = {
     "rtb_conv2d_packed_weight_size": (_i64, [_i64] * 4),
     "rtb_conv2d_prepack_weight": (_i, [_p, _i64, _i64, _i64, _i64, _p, _p, _p]),
     "rtb_conv2d_fwd_packed": (_i, [_p] + [_i64] * 11 + [_p, _p, _p, _p, _i, _p, _i, _i, _p]),
+    "rtb_conv2d_prepack_weight_lo": (_i, [_p, _i64, _i64, _i64, _i64, _p, _p, _p, _p]),
+    "rtb_conv2d_fwd_packed_lo": (_i, [_p] + [_i64] * 11 + [_p, _p, _p, _p, _p, _i, _p, _i, _i, _p]),
     "rtb_nchw_to_nhwc_padded": (_i, [_p, _i64, _i64, _i64, _i64, _p, _p, _p]),
     "rtb_max_pool2d": (_i, [_p] + [_i64] * 10 + [_p, _p, _i, _p]),
     "rtb_global_avg_pool": (_i, [_p] + [_i64] * 4 + [_p, _p, _i, _p]),

@@ -639,6 +639,16 @@ int rtb_conv2d_prepack_weight(rtb_ctx* ctx, int64_t Co, int64_t Ci, int64_t kh, 
                                pick_stream(ctx, stream));
 }
 
+int rtb_conv2d_prepack_weight_lo(rtb_ctx* ctx, int64_t Co, int64_t Ci, int64_t kh, int64_t kw,
+                                 const float* w, float* w_packed, float* w_lo, void* stream) {
+  RTB_CHECK_CTX(ctx);
+  if (Co <= 0 || Ci <= 0 || kh <= 0 || kw <= 0 || !w || !w_packed || !w_lo)
+    return set_error(RTB_E_INVALID, "prepack: bad arguments");
+  DeviceGuard g(ctx->device);
+  return launch_prepack_weight(w, Co, Ci, kh, kw, round_up(Ci, 4), w_packed, w_lo,
+                               pick_stream(ctx, stream));
+}
+
 int rtb_nchw_to_nhwc_padded(rtb_ctx* ctx, int64_t N, int64_t C, int64_t H, int64_t W,
                             const float* x, float* y, void* stream) {
   RTB_CHECK_CTX(ctx);
@@ -711,14 +721,14 @@ static int conv_packed_impl(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int6
                             int64_t ph, int64_t pw, const float* x_nhwc_padded,
                             const float* w_packed, const float* bias, const float* residual,
                             int act, float* y, int y_layout, int precision, void* stream,
-                            bool allow_workspace) {
+                            bool allow_workspace, const float* w_lo = nullptr) {
   RTB_CHECK_CTX(ctx);
   int64_t Ho, Wo;
   int st = conv_check(N, Ci, H, W, Co, kh, kw, sh, sw, ph, pw, &Ho, &Wo);
   if (st) return st;
   if (N == 0) return RTB_OK;
   if (!x_nhwc_padded || !w_packed || !y) return set_error(RTB_E_INVALID, "conv: null pointer");
-  if (!aligned16(x_nhwc_padded) || !aligned16(w_packed))
+  if (!aligned16(x_nhwc_padded) || !aligned16(w_packed) || (w_lo && !aligned16(w_lo)))
     return set_error(RTB_E_INVALID, "conv: packed input/weight must be 16-byte aligned");
   if (y_layout != RTB_LAYOUT_NCHW && y_layout != RTB_LAYOUT_NHWC)
     return set_error(RTB_E_INVALID, "conv: bad y_layout");
@@ -728,7 +738,7 @@ static int conv_packed_impl(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int6
   DeviceGuard g(ctx->device);
   return conv_core(ctx, N, Ci, H, W, Co, kh, kw, sh, sw, ph, pw, Ho, Wo, x_nhwc_padded, w_packed,
                    bias, residual, act, y, y_layout, split3, pick_stream(ctx, stream),
-                   allow_workspace);
+                   allow_workspace, split3 ? w_lo : nullptr);
 }
 
 }  // extern "C"
@@ -753,6 +763,15 @@ int rtb_conv2d_fwd_packed(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_
                           void* stream) {
   return conv_packed_impl(ctx, N, Ci, H, W, Co, kh, kw, sh, sw, ph, pw, x_nhwc_padded, w_packed,
                           bias, residual, act, y, y_layout, precision, stream, true);
+}
+
+int rtb_conv2d_fwd_packed_lo(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, int64_t Co,
+                             int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw,
+                             const float* x_nhwc_padded, const float* w_packed, const float* w_lo,
+                             const float* bias, const float* residual, int act, float* y,
+                             int y_layout, int precision, void* stream) {
+  return conv_packed_impl(ctx, N, Ci, H, W, Co, kh, kw, sh, sw, ph, pw, x_nhwc_padded, w_packed,
+                          bias, residual, act, y, y_layout, precision, stream, true, w_lo);
 }
 
 int rtb_conv2d_fwd(rtb_ctx* ctx, int64_t N, int64_t Ci, int64_t H, int64_t W, int64_t Co,

@@ -758,6 +758,7 @@ struct ResNet18::Impl {
   std::vector<ConvSpec> specs;
   std::vector<Tensor> w, b;    // folded conv weights [Co,Ci,k,k] / bias [Co] (device)
   std::vector<Tensor> wp;      // prepacked weights [Co, k*k*Cp] (device)
+  std::vector<Tensor> wlo;     // their 3xTF32 low parts, same layout (device)
   Tensor fc_w, fc_b;           // [1000,512], [1000] (device)
   int64_t cap_batch = 0;
   Tensor bufA, bufB, bufC, bufD, pooled;  // NHWC activation buffers
@@ -791,11 +792,13 @@ ResNet18::ResNet18(uint64_t seed, int device, int prec) : impl_(new Impl) {
     const int64_t n = rtb_conv2d_packed_weight_size((int64_t)c.co, (int64_t)c.ci, (int64_t)c.k,
                                                     (int64_t)c.k);
     Tensor packed = Tensor::empty({(size_t)n}, d);
-    chk(rtb_conv2d_prepack_weight(context(device), (int64_t)c.co, (int64_t)c.ci, (int64_t)c.k,
-                                  (int64_t)c.k, I.w.back().device_ptr(), packed.device_ptr(),
-                                  nullptr),
+    Tensor lo = Tensor::empty({(size_t)n}, d);
+    chk(rtb_conv2d_prepack_weight_lo(context(device), (int64_t)c.co, (int64_t)c.ci, (int64_t)c.k,
+                                     (int64_t)c.k, I.w.back().device_ptr(), packed.device_ptr(),
+                                     lo.device_ptr(), nullptr),
         "prepack");
     I.wp.push_back(packed);
+    I.wlo.push_back(lo);
   }
   const float k = 1.0f / std::sqrt(512.0f);
   I.fc_w = Tensor::uniform({1000, 512}, seed, 100, -k, k, d);
@@ -856,11 +859,11 @@ void ResNet18::forward_device(int64_t B, const float* x_nchw, float* logits, voi
   auto conv = [&](size_t i, const float* x, int64_t H, int64_t W, float* y, const float* res,
                   bool relu) {
     const auto& c = I.specs[i];
-    chk(rtb_conv2d_fwd_packed(ctx, B, (int64_t)c.ci, H, W, (int64_t)c.co, (int64_t)c.k,
-                              (int64_t)c.k, (int64_t)c.s, (int64_t)c.s, (int64_t)c.p,
-                              (int64_t)c.p, x, I.wp[i].device_ptr(), I.b[i].device_ptr(), res,
-                              relu ? RTB_ACT_RELU : RTB_ACT_NONE, y, RTB_LAYOUT_NHWC, I.prec,
-                              stream),
+    chk(rtb_conv2d_fwd_packed_lo(ctx, B, (int64_t)c.ci, H, W, (int64_t)c.co, (int64_t)c.k,
+                                 (int64_t)c.k, (int64_t)c.s, (int64_t)c.s, (int64_t)c.p,
+                                 (int64_t)c.p, x, I.wp[i].device_ptr(), I.wlo[i].device_ptr(),
+                                 I.b[i].device_ptr(), res, relu ? RTB_ACT_RELU : RTB_ACT_NONE, y,
+                                 RTB_LAYOUT_NHWC, I.prec, stream),
         "resnet conv");
     return (H + 2 * (int64_t)c.p - (int64_t)c.k) / (int64_t)c.s + 1;
   };
