@@ -57,30 +57,30 @@ L2_BYTES = 126 * 1024 * 1024
 # its command are summarised in the named profiles/ file.
 TRAFFIC = {
     "resnet18": (5.061e9, "profiles/resnet18_fwd_launches.md"),
-    "conv": (13.52e6, "profiles/conv2d_bias_relu_r50s2_3x3.md"),
-    "conv_r50s4": (12.77e6, "profiles/kernel_counters_gemm_conv.md"),
-    "gemm1024": (8.49e6, "profiles/kernel_counters_gemm_conv.md"),
+    "conv": (14.16e6, "profiles/conv2d_bias_relu_r50s2_3x3.md"),
+    "conv_r50s4": (22.20e6, "profiles/kernel_counters_gemm_conv.md"),
+    "gemm1024": (8.48e6, "profiles/kernel_counters_gemm_conv.md"),
     "gemm8192": (5.228e9, "profiles/sgemm_8192_3xtf32.md"),
     "gemm_m16": (272.7e6, "profiles/sgemm_small_m16_8192.md"),
     "gemm_m256": (280.6e6, "profiles/kernel_counters_gemm_conv.md"),
-    "mlp": (665.2e6, "profiles/kernel_counters_gemm_conv.md"),
-    "linear_norm": (154.7e6, "profiles/linear_norm_relu_8192x1024x4096.md"),
+    "mlp": (910.7e6, "profiles/kernel_counters_gemm_conv.md"),
+    "linear_norm": (208.1e6, "profiles/linear_norm_relu_8192x1024x4096.md"),
 }
 # Tensor-pipe activity of each workload's dominant kernel(s) as ncu counts it
 # (sm__pipe_tensor_cycles_active, % of elapsed cycles), from the named capture.
 TENSOR_PIPE = {
     "resnet18": (0.456, "profiles/resnet18_fwd_launches.md"),
-    "conv": (0.340, "profiles/conv2d_bias_relu_r50s2_3x3.md"),
-    "conv_r50s4": (0.248, "profiles/kernel_counters_gemm_conv.md"),
-    "gemm1024": (0.185, "profiles/kernel_counters_gemm_conv.md"),
+    "conv": (0.338, "profiles/conv2d_bias_relu_r50s2_3x3.md"),
+    "conv_r50s4": (0.302, "profiles/kernel_counters_gemm_conv.md"),
+    "gemm1024": (0.2015, "profiles/kernel_counters_gemm_conv.md"),
     "gemm8192": (0.747, "profiles/sgemm_8192_3xtf32.md"),
-    "gemm_m256": (0.455, "profiles/kernel_counters_gemm_conv.md"),
-    "mlp": (0.526, "profiles/kernel_counters_gemm_conv.md"),
-    "linear_norm": (0.564, "profiles/linear_norm_relu_8192x1024x4096.md"),
+    "gemm_m256": (0.504, "profiles/kernel_counters_gemm_conv.md"),
+    "mlp": (0.677, "profiles/kernel_counters_gemm_conv.md"),
+    "linear_norm": (0.685, "profiles/linear_norm_relu_8192x1024x4096.md"),
 }
 # DRAM bytes per launch of a workload's second kernel (roofline.secondary)
 TRAFFIC_SECONDARY = {
-    "linear_norm": (211.1e6, "profiles/linear_norm_relu_8192x1024x4096.md"),
+    "linear_norm": (211.2e6, "profiles/linear_norm_relu_8192x1024x4096.md"),
 }
 PRECISION = [0]  # rtb precision enum used by every workload call (0 = 3xTF32, 1 = TF32)
 MMAS_PER_MAC = [3]
