@@ -43,6 +43,7 @@
 namespace rtb {
 
 constexpr int kBM = 128;
+constexpr uint32_t kConvSleepNs = 64;  // converters' back-off between barrier tests
 constexpr int kBK = 32;                      // fp32 elements per k-block (128 B)
 constexpr int kABytes = kBM * kBK * 4;       // 16 KB
 constexpr int kSmemLimit = 232448;           // 227 KB dynamic shared memory per CTA
@@ -648,6 +649,11 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
       int g = 0;  // accumulation-unit counter (selects the TMEM partial buffer)
       int ja = 0;  // converted-k-block ring slot (3xTF32)
       uint32_t pa = 0;
+      // Lane 0: the next k-block's ready barrier tested complete halfway
+      // through this k-block's MMAs.  A wait on a complete barrier still costs
+      // the MMA warp ~200 clocks of shared-memory latency in the loaded kernel
+      // (B200 trace), which the test hides behind the MMA issue.
+      int next_ready = 0;
       bool ok = true;
       for (int w = blockIdx.x; w < p.num_units && ok && !*abort_flag; w += gridDim.x) {
         const WorkUnit u = work_unit(p, w);
@@ -664,11 +670,21 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
           const int kend = (kb0 + p.kb_per_acc) < u.kb1 ? (kb0 + p.kb_per_acc) : u.kb1;
           for (int kb = kb0; kb < kend; ++kb) {
             uint64_t* ready = SPLIT ? &conv_bar[ja] : &full_bar[s];
-            if (!warp_wait(ready, SPLIT ? pa : ph,
-                           SPLIT ? DEV_TIMEOUT_CONV : DEV_TIMEOUT_FULL)) {
+            // the next k-block's barrier and phase (it follows this one in the
+            // ring whatever unit or tile it belongs to; its previous phase was
+            // waited for already and the one after needs this k-block's MMAs,
+            // so the parity test cannot alias)
+            const int jn = (ja + 1 == kAS) ? 0 : ja + 1;
+            const int sn = (s + 1 == S) ? 0 : s + 1;
+            uint64_t* ready_n = SPLIT ? &conv_bar[jn] : &full_bar[sn];
+            const uint32_t par_n =
+                SPLIT ? (ja + 1 == kAS ? pa ^ 1u : pa) : (s + 1 == S ? ph ^ 1u : ph);
+            if (!__shfl_sync(0xffffffffu, next_ready, 0) &&
+                !warp_wait(ready, SPLIT ? pa : ph, SPLIT ? DEV_TIMEOUT_CONV : DEV_TIMEOUT_FULL)) {
               ok = false;
               break;
             }
+            next_ready = 0;
             if (lane == 0 && kb == u.kb0 && tj < kTraceTiles) trace_stamp(p, 3 + 6 * tj);
             tc_fence_after();
             // cp.async-gathered A (TF32 mode has no converter pass): make the
@@ -683,6 +699,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
             const uint32_t a_lo = a_hi + (uint32_t)kBK;
 #pragma unroll
             for (int k = 0; k < kBK / 8; ++k) {
+              if (k == kBK / 8 - 1 && lane == 0) next_ready = mbar_test_wait(ready_n, par_n);
               // A (K-major, SW128): +32 B per 8-element k step inside the 128 B row.
               // B MN-major (SW128 with 32 B atoms): +1024 B = 8 K-rows per k step;
               // LBO = 4096 B between 32-column boxes, SBO = 512 B per 4 K-rows.
@@ -1061,11 +1078,11 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
       for (int kb = u.kb0; kb < u.kb1; ++kb, ++q) {
         // every lane waits (acquire for its own smem reads); tcgen05.st is
         // .sync.aligned, so the warp proceeds only if all lanes got through
-        bool got = mbar_wait_bounded(&full_bar[s], ph, abort_flag, p.err, DEV_TIMEOUT_LOADED,
-                                     p.timeout_ns);
+        bool got = mbar_wait_bounded_sleep(&full_bar[s], ph, abort_flag, p.err,
+                                           DEV_TIMEOUT_LOADED, p.timeout_ns, kConvSleepNs);
         if (q >= kAS)
-          got = got && mbar_wait_bounded(&empty_bar[s_rel], ph_rel, abort_flag, p.err,
-                                         DEV_TIMEOUT_TMEM_A, p.timeout_ns);
+          got = got && mbar_wait_bounded_sleep(&empty_bar[s_rel], ph_rel, abort_flag, p.err,
+                                               DEV_TIMEOUT_TMEM_A, p.timeout_ns, kConvSleepNs);
         if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           break;

@@ -67,6 +67,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test of phase `parity` of `bar` (acquire when it succeeds).
+__device__ __forceinline__ int mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return (int)ok;
+}
+
 // Bounded wait on phase `parity` of `bar`.  Returns false on timeout or when
 // another thread of the CTA has already aborted (abort flag in shared memory);
 // on timeout records `code` in *err and raises the abort flag.
@@ -79,6 +92,31 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((++spins & 63u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > timeout_ns) {
+        if (err) atomicCAS(err, 0, code);
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+
+// The same wait for threads that are usually early (the converters, a k-block
+// or more ahead of the MMAs): after each unsuccessful test the thread sleeps
+// `sleep_ns`, so a warp group of early waiters does not keep the barrier unit
+// busy while the MMA warp's own waits go through it.
+__device__ __forceinline__ bool mbar_wait_bounded_sleep(uint64_t* bar, uint32_t parity,
+                                                        volatile int* abort_flag, int* err,
+                                                        int code, uint64_t timeout_ns,
+                                                        uint32_t sleep_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    __nanosleep(sleep_ns);
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((++spins & 15u) == 0) {
       if (*abort_flag) return false;
       if (globaltimer_ns() - t0 > timeout_ns) {
         if (err) atomicCAS(err, 0, code);
