@@ -522,3 +522,24 @@ def test_cuda_graph_capture_and_replay(gpu, orc):
                                                      padding=1))
         assert float((y.double() - yref).norm() / yref.norm()) <= 1e-5
     assert gpu.get_context(0).device_error() == 0
+
+
+@pytest.mark.parametrize("trans_b", [False, True])
+@pytest.mark.parametrize("n,k", [(333, 517), (70, 1031), (1000, 96)])
+def test_prepass_low_part_ragged(gpu, orc, n, k, trans_b):
+    """GEMMs of >= 16 M-tiles get B's 3xTF32 low part from the once-per-call
+    prepass (TMA-loaded beside B) instead of the converters: ragged N and K
+    (the prepass pads its rows to a multiple of 4 floats), B as a [K,N]
+    matrix or as the [N,K] Linear-weight view, 128- and 64-column tiles,
+    bias + ReLU, against float64."""
+    m = 2048 + 17
+    a = orc.normal((m, k), 7, 0)
+    w = orc.normal((n, k), 7, 1) if trans_b else orc.normal((k, n), 7, 1)
+    bias = orc.uniform((n,), 7, 2, -0.5, 0.5)
+    bm = w.T if trans_b else w
+    pre = orc.matmul_f64(a, np.ascontiguousarray(bm)) + bias.astype(np.float64)
+    bd = _dev(w).t() if trans_b else _dev(w)
+    c = _host(gpu.sgemm(_dev(a), bd, bias=_dev(bias), act=gpu.ACT_RELU, precision=0))
+    ref = np.maximum(pre, 0.0)
+    assert orc.rel_frob(c, ref) <= TOL[0]
+    assert _relu_pattern_ok(c, pre)
