@@ -965,12 +965,11 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
         };
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
-          // the chunk's TMEM reads (partial, its hi.lo half, the running sum)
-          // are issued together and waited for once
-          uint32_t r[32], q[32], q2[32];
+          // the chunk's partial reads (and its hi.lo half) are issued together
+          // and waited for once; the running sum's after the partial is free
+          uint32_t r[32], q[32];
           tmem_ld_32x32b_x32(t_part + (uint32_t)c, r);
           if (Cfg::kWide) tmem_ld_32x32b_x32(t_part + (uint32_t)(BN + c), q);
-          if (SPLIT && a > 0) tmem_ld_32x32b_x32(t_run + (uint32_t)c, q2);
           tmem_ld_wait();
           if (c + 32 == BN) {
             tc_fence_before();
@@ -982,9 +981,11 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
               r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(q[j]));
           }
           if (SPLIT && a > 0) {
+            tmem_ld_32x32b_x32(t_run + (uint32_t)c, q);
+            tmem_ld_wait();
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-              r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(q2[j]));
+              r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(q[j]));
           }
           if (via_run) {
             // running sum; after the last unit the finished tile, which leaves
