@@ -69,7 +69,7 @@ TRAFFIC = {
 # Tensor-pipe activity of each workload's dominant kernel(s) as ncu counts it
 # (sm__pipe_tensor_cycles_active, % of elapsed cycles), from the named capture.
 TENSOR_PIPE = {
-    "resnet18": (0.456, "profiles/resnet18_fwd_launches.md"),
+    "resnet18": (0.485, "profiles/resnet18_fwd_launches.md"),
     "conv": (0.338, "profiles/conv2d_bias_relu_r50s2_3x3.md"),
     "conv_r50s4": (0.302, "profiles/kernel_counters_gemm_conv.md"),
     "gemm1024": (0.2015, "profiles/kernel_counters_gemm_conv.md"),
