@@ -43,7 +43,7 @@ enum {
   RTB_E_OOM = 2,         /* device or host allocation failed */
   RTB_E_CUDA = 3,        /* CUDA runtime / driver error */
   RTB_E_TIMEOUT = 4,     /* a device-side bounded wait expired */
-  RTB_E_UNSUPPORTED = 5, /* valid request this build does not implement */
+  RTB_E_UNSUPPORTED = 5, /* valid request the library does not implement */
   RTB_E_NCCL = 6         /* NCCL error */
 };
 
