@@ -18,7 +18,7 @@ Workloads (default: resnet18):
             8192/16384 N-split across the GPUs, the GEMM epilogue storing every
             tile into all ranks' C over NVLink (RTB_NSPLIT_NCCL=1: GEMM then NCCL
             all-gather instead); strong scaling: one problem per job.
-  gemm_m16, gemm_m64, gemm_m256
+  gemm_m16, gemm_m32, gemm_m64, gemm_m128, gemm_m256
             skinny f32 matmul M x 8192 x 8192, seed 4 (HBM-bound for M < 128:
             roofline in GB/s).  Replicas at N>1.
   mlp       3-layer MLP forward, batch 4096, 1024->4096->4096->1024, seed 2.  Replicas.
@@ -524,7 +524,7 @@ class ConvBwdWorkload:
 
 
 # f32 matmul shapes (M, N, K, seed): the 1024^3 workload and the large-GEMM
-# sweep (square 2048..16384, skinny M = 16/64/256 with N = K = 8192).
+# sweep (square 2048..16384, skinny M = 16/32/64/128/256 with N = K = 8192).
 GEMM_SHAPES = {
     "gemm1024": (1024, 1024, 1024, 0),
     "gemm2048": (2048, 2048, 2048, 4),
@@ -532,7 +532,9 @@ GEMM_SHAPES = {
     "gemm8192": (8192, 8192, 8192, 4),
     "gemm16384": (16384, 16384, 16384, 4),
     "gemm_m16": (16, 8192, 8192, 4),
+    "gemm_m32": (32, 8192, 8192, 4),
     "gemm_m64": (64, 8192, 8192, 4),
+    "gemm_m128": (128, 8192, 8192, 4),
     "gemm_m256": (256, 8192, 8192, 4),
 }
 

@@ -473,6 +473,45 @@ static int check_act(int act) {
   return RTB_OK;
 }
 
+// Skinny products in 3xTF32 (up to 128 rows against many columns: a small
+// batch through a large weight) run as C^T = B^T . A^T.  The 128-row tiles
+// then walk B, the large operand, 16 KB of it per k-block split once per
+// element by the converter warps (a 64-column tile of the direct form reads
+// 8 KB of B in the same k-block time, and leaves most of its 128 rows empty),
+// while A becomes the narrow B operand that stays in L2.  The transposed tile
+// leaves through the channel-major (NCHW) epilogue with the channel stride
+// set to ldc, and the caller's bias becomes a per-row bias there.
+// RTB_SKINNY_T=0 turns this off, 2 takes it wherever it is legal.
+static bool skinny_transposed(const GemmDesc& d, int64_t M, int64_t N, int64_t K, int64_t ldc) {
+  static const int env = [] {
+    const char* v = std::getenv("RTB_SKINNY_T");
+    return v ? std::atoi(v) : 1;
+  }();
+  if (env == 0 || !d.split3 || d.residual || M > 128 || ldc > INT32_MAX) return false;
+  return env == 2 || (N >= 2048 && K >= 256);
+}
+
+static GemmDesc transposed_desc(const GemmDesc& d) {
+  GemmDesc t;
+  t.M = d.N;
+  t.N = d.M;
+  t.K = d.K;
+  t.A = d.B;  // [K,N] row-major (MN-major A) or [N,K] (K-major A)
+  t.lda = d.ldb;
+  t.a_mn_major = d.b_mn_major;
+  t.B = d.A;  // A's K-major [M,K] storage is B^T's K-major [N', K] form
+  t.ldb = d.lda;
+  t.b_mn_major = 0;
+  t.C = d.C;
+  t.ldc = d.ldc;
+  t.out_mode = 1;  // element (row n', channel m) at m * hw + n' with one "image"
+  t.hw = (int)d.ldc;
+  t.row_bias = d.bias;
+  t.act = d.act;
+  t.split3 = d.split3;
+  return t;
+}
+
 // One 2-D GEMM on the current device/stream (helper for single and batched).
 // residual (optional, same indexing as C): C = act(A.B + bias + residual);
 // residual == C accumulates into C.
@@ -527,7 +566,12 @@ static int sgemm_one(rtb_ctx* ctx, int64_t M, int64_t N, int64_t K, const float*
       const char* v = std::getenv("RTB_SMALLM");
       return !(v && v[0] == '0');
     }();
-    st = (smallm_on && M <= kSmallMMax && !residual) ? smallm_run(ctx, d, s) : gemm_run(ctx, d, s);
+    if (smallm_on && M <= kSmallMMax && !residual)
+      st = smallm_run(ctx, d, s);
+    else if (skinny_transposed(d, M, N, K, ldc))
+      st = gemm_run(ctx, transposed_desc(d), s);
+    else
+      st = gemm_run(ctx, d, s);
   }
   ws_free(wsA, s);
   ws_free(wsB, s);

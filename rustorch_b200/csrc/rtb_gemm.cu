@@ -146,6 +146,10 @@ int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
   if (d.M <= 0 || d.N <= 0 || d.K <= 0) return set_error(RTB_E_INVALID, "gemm_run: empty problem");
   if (d.M > INT32_MAX || d.N > INT32_MAX || d.K > INT32_MAX)
     return set_error(RTB_E_UNSUPPORTED, "gemm_run: dimension exceeds 2^31-1");
+  if (d.a_mn_major && (!d.split3 || d.gather != 0))
+    return set_error(RTB_E_INVALID, "gemm_run: an MN-major A needs 3xTF32 and no conv producer");
+  if (d.row_bias && (d.out_mode != 1 || d.bias))
+    return set_error(RTB_E_INVALID, "gemm_run: a row bias needs the transposed output, no column bias");
   static const int tail_env = env_int("RTB_TAIL_SPLIT", 1);
   const bool can_split = tail_env && d.allow_workspace;
   const int64_t num_kb64 = (d.K + kBK - 1) / kBK;
@@ -190,6 +194,11 @@ int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
     const int swz = (d.Cp * 4 == 32 || d.Cp * 4 == 64) ? d.Cp * 4 : 0;
     st = make_tmap_im2col(&tmA, d.x, d.Nimg, d.H, d.W, d.Cp, d.R, d.S, d.sh, d.sw, d.ph, d.pw,
                           (uint32_t)d.Cp, kBM, swz);
+  } else if (d.a_mn_major) {
+    // [K, M] row-major: unswizzled [32 k][128 m] boxes (512-byte rows), read
+    // by the converters only
+    st = make_tmap_2d_swz(&tmA, d.A, (uint64_t)d.M, (uint64_t)d.K, (uint64_t)d.lda, kBM, kBK,
+                          kTmapSwizzleNone);
   } else {
     st = make_tmap_2d(&tmA, d.A, (uint64_t)d.K, (uint64_t)d.M, (uint64_t)d.lda, kBK, kBM, false);
   }
@@ -213,8 +222,9 @@ int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
   // 1.0e-5), against the 1e-5 bound.
   static const int kb_acc_env = env_int("RTB_KB_PER_ACC", 0);
   p.kb_per_acc = d.split3 ? (kb_acc_env > 0 ? kb_acc_env : 8) : p.num_kb;
-  // L2 prefetch measured no gain on B200 (the ring already hides the latency):
-  // off unless RTB_PREFETCH_KB asks for it.
+  // L2 prefetch measured no gain on B200 (the ring already hides the latency,
+  // also for the transposed skinny GEMM that streams B from DRAM: 2-16
+  // k-blocks ahead within 1%): off unless RTB_PREFETCH_KB asks for it.
   static const int pf_env = env_int("RTB_PREFETCH_KB", 0);
   p.prefetch_kb = pf_env > 0 ? pf_env : 0;
   p.split_trunc = trunc_split_enabled();
@@ -238,6 +248,7 @@ int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
   p.act = d.act;
   p.out_mode = d.out_mode;
   p.hw = d.hw;
+  p.row_bias = d.row_bias;
   p.peer_c = d.peer_c;
   p.npeers = d.npeers;
   p.col_off = d.col_off;
@@ -246,7 +257,8 @@ int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
   auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
   p.vec_ok = (d.out_mode == 0) && al16(d.C) && (d.ldc % 4 == 0) && (!d.bias || al16(d.bias)) &&
              (!d.residual || (al16(d.residual) && d.ldr % 4 == 0));
-  p.vec4_nchw = (d.out_mode == 1) && al16(d.C) && (!d.residual || al16(d.residual));
+  p.vec4_nchw = (d.out_mode == 1) && al16(d.C) && (!d.residual || al16(d.residual)) &&
+                (!d.row_bias || al16(d.row_bias));
   // Row-major C leaves through TMA stores when the tensor map can describe it.
   CUtensorMap tmC;
   std::memset(&tmC, 0, sizeof tmC);

@@ -15,7 +15,10 @@
 //            rows into the swizzled A tile, zero-filling padding taps
 // A operand modes: 0 = tiled TMA of a K-major matrix; 1 = cp.async im2col
 // gather (any Cp % 4 == 0); 2 = TMA im2col (Cp % 32 == 0: every k-block is one
-// filter tap x 32 channels, fetched by one bulk tensor copy per k-block).
+// filter tap x 32 channels, fetched by one bulk tensor copy per k-block);
+// 3 = multi-tap TMA im2col; 4 = tiled TMA of an MN-major matrix ([K, M]
+// row-major, 3xTF32 only: the converters read the unswizzled [32 k][128 m]
+// tile column-wise, so the MMAs never see its layout).
 // The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
 // of tile i overlaps the mainloop of tile i+1.
 //
@@ -70,6 +73,7 @@ struct GemmParams {
   int out_mode;          // 0: C[m*ldc+n]; 1: NCHW scatter, m=(img,pix), C[(img*N+n)*hw+pix];
                          // 2: every rank's C, peer_c[r][m*ldc + col_off + n] (N-split)
   int hw;                // Ho*Wo for out_mode 1
+  const float* row_bias; // out_mode 1: [M] bias per row (C^T of a skinny GEMM), or null
   int vec_ok;            // 16-byte aligned C/residual/bias with ldc, ldr % 4 == 0
   int c_tma;             // out_mode 0 with a TMA-storable C (tmC valid)
   int vec4_nchw;         // out_mode 1: C and residual 16-byte aligned
@@ -401,6 +405,9 @@ __device__ __forceinline__ void epilogue_nchw_chunk(const GemmParams& p, uint32_
       const float* rbase =
           p.residual ? p.residual + ((int64_t)img * p.N + n0) * p.hw + pix : nullptr;
       float* cbase = p.C + ((int64_t)img * p.N + n0) * p.hw + pix;
+      // per-row bias of the 4 rows (16-byte aligned: checked by the host)
+      const float4 rb = p.row_bias ? __ldg(reinterpret_cast<const float4*>(p.row_bias + m))
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
       for (int h = 0; h < 2; ++h) {  // two halves of 4 channels: loads, then stores
         float4 o[4];
@@ -410,6 +417,9 @@ __device__ __forceinline__ void epilogue_nchw_chunk(const GemmParams& p, uint32_
           o[k] = lds128(buf + (ch * kBM + 4 * q) * 4);
           const float bv = p.bias ? lds32(sb + ch * 4) : 0.0f;
           o[k].x += bv; o[k].y += bv; o[k].z += bv; o[k].w += bv;
+          if (p.row_bias) {
+            o[k].x += rb.x; o[k].y += rb.y; o[k].z += rb.z; o[k].w += rb.w;
+          }
           if (rbase && n0 + ch < p.N) {
             const float4 r4 = __ldg(reinterpret_cast<const float4*>(rbase + (int64_t)ch * p.hw));
             o[k].x += r4.x; o[k].y += r4.y; o[k].z += r4.z; o[k].w += r4.w;
@@ -429,12 +439,14 @@ __device__ __forceinline__ void epilogue_nchw_chunk(const GemmParams& p, uint32_
       const int l = et & 31;
       int64_t pb[4];
       bool pv[4];
+      float rbv[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int me = m0 + l + 32 * j;
         pv[j] = me < p.M;
         const int im = pv[j] ? me / p.hw : 0;
         pb[j] = pv[j] ? ((int64_t)im * p.N + n0) * p.hw + (me - im * p.hw) : 0;
+        rbv[j] = (pv[j] && p.row_bias) ? __ldg(p.row_bias + me) : 0.0f;
       }
 #pragma unroll 1
       for (int k = 0; k < 8; ++k) {
@@ -444,6 +456,10 @@ __device__ __forceinline__ void epilogue_nchw_chunk(const GemmParams& p, uint32_
         float sv[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) sv[j] = lds32(buf + (ch * kBM + l + 32 * j) * 4) + bv;
+        if (p.row_bias) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) sv[j] += rbv[j];
+        }
         if (p.residual) {
 #pragma unroll
           for (int j = 0; j < 4; ++j)
@@ -468,6 +484,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
   constexpr bool IM2COL = (A_MODE == 2 || A_MODE == 3);
   constexpr bool MULTITAP = (A_MODE == 3);
   static_assert(!MULTITAP || SPLIT, "multi-tap im2col tiles are read by the 3xTF32 converters");
+  static_assert(A_MODE != 4 || SPLIT, "MN-major A tiles are read by the 3xTF32 converters");
   using Cfg = GemmCfgFor<BN, SPLIT, A_MODE>;
   using Roles = GemmRoles<SPLIT, GATHER>;
   constexpr int S = Cfg::kStages;
@@ -590,6 +607,8 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
             if (A_MODE == 0) {
               tma_prefetch_2d(&tmA, kp * kBK, tm * kBM);
               if (B_MN == 0) tma_prefetch_2d(&tmB, kp * kBK, tn * BN);
+            } else if (A_MODE == 4) {
+              tma_prefetch_2d(&tmA, tm * kBM, kp * kBK);
             } else if (IM2COL && !MULTITAP) {
               const int k0 = kp * kBK, tap = k0 / p.Cp, rr = tap / p.S;
               tma_prefetch_im2col_4d(&tmA, k0 - tap * p.Cp, a_w, a_h, a_n,
@@ -598,6 +617,9 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
           }
           if (A_MODE == 0) {
             tma_load_2d(sA + s * kABytes, &tmA, &full_bar[s], kb * kBK, tm * kBM);
+          } else if (A_MODE == 4) {
+            // [32 k][128 m] box of the [K, M] matrix (m is the inner coordinate)
+            tma_load_2d(sA + s * kABytes, &tmA, &full_bar[s], tm * kBM, kb * kBK);
           } else if (MULTITAP) {
             // tap j of the k-block -> dense [128 pixels][Cp] block j of the A tile
             for (int j = 0; j < ntaps; ++j) {
@@ -1114,6 +1136,14 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
             if (4 * q < kvalid)
               av[q] = lds128(a0 + (q >> l) * (kBM * p.Cp * 4) + (((q & mask) ^ swz) << 4));
           }
+        } else if (A_MODE == 4) {
+          // MN-major tile: k-row k is 512 bytes (128 m values); this thread's
+          // row is one float of each, so a warp reads one 128-byte line per k
+          const uint32_t a0 = smem_u32(sA + s * kABytes) + row * 4;
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            av[j] = make_float4(lds32(a0 + (4 * j) * 512), lds32(a0 + (4 * j + 1) * 512),
+                                lds32(a0 + (4 * j + 2) * 512), lds32(a0 + (4 * j + 3) * 512));
         } else {
 #pragma unroll
           for (int j = 0; j < 8; ++j) av[j] = lds128(arow + ((j ^ (row & 7)) << 4));

@@ -41,6 +41,14 @@ int launch_prec(rtb_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB,
     if constexpr (SPLIT) return launch_variant<BN, SPLIT, 3, 0>(ctx, tmA, tmB, tmBlo, tmC, p, s);
     else return set_error(RTB_E_INVALID, "multi-tap im2col needs the 3xTF32 converters");
   }
+  if (d.a_mn_major) {
+    if constexpr (SPLIT) {
+      if (d.b_mn_major) return set_error(RTB_E_INVALID, "MN-major A takes a K-major B");
+      return launch_variant<BN, SPLIT, 4, 0>(ctx, tmA, tmB, tmBlo, tmC, p, s);
+    } else {
+      return set_error(RTB_E_INVALID, "MN-major A tiles need the 3xTF32 converters");
+    }
+  }
   if (d.b_mn_major) return launch_variant<BN, SPLIT, 0, 1>(ctx, tmA, tmB, tmBlo, tmC, p, s);
   return launch_variant<BN, SPLIT, 0, 0>(ctx, tmA, tmB, tmBlo, tmC, p, s);
 }

@@ -123,6 +123,13 @@ struct GemmDesc {
   int split3 = 1;     // 3xTF32 (1) or TF32 (0)
   int bn = 0;         // 0 = heuristic
   int allow_workspace = 1;  // 0: never allocate (tail balancing off)
+  // A given MN-major: [K, M] row-major with row stride lda (3xTF32, no conv
+  // producer; the converters read the tile transposed).  Used by the skinny
+  // GEMM's transposed form, whose A is the caller's [K,N] B.
+  int a_mn_major = 0;
+  // bias per row of C (out_mode 1 only): the transposed skinny GEMM's bias,
+  // which indexes the caller's columns
+  const float* row_bias = nullptr;
 };
 
 // Validated launch of the tcgen05 engine (A/B already TMA-compatible).
@@ -132,7 +139,8 @@ int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream);
 // CUDA cores with B streamed once from HBM (rtb_smallm.cu).  Measured on B200
 // for M x 8192 x 8192 (B row-major): 52.9 / 54.2 / 68.6 / 123.2 us at M = 1 /
 // 8 / 16 / 32 against 106.9-109.3 us for the 128-row tensor-core tile (M = 48,
-// 64), so rows beyond 16 go to the tensor cores.
+// 64) and 73-79 us for the tensor cores' transposed form (C^T = B^T . A^T,
+// which takes 72.5-78 us at M = 16), so rows beyond 16 go to the tensor cores.
 constexpr int64_t kSmallMMax = 16;
 int smallm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream);
 

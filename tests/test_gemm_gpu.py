@@ -543,3 +543,47 @@ def test_prepass_low_part_ragged(gpu, orc, n, k, trans_b):
     ref = np.maximum(pre, 0.0)
     assert orc.rel_frob(c, ref) <= TOL[0]
     assert _relu_pattern_ok(c, pre)
+
+
+@pytest.mark.parametrize("m", [17, 33, 64, 65, 100, 128])
+@pytest.mark.parametrize("n,k", [(2052, 300), (2051, 257), (4096, 1000)])
+@pytest.mark.parametrize("trans_b", [0, 1])
+def test_skinny_transposed_path(gpu, orc, m, n, k, trans_b):
+    """3xTF32 products of 17..128 rows against >= 2048 columns (K >= 256) run
+    as C^T = B^T . A^T: B's [K,N] storage read as an MN-major A operand (or
+    the Linear weight's [N,K] as a K-major one; N or K not a multiple of 4
+    packs it first), A as the narrow operand (64 columns up to 64 rows, else
+    128), the tile transposed on the way out and the bias added per row of
+    C^T.  Ragged N (a partial last 128-row tile) and K, bias + ReLU, against
+    float64."""
+    a = orc.normal((m, k), 11, 1)
+    w = orc.normal((n, k), 11, 2) if trans_b else orc.normal((k, n), 11, 2)
+    bm = w.T if trans_b else w
+    bias = orc.uniform((n,), 11, 3, -0.5, 0.5)
+    pre = orc.matmul_f64(a, np.ascontiguousarray(bm)) + bias.astype(np.float64)
+    bd = _dev(w).t() if trans_b else _dev(w)
+    y = _host(gpu.sgemm(_dev(a), bd, bias=_dev(bias), act=gpu.ACT_RELU, precision=0))
+    ref = np.maximum(pre, 0.0)
+    assert orc.rel_frob(y, ref) <= TOL[0]
+    scale = max(1.0, float(np.sqrt(np.mean(pre * pre))))
+    assert _relu_pattern_ok(y / scale, pre / scale)
+
+
+@pytest.mark.parametrize("pad", [4, 3])
+@pytest.mark.parametrize("act", [0, 2, 3])
+def test_skinny_transposed_strided_output(gpu, orc, pad, act):
+    """The transposed skinny path writing into a view of a wider buffer
+    (ldc = N + 4: 16-byte stores; ldc = N + 3: the element-wise stores),
+    no bias or sigmoid / tanh; the padding columns stay untouched."""
+    m, n, k = 48, 2304, 512
+    a = orc.normal((m, k), 12, 1)
+    b = orc.normal((k, n), 12, 2)
+    bias = orc.uniform((n,), 12, 3, -0.5, 0.5) if act else None
+    pre = orc.matmul_f64(a, b) + (bias.astype(np.float64) if act else 0.0)
+    buf = torch.full((m, n + pad), 7.0, device="cuda")
+    out = buf[:, :n]
+    gpu.sgemm(_dev(a), _dev(b), bias=_dev(bias) if act else None, act=act, out=out)
+    got = _host(buf)
+    ref = {0: pre, 2: 1.0 / (1.0 + np.exp(-pre)), 3: np.tanh(pre)}[act]
+    assert orc.rel_frob(got[:, :n], ref) <= TOL[0]
+    assert np.all(got[:, n:] == 7.0)
