@@ -323,6 +323,73 @@ __global__ void max_pool_nhwc4_kernel(const float4* __restrict__ x, float4* __re
   }
 }
 
+// 3x3 stride-2 NHWC max pool (ResNet's), C % 4 == 0: a thread owns one 4-channel
+// group of one output column and walks a strip of `rows` output rows.  Output
+// row oh reads input rows 2oh-ph .. 2oh-ph+2 and the next one starts at the
+// last of them, so each row's horizontal maximum over its three columns is
+// carried over: 6 float4 loads per output instead of 9.  Taking the maxima
+// of each row first, then over the rows in order, with the strict > and the
+// -inf start of ops::max_pool2d keeps its result bit for bit (the first
+// occurrence of the maximum in row-major window order; NaN never wins).
+__device__ __forceinline__ void max4_into(float4& m, const float4 v) {
+  if (v.x > m.x) m.x = v.x;
+  if (v.y > m.y) m.y = v.y;
+  if (v.z > m.z) m.z = v.z;
+  if (v.w > m.w) m.w = v.w;
+}
+
+__global__ void max_pool3s2_nhwc4_kernel(const float4* __restrict__ x, float4* __restrict__ y,
+                                         int N, int C4, int H, int W, int Ho, int Wo, int ph,
+                                         int pw, int rows) {
+  griddep_wait();  // launched with programmatic stream serialization
+  griddep_launch_dependents();
+  const int strips = (Ho + rows - 1) / rows;
+  const int64_t total = (int64_t)N * strips * Wo * C4;
+  const float4 ninf = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int c = (int)(i % C4);
+    int64_t t = i / C4;
+    const int ow = (int)(t % Wo);
+    t /= Wo;
+    const int strip = (int)(t % strips);
+    const int n = (int)(t / strips);
+    const int iw0 = 2 * ow - pw;
+    const bool v0 = iw0 >= 0 && iw0 < W, v1 = iw0 + 1 >= 0 && iw0 + 1 < W,
+               v2 = iw0 + 2 >= 0 && iw0 + 2 < W;
+    const float4* xn = x + (int64_t)n * H * W * C4 + c;
+    // the horizontal maximum of input row hh over the window's columns
+    auto hrow = [&](int hh) -> float4 {
+      float4 m = ninf;
+      if (hh < 0 || hh >= H) return m;
+      const float4* xr = xn + (int64_t)hh * W * C4;
+      float4 a = ninf, b = ninf, d = ninf;
+      if (v0) a = __ldg(xr + (int64_t)iw0 * C4);
+      if (v1) b = __ldg(xr + (int64_t)(iw0 + 1) * C4);
+      if (v2) d = __ldg(xr + (int64_t)(iw0 + 2) * C4);
+      if (v0) max4_into(m, a);
+      if (v1) max4_into(m, b);
+      if (v2) max4_into(m, d);
+      return m;
+    };
+    const int oh0 = strip * rows;
+    const int oh1 = oh0 + rows < Ho ? oh0 + rows : Ho;
+    float4 carry = hrow(2 * oh0 - ph);
+    float4* yo = y + ((int64_t)n * Ho * Wo + ow) * C4 + c;
+    for (int oh = oh0; oh < oh1; ++oh) {
+      const int r0 = 2 * oh - ph;
+      const float4 a = hrow(r0 + 1);
+      const float4 b = hrow(r0 + 2);
+      float4 m = ninf;
+      max4_into(m, carry);
+      max4_into(m, a);
+      max4_into(m, b);
+      yo[(int64_t)oh * Wo * C4] = m;
+      carry = b;
+    }
+  }
+}
+
 // Generic NHWC fallback (any C), one thread per output element.
 __global__ void max_pool_nhwc_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t N,
                                      int64_t C, int64_t H, int64_t W, int64_t Ho, int64_t Wo,
@@ -623,6 +690,21 @@ int launch_max_pool2d(const float* x, float* y, int64_t N, int64_t C, int64_t H,
     max_pool_nchw_kernel<<<grid_for(total), kThreads, 0, s>>>(x, y, N, C, H, W, Ho, Wo, (int)kh,
                                                              (int)kw, (int)sh, (int)sw, (int)ph,
                                                              (int)pw);
+  else if (C % 4 == 0 && kh == 3 && kw == 3 && sh == 2 && sw == 2 && N < INT32_MAX &&
+           H < INT32_MAX && W < INT32_MAX && C / 4 < INT32_MAX &&
+           (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0)
+  {
+    // strips of 8 output rows: ResNet-18's [256, 112, 112, 64] input gives
+    // 1.6M threads, several waves of the SMs
+    const int rows = 8;
+    const int64_t strips = (Ho + rows - 1) / rows;
+    cudaError_t e = launch_pdl(max_pool3s2_nhwc4_kernel,
+                               dim3(grid_for(N * strips * Wo * (C / 4))), dim3(kThreads), 0, s,
+                               reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(y),
+                               (int)N, (int)(C / 4), (int)H, (int)W, (int)Ho, (int)Wo, (int)ph,
+                               (int)pw, rows);
+    if (e != cudaSuccess) return cuda_status(e, "max_pool2d launch");
+  }
   else if (C % 4 == 0 && total / 4 < INT32_MAX && N * H * W * C < INT32_MAX * 4LL &&
            (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0)
   {

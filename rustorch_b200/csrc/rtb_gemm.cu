@@ -146,6 +146,8 @@ int gemm_run(rtb_ctx* ctx, const GemmDesc& d, cudaStream_t stream) {
   if (d.M <= 0 || d.N <= 0 || d.K <= 0) return set_error(RTB_E_INVALID, "gemm_run: empty problem");
   if (d.M > INT32_MAX || d.N > INT32_MAX || d.K > INT32_MAX)
     return set_error(RTB_E_UNSUPPORTED, "gemm_run: dimension exceeds 2^31-1");
+  if (d.gather == 3 && d.Cp != 8 && d.Cp != 16)
+    return set_error(RTB_E_INVALID, "gemm_run: multi-tap im2col takes 8 or 16 channels");
   if (d.a_mn_major && (!d.split3 || d.gather != 0))
     return set_error(RTB_E_INVALID, "gemm_run: an MN-major A needs 3xTF32 and no conv producer");
   if (d.row_bias && (d.out_mode != 1 || d.bias))

@@ -177,6 +177,26 @@ def test_max_pool_bit_exact(gpu, orc):
     np.testing.assert_array_equal(yh.transpose(0, 3, 1, 2), ref)
 
 
+@pytest.mark.parametrize("n,c,h,w,pad", [(3, 4, 13, 9, 1), (2, 12, 33, 34, 0), (1, 8, 14, 15, 1),
+                                          (2, 64, 112, 112, 1)])
+def test_max_pool_nhwc_3x3s2_bit_exact(gpu, orc, n, c, h, w, pad):
+    """The 3x3 stride-2 NHWC kernel (row maxima carried between output rows)
+    against ops::max_pool2d bit for bit: odd sizes, strips of 8 output rows
+    cut at 7 and 17 rows, ties between +0 and -0 (the first in window order
+    wins), NaN (never wins) and -inf inputs."""
+    x = orc.normal((n, c, h, w), 8, 3)
+    rng = np.random.default_rng(8)
+    special = np.array([0.0, -0.0, np.nan, -np.inf, 0.0, -0.0], np.float32)
+    mask = rng.random(x.shape) < 0.3
+    x[mask] = special[rng.integers(0, len(special), int(mask.sum()))]
+    x[0, 0, :, :] = rng.choice(np.array([0.0, -0.0], np.float32), (h, w))  # a plane of ties
+    ref = orc.max_pool2d(x, (3, 3), (2, 2), (pad, pad))
+    yh = _host(gpu.max_pool2d(_dev(x.transpose(0, 2, 3, 1)), padding=(pad, pad),
+                              layout=gpu.LAYOUT_NHWC))
+    got = np.ascontiguousarray(yh.transpose(0, 3, 1, 2))
+    np.testing.assert_array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
 def test_global_avg_pool(gpu, orc):
     x = orc.normal((4, 512, 7, 7), 8, 2)
     ref = orc.global_avg_pool(x)
