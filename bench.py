@@ -62,6 +62,7 @@ TRAFFIC = {
     "gemm1024": (8.48e6, "profiles/kernel_counters_gemm_conv.md"),
     "gemm8192": (5.228e9, "profiles/sgemm_8192_3xtf32.md"),
     "gemm_m16": (272.7e6, "profiles/sgemm_small_m16_8192.md"),
+    "gemm_m64": (277.7e6, "profiles/sgemm_skinny_m64_transposed.md"),
     "gemm_m256": (280.6e6, "profiles/kernel_counters_gemm_conv.md"),
     "mlp": (910.7e6, "profiles/kernel_counters_gemm_conv.md"),
     "linear_norm": (208.1e6, "profiles/linear_norm_relu_8192x1024x4096.md"),
@@ -69,11 +70,12 @@ TRAFFIC = {
 # Tensor-pipe activity of each workload's dominant kernel(s) as ncu counts it
 # (sm__pipe_tensor_cycles_active, % of elapsed cycles), from the named capture.
 TENSOR_PIPE = {
-    "resnet18": (0.485, "profiles/resnet18_fwd_launches.md"),
+    "resnet18": (0.488, "profiles/resnet18_fwd_launches.md"),
     "conv": (0.338, "profiles/conv2d_bias_relu_r50s2_3x3.md"),
     "conv_r50s4": (0.302, "profiles/kernel_counters_gemm_conv.md"),
     "gemm1024": (0.2015, "profiles/kernel_counters_gemm_conv.md"),
     "gemm8192": (0.747, "profiles/sgemm_8192_3xtf32.md"),
+    "gemm_m64": (0.289, "profiles/sgemm_skinny_m64_transposed.md"),
     "gemm_m256": (0.504, "profiles/kernel_counters_gemm_conv.md"),
     "mlp": (0.677, "profiles/kernel_counters_gemm_conv.md"),
     "linear_norm": (0.685, "profiles/linear_norm_relu_8192x1024x4096.md"),

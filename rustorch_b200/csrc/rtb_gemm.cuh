@@ -162,7 +162,7 @@ __device__ __forceinline__ void trace_stamp(const GemmParams& p, int slot) {
 // but its 256-column partial leaves TMEM room for one partial buffer only,
 // and the MMAs idling while the epilogue drains it cost more than the third
 // instruction per k-step: three N=128 MMAs, double-buffered partials.)
-template <int BN, bool SPLIT, bool BLO = false, bool HIS = false>
+template <int BN, bool SPLIT, bool BLO = false>
 struct GemmCfg {
   static constexpr int kBBytes = BN * kBK * 4;
   // TMEM: the partial-sum buffer(s); with 3xTF32 one fp32 running sum the
@@ -176,22 +176,10 @@ struct GemmCfg {
   // shared-memory plane of kAStages slots.
   static_assert(!BLO || SPLIT, "BLO is a 3xTF32 layout");
   static constexpr bool kWide = SPLIT && BN == 64;
-  // HIS (wide mode, A tile in the 128B-swizzled K-major layout): the hi.[B |
-  // B_lo] MMA reads A's hi part from the raw shared-memory tile (the tensor
-  // core truncates fp32 to TF32 itself), so a TMEM A stage holds only the lo
-  // part: twice the stages, twice the converters' lead over the MMAs.  Per
-  // k-block the shared-memory read port then carries 40 KB of MMA operands
-  // and 16 KB of converter reads (~440 clocks at 128 B/clock), under the
-  // mode's k-block time; a 128-column tile would need 96 KB and is not built
-  // this way.
-  static_assert(!HIS || kWide, "A's hi part from shared memory is a wide-mode layout");
-  static constexpr bool kHiSmem = HIS;
-  static constexpr int kAStageCols = HIS ? kBK : 2 * kBK;  // TMEM columns of one A stage
   static constexpr int kAccW = kWide ? 2 * BN : BN;  // TMEM columns of one partial buffer
   static constexpr int kAccCols = 2 * kAccW + (SPLIT ? BN : 0);
-  static constexpr int kAStagesRaw = SPLIT ? (512 - kAccCols) / kAStageCols : 0;
-  static constexpr int kAStagesMax = HIS ? 6 : 4;
-  static constexpr int kAStages = kAStagesRaw > kAStagesMax ? kAStagesMax : kAStagesRaw;
+  static constexpr int kAStagesRaw = SPLIT ? (512 - kAccCols) / (2 * kBK) : 0;
+  static constexpr int kAStages = kAStagesRaw > 4 ? 4 : kAStagesRaw;
   static constexpr bool kBloInStage = kWide || BLO;
   static constexpr int kBStage = kBloInStage ? 2 * kBBytes : kBBytes;  // B slot of a ring stage
   static constexpr int kBloBytes = (SPLIT && !kBloInStage) ? kAStages * kBBytes : 0;
@@ -208,7 +196,7 @@ struct GemmCfg {
   static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
   static constexpr int kSmemBytes =
       kStages * kStageBytes + kBloBytes + kOutBytes + kSmemReserve;
-  static constexpr int kTmemNeed = kAccCols + kAStages * kAStageCols;
+  static constexpr int kTmemNeed = kAccCols + kAStages * 2 * kBK;
   static constexpr int kTmemCols = kTmemNeed <= 128 ? 128 : (kTmemNeed <= 256 ? 256 : 512);
   static_assert(kTmemNeed <= 512, "TMEM holds 512 columns");
   static_assert(!SPLIT || kAStages >= 2, "3xTF32 needs BN <= 128 (two TMEM A stages)");
@@ -217,16 +205,10 @@ struct GemmCfg {
 };
 
 // The configuration a kernel variant uses: B_lo in the ring stage for every
-// 3xTF32 producer but the multi-tap im2col (whose tiles the converters read in
-// their own layout); in the wide mode, A's hi part read from shared memory
-// where the A tile is in the 128B-swizzled K-major layout (tiled TMA, cp.async
-// gather, one-tap TMA im2col).  The multi-tap tiles' 64B / 32B-swizzled tap
-// blocks could be read the same way (SWIZZLE_64B / 32B descriptors, blocks past
-// the last tap zeroed): measured on the ResNet-18 stem, no change in the
-// forward's time, so they keep both parts in TMEM.
+// 3xTF32 producer whose A tile is in the swizzled K-major layout (all but the
+// multi-tap im2col, whose tiles the converters read in their own layout).
 template <int BN, bool SPLIT, int A_MODE>
-using GemmCfgFor = GemmCfg<BN, SPLIT, SPLIT && A_MODE != 3,
-                           SPLIT && BN == 64 && (A_MODE == 0 || A_MODE == 1 || A_MODE == 2)>;
+using GemmCfgFor = GemmCfg<BN, SPLIT, SPLIT && A_MODE != 3>;
 
 template <bool SPLIT, bool GATHER>
 struct GemmRoles {  // GATHER: the cp.async im2col producer warps are present
@@ -727,18 +709,16 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
             next_ready = 0;
             if (lane == 0 && kb == u.kb0 && tj < kTraceTiles) trace_stamp(p, 3 + 6 * tj);
             tc_fence_after();
-            // cp.async-gathered A read by the tensor core (TF32 mode, or the
-            // wide mode's hi part): make the generic-proxy writes visible to
-            // the tensor core's async proxy.
-            if (GATHER && (!SPLIT || Cfg::kHiSmem)) fence_proxy_async_smem();
+            // cp.async-gathered A (TF32 mode has no converter pass): make the
+            // generic-proxy writes visible to the tensor core's async proxy.
+            if (GATHER && !SPLIT) fence_proxy_async_smem();
             const uint32_t a_addr = smem_u32(sA + s * kABytes);
             const uint32_t b_addr = smem_u32(sB + s * Cfg::kBStage);
             const uint32_t blo_addr =
                 Cfg::kBloInStage ? b_addr + (uint32_t)kBBytes : smem_u32(sBlo + ja * kBBytes);
-            // 3xTF32: A's hi / lo k-block in TMEM columns (lane 0 = tile row 0);
-            // kHiSmem: only the lo part, the hi part is the raw tile at a_addr
-            const uint32_t a_hi = tmem_base + (uint32_t)(Cfg::kAccCols + ja * Cfg::kAStageCols);
-            const uint32_t a_lo = a_hi + (uint32_t)(Cfg::kHiSmem ? 0 : kBK);
+            // 3xTF32: A's hi / lo k-block in TMEM columns (lane 0 = tile row 0)
+            const uint32_t a_hi = tmem_base + (uint32_t)(Cfg::kAccCols + ja * 2 * kBK);
+            const uint32_t a_lo = a_hi + (uint32_t)kBK;
 #pragma unroll
             for (int k = 0; k < kBK / 8; ++k) {
               if (k == kBK / 8 - 1 && lane == 0) next_ready = mbar_test_wait(ready_n, par_n);
@@ -752,12 +732,7 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
               if (Cfg::kWide) {
                 // one MMA of twice the tile width over [B | B_lo] (hi.hi and
                 // hi.lo side by side), then lo.hi into the hi.hi columns
-                if (Cfg::kHiSmem) {
-                  const uint64_t da = umma_desc(a_addr + k * 32, 16, 1024, kLayoutSW128);
-                  umma_tf32_e(d_tmem, da, db, idesc_w, acc);
-                } else {
-                  umma_tf32_ts_e(d_tmem, a_hi + k * 8, db, idesc_w, acc);
-                }
+                umma_tf32_ts_e(d_tmem, a_hi + k * 8, db, idesc_w, acc);
                 umma_tf32_ts_e(d_tmem, a_lo + k * 8, db, idesc, 1u);
               } else if (SPLIT) {
                 const uint64_t dbl =
@@ -1193,22 +1168,9 @@ __global__ void __launch_bounds__(GemmRoles<SPLIT, A_MODE == 1>::kThreads, 1)
             lo[4 * j + e] = __float_as_uint(x[e] - __uint_as_float(h));
           }
         }
-        const uint32_t t_a = t_lane + (uint32_t)(Cfg::kAccCols + ja * Cfg::kAStageCols);
-        if (Cfg::kHiSmem) {
-          // the MMA reads the hi part from the tile itself: written back in
-          // place only when it is not the raw value (round-to-nearest hi)
-          tmem_st_32x32b_x32(t_a, lo);
-          if (!p.split_trunc) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              sts128(arow + ((j ^ (row & 7)) << 4),
-                     make_float4(__uint_as_float(hi[4 * j]), __uint_as_float(hi[4 * j + 1]),
-                                 __uint_as_float(hi[4 * j + 2]), __uint_as_float(hi[4 * j + 3])));
-          }
-        } else {
-          tmem_st_32x32b_x32(t_a, hi);
-          tmem_st_32x32b_x32(t_a + (uint32_t)kBK, lo);
-        }
+        const uint32_t t_a = t_lane + (uint32_t)(Cfg::kAccCols + ja * 2 * kBK);
+        tmem_st_32x32b_x32(t_a, hi);
+        tmem_st_32x32b_x32(t_a + (uint32_t)kBK, lo);
         if (!b_conv) {
         } else if (p.split_trunc) {
 #pragma unroll

@@ -1,16 +1,13 @@
-"""The 64-column (wide) 3xTF32 mode reads A's hi part straight from the
-shared-memory tile where that tile is in the 128B-swizzled K-major layout
-(tiled TMA, cp.async gather, one-tap TMA im2col): the tensor core's own TF32
-truncation of the raw fp32 values, so only A's low part goes through TMEM.
-These tests cover what the parity suite does not:
+"""3xTF32 split modes beyond the parity suite's defaults:
 
-- the round-to-nearest hi (RTB_SPLIT_TRUNC=0, read once per process, hence a
-  subprocess), which the converters write back into the tile the MMA reads,
-  for every producer of that layout (the multi-tap tiles keep both parts in
-  TMEM and are checked alongside);
+- the round-to-nearest hi part (RTB_SPLIT_TRUNC=0, read once per process,
+  hence a subprocess) instead of the tensor core's own truncation, for every
+  A producer of the 64-column (wide) mode: tiled TMA, one-tap and multi-tap
+  TMA im2col, cp.async gather;
 - non-finite input pixels in convs whose last k-block holds fewer filter taps
-  than it has room for (multi-tap im2col, Cp = 8 and 16): outputs whose
-  window misses them stay finite and exact, as in the reference."""
+  than it has room for (multi-tap im2col, Cp = 8 and 16): the converters
+  zero the k columns past the last tap, so outputs whose window misses the
+  non-finite pixels stay finite and exact, as in the reference."""
 import os
 import subprocess
 import sys
@@ -90,9 +87,8 @@ print(repr(errs))
 
 
 def test_round_to_nearest_hi_written_back(gpu):
-    """RTB_SPLIT_TRUNC=0: the hi part is TF32 rounded to nearest, which the
-    converters write back into the shared-memory tile the MMA reads; every
-    producer of the wide mode within the 3xTF32 bound."""
+    """RTB_SPLIT_TRUNC=0: the hi part is TF32 rounded to nearest (lo = x - hi
+    exactly), every producer of the wide mode within the 3xTF32 bound."""
     env = dict(os.environ, RTB_SPLIT_TRUNC="0")
     r = subprocess.run([sys.executable, "-c", _RNA_SCRIPT, ROOT], env=env, capture_output=True,
                        text=True, timeout=300)
