@@ -1152,7 +1152,9 @@ def _time_graph_steps(torch, fn, steps, warmup, dev, dist=None):
     torch.cuda.current_stream(dev).wait_stream(side)
     torch.cuda.synchronize(dev)
     g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
+    # thread-local capture: other host threads (the process group's watchdog
+    # at N > 1) keep using CUDA while this thread captures
+    with torch.cuda.graph(g, capture_error_mode="thread_local"):
         for _ in range(steps):
             fn()
     torch.cuda.synchronize(dev)
